@@ -1,0 +1,444 @@
+#!/usr/bin/env python3
+"""Benchmark: Llama-70B-shaped Q4_0 decode on N B200s.
+
+One step = one generated token (batch 1) through the whole model: token embedding,
+80 decoder layers (fused Q4_0 dequant-matvecs, INT8-KV flash-decode attention),
+final RMSNorm + vocab matvec + greedy argmax, tensor-parallel over N GPUs with an
+NCCL all-reduce after o_proj and down_proj. Weights (39 GB) are synthetic
+N(0, 0.02), quantized to Q4_0 on the device; the INT8 KV cache is filled with
+N(0, 1) rows to ~3968 positions of a 4096 capacity, so decode runs at ~4K context.
+
+Reported on the same JSON line:
+  value      device-timed tokens/s (CUDA events, max over ranks; weights >> L2)
+  e2e        the same through ssd_model_decode_token: host token in (pinned H2D),
+             graph, next token out (D2H), synchronised every step
+  roofline   the dominant kernel (gate/up dequant-matvec + SwiGLU) timed alone on
+             the model's own layer weights, algorithmic bytes / event time
+  kernels    BASELINE config 0: Q4_0 4096x4096 matvec GB/s (32 rotating copies, 302 MB)
+  cpu_baseline  the oracle's restatement of the reference layer step on packed Q4_0
+             (src/inference/transformer.rs:283-399 with matvec_quantized_cpu), all host
+             cores, one layer timed and extrapolated to 80 layers + logits
+`--impl reference` times that CPU restatement alone (rank 0) and prints its line.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ssd-llm_b200"))
+sys.path.insert(0, ROOT)
+
+Q4_0 = 2
+CFG70B = dict(n_layers=80, n_embd=8192, n_head=64, n_head_kv=8, head_dim=128, n_ff=28672,
+              vocab=128256, wtype=Q4_0, out_type=Q4_0, embd_type=Q4_0, kv_capacity=4096,
+              theta=5e5, eps=1e-5)
+PROMPT = 3968
+Q40_BYTES = 18 / 32  # bytes per Q4_0 weight
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region (reads settings, changes none)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc:
+            return None
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                if int(p[0]) in self.gpus:
+                    rows.append(p)
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# -------------------------------------------------------------- CPU baseline
+def cpu_layer_inputs(cfg, seed=0):
+    """One 70B-shaped layer (packed Q4_0, reference layout) + an INT8 cache of PROMPT rows,
+    generated on the host (numpy + the oracle's quantizer)."""
+    import numpy as np
+    from oracle import oracle as ora
+    rng = np.random.default_rng(seed)
+    E, F, kvd = cfg["n_embd"], cfg["n_ff"], cfg["n_head_kv"] * cfg["head_dim"]
+    shapes = (("attn_q", (E, E)), ("attn_k", (kvd, E)), ("attn_v", (kvd, E)),
+              ("attn_output", (E, E)), ("ffn_gate", (F, E)), ("ffn_up", (F, E)),
+              ("ffn_down", (E, F)))
+    W = {}
+    for n, s in shapes:
+        w = rng.standard_normal(s, dtype=np.float32)
+        w *= np.float32(0.02)
+        W[n] = ora.quantize(w, ora.Q4_0)
+        del w
+    norms = [np.ones(E, np.float32), np.ones(E, np.float32)]
+    cap = cfg["kv_capacity"]
+    caches = []
+    for _ in range(2):
+        caches.append(rng.integers(-127, 128, (cap, kvd), dtype=np.int8))
+        caches.append((rng.random(cap, dtype=np.float32) * 0.03 + 0.01).astype(np.float32))
+    layer = ora.Layer(E, cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"], F, ora.Q4_0,
+                      *(W[n] for n, _ in shapes), *norms, theta=cfg["theta"], eps=cfg["eps"])
+    h = rng.standard_normal(E, dtype=np.float32)
+    return layer, caches, h
+
+
+def cpu_token_time(cfg, layer_samples, threads):
+    """Seconds per token of the restated reference CPU path: measured layer steps
+    (median) x n_layers + one measured vocab matvec (fused_rmsnorm_linear's matvec)."""
+    import numpy as np
+    from oracle import oracle as ora
+    layer, (kc, ks, vc, vs), h = cpu_layer_inputs(cfg)
+    t_layers = []
+    for _ in range(layer_samples):
+        hh = h.copy()
+        t0 = time.perf_counter()
+        layer.step(hh, PROMPT, kc, ks, vc, vs, mode=1, threads=threads)
+        t_layers.append(time.perf_counter() - t0)
+    rng = np.random.default_rng(1)
+    vocab_rows = 16032  # 1/8 of the vocab, scaled by 8 (bounded host memory and time)
+    wout = ora.quantize(rng.standard_normal((vocab_rows, cfg["n_embd"]), dtype=np.float32)
+                        * np.float32(0.02), ora.Q4_0)
+    t0 = time.perf_counter()
+    ora.matvec_quantized(wout, h, vocab_rows, cfg["n_embd"], ora.Q4_0, threads=threads)
+    t_logits = (time.perf_counter() - t0) * (cfg["vocab"] / vocab_rows)
+    t_layer = statistics.median(t_layers)
+    return cfg["n_layers"] * t_layer + t_logits, t_layers, t_logits
+
+
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    """--impl reference: the oracle port of the reference CPU path, rank 0 only."""
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    from oracle import oracle as ora
+    ora.build()
+    threads = os.cpu_count() or 1
+    cfg = dict(CFG70B)
+    t0 = time.perf_counter()
+    samples = max(1, args.steps)
+    t_tok, t_layers, t_logits = cpu_token_time(cfg, max(1, args.warmup) + samples, threads)
+    t_layers = t_layers[max(1, args.warmup):]
+    t_tok = cfg["n_layers"] * statistics.median(t_layers) + t_logits
+    value = 1.0 / t_tok
+    line = {
+        "impl": "reference", "metric": "decode tokens/s (Llama-70B-shape Q4_0, batch 1)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_tok * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama70b_q4_0_decode_b1", "n_layers": 80, "hidden": 8192,
+                   "heads": 64, "kv_heads": 8, "ffn": 28672, "vocab": 128256,
+                   "context": PROMPT, "kv": "int8"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "cpu": cpu_model_name(),
+                         "sample": f"{len(t_layers)} timed 70B-shape layer steps (packed Q4_0, "
+                                   f"INT8 KV at {PROMPT}) x 80 layers + vocab matvec; "
+                                   "extrapolated"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ CUDA arm
+def time_matvec_config0(ctx, torch, ssdllm, peak):
+    """Q4_0 4096x4096 matvec GB/s over 32 rotating weight copies
+    (302 MB > 2x L2), 64 launches per CUDA graph replay, with and without PDL."""
+    rows = cols = 4096
+    copies = [ssdllm.Weight.synth(ctx, Q4_0, 0, 900 + i, 0.02, cols, 0, rows, 0, cols)
+              for i in range(32)]
+    x = torch.randn(cols, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+    y = torch.zeros(rows, device="cuda")
+    res = {}
+    for pdl in (False, True):
+        ctx.set_pdl(pdl)
+        for w in copies[:2]:
+            ssdllm.matvec(ctx, w, x, y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(64):
+                ssdllm.matvec(ctx, copies[i % 32], x, y)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * 64)
+        alg = rows * cols * Q40_BYTES + cols * 4 + rows * 4
+        res["pdl" if pdl else "plain"] = {"us_per_launch": us, "gbs": alg / us / 1e3,
+                                          "frac_of_peak": alg / us / 1e3 / peak}
+        del g
+    ctx.set_pdl(False)
+    for w in copies:
+        w.free()
+    best = max(res.values(), key=lambda r: r["gbs"])
+    return {"shape": [rows, cols], "algorithmic_bytes": rows * cols * Q40_BYTES + cols * 8,
+            **{k: round(v, 3) if isinstance(v, float) else v for k, v in best.items()},
+            "variants": res}
+
+
+def time_dominant_kernel(ctx, model, torch, ssdllm, cfg, world):
+    """The fused gate/up + SwiGLU dequant-matvec on every layer's own weights, in layer
+    order (each launch reads a different 2 x ff_local x 8192 Q4_0 slab, never in L2)."""
+    E = cfg["n_embd"]
+    ff_local = cfg["n_ff"] // world
+    x = torch.randn(E, device="cuda")
+    act = torch.zeros(ff_local, device="cuda")
+    ws = [(model.weight("ffn_gate", l), model.weight("ffn_up", l), model.norm("ffn_norm", l))
+          for l in range(cfg["n_layers"])]
+
+    class _T:  # borrowed device pointer as a tensor-like for the binding
+        def __init__(self, p):
+            self.p = p
+
+        def data_ptr(self):
+            return self.p
+
+    ctx.set_pdl(True)
+    for wg, wu, nw in ws[:2]:
+        ssdllm.fused_swiglu(ctx, wg, wu, x, _T(nw), cfg["eps"], act)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for wg, wu, nw in ws:
+        ssdllm.fused_swiglu(ctx, wg, wu, x, _T(nw), cfg["eps"], act)
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.set_pdl(False)
+    us = e0.elapsed_time(e1) * 1e3 / len(ws)
+    alg = 2 * ff_local * E * Q40_BYTES + 2 * E * 4 + ff_local * 4
+    return us, alg
+
+
+def run_cuda(args):
+    import numpy as np  # noqa: F401
+    import torch
+    import torch.distributed as dist
+    import ssdllm
+
+    rank, world, local = env_rank()
+    assert world == args.gpus, f"WORLD_SIZE {world} != --gpus {args.gpus}"
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    peak, peak_src = measured_peaks()
+    cfg = dict(CFG70B)
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    ctx = ssdllm.Context(local)
+    model = ssdllm.Model(ctx, **cfg, tp_rank=rank, tp_size=world)
+    try:
+        if world > 1:
+            obj = [ssdllm.Model.unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            model.tp_init(obj[0])
+        t0 = time.perf_counter()
+        model.synth_weights(seed=0, std=0.02)
+        total = args.warmup + 2 * args.steps + 1
+        prompt = min(PROMPT, cfg["kv_capacity"] - total)
+        assert prompt > 0, "too many steps for the 4096-position cache"
+        model.synth_kv(seed=1, n=prompt)
+        setup_s = time.perf_counter() - t0
+        stream = torch.cuda.ExternalStream(ssdllm_stream(ctx, ssdllm))
+        model.decode_token(1, use_graph=True)  # capture the graph
+        for _ in range(args.warmup - 1):
+            model.decode_step(True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(list(range(world)) if rank == 0 else []) as clk:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                model.decode_step(True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+        ms = e0.elapsed_time(e1)
+        # e2e: host token in, host token out through the public API, every step
+        t = 5
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        f0.record(stream)
+        for _ in range(args.steps):
+            t = model.decode_token(t, use_graph=True)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = f0.elapsed_time(f1)
+        if world > 1:
+            tt = torch.tensor([ms, ms_e2e], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms, ms_e2e = float(tt[0]), float(tt[1])
+        launches = model.launches_per_step()
+        dom_us, dom_bytes = time_dominant_kernel(ctx, model, torch, ssdllm, cfg, world)
+        if world > 1:
+            tt = torch.tensor([dom_us], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            dom_us = float(tt[0])
+        k0 = time_matvec_config0(ctx, torch, ssdllm, peak) if rank == 0 else None
+        clocks = clk.summary() if rank == 0 else None
+    finally:
+        model.free()  # releases the graph holding NCCL calls before the process group
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as ora
+        ora.build()
+        threads = os.cpu_count() or 1
+        t_tok, t_layers, _ = cpu_token_time(cfg, 3, threads)
+        cpu = {"value": 1.0 / t_tok, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "cpu": cpu_model_name(),
+               "sample": f"{len(t_layers)} timed 70B-shape layer steps (packed Q4_0, INT8 KV "
+                         f"at {PROMPT}) x 80 layers + vocab matvec; extrapolated"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    tok_s = args.steps / (ms / 1e3)
+    dom_gbs = dom_bytes / dom_us / 1e3
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(f"swiglu_tp{world}")
+    line = {
+        "metric": "decode tokens/s (Llama-70B-shape Q4_0, batch 1)",
+        "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama70b_q4_0_decode_b1", "n_layers": cfg["n_layers"],
+                   "hidden": 8192, "heads": 64, "kv_heads": 8, "ffn": 28672,
+                   "vocab": 128256, "context": prompt, "kv": "int8", "tp": world,
+                   "l2": "not flushed: 39 GB of weights per token >> 126 MB L2",
+                   "weights_gb_per_gpu": round(weight_bytes(cfg) / world / 1e9, 2)},
+        "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "hbm", "kernel": "fused gate/up Q4_0 matvec + SwiGLU",
+                     "achieved": dom_gbs, "peak": peak, "peak_source": peak_src,
+                     "unit": "GB/s", "frac": dom_gbs / peak, "traffic": traffic,
+                     "us_per_launch": dom_us, "algorithmic_bytes": dom_bytes,
+                     "decode_weight_stream_gbs": weight_bytes(cfg) / world / (ms / args.steps)
+                     / 1e6},
+        "cpu_baseline": cpu,
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+        "kernels": {"q4_0_matvec_4096x4096": k0},
+        "setup_s": setup_s,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def weight_bytes(cfg):
+    E, F, V = cfg["n_embd"], cfg["n_ff"], cfg["vocab"]
+    kvd = cfg["n_head_kv"] * cfg["head_dim"]
+    per_layer = (2 * E * E + 2 * kvd * E + 3 * F * E) * Q40_BYTES
+    return cfg["n_layers"] * per_layer + V * E * Q40_BYTES
+
+
+def ssdllm_stream(ctx, ssdllm):
+    import ctypes
+    s = ctypes.c_void_p()
+    ssdllm.check(ssdllm.lib().ssd_ctx_stream(ctx.h, ctypes.byref(s)))
+    return s.value
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override n_layers (debug only; the headline uses 80)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 1:
+        args.warmup = 1
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_cuda(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

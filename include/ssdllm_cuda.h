@@ -1,0 +1,296 @@
+/*
+ * ssdllm_cuda.h — C ABI of the B200 (sm_100a) compute backend for ssd-llm.
+ *
+ * This is the drop-in boundary for ssd-llm's compute backend (`src/metal`): the
+ * operator surface that `src/inference` calls on `MetalCompute` / `MetalGpu`.
+ * Every entry point below names the reference interface it replaces
+ * (path:line inside quantumnic/ssd-llm). The Rust side binds these with an
+ * `extern "C"` block and keeps the `MetalCompute` method
+ * signatures.
+ *
+ * Conventions
+ *  - Every call returns an int status: SSD_OK (0) or one of SSD_ERR_*. No call
+ *    returns silent zeros for an unsupported type (the reference does,
+ *    src/metal/compute.rs:672-675); it returns SSD_ERR_TYPE instead.
+ *    ssd_last_error() gives a message for the calling thread's last failure.
+ *  - Pointers named *_dev are device pointers; `stream` is a cudaStream_t
+ *    (NULL = the context's own stream). Device-pointer calls are stream-ordered
+ *    and asynchronous; they allocate nothing on the hot path.
+ *  - Calls named *_host take host slices, copy in, compute, copy out and
+ *    synchronise: they keep the reference's synchronous semantics
+ *    (src/metal/gpu.rs:531-532).
+ *  - Weights are uploaded once (ssd_weight_upload) in the reference's GGUF block
+ *    layout and stay HBM-resident in a library-owned layout until freed.
+ *  - Quantized block layouts are the reference's own (not llama.cpp's): Q4_0
+ *    element 2j is the low nibble of byte j, 2j+1 the high nibble
+ *    (src/metal/compute.rs:693-699); Q4_K as src/metal/compute.rs:718-744.
+ */
+#ifndef SSDLLM_CUDA_H
+#define SSDLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SSD_ABI_VERSION 1
+
+/* status codes */
+#define SSD_OK 0
+#define SSD_ERR_ARG 1     /* null pointer, bad size */
+#define SSD_ERR_TYPE 2    /* unsupported GgmlType */
+#define SSD_ERR_SHAPE 3   /* dimensions inconsistent with the type's block size */
+#define SSD_ERR_CUDA 4    /* a CUDA runtime call failed */
+#define SSD_ERR_TIMEOUT 5 /* a bounded device-side wait gave up */
+#define SSD_ERR_NCCL 6    /* an NCCL call failed */
+#define SSD_ERR_NOMEM 7   /* device allocation failed */
+#define SSD_ERR_STATE 8   /* call out of order (e.g. engine not built) */
+
+/* GgmlType ids, src/model/gguf.rs:16-47 */
+#define SSD_TYPE_F32 0
+#define SSD_TYPE_F16 1
+#define SSD_TYPE_Q4_0 2
+#define SSD_TYPE_Q8_0 8
+#define SSD_TYPE_Q4_K 12
+
+typedef struct ssd_ctx ssd_ctx;
+typedef struct ssd_weight ssd_weight;
+typedef struct ssd_kv_cache ssd_kv_cache;
+typedef struct ssd_model ssd_model;
+
+/* ---------------------------------------------------------------- basics */
+int ssd_abi_version(void);
+const char* ssd_status_str(int status);
+/* Message of the calling thread's last failed call ("" if none). */
+const char* ssd_last_error(void);
+
+/* Context: one per device, owns a stream.
+ * Replaces MetalCompute::new (src/metal/compute.rs:47-72) and MetalGpu::new
+ * (src/metal/gpu.rs:73-160), which the reference constructs per forward pass
+ * and per token (src/inference/transformer.rs:301-302, :704). ssd_ctx_get()
+ * returns a process-wide cached context for the device, so per-token
+ * construction costs nothing; ssd_ctx_create() makes a private one. */
+int ssd_ctx_create(int device, ssd_ctx** out);
+int ssd_ctx_get(int device, ssd_ctx** out);
+int ssd_ctx_destroy(ssd_ctx* ctx);
+int ssd_ctx_stream(ssd_ctx* ctx, void** stream_out);
+int ssd_ctx_sync(ssd_ctx* ctx);
+/* Launch the context's standalone kernels (ssd_matvec and the fused matvecs) with
+ * programmatic dependent launch, so a kernel's weight prefetch overlaps the tail
+ * of the kernel before it on the same stream (default off). The decode engine
+ * always uses it. No reference counterpart (Metal commits each dispatch and waits,
+ * src/metal/gpu.rs:531-532). */
+int ssd_ctx_set_pdl(ssd_ctx* ctx, int on);
+/* Number of SMs and device name. No reference counterpart (reports only). */
+int ssd_ctx_info(ssd_ctx* ctx, int* num_sms, char* name, size_t name_len);
+/* Synchronous copies between host memory and device memory of the context. The
+ * reference copies every operand per call (src/metal/gpu.rs:499-505, :1253); here
+ * callers copy explicitly, once. */
+int ssd_copy_to_device(ssd_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes);
+int ssd_copy_to_host(ssd_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes);
+
+/* --------------------------------------------------------------- weights */
+/* Upload a [rows x cols] tensor given in the reference block layout.
+ * Replaces the per-call weight copies of MetalGpu (src/metal/gpu.rs:499-505,
+ * :770-785): the weight is uploaded once and stays HBM-resident.
+ * Supported: Q4_0, Q8_0, Q4_K, F32. cols must be a multiple of the block size. */
+int ssd_weight_upload(ssd_ctx* ctx, const void* host_raw, size_t bytes, int ggml_type, int rows,
+                      int cols, ssd_weight** out);
+/* Same as ssd_weight_upload (src/metal/gpu.rs:499-505), from a device buffer in the
+ * reference block layout (stream-ordered). */
+int ssd_weight_upload_device(ssd_ctx* ctx, const void* raw_dev, size_t bytes, int ggml_type,
+                             int rows, int cols, ssd_weight** out, void* stream);
+/* Copy the weight back in the reference block layout (host buffer of raw_bytes), free
+ * it, query it. No reference counterpart (the reference never keeps device weights). */
+int ssd_weight_download(ssd_ctx* ctx, const ssd_weight* w, void* host_raw, size_t bytes);
+int ssd_weight_free(ssd_weight* w);
+int ssd_weight_info(const ssd_weight* w, int* ggml_type, int* rows, int* cols,
+                    size_t* raw_bytes);
+/* Bytes of one row of `cols` elements in the reference layout (0 if unsupported). */
+size_t ssd_row_bytes(int ggml_type, int64_t cols);
+
+/* Synthetic weights for benchmarks: element (r, c) of a [total_rows x total_cols]
+ * matrix is N(0, std^2) drawn from a counter-based hash of (seed, tensor_id, r, c)
+ * and quantized per block with ssd_quantize's rules. The [row0, row0+rows) x
+ * [col0, col0+cols) window is materialised, so tensor-parallel shards are exact
+ * slices of the same global matrix. No reference counterpart (test inputs). */
+int ssd_weight_synth(ssd_ctx* ctx, int ggml_type, uint64_t seed, uint32_t tensor_id,
+                     float std_dev, int64_t total_cols, int row0, int rows, int col0, int cols,
+                     ssd_weight** out, void* stream);
+/* f32 N(mean, std^2) values of the same generator, row-major window.
+ * No reference counterpart (test and benchmark inputs). */
+int ssd_synth_f32(ssd_ctx* ctx, uint64_t seed, uint32_t tensor_id, float mean, float std_dev,
+                  int64_t total_cols, int row0, int rows, int col0, int cols, float* out_dev,
+                  void* stream);
+
+/* -------------------------------------------------- quantize / dequantize */
+/* f32 rows -> reference block layout (device). No reference counterpart: the
+ * reference ships no quantizer for these formats; this is the inverse of its
+ * decoders src/metal/compute.rs:680-750, :904-925 (builder's rule:
+ * Q4_0 d = m/-8 with m the signed value of largest magnitude; Q8_0 d = amax/127;
+ * Q4_K 6-bit scales/mins over 32-wide sub-blocks). */
+int ssd_quantize(ssd_ctx* ctx, const float* x_dev, int rows, int cols, int ggml_type,
+                 void* raw_out_dev, void* stream);
+/* Packed -> f32 [rows x cols], bit-exact with dequantize_to_f32
+ * (src/ssd/streamer.rs:93-180) and the Q4_K element formula of
+ * matvec_q4_k_cpu (src/metal/compute.rs:718-744). */
+int ssd_dequantize(ssd_ctx* ctx, const ssd_weight* w, float* out_dev, void* stream);
+
+/* ------------------------------------------------------------- matvecs */
+/* y = W x. Replaces MetalCompute::matvec_quantized (src/metal/compute.rs:157-191)
+ * and the matvec_q4_0 / matvec_q8_0 / matvec_q4_k Metal kernels
+ * (src/metal/shaders/kernels.metal:166-273, :575-604). */
+int ssd_matvec(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev, float* y_dev, void* stream);
+/* y = base + W x (base may alias y): matvec plus the residual add of
+ * src/inference/transformer.rs:369-371. */
+int ssd_matvec_residual(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev,
+                        const float* base_dev, float* y_dev, void* stream);
+/* logits = W rmsnorm(x, norm_w): MetalCompute::fused_rmsnorm_linear_f32
+ * (src/metal/compute.rs:348-372, CPU :557-577) with a quantized W. eps as given
+ * (the reference hard-codes 1e-5). */
+int ssd_fused_rmsnorm_matvec(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev,
+                             const float* norm_w_dev, float eps, float* y_dev, void* stream);
+/* Q,K,V = (Wq,Wk,Wv) rmsnorm(x) with RoPE on Q and K at `position`:
+ * MetalCompute::fused_qkv_rope_f32 (src/metal/compute.rs:296-326, CPU :509-529)
+ * with the attention pre-norm of transformer.rs:323-326 folded in when
+ * norm_w_dev is non-NULL. */
+int ssd_fused_qkv_rope(ssd_ctx* ctx, const ssd_weight* wq, const ssd_weight* wk,
+                       const ssd_weight* wv, const float* x_dev, const float* norm_w_dev,
+                       float eps, int head_dim, int position, float theta, float* q_dev,
+                       float* k_dev, float* v_dev, void* stream);
+/* act = silu(Wg n) * (Wu n), n = rmsnorm(x, norm_w) (or x when norm_w is NULL):
+ * the fused SwiGLU of MetalGpu::feed_forward_f32 (src/metal/gpu.rs:789-841,
+ * src/inference/feed_forward.rs:17-44). */
+int ssd_fused_swiglu(ssd_ctx* ctx, const ssd_weight* w_gate, const ssd_weight* w_up,
+                     const float* x_dev, const float* norm_w_dev, float eps, float* act_dev,
+                     void* stream);
+
+/* ------------------------------------------------------ elementwise ops */
+/* In-place RMSNorm: MetalCompute::rmsnorm_f32 (src/metal/compute.rs:193-202, :580-588). */
+int ssd_rmsnorm(ssd_ctx* ctx, float* x_dev, const float* w_dev, int n, float eps, void* stream);
+/* hidden += attn; out = rmsnorm(hidden, w): MetalCompute::fused_post_attn_norm_f32
+ * (src/metal/compute.rs:328-346, :536-555). */
+int ssd_fused_post_attn_norm(ssd_ctx* ctx, float* hidden_dev, const float* attn_dev,
+                             const float* w_dev, int n, float eps, float* out_dev, void* stream);
+/* In-place softmax: MetalCompute::softmax_f32 (src/metal/compute.rs:204-213, :604-620). */
+int ssd_softmax(ssd_ctx* ctx, float* x_dev, int n, void* stream);
+/* In-place multi-head RoPE (src/metal/compute.rs:482-506). */
+int ssd_rope(ssd_ctx* ctx, float* x_dev, int len, int head_dim, int n_heads, int position,
+             float theta, void* stream);
+/* In-place SiLU (src/metal/compute.rs:641-645). */
+int ssd_silu(ssd_ctx* ctx, float* x_dev, int n, void* stream);
+/* Greedy argmax, LAST index on ties (src/inference/sampler.rs:572-578). */
+int ssd_argmax(ssd_ctx* ctx, const float* v_dev, int n, int32_t* idx_dev, void* stream);
+
+/* ------------------------------------------------------ INT8 KV + attention */
+/* Device INT8 KV cache for one layer: K and V [capacity][kv_dim] int8 plus one
+ * f32 scale per (position, K or V) spanning all KV heads, as
+ * QuantizedLayerKvCache (src/inference/quantized_kv_cache.rs:88-130). */
+int ssd_kv_create(ssd_ctx* ctx, int capacity, int n_head_kv, int head_dim, ssd_kv_cache** out);
+int ssd_kv_free(ssd_kv_cache* kv);
+/* Device pointers of the cache arrays (QuantizedLayerKvCache's keys/values/scales,
+ * src/inference/quantized_kv_cache.rs:88-95), for tests and direct filling. */
+int ssd_kv_pointers(ssd_kv_cache* kv, int8_t** k_dev, int8_t** v_dev, float** k_scale_dev,
+                    float** v_scale_dev);
+/* Quantize k, v [kv_dim] into row `position`: QuantizedLayerKvCache::append
+ * (src/inference/quantized_kv_cache.rs:107-110) with QuantizedVec::quantize (:23-41),
+ * bit-exact. */
+int ssd_kv_append(ssd_ctx* ctx, ssd_kv_cache* kv, const float* k_dev, const float* v_dev,
+                  int position, void* stream);
+/* ssd_kv_append for `rows` consecutive positions from [rows][kv_dim] f32 (cache
+ * filling; src/inference/quantized_kv_cache.rs:107-110 per row). */
+int ssd_kv_append_rows(ssd_ctx* ctx, ssd_kv_cache* kv, const float* k_dev, const float* v_dev,
+                       int position, int rows, void* stream);
+/* Decode attention of q [n_head*head_dim] over cache positions [0, seq_len):
+ * MetalCompute::flash_attention_f32 (src/metal/compute.rs:217-258) over the INT8
+ * cache, with the math of flash_attention_cached
+ * (src/inference/flash_attention.rs:68-135): split-K online softmax, GQA
+ * kv_h = h / (n_head / n_head_kv). out [n_head*head_dim]. */
+int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev, int n_head,
+                       int seq_len, float* out_dev, void* stream);
+
+/* ------------------------------------------------- host-slice operators */
+/* MetalCompute::matvec_quantized (src/metal/compute.rs:157-191) with its exact
+ * signature semantics: raw weight bytes, x and y on the host; uploads, computes,
+ * downloads and synchronises. */
+int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, size_t w_bytes,
+                              const float* x, float* y, int out_dim, int in_dim, int ggml_type);
+
+/* ------------------------------------------------------- decode engine */
+/* Llama-shaped decoder with HBM-resident quantized weights, INT8 KV cache and
+ * optional row-sharded tensor parallelism. Replaces forward_pass / generate's
+ * per-token loop (src/inference/transformer.rs:283-399, :681-770).
+ * tp_size > 1 needs ssd_model_tp_init before building. */
+typedef struct {
+    int n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab;
+    int wtype;        /* layer weight type (Q4_0 / Q8_0 / Q4_K) */
+    int out_type;     /* output.weight type */
+    int embd_type;    /* token_embd type (F32 / Q4_0 / Q8_0) */
+    int kv_capacity;  /* INT8 KV positions */
+    float theta, eps;
+    int tp_rank, tp_size;
+} ssd_model_config;
+
+int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* cfg, ssd_model** out);
+/* The [row0, row0+nrows) x [col0, col0+ncols) slice of global tensor `name` that
+ * rank cfg->tp_rank keeps (host only, needs no device). Row-sharded: attn_q,
+ * ffn_gate, ffn_up, output; column-sharded: attn_output, ffn_down; replicated:
+ * attn_k, attn_v, token_embd. Replaces the row split of parallel_matvec
+ * (src/inference/tensor_parallel.rs:47-64), which only split rows. */
+int ssd_shard_range(const ssd_model_config* cfg, const char* name, int layer, int* row0,
+                    int* nrows, int* col0, int* ncols);
+int ssd_model_free(ssd_model* m);
+/* NCCL communicator for tensor parallelism: unique_id is the 128-byte
+ * ncclUniqueId rank 0 got from ssd_tp_unique_id and shared out of band. Replaces the
+ * thread spawn/join of src/inference/tensor_parallel.rs:69-103 (one process per GPU). */
+int ssd_tp_unique_id(uint8_t out[128]);
+int ssd_model_tp_init(ssd_model* m, const uint8_t unique_id[128]);
+/* Fill every weight with ssd_weight_synth (this rank's shard of the global tensors).
+ * No reference counterpart (benchmark inputs; the reference loads GGUF files). */
+int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_dev);
+/* Set one tensor from host data in the reference layout (full, unsharded tensor;
+ * the rank keeps its shard). name: attn_q, attn_k, attn_v, attn_output,
+ * ffn_gate, ffn_up, ffn_down, attn_norm, ffn_norm (layer >= 0) or token_embd,
+ * output_norm, output (layer = -1): the GGUF names of src/model/gguf.rs:410-416. */
+int ssd_model_set_tensor(ssd_model* m, const char* name, int layer, const void* host_raw,
+                         size_t bytes);
+/* Fill the KV cache of every layer at positions [0, n) (both K and V rows drawn
+ * N(0,1) by the synthetic generator, then INT8-quantized) and set the position.
+ * No reference counterpart (benchmark inputs). */
+int ssd_model_synth_kv(ssd_model* m, uint64_t seed, int n);
+/* Sequence position (the `position` argument of forward_pass,
+ * src/inference/transformer.rs:283-291); cache rows beyond it are ignored. */
+int ssd_model_set_position(ssd_model* m, int pos);
+int ssd_model_get_position(ssd_model* m, int* pos);
+/* One decode step (one iteration of generate's loop, src/inference/transformer.rs:681-770)
+ * from the token id in the model's device token slot: embed, all layers at the current
+ * position, final norm, logits, argmax -> next token in the slot; position += 1.
+ * Captured into a CUDA graph on first use when use_graph != 0. */
+int ssd_model_decode_step(ssd_model* m, int use_graph);
+/* Host token in, host token out: ssd_model_decode_step with the H2D and D2H copies
+ * (generate's embed -> forward_pass -> sample, src/inference/transformer.rs:732-770). */
+int ssd_model_decode_token(ssd_model* m, int32_t token_in, int32_t* token_out, int use_graph);
+/* Device pointers of the decode state: hidden [n_embd] (generate's hidden_state,
+ * src/inference/transformer.rs:637), logits [vocab/tp], token. */
+int ssd_model_state(ssd_model* m, float** hidden_dev, float** logits_dev, int32_t** token_dev);
+/* This rank's shard of a model tensor (names as ssd_model_set_tensor), owned by the
+ * model: for timing a layer's kernels in isolation. No reference counterpart. */
+int ssd_model_weight(ssd_model* m, const char* name, int layer, ssd_weight** out);
+/* Device pointer of a layer norm weight ("attn_norm", "ffn_norm") or "output_norm"
+ * (layer -1); the RMSNorm weights of src/inference/transformer.rs:323-357. */
+int ssd_model_norm(ssd_model* m, const char* name, int layer, float** out);
+/* The INT8 KV cache of one layer, all KV heads (QuantizedKvCache::layer,
+ * src/inference/quantized_kv_cache.rs:160-237). */
+int ssd_model_kv(ssd_model* m, int layer, ssd_kv_cache** out);
+/* One layer of forward_pass (src/inference/transformer.rs:312-394) on the model's
+ * hidden state at the current position (layer parity tests). */
+int ssd_model_layer_step(ssd_model* m, int layer);
+/* Kernel launches issued by one decode step. No reference counterpart (reports). */
+int ssd_model_launches_per_step(ssd_model* m, int* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SSDLLM_CUDA_H */

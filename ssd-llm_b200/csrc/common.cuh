@@ -1,0 +1,199 @@
+// common.cuh — shared definitions of the sm_100a backend (internal).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "../../include/ssdllm_cuda.h"
+
+namespace ssd {
+
+// --------------------------------------------------------------- errors
+void set_error(const char* fmt, ...);
+
+#define SSD_CK(call)                                                                  \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) {                                                      \
+            ::ssd::set_error("%s:%d %s: %s", __FILE__, __LINE__, #call,               \
+                             cudaGetErrorString(e_));                                 \
+            return SSD_ERR_CUDA;                                                      \
+        }                                                                             \
+    } while (0)
+
+#define SSD_REQ(cond, code, ...)                                                      \
+    do {                                                                              \
+        if (!(cond)) {                                                                \
+            ::ssd::set_error(__VA_ARGS__);                                            \
+            return (code);                                                            \
+        }                                                                             \
+    } while (0)
+
+#define SSD_TRY(expr)                                                                 \
+    do {                                                                              \
+        int s_ = (expr);                                                              \
+        if (s_ != SSD_OK) return s_;                                                  \
+    } while (0)
+
+// Checks the last launch error (async errors surface at the next sync).
+#define SSD_CK_LAUNCH() SSD_CK(cudaGetLastError())
+
+// ------------------------------------------------------------- handles
+}  // namespace ssd
+
+struct ssd_ctx {
+    int device = 0;
+    int num_sms = 0;
+    size_t smem_optin = 0;
+    char name[256] = {0};
+    cudaStream_t stream = nullptr;
+    bool cached = false;  // owned by the process-wide cache; destroy is a no-op
+    bool pdl = false;     // standalone launches use programmatic dependent launch
+    // Scratch for the host-slice operators and split-K attention partials.
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    unsigned long long* argmax_key = nullptr;  // 8-byte (value, index) slot
+};
+
+// Device layout of a quantized tensor (library-owned): structure of arrays so that
+// every lane's load is an aligned 16-byte vector and a warp reads contiguous bytes.
+//   Q4_0: qs = [rows][cols/32][16 B nibbles], meta = [rows][cols/32] f16 scales
+//   Q8_0: qs = [rows][cols/32][32 B int8],   meta = [rows][cols/32] f16 scales
+//   Q4_K: qs = [rows][cols/256][128 B],      meta = [rows][cols/256][16 B: d, dmin, 12 B sc]
+//   F32 : qs = [rows][cols] f32
+// The bytes are the reference's bytes, regrouped; nothing is re-quantized.
+struct ssd_weight {
+    ssd_ctx* ctx = nullptr;
+    int type = 0;
+    int rows = 0, cols = 0;
+    uint8_t* qs = nullptr;
+    uint8_t* meta = nullptr;
+    void* base = nullptr;  // allocation
+    size_t alloc_bytes = 0;
+};
+
+struct ssd_kv_cache {
+    ssd_ctx* ctx = nullptr;
+    int capacity = 0, n_head_kv = 0, head_dim = 0, kv_dim = 0;
+    int8_t* k = nullptr;
+    int8_t* v = nullptr;
+    float* k_scale = nullptr;
+    float* v_scale = nullptr;
+    void* base = nullptr;
+};
+
+namespace ssd {
+
+// ------------------------------------------------------ device helpers
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+// Byte-granular float construction: byte k of `lo` (which holds 0x80 | q) placed in
+// byte 2 under exponent byte 0x3F gives the float 1 + q/128 exactly.
+__device__ __forceinline__ float biased_nib(uint32_t lo, int k) {
+    return __uint_as_float(__byte_perm(lo, 0x3F000000u, 0x7044u | (k << 8)));
+}
+// 2^23 + byte k of `b` (an unsigned byte), exact.
+__device__ __forceinline__ float magic_byte(uint32_t b, int k) {
+    return __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7440u | k));
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+// Programmatic dependent launch: wait for the producer grid / let dependents launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Counter-based generator: splitmix64 finaliser of (seed, tensor, index).
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+// N(0,1) for element `idx` of tensor `tid` (Box-Muller on two 24-bit uniforms).
+__device__ __forceinline__ float synth_normal(uint64_t seed, uint32_t tid, uint64_t idx) {
+    uint64_t h = mix64(seed ^ mix64(((uint64_t)tid << 40) ^ idx));
+    float u1 = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    float u2 = (float)((uint32_t)(h >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ------------------------------------------------------------ host side
+inline int type_block(int type) {
+    switch (type) {
+        case SSD_TYPE_Q4_0:
+        case SSD_TYPE_Q8_0: return 32;
+        case SSD_TYPE_Q4_K: return 256;
+        case SSD_TYPE_F32:
+        case SSD_TYPE_F16: return 1;
+        default: return 0;
+    }
+}
+inline int type_block_bytes(int type) {
+    switch (type) {
+        case SSD_TYPE_Q4_0: return 18;
+        case SSD_TYPE_Q8_0: return 34;
+        case SSD_TYPE_Q4_K: return 144;
+        case SSD_TYPE_F32: return 4;
+        case SSD_TYPE_F16: return 2;
+        default: return 0;
+    }
+}
+
+inline cudaStream_t pick_stream(ssd_ctx* ctx, void* s) {
+    return s ? (cudaStream_t)s : ctx->stream;
+}
+
+int check_ctx(ssd_ctx* ctx);
+int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out);
+int ensure_scratch(ssd_ctx* ctx, size_t bytes);
+
+// Launch with the programmatic-stream-serialization attribute (PDL) so that the
+// kernel's pre-wait prologue (weight prefetch) overlaps the previous kernel's tail.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+}  // namespace ssd

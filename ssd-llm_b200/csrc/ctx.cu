@@ -1,0 +1,639 @@
+// ctx.cu — context, errors, HBM-resident weights, (de)quantization and synthetic inputs.
+//
+// Replaces MetalCompute::new / MetalGpu::new (src/metal/compute.rs:47-72,
+// src/metal/gpu.rs:73-160) and the streamer's dequantize_to_f32
+// (src/ssd/streamer.rs:93-180).
+#include <stdarg.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ssd {
+
+static thread_local char g_err[1024];
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int check_ctx(ssd_ctx* ctx) {
+    SSD_REQ(ctx != nullptr, SSD_ERR_ARG, "null context");
+    SSD_CK(cudaSetDevice(ctx->device));
+    return SSD_OK;
+}
+
+int ensure_scratch(ssd_ctx* ctx, size_t bytes) {
+    if (ctx->scratch_bytes >= bytes) return SSD_OK;
+    if (ctx->scratch) {
+        SSD_CK(cudaStreamSynchronize(ctx->stream));
+        SSD_CK(cudaFree(ctx->scratch));
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+    }
+    size_t b = bytes < (1u << 20) ? (1u << 20) : bytes;
+    if (cudaMalloc(&ctx->scratch, b) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("scratch allocation of %zu bytes failed", b);
+        return SSD_ERR_NOMEM;
+    }
+    ctx->scratch_bytes = b;
+    return SSD_OK;
+}
+
+// ----------------------------------------------------- layout kernels
+
+// Reference layout (AoS blocks) -> library layout (SoA). One thread per block.
+__global__ void k_repack(const uint8_t* __restrict__ raw, int type, int64_t nblocks,
+                         uint8_t* __restrict__ qs, uint8_t* __restrict__ meta) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    if (type == SSD_TYPE_Q4_0) {
+        const uint8_t* s = raw + i * 18;
+        uint8_t* d = qs + i * 16;
+#pragma unroll
+        for (int j = 0; j < 16; j++) d[j] = s[2 + j];
+        meta[2 * i] = s[0];
+        meta[2 * i + 1] = s[1];
+    } else if (type == SSD_TYPE_Q8_0) {
+        const uint8_t* s = raw + i * 34;
+        uint8_t* d = qs + i * 32;
+#pragma unroll
+        for (int j = 0; j < 32; j++) d[j] = s[2 + j];
+        meta[2 * i] = s[0];
+        meta[2 * i + 1] = s[1];
+    } else {  // Q4_K
+        const uint8_t* s = raw + i * 144;
+        uint8_t* d = qs + i * 128;
+#pragma unroll 8
+        for (int j = 0; j < 128; j++) d[j] = s[16 + j];
+#pragma unroll
+        for (int j = 0; j < 16; j++) meta[i * 16 + j] = s[j];
+    }
+}
+
+__global__ void k_unpack(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ meta, int type,
+                         int64_t nblocks, uint8_t* __restrict__ raw) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    if (type == SSD_TYPE_Q4_0) {
+        uint8_t* d = raw + i * 18;
+        d[0] = meta[2 * i];
+        d[1] = meta[2 * i + 1];
+        for (int j = 0; j < 16; j++) d[2 + j] = qs[i * 16 + j];
+    } else if (type == SSD_TYPE_Q8_0) {
+        uint8_t* d = raw + i * 34;
+        d[0] = meta[2 * i];
+        d[1] = meta[2 * i + 1];
+        for (int j = 0; j < 32; j++) d[2 + j] = qs[i * 32 + j];
+    } else {
+        uint8_t* d = raw + i * 144;
+        for (int j = 0; j < 16; j++) d[j] = meta[i * 16 + j];
+        for (int j = 0; j < 128; j++) d[16 + j] = qs[i * 128 + j];
+    }
+}
+
+// ------------------------------------------------------- quantizers
+// Builder's quantizers (the reference has none for these formats), exact inverses
+// of the reference decoders. Every float operation is an explicit round-to-nearest
+// intrinsic so the device result is bit-identical to the host restatement.
+
+__device__ void quant_block_q4_0(const float* x, uint8_t* nib16, uint16_t* d_out) {
+    float amax = 0.0f, m = 0.0f;
+    for (int j = 0; j < 32; j++) {
+        float a = fabsf(x[j]);
+        if (a > amax) {
+            amax = a;
+            m = x[j];
+        }
+    }
+    float d = __fdiv_rn(m, -8.0f);
+    float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    *d_out = __half_as_ushort(__float2half_rn(d));
+    for (int j = 0; j < 16; j++) {
+        int q0 = (int)floorf(__fadd_rn(__fmul_rn(x[2 * j], id), 8.5f));
+        int q1 = (int)floorf(__fadd_rn(__fmul_rn(x[2 * j + 1], id), 8.5f));
+        q0 = min(15, max(0, q0));
+        q1 = min(15, max(0, q1));
+        nib16[j] = (uint8_t)(q0 | (q1 << 4));
+    }
+}
+
+__device__ void quant_block_q8_0(const float* x, int8_t* q32, uint16_t* d_out) {
+    float amax = 0.0f;
+    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(x[j]));
+    float d = __fdiv_rn(amax, 127.0f);
+    float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    *d_out = __half_as_ushort(__float2half_rn(d));
+    for (int j = 0; j < 32; j++) {
+        int q = (int)roundf(__fmul_rn(x[j], id));
+        q32[j] = (int8_t)min(127, max(-127, q));
+    }
+}
+
+// Q4_K super-block: meta16 = f16 d, f16 dmin, 12 bytes of 6-bit (scale, min);
+// qs128 = 16 nibble bytes per 32-wide sub-block (element 2j = low nibble of byte j).
+__device__ void quant_block_q4_k(const float* x, uint8_t* meta16, uint8_t* qs128) {
+    float scale[8], mins[8], max_scale = 0.0f, max_min = 0.0f;
+    for (int s = 0; s < 8; s++) {
+        float lo = 0.0f, hi = 0.0f;
+        for (int j = 0; j < 32; j++) {
+            float v = x[s * 32 + j];
+            if (v < lo) lo = v;
+            if (v > hi) hi = v;
+        }
+        scale[s] = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
+        mins[s] = -lo;
+        if (scale[s] > max_scale) max_scale = scale[s];
+        if (mins[s] > max_min) max_min = mins[s];
+    }
+    __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
+    __half mh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
+    float d = __half2float(dh), dmin = __half2float(mh);
+    uint16_t db = __half_as_ushort(dh), mb = __half_as_ushort(mh);
+    meta16[0] = db & 0xFF;
+    meta16[1] = db >> 8;
+    meta16[2] = mb & 0xFF;
+    meta16[3] = mb >> 8;
+    uint8_t sc6[8], m6[8];
+    for (int s = 0; s < 8; s++) {
+        sc6[s] = (uint8_t)(d > 0.0f ? min(63, max(0, (int)roundf(__fdiv_rn(scale[s], d)))) : 0);
+        m6[s] = (uint8_t)(dmin > 0.0f ? min(63, max(0, (int)roundf(__fdiv_rn(mins[s], dmin)))) : 0);
+    }
+    uint8_t* sc = meta16 + 4;
+    for (int s = 0; s < 4; s++) {
+        sc[s] = (uint8_t)((sc6[s] & 0x3F) | ((sc6[s + 4] & 0x3) << 6));
+        sc[s + 4] = (uint8_t)((m6[s] & 0x3F) | ((m6[s + 4] & 0x3) << 6));
+        sc[s + 8] = (uint8_t)((sc6[s + 4] >> 2) | ((m6[s + 4] >> 2) << 4));
+    }
+    for (int s = 0; s < 8; s++) {
+        float es = __fmul_rn(d, (float)sc6[s]);
+        float em = __fmul_rn(dmin, (float)m6[s]);
+        for (int j = 0; j < 16; j++) {
+            int q0 = 0, q1 = 0;
+            if (es > 0.0f) {
+                q0 = min(15, max(0, (int)roundf(__fdiv_rn(__fadd_rn(x[s * 32 + 2 * j], em), es))));
+                q1 = min(15, max(0, (int)roundf(__fdiv_rn(__fadd_rn(x[s * 32 + 2 * j + 1], em), es))));
+            }
+            qs128[s * 16 + j] = (uint8_t)(q0 | (q1 << 4));
+        }
+    }
+}
+
+// f32 rows -> reference block layout.
+__global__ void k_quantize_raw(const float* __restrict__ x, int type, int64_t nblocks,
+                               uint8_t* __restrict__ raw) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    if (type == SSD_TYPE_Q4_0) {
+        uint8_t* o = raw + i * 18;
+        uint16_t d;
+        uint8_t nib[16];
+        quant_block_q4_0(x + i * 32, nib, &d);
+        o[0] = d & 0xFF;
+        o[1] = d >> 8;
+        for (int j = 0; j < 16; j++) o[2 + j] = nib[j];
+    } else if (type == SSD_TYPE_Q8_0) {
+        uint8_t* o = raw + i * 34;
+        uint16_t d;
+        int8_t q[32];
+        quant_block_q8_0(x + i * 32, q, &d);
+        o[0] = d & 0xFF;
+        o[1] = d >> 8;
+        for (int j = 0; j < 32; j++) o[2 + j] = (uint8_t)q[j];
+    } else {
+        uint8_t* o = raw + i * 144;
+        quant_block_q4_k(x + i * 256, o, o + 16);
+    }
+}
+
+// Synthetic N(0, std^2) weights, generated and quantized straight into the
+// library layout. Block i of the window -> global (row, col) -> hashed normals.
+__global__ void k_synth_weight(int type, uint64_t seed, uint32_t tid, float std_dev,
+                               int64_t total_cols, int row0, int rows, int col0, int cols,
+                               uint8_t* __restrict__ qs, uint8_t* __restrict__ meta) {
+    int bs = (type == SSD_TYPE_Q4_K) ? 256 : 32;
+    int64_t bpr = cols / bs;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * bpr) return;
+    int64_t r = i / bpr, b = i % bpr;
+    uint64_t base = (uint64_t)(row0 + r) * (uint64_t)total_cols + (uint64_t)(col0 + b * bs);
+    float x[256];
+    for (int j = 0; j < bs; j++) x[j] = __fmul_rn(synth_normal(seed, tid, base + j), std_dev);
+    if (type == SSD_TYPE_Q4_0) {
+        uint16_t d;
+        uint8_t nib[16];
+        quant_block_q4_0(x, nib, &d);
+        uint4 v;
+        memcpy(&v, nib, 16);
+        reinterpret_cast<uint4*>(qs)[i] = v;
+        reinterpret_cast<uint16_t*>(meta)[i] = d;
+    } else if (type == SSD_TYPE_Q8_0) {
+        uint16_t d;
+        int8_t q[32];
+        quant_block_q8_0(x, q, &d);
+        uint4 v[2];
+        memcpy(v, q, 32);
+        reinterpret_cast<uint4*>(qs)[2 * i] = v[0];
+        reinterpret_cast<uint4*>(qs)[2 * i + 1] = v[1];
+        reinterpret_cast<uint16_t*>(meta)[i] = d;
+    } else {
+        quant_block_q4_k(x, meta + i * 16, qs + i * 128);
+    }
+}
+
+__global__ void k_synth_f32(uint64_t seed, uint32_t tid, float mean, float std_dev,
+                            int64_t total_cols, int row0, int rows, int col0, int cols,
+                            float* __restrict__ out) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * cols) return;
+    int64_t r = i / cols, c = i % cols;
+    uint64_t idx = (uint64_t)(row0 + r) * (uint64_t)total_cols + (uint64_t)(col0 + c);
+    out[i] = __fadd_rn(__fmul_rn(synth_normal(seed, tid, idx), std_dev), mean);
+}
+
+// ----------------------------------------------------------- dequant
+// Bit-exact with src/ssd/streamer.rs:128-180 (q as f32 * scale, one rounding) and
+// the Q4_K element formula src/metal/compute.rs:735-741 (two roundings, no FMA).
+__global__ void k_dequant(const ssd_weight w, float* __restrict__ out) {
+    int64_t n = (int64_t)w.rows * w.cols;
+    int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;  // 8 elements
+    if (e0 >= n) return;
+    float v[8];
+    if (w.type == SSD_TYPE_F32) {
+        for (int t = 0; t < 8; t++) v[t] = reinterpret_cast<const float*>(w.qs)[e0 + t];
+    } else if (w.type == SSD_TYPE_Q4_0) {
+        int64_t blk = e0 / 32;
+        int j0 = (int)(e0 % 32) / 2;  // byte index
+        float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
+        const uint8_t* q = w.qs + blk * 16 + j0;
+        for (int t = 0; t < 4; t++) {
+            v[2 * t] = __fmul_rn((float)((int)(q[t] & 0x0F) - 8), s);
+            v[2 * t + 1] = __fmul_rn((float)((int)(q[t] >> 4) - 8), s);
+        }
+    } else if (w.type == SSD_TYPE_Q8_0) {
+        int64_t blk = e0 / 32;
+        float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
+        const int8_t* q = reinterpret_cast<const int8_t*>(w.qs) + e0;
+        for (int t = 0; t < 8; t++) v[t] = __fmul_rn((float)q[t], s);
+    } else {  // Q4_K
+        int64_t sbk = e0 / 256;
+        int within = (int)(e0 % 256);
+        int sb = within / 32, j0 = (within % 32) / 2;
+        const uint8_t* m = w.meta + sbk * 16;
+        float d = f16_bits_to_f32((uint16_t)(m[0] | (m[1] << 8)));
+        float dmin = f16_bits_to_f32((uint16_t)(m[2] | (m[3] << 8)));
+        const uint8_t* sc = m + 4;
+        int s6, m6;
+        if (sb < 4) {
+            s6 = sc[sb] & 0x3F;
+            m6 = sc[sb + 4] & 0x3F;
+        } else {
+            s6 = (sc[sb - 4] >> 6) | ((sc[sb + 4] & 0x0F) << 2);
+            m6 = (sc[sb] >> 6) | ((sc[sb + 4] >> 4) << 2);
+        }
+        float scale = __fmul_rn(d, (float)s6), mn = __fmul_rn(dmin, (float)m6);
+        const uint8_t* q = w.qs + sbk * 128 + sb * 16 + j0;
+        for (int t = 0; t < 4; t++) {
+            v[2 * t] = __fsub_rn(__fmul_rn(scale, (float)(q[t] & 0x0F)), mn);
+            v[2 * t + 1] = __fsub_rn(__fmul_rn(scale, (float)(q[t] >> 4)), mn);
+        }
+    }
+    for (int t = 0; t < 8; t++) out[e0 + t] = v[t];
+}
+
+static std::mutex g_ctx_mu;
+static ssd_ctx* g_ctx_cache[64] = {nullptr};
+
+}  // namespace ssd
+
+using namespace ssd;
+
+// =============================================================== C ABI
+
+extern "C" int ssd_abi_version(void) { return SSD_ABI_VERSION; }
+
+extern "C" const char* ssd_status_str(int s) {
+    switch (s) {
+        case SSD_OK: return "ok";
+        case SSD_ERR_ARG: return "invalid argument";
+        case SSD_ERR_TYPE: return "unsupported ggml type";
+        case SSD_ERR_SHAPE: return "shape mismatch";
+        case SSD_ERR_CUDA: return "CUDA error";
+        case SSD_ERR_TIMEOUT: return "device wait timed out";
+        case SSD_ERR_NCCL: return "NCCL error";
+        case SSD_ERR_NOMEM: return "out of device memory";
+        case SSD_ERR_STATE: return "invalid state";
+        default: return "unknown status";
+    }
+}
+
+extern "C" const char* ssd_last_error(void) { return g_err; }
+
+extern "C" int ssd_ctx_create(int device, ssd_ctx** out) {
+    SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
+    int n = 0;
+    SSD_CK(cudaGetDeviceCount(&n));
+    SSD_REQ(device >= 0 && device < n, SSD_ERR_ARG, "device %d out of range (%d)", device, n);
+    SSD_CK(cudaSetDevice(device));
+    cudaDeviceProp p;
+    SSD_CK(cudaGetDeviceProperties(&p, device));
+    SSD_REQ(p.major >= 10, SSD_ERR_ARG, "device %d is sm_%d%d; this library is built for sm_100a",
+            device, p.major, p.minor);
+    ssd_ctx* c = new ssd_ctx();
+    c->device = device;
+    c->num_sms = p.multiProcessorCount;
+    c->smem_optin = p.sharedMemPerBlockOptin;
+    snprintf(c->name, sizeof(c->name), "%s", p.name);
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&c->argmax_key, 64) != cudaSuccess) {
+        set_error("context setup failed: %s", cudaGetErrorString(cudaGetLastError()));
+        delete c;
+        return SSD_ERR_CUDA;
+    }
+    *out = c;
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_get(int device, ssd_ctx** out) {
+    SSD_REQ(out != nullptr && device >= 0 && device < 64, SSD_ERR_ARG, "bad device/out");
+    std::lock_guard<std::mutex> lk(g_ctx_mu);
+    if (!g_ctx_cache[device]) {
+        ssd_ctx* c = nullptr;
+        SSD_TRY(ssd_ctx_create(device, &c));
+        c->cached = true;
+        g_ctx_cache[device] = c;
+    }
+    *out = g_ctx_cache[device];
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_destroy(ssd_ctx* ctx) {
+    if (!ctx || ctx->cached) return SSD_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->argmax_key) cudaFree(ctx->argmax_key);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_stream(ssd_ctx* ctx, void** s) {
+    SSD_REQ(ctx && s, SSD_ERR_ARG, "null arg");
+    *s = (void*)ctx->stream;
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_sync(ssd_ctx* ctx) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_CK(cudaStreamSynchronize(ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_set_pdl(ssd_ctx* ctx, int on) {
+    SSD_REQ(ctx != nullptr, SSD_ERR_ARG, "null ctx");
+    ctx->pdl = on != 0;
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_info(ssd_ctx* ctx, int* num_sms, char* name, size_t name_len) {
+    SSD_REQ(ctx != nullptr, SSD_ERR_ARG, "null ctx");
+    if (num_sms) *num_sms = ctx->num_sms;
+    if (name && name_len) snprintf(name, name_len, "%s", ctx->name);
+    return SSD_OK;
+}
+
+extern "C" int ssd_copy_to_device(ssd_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(dst && src, SSD_ERR_ARG, "null pointer");
+    SSD_CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    SSD_CK(cudaStreamSynchronize(ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_copy_to_host(ssd_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(dst && src, SSD_ERR_ARG, "null pointer");
+    SSD_CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    SSD_CK(cudaStreamSynchronize(ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" size_t ssd_row_bytes(int type, int64_t cols) {
+    int bs = type_block(type);
+    if (!bs || cols % bs) return 0;
+    return (size_t)(cols / bs) * (size_t)type_block_bytes(type);
+}
+
+namespace ssd {
+int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
+    SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
+    SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
+                type == SSD_TYPE_F32,
+            SSD_ERR_TYPE, "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, F32=0)", type);
+    SSD_REQ(rows > 0 && cols > 0, SSD_ERR_SHAPE, "empty tensor %dx%d", rows, cols);
+    int bs = type_block(type);
+    SSD_REQ(cols % bs == 0, SSD_ERR_SHAPE, "cols %d not a multiple of block %d", cols, bs);
+    int64_t nb = (int64_t)rows * (cols / bs);
+    size_t qs_bytes, meta_bytes;
+    if (type == SSD_TYPE_Q4_0) {
+        qs_bytes = nb * 16;
+        meta_bytes = nb * 2;
+    } else if (type == SSD_TYPE_Q8_0) {
+        qs_bytes = nb * 32;
+        meta_bytes = nb * 2;
+    } else if (type == SSD_TYPE_Q4_K) {
+        qs_bytes = nb * 128;
+        meta_bytes = nb * 16;
+    } else {
+        qs_bytes = (size_t)rows * cols * 4;
+        meta_bytes = 0;
+    }
+    size_t qs_pad = (qs_bytes + 255) & ~(size_t)255;
+    size_t total = qs_pad + meta_bytes + 256;
+    void* p = nullptr;
+    if (cudaMalloc(&p, total) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("weight allocation of %zu bytes failed", total);
+        return SSD_ERR_NOMEM;
+    }
+    ssd_weight* w = new ssd_weight();
+    w->ctx = ctx;
+    w->type = type;
+    w->rows = rows;
+    w->cols = cols;
+    w->base = p;
+    w->alloc_bytes = total;
+    w->qs = (uint8_t*)p;
+    w->meta = meta_bytes ? (uint8_t*)p + qs_pad : nullptr;
+    *out = w;
+    return SSD_OK;
+}
+}  // namespace ssd
+
+extern "C" int ssd_weight_upload_device(ssd_ctx* ctx, const void* raw_dev, size_t bytes, int type,
+                                        int rows, int cols, ssd_weight** out, void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(raw_dev != nullptr, SSD_ERR_ARG, "null raw pointer");
+    size_t need = ssd_row_bytes(type, cols) * (size_t)rows;
+    SSD_REQ(type_block(type) != 0, SSD_ERR_TYPE, "ggml type %d not supported", type);
+    SSD_REQ(need != 0 && bytes == need, SSD_ERR_SHAPE,
+            "got %zu bytes, %dx%d of type %d needs %zu", bytes, rows, cols, type, need);
+    ssd_weight* w = nullptr;
+    SSD_TRY(alloc_weight(ctx, type, rows, cols, &w));
+    cudaStream_t s = pick_stream(ctx, stream);
+    if (type == SSD_TYPE_F32) {
+        if (cudaMemcpyAsync(w->qs, raw_dev, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+            ssd_weight_free(w);
+            SSD_CK(cudaGetLastError());
+        }
+    } else {
+        int64_t nb = (int64_t)rows * (cols / type_block(type));
+        k_repack<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>((const uint8_t*)raw_dev, type, nb,
+                                                              w->qs, w->meta);
+        if (cudaGetLastError() != cudaSuccess) {
+            ssd_weight_free(w);
+            set_error("repack launch failed");
+            return SSD_ERR_CUDA;
+        }
+    }
+    *out = w;
+    return SSD_OK;
+}
+
+extern "C" int ssd_weight_upload(ssd_ctx* ctx, const void* host_raw, size_t bytes, int type,
+                                 int rows, int cols, ssd_weight** out) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(host_raw != nullptr && out != nullptr, SSD_ERR_ARG, "null argument");
+    size_t need = ssd_row_bytes(type, cols) * (size_t)rows;
+    SSD_REQ(type_block(type) != 0, SSD_ERR_TYPE, "ggml type %d not supported", type);
+    SSD_REQ(need != 0 && bytes == need, SSD_ERR_SHAPE,
+            "got %zu bytes, %dx%d of type %d needs %zu", bytes, rows, cols, type, need);
+    void* staging = nullptr;
+    if (cudaMalloc(&staging, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("staging allocation of %zu bytes failed", bytes);
+        return SSD_ERR_NOMEM;
+    }
+    int st = SSD_OK;
+    if (cudaMemcpyAsync(staging, host_raw, bytes, cudaMemcpyHostToDevice, ctx->stream) !=
+        cudaSuccess) {
+        set_error("upload copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+        st = SSD_ERR_CUDA;
+    }
+    if (st == SSD_OK) st = ssd_weight_upload_device(ctx, staging, bytes, type, rows, cols, out, nullptr);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(staging);
+    return st;
+}
+
+extern "C" int ssd_weight_download(ssd_ctx* ctx, const ssd_weight* w, void* host_raw,
+                                   size_t bytes) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(w && host_raw, SSD_ERR_ARG, "null argument");
+    size_t need = ssd_row_bytes(w->type, w->cols) * (size_t)w->rows;
+    SSD_REQ(bytes == need, SSD_ERR_SHAPE, "need %zu bytes, got %zu", need, bytes);
+    if (w->type == SSD_TYPE_F32) {
+        SSD_CK(cudaMemcpy(host_raw, w->qs, bytes, cudaMemcpyDeviceToHost));
+        return SSD_OK;
+    }
+    void* staging = nullptr;
+    SSD_CK(cudaMalloc(&staging, bytes));
+    int64_t nb = (int64_t)w->rows * (w->cols / type_block(w->type));
+    k_unpack<<<(unsigned)((nb + 255) / 256), 256, 0, ctx->stream>>>(w->qs, w->meta, w->type, nb,
+                                                                    (uint8_t*)staging);
+    cudaError_t e = cudaMemcpyAsync(host_raw, staging, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(staging);
+    SSD_CK(e);
+    return SSD_OK;
+}
+
+extern "C" int ssd_weight_free(ssd_weight* w) {
+    if (!w) return SSD_OK;
+    if (w->base) {
+        cudaSetDevice(w->ctx->device);
+        cudaFree(w->base);
+    }
+    delete w;
+    return SSD_OK;
+}
+
+extern "C" int ssd_weight_info(const ssd_weight* w, int* type, int* rows, int* cols,
+                               size_t* raw_bytes) {
+    SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
+    if (type) *type = w->type;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (raw_bytes) *raw_bytes = ssd_row_bytes(w->type, w->cols) * (size_t)w->rows;
+    return SSD_OK;
+}
+
+extern "C" int ssd_weight_synth(ssd_ctx* ctx, int type, uint64_t seed, uint32_t tensor_id,
+                                float std_dev, int64_t total_cols, int row0, int rows, int col0,
+                                int cols, ssd_weight** out, void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K, SSD_ERR_TYPE,
+            "synthetic weights support Q4_0/Q8_0/Q4_K, not %d", type);
+    int bs = type_block(type);
+    SSD_REQ(col0 % bs == 0 && cols % bs == 0 && col0 + cols <= total_cols && row0 >= 0,
+            SSD_ERR_SHAPE, "window not block aligned");
+    ssd_weight* w = nullptr;
+    SSD_TRY(alloc_weight(ctx, type, rows, cols, &w));
+    int64_t nb = (int64_t)rows * (cols / bs);
+    cudaStream_t s = pick_stream(ctx, stream);
+    int threads = type == SSD_TYPE_Q4_K ? 64 : 128;
+    k_synth_weight<<<(unsigned)((nb + threads - 1) / threads), threads, 0, s>>>(
+        type, seed, tensor_id, std_dev, total_cols, row0, rows, col0, cols, w->qs, w->meta);
+    if (cudaGetLastError() != cudaSuccess) {
+        ssd_weight_free(w);
+        set_error("synth launch failed");
+        return SSD_ERR_CUDA;
+    }
+    *out = w;
+    return SSD_OK;
+}
+
+extern "C" int ssd_synth_f32(ssd_ctx* ctx, uint64_t seed, uint32_t tensor_id, float mean,
+                             float std_dev, int64_t total_cols, int row0, int rows, int col0,
+                             int cols, float* out_dev, void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(out_dev && rows > 0 && cols > 0, SSD_ERR_ARG, "bad arguments");
+    int64_t n = (int64_t)rows * cols;
+    k_synth_f32<<<(unsigned)((n + 255) / 256), 256, 0, pick_stream(ctx, stream)>>>(
+        seed, tensor_id, mean, std_dev, total_cols, row0, rows, col0, cols, out_dev);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_quantize(ssd_ctx* ctx, const float* x_dev, int rows, int cols, int type,
+                            void* raw_out_dev, void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(x_dev && raw_out_dev, SSD_ERR_ARG, "null pointer");
+    SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K, SSD_ERR_TYPE,
+            "quantize supports Q4_0/Q8_0/Q4_K, not %d", type);
+    int bs = type_block(type);
+    SSD_REQ(rows > 0 && cols > 0 && cols % bs == 0, SSD_ERR_SHAPE, "cols %d not a multiple of %d",
+            cols, bs);
+    int64_t nb = (int64_t)rows * (cols / bs);
+    k_quantize_raw<<<(unsigned)((nb + 127) / 128), 128, 0, pick_stream(ctx, stream)>>>(
+        x_dev, type, nb, (uint8_t*)raw_out_dev);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_dequantize(ssd_ctx* ctx, const ssd_weight* w, float* out_dev, void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(w && out_dev, SSD_ERR_ARG, "null pointer");
+    int64_t n = (int64_t)w->rows * w->cols;
+    SSD_REQ(n % 8 == 0, SSD_ERR_SHAPE, "element count must be a multiple of 8");
+    int64_t threads = n / 8;
+    k_dequant<<<(unsigned)((threads + 255) / 256), 256, 0, pick_stream(ctx, stream)>>>(*w, out_dev);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}

@@ -1,0 +1,60 @@
+// matvec.cuh — fused GGUF dequant-matvec for sm_100a (internal interface).
+#pragma once
+#include "common.cuh"
+
+namespace ssd {
+
+// How virtual rows map onto up to three weight tensors of the same type and width.
+enum MapMode { MAP_PLAIN = 0, MAP_QKV = 1, MAP_SWIGLU = 2 };
+// What the kernel does with each finished row.
+enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV_ROPE = 3, EPI_ARGMAX = 4 };
+
+struct MvArgs {
+    // weights (library layout); all segments share type and cols
+    const uint8_t* qs[3];
+    const uint8_t* meta[3];
+    int seg_rows[3];
+    int map;
+    int rows;  // virtual rows
+    int cols;
+    // prologue: x_eff = x (+ x_add); optional writeback of x_eff by CTA 0;
+    // optional RMSNorm: order 0 = v*(inv*w) (rmsnorm_f32_fast_scalar),
+    // order 1 = (v*inv)*w (fused_post_attn_norm / fused_rmsnorm_linear).
+    const float* x;
+    const float* x_add;
+    float* x_writeback;
+    const float* norm_w;
+    float eps;
+    int norm_order;
+    // epilogue
+    float* y;           // STORE/RESID/SWIGLU out, QKV q out, ARGMAX logits (may be null)
+    const float* base;  // RESID base (may alias y)
+    float* y_k;         // QKV k out
+    float* y_v;         // QKV v out
+    int head_dim;
+    float theta;
+    int position;
+    const int* position_dev;  // if non-null, position is read from device memory
+    unsigned long long* argmax_key;
+    int index_offset;  // added to row index for ARGMAX (tensor-parallel vocab shards)
+};
+
+// Launches y = f(W x) with the given epilogue. pdl: launch with programmatic
+// stream serialization so the weight prefetch overlaps the previous kernel.
+int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a, cudaStream_t s, bool pdl);
+
+// Fills an MvArgs for a single plain weight.
+inline MvArgs mv_plain(const ssd_weight* w, const float* x, float* y) {
+    MvArgs a = {};
+    a.qs[0] = w->qs;
+    a.meta[0] = w->meta;
+    a.seg_rows[0] = w->rows;
+    a.map = MAP_PLAIN;
+    a.rows = w->rows;
+    a.cols = w->cols;
+    a.x = x;
+    a.y = y;
+    return a;
+}
+
+}  // namespace ssd

@@ -1,0 +1,731 @@
+// model.cu — decode engine: HBM-resident quantized layers, INT8 KV cache, row-sharded
+// tensor parallelism over NCCL, one CUDA graph per decode token.
+//
+// Replaces forward_pass and the per-token loop of generate
+// (src/inference/transformer.rs:283-399, :681-770) on the compute side: per layer
+//   attn_in = rms_norm(h)                                   transformer.rs:323-326
+//   q,k,v   = fused_qkv_rope(attn_in)                       attention.rs:188-196
+//   kv_cache.append(k, v)   (INT8, quantized_kv_cache.rs:107-110)
+//   a       = attention(q, cache) ; o = Wo a                attention.rs:198-239
+//   ffn_in  = fused_post_attn_norm(h += o)                  transformer.rs:350-357
+//   h      += down(silu(gate ffn_in) * up ffn_in)           feed_forward.rs:17-44
+// then logits = output * rmsnorm(h) and the greedy argmax (transformer.rs:690-741).
+//
+// Kernel sequence per layer (TP = 1): QKV+RoPE (norm folded) -> KV append ->
+// attention (2 kernels) -> Wo + residual -> gate/up + SwiGLU (norm folded) ->
+// down + residual. With TP = N, Wo and down write partial sums that an NCCL
+// all-reduce completes; the residual add is folded into the next kernel's prologue.
+#include <nccl.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "matvec.cuh"
+#include "ops.cuh"
+
+#define SSD_NCCL(call)                                                                \
+    do {                                                                              \
+        ncclResult_t r_ = (call);                                                     \
+        if (r_ != ncclSuccess) {                                                      \
+            ::ssd::set_error("%s:%d %s: %s", __FILE__, __LINE__, #call,               \
+                             ncclGetErrorString(r_));                                 \
+            return SSD_ERR_NCCL;                                                      \
+        }                                                                             \
+    } while (0)
+
+namespace ssd {
+struct Layer {
+    ssd_weight *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr;
+    ssd_weight *wg = nullptr, *wu = nullptr, *wd = nullptr;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    ssd_kv_cache* kv = nullptr;
+};
+
+__global__ void k_add(float* out, const float* a, const float* b, int n) {
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __fadd_rn(a[i], b[i]);
+}
+}  // namespace ssd
+
+using namespace ssd;
+
+struct ssd_model {
+    ssd_ctx* ctx = nullptr;
+    ssd_model_config cfg = {};
+    // this rank's shard
+    int nq_local = 0, nkv_local = 0, kv_head0 = 0, ff_local = 0, vocab_local = 0, vocab0 = 0;
+    int q_rows = 0, kv_rows = 0, embd_cols_local = 0, ff0 = 0, embd0 = 0;
+    std::vector<Layer> layers;
+    ssd_weight* tok_embd = nullptr;
+    ssd_weight* output = nullptr;
+    float* out_norm = nullptr;
+    // decode state (device)
+    void* state = nullptr;
+    float *h_a = nullptr, *h_b = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
+    float *attn = nullptr, *act = nullptr, *part = nullptr, *p1 = nullptr, *p2 = nullptr;
+    float* logits = nullptr;
+    int32_t* token = nullptr;
+    int* pos = nullptr;
+    unsigned long long* key = nullptr;
+    int32_t* pinned = nullptr;  // 2 pinned ints: token in / token out
+    // tensor parallel
+    ncclComm_t comm = nullptr;
+    // graph
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+};
+
+static int tp_size(const ssd_model* m) { return m->cfg.tp_size < 1 ? 1 : m->cfg.tp_size; }
+
+extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_model** out) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(c && out, SSD_ERR_ARG, "null argument");
+    const int N = c->tp_size < 1 ? 1 : c->tp_size;
+    SSD_REQ(c->tp_rank >= 0 && c->tp_rank < N, SSD_ERR_ARG, "tp_rank %d outside [0, %d)",
+            c->tp_rank, N);
+    SSD_REQ(c->n_layers > 0 && c->n_embd > 0 && c->n_head > 0 && c->n_head_kv > 0 &&
+                c->head_dim > 0 && c->n_ff > 0 && c->vocab > 0 && c->kv_capacity > 0,
+            SSD_ERR_ARG, "non-positive model dimension");
+    SSD_REQ(c->n_head * c->head_dim == c->n_embd, SSD_ERR_SHAPE,
+            "n_head*head_dim must equal n_embd (attention.rs:236 projects n_embd x n_embd)");
+    SSD_REQ(c->n_head % c->n_head_kv == 0, SSD_ERR_SHAPE, "n_head %% n_head_kv != 0");
+    SSD_REQ(c->n_head_kv % N == 0 && c->n_ff % (2 * N) == 0 && c->vocab % N == 0 &&
+                c->n_embd % N == 0,
+            SSD_ERR_SHAPE, "dimensions do not shard over %d ranks", N);
+    const int bs = type_block(c->wtype);
+    SSD_REQ(bs == 32 || bs == 256, SSD_ERR_TYPE, "layer weight type %d not supported", c->wtype);
+    SSD_REQ((c->n_embd / N) % bs == 0 && (c->n_ff / N) % bs == 0, SSD_ERR_SHAPE,
+            "column shards must be whole %d-wide blocks", bs);
+    SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
+                c->embd_type == SSD_TYPE_Q8_0,
+            SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
+    SSD_REQ(type_block(c->out_type) == 32 || type_block(c->out_type) == 256, SSD_ERR_TYPE,
+            "output type %d not supported", c->out_type);
+
+    ssd_model* m = new ssd_model();
+    m->ctx = ctx;
+    m->cfg = *c;
+    m->cfg.tp_size = N;
+    const int r = c->tp_rank;
+    m->nkv_local = c->n_head_kv / N;
+    m->kv_head0 = r * m->nkv_local;
+    m->nq_local = c->n_head / N;
+    m->q_rows = m->nq_local * c->head_dim;
+    m->kv_rows = c->n_head_kv * c->head_dim;  // K/V projections are replicated
+    m->embd_cols_local = c->n_embd / N;
+    m->embd0 = r * m->embd_cols_local;
+    m->ff_local = c->n_ff / N;
+    m->ff0 = r * m->ff_local;
+    m->vocab_local = c->vocab / N;
+    m->vocab0 = r * m->vocab_local;
+    m->layers.resize(c->n_layers);
+
+    // decode state
+    const int E = c->n_embd;
+    const size_t pf = attn_partial_floats(m->nq_local, c->kv_capacity, c->head_dim);
+    size_t floats = 0;
+    auto take = [&](size_t n) {
+        size_t off = floats;
+        floats += (n + 63) & ~(size_t)63;
+        return off;
+    };
+    const size_t o_ha = take(E), o_hb = take(E), o_q = take(m->q_rows), o_k = take(m->kv_rows),
+                 o_v = take(m->kv_rows), o_attn = take(m->q_rows), o_act = take(m->ff_local),
+                 o_part = take(pf), o_p1 = take(E), o_p2 = take(E), o_log = take(m->vocab_local),
+                 o_misc = take(64);
+    if (cudaMalloc(&m->state, floats * 4) != cudaSuccess) {
+        cudaGetLastError();
+        delete m;
+        set_error("decode state allocation failed");
+        return SSD_ERR_NOMEM;
+    }
+    cudaMemset(m->state, 0, floats * 4);
+    float* S = (float*)m->state;
+    m->h_a = S + o_ha;
+    m->h_b = S + o_hb;
+    m->q = S + o_q;
+    m->k = S + o_k;
+    m->v = S + o_v;
+    m->attn = S + o_attn;
+    m->act = S + o_act;
+    m->part = S + o_part;
+    m->p1 = S + o_p1;
+    m->p2 = S + o_p2;
+    m->logits = S + o_log;
+    m->key = reinterpret_cast<unsigned long long*>(S + o_misc);
+    m->token = reinterpret_cast<int32_t*>(S + o_misc + 4);
+    m->pos = reinterpret_cast<int*>(S + o_misc + 8);
+    if (cudaHostAlloc(&m->pinned, 16, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(m->state);
+        delete m;
+        set_error("pinned staging allocation failed");
+        return SSD_ERR_NOMEM;
+    }
+    for (auto& L : m->layers) {
+        int st = ssd_kv_create(ctx, c->kv_capacity, c->n_head_kv, c->head_dim, &L.kv);
+        if (st != SSD_OK) {
+            ssd_model_free(m);
+            return st;
+        }
+    }
+    *out = m;
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_free(ssd_model* m) {
+    if (!m) return SSD_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    for (auto& L : m->layers) {
+        ssd_weight_free(L.wq);
+        ssd_weight_free(L.wk);
+        ssd_weight_free(L.wv);
+        ssd_weight_free(L.wo);
+        ssd_weight_free(L.wg);
+        ssd_weight_free(L.wu);
+        ssd_weight_free(L.wd);
+        if (L.attn_norm) cudaFree(L.attn_norm);
+        if (L.ffn_norm) cudaFree(L.ffn_norm);
+        ssd_kv_free(L.kv);
+    }
+    ssd_weight_free(m->tok_embd);
+    ssd_weight_free(m->output);
+    if (m->out_norm) cudaFree(m->out_norm);
+    if (m->comm) ncclCommDestroy(m->comm);
+    if (m->state) cudaFree(m->state);
+    if (m->pinned) cudaFreeHost(m->pinned);
+    delete m;
+    return SSD_OK;
+}
+
+extern "C" int ssd_tp_unique_id(uint8_t out[128]) {
+    SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    ncclUniqueId id;
+    SSD_NCCL(ncclGetUniqueId(&id));
+    memcpy(out, &id, 128);
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_tp_init(ssd_model* m, const uint8_t uid[128]) {
+    SSD_REQ(m && uid, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    if (tp_size(m) == 1) return SSD_OK;
+    SSD_REQ(m->comm == nullptr, SSD_ERR_STATE, "communicator already initialised");
+    ncclUniqueId id;
+    memcpy(&id, uid, 128);
+    SSD_NCCL(ncclCommInitRank(&m->comm, tp_size(m), id, m->cfg.tp_rank));
+    return SSD_OK;
+}
+
+// ------------------------------------------------------------------ weights
+
+// Which slice of a global tensor this rank keeps. Row-sharded: attn_q (by heads),
+// ffn_gate, ffn_up, output (by vocab rows). Column-sharded: attn_output (by the
+// rank's q-head columns), ffn_down (by the rank's FFN columns). Replicated:
+// attn_k, attn_v (every rank needs the full K/V row for the INT8 scale, which
+// spans all KV heads: quantized_kv_cache.rs:107-110) and token_embd.
+struct Shard {
+    int rows, cols;   // global shape
+    int row0, nrows;  // kept rows
+    int col0, ncols;  // kept cols
+    int type;
+    uint32_t tid;     // synthetic-generator tensor id
+};
+
+static int shard_range(const ssd_model_config& c, const std::string& name, int layer, Shard& s) {
+    const int N = c.tp_size < 1 ? 1 : c.tp_size, r = c.tp_rank;
+    const int E = c.n_embd, F = c.n_ff, KV = c.n_head_kv * c.head_dim;
+    const int qr = (c.n_head / N) * c.head_dim, ec = E / N, fl = F / N, vl = c.vocab / N;
+    if (layer < 0) {
+        if (name == "token_embd") {
+            s = Shard{c.vocab, E, 0, c.vocab, 0, E, c.embd_type, 1000001u};
+            return SSD_OK;
+        }
+        if (name == "output") {
+            s = Shard{c.vocab, E, r * vl, vl, 0, E, c.out_type, 1000002u};
+            return SSD_OK;
+        }
+        set_error("unknown global tensor '%s'", name.c_str());
+        return SSD_ERR_ARG;
+    }
+    SSD_REQ(layer < c.n_layers, SSD_ERR_ARG, "layer %d out of range", layer);
+    const uint32_t base = (uint32_t)layer * 16u;
+    if (name == "attn_q")
+        s = Shard{E, E, r * qr, qr, 0, E, c.wtype, base + 0};
+    else if (name == "attn_k")
+        s = Shard{KV, E, 0, KV, 0, E, c.wtype, base + 1};
+    else if (name == "attn_v")
+        s = Shard{KV, E, 0, KV, 0, E, c.wtype, base + 2};
+    else if (name == "attn_output")
+        s = Shard{E, E, 0, E, r * ec, ec, c.wtype, base + 3};
+    else if (name == "ffn_gate")
+        s = Shard{F, E, r * fl, fl, 0, E, c.wtype, base + 4};
+    else if (name == "ffn_up")
+        s = Shard{F, E, r * fl, fl, 0, E, c.wtype, base + 5};
+    else if (name == "ffn_down")
+        s = Shard{E, F, 0, E, r * fl, fl, c.wtype, base + 6};
+    else {
+        set_error("unknown layer tensor '%s'", name.c_str());
+        return SSD_ERR_ARG;
+    }
+    return SSD_OK;
+}
+
+static ssd_weight** slot_of(ssd_model* m, const std::string& name, int layer) {
+    if (layer < 0) return name == "token_embd" ? &m->tok_embd : &m->output;
+    Layer& L = m->layers[layer];
+    if (name == "attn_q") return &L.wq;
+    if (name == "attn_k") return &L.wk;
+    if (name == "attn_v") return &L.wv;
+    if (name == "attn_output") return &L.wo;
+    if (name == "ffn_gate") return &L.wg;
+    if (name == "ffn_up") return &L.wu;
+    return &L.wd;
+}
+
+static int shard_of(ssd_model* m, const std::string& name, int layer, Shard& s,
+                    ssd_weight**& slot) {
+    SSD_TRY(shard_range(m->cfg, name, layer, s));
+    slot = slot_of(m, name, layer);
+    return SSD_OK;
+}
+
+extern "C" int ssd_shard_range(const ssd_model_config* c, const char* name, int layer, int* row0,
+                               int* nrows, int* col0, int* ncols) {
+    SSD_REQ(c && name, SSD_ERR_ARG, "null argument");
+    Shard s;
+    SSD_TRY(shard_range(*c, std::string(name), layer, s));
+    if (row0) *row0 = s.row0;
+    if (nrows) *nrows = s.nrows;
+    if (col0) *col0 = s.col0;
+    if (ncols) *ncols = s.ncols;
+    return SSD_OK;
+}
+
+static int set_norm(ssd_model* m, float** slot, const void* host, size_t bytes) {
+    const size_t need = (size_t)m->cfg.n_embd * 4;
+    SSD_REQ(bytes == need, SSD_ERR_SHAPE, "norm weight needs %zu bytes, got %zu", need, bytes);
+    if (!*slot) SSD_CK(cudaMalloc(slot, need));
+    SSD_CK(cudaMemcpy(*slot, host, need, cudaMemcpyHostToDevice));
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_set_tensor(ssd_model* m, const char* cname, int layer, const void* host,
+                                    size_t bytes) {
+    SSD_REQ(m && cname && host, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    const std::string name(cname);
+    if (layer >= 0 && name == "attn_norm") {
+        SSD_REQ(layer < m->cfg.n_layers, SSD_ERR_ARG, "layer out of range");
+        return set_norm(m, &m->layers[layer].attn_norm, host, bytes);
+    }
+    if (layer >= 0 && name == "ffn_norm") {
+        SSD_REQ(layer < m->cfg.n_layers, SSD_ERR_ARG, "layer out of range");
+        return set_norm(m, &m->layers[layer].ffn_norm, host, bytes);
+    }
+    if (layer < 0 && name == "output_norm") return set_norm(m, &m->out_norm, host, bytes);
+    Shard s;
+    ssd_weight** slot = nullptr;
+    SSD_TRY(shard_of(m, name, layer, s, slot));
+    const size_t rb = ssd_row_bytes(s.type, s.cols);
+    SSD_REQ(rb != 0 && bytes == rb * (size_t)s.rows, SSD_ERR_SHAPE,
+            "%s: %zu bytes given, %dx%d of type %d needs %zu", cname, bytes, s.rows, s.cols, s.type,
+            rb * (size_t)s.rows);
+    const int bs = type_block(s.type);
+    const size_t kb = ssd_row_bytes(s.type, s.ncols);
+    std::vector<uint8_t> buf(kb * (size_t)s.nrows);
+    const uint8_t* src = (const uint8_t*)host;
+    const size_t coff = (size_t)(s.col0 / bs) * type_block_bytes(s.type);
+    for (int r = 0; r < s.nrows; r++)
+        memcpy(buf.data() + (size_t)r * kb, src + (size_t)(s.row0 + r) * rb + coff, kb);
+    ssd_weight* w = nullptr;
+    SSD_TRY(ssd_weight_upload(m->ctx, buf.data(), buf.size(), s.type, s.nrows, s.ncols, &w));
+    ssd_weight_free(*slot);
+    *slot = w;
+    if (m->exec) {  // weights changed: the captured graph holds the old pointers
+        cudaGraphExecDestroy(m->exec);
+        cudaGraphDestroy(m->graph);
+        m->exec = nullptr;
+        m->graph = nullptr;
+    }
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_dev) {
+    SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");
+    SSD_TRY(check_ctx(m->ctx));
+    const auto& c = m->cfg;
+    static const char* names[] = {"attn_q", "attn_k", "attn_v", "attn_output",
+                                  "ffn_gate", "ffn_up", "ffn_down"};
+    auto synth = [&](const char* nm, int layer, float sd) -> int {
+        Shard s;
+        ssd_weight** slot = nullptr;
+        SSD_TRY(shard_of(m, nm, layer, s, slot));
+        ssd_weight* w = nullptr;
+        if (s.type == SSD_TYPE_F32) {
+            SSD_TRY(alloc_weight(m->ctx, SSD_TYPE_F32, s.nrows, s.ncols, &w));
+            SSD_TRY(ssd_synth_f32(m->ctx, seed, s.tid, 0.0f, sd, s.cols, s.row0, s.nrows, s.col0,
+                                  s.ncols, (float*)w->qs, nullptr));
+        } else {
+            SSD_TRY(ssd_weight_synth(m->ctx, s.type, seed, s.tid, sd, s.cols, s.row0, s.nrows,
+                                     s.col0, s.ncols, &w, nullptr));
+        }
+        ssd_weight_free(*slot);
+        *slot = w;
+        return SSD_OK;
+    };
+    auto norm = [&](float** slot, uint32_t tid) -> int {
+        if (!*slot) SSD_CK(cudaMalloc(slot, (size_t)c.n_embd * 4));
+        return ssd_synth_f32(m->ctx, seed, tid, 1.0f, 0.02f, c.n_embd, 0, 1, 0, c.n_embd, *slot,
+                             nullptr);
+    };
+    for (int l = 0; l < c.n_layers; l++) {
+        for (const char* nm : names) SSD_TRY(synth(nm, l, std_dev));
+        SSD_TRY(norm(&m->layers[l].attn_norm, (uint32_t)l * 16u + 8u));
+        SSD_TRY(norm(&m->layers[l].ffn_norm, (uint32_t)l * 16u + 9u));
+    }
+    SSD_TRY(synth("token_embd", -1, 1.0f));
+    SSD_TRY(synth("output", -1, std_dev));
+    SSD_TRY(norm(&m->out_norm, 1000003u));
+    SSD_CK(cudaStreamSynchronize(m->ctx->stream));
+    if (m->exec) {
+        cudaGraphExecDestroy(m->exec);
+        cudaGraphDestroy(m->graph);
+        m->exec = nullptr;
+        m->graph = nullptr;
+    }
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_synth_kv(ssd_model* m, uint64_t seed, int n) {
+    SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");
+    SSD_TRY(check_ctx(m->ctx));
+    const auto& c = m->cfg;
+    SSD_REQ(n >= 0 && n < c.kv_capacity, SSD_ERR_SHAPE, "n %d outside [0, %d)", n, c.kv_capacity);
+    const int kvd = c.n_head_kv * c.head_dim;
+    if (n > 0) {
+        const int chunk = 256;
+        float* tmp = nullptr;
+        SSD_CK(cudaMalloc(&tmp, (size_t)2 * chunk * kvd * 4));
+        int st = SSD_OK;
+        for (int l = 0; l < c.n_layers && st == SSD_OK; l++) {
+            for (int p0 = 0; p0 < n && st == SSD_OK; p0 += chunk) {
+                const int rows = n - p0 < chunk ? n - p0 : chunk;
+                // K and V rows N(0, 1): element (pos, i) of tensors 2000000 + 2l (+1)
+                st = ssd_synth_f32(m->ctx, seed, 2000000u + 2u * l, 0.0f, 1.0f, kvd, p0, rows, 0,
+                                   kvd, tmp, nullptr);
+                if (st == SSD_OK)
+                    st = ssd_synth_f32(m->ctx, seed, 2000001u + 2u * l, 0.0f, 1.0f, kvd, p0, rows,
+                                       0, kvd, tmp + (size_t)chunk * kvd, nullptr);
+                if (st == SSD_OK)
+                    st = launch_kv_append(m->layers[l].kv, tmp, tmp + (size_t)chunk * kvd, p0,
+                                          nullptr, rows, m->ctx->stream, false);
+            }
+        }
+        cudaStreamSynchronize(m->ctx->stream);
+        cudaFree(tmp);
+        SSD_TRY(st);
+    }
+    return ssd_model_set_position(m, n);
+}
+
+extern "C" int ssd_model_set_position(ssd_model* m, int pos) {
+    SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(pos >= 0 && pos < m->cfg.kv_capacity, SSD_ERR_SHAPE, "position %d outside [0, %d)", pos,
+            m->cfg.kv_capacity);
+    SSD_CK(cudaMemcpyAsync(m->pos, &pos, 4, cudaMemcpyHostToDevice, m->ctx->stream));
+    SSD_CK(cudaStreamSynchronize(m->ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_get_position(ssd_model* m, int* pos) {
+    SSD_REQ(m && pos, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_CK(cudaMemcpyAsync(pos, m->pos, 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    SSD_CK(cudaStreamSynchronize(m->ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_state(ssd_model* m, float** hidden, float** logits, int32_t** token) {
+    SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");
+    if (hidden) *hidden = m->h_a;
+    if (logits) *logits = m->logits;
+    if (token) *token = m->token;
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_weight(ssd_model* m, const char* name, int layer, ssd_weight** out) {
+    SSD_REQ(m && name && out, SSD_ERR_ARG, "null argument");
+    Shard s;
+    ssd_weight** slot = nullptr;
+    SSD_TRY(shard_of(m, std::string(name), layer, s, slot));
+    SSD_REQ(*slot != nullptr, SSD_ERR_STATE, "tensor %s (layer %d) not set", name, layer);
+    *out = *slot;
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_norm(ssd_model* m, const char* name, int layer, float** out) {
+    SSD_REQ(m && name && out, SSD_ERR_ARG, "null argument");
+    const std::string n(name);
+    float* p = nullptr;
+    if (layer < 0 && n == "output_norm") {
+        p = m->out_norm;
+    } else {
+        SSD_REQ(layer >= 0 && layer < m->cfg.n_layers, SSD_ERR_ARG, "layer out of range");
+        if (n == "attn_norm") p = m->layers[layer].attn_norm;
+        else if (n == "ffn_norm") p = m->layers[layer].ffn_norm;
+        else SSD_REQ(false, SSD_ERR_ARG, "unknown norm '%s'", name);
+    }
+    SSD_REQ(p != nullptr, SSD_ERR_STATE, "norm %s not set", name);
+    *out = p;
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_kv(ssd_model* m, int layer, ssd_kv_cache** out) {
+    SSD_REQ(m && out && layer >= 0 && layer < m->cfg.n_layers, SSD_ERR_ARG, "bad arguments");
+    *out = m->layers[layer].kv;
+    return SSD_OK;
+}
+
+// --------------------------------------------------------------- sequence
+
+static int check_weights(ssd_model* m) {
+    for (int l = 0; l < m->cfg.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        SSD_REQ(L.wq && L.wk && L.wv && L.wo && L.wg && L.wu && L.wd && L.attn_norm && L.ffn_norm,
+                SSD_ERR_STATE, "layer %d has unset tensors", l);
+    }
+    SSD_REQ(m->tok_embd && m->output && m->out_norm, SSD_ERR_STATE, "global tensors unset");
+    if (tp_size(m) > 1) SSD_REQ(m->comm != nullptr, SSD_ERR_STATE, "tp_size > 1 needs tp_init");
+    return SSD_OK;
+}
+
+// Enqueues one layer on stream s. `h` is the residual stream on entry; `pend` a
+// pending partial sum (TP) to add first, or null. On return `h`/`pend` describe
+// the new residual stream.
+static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStream_t s, int& nl) {
+    const auto& c = m->cfg;
+    const Layer& L = m->layers[l];
+    const bool tp = tp_size(m) > 1;
+    float* h_other = (h == m->h_a) ? m->h_b : m->h_a;
+    // 1. QKV + RoPE with the pre-attention RMSNorm folded in
+    MvArgs a = {};
+    a.qs[0] = L.wq->qs;
+    a.qs[1] = L.wk->qs;
+    a.qs[2] = L.wv->qs;
+    a.meta[0] = L.wq->meta;
+    a.meta[1] = L.wk->meta;
+    a.meta[2] = L.wv->meta;
+    a.seg_rows[0] = m->q_rows;
+    a.seg_rows[1] = m->kv_rows;
+    a.seg_rows[2] = m->kv_rows;
+    a.map = MAP_QKV;
+    a.rows = m->q_rows + 2 * m->kv_rows;
+    a.cols = c.n_embd;
+    a.x = h;
+    if (pend) {  // hidden += partial (all-reduced), written back for the residual path
+        a.x_add = pend;
+        a.x_writeback = h_other;
+    }
+    a.norm_w = L.attn_norm;
+    a.eps = c.eps;
+    a.norm_order = 0;
+    a.y = m->q;
+    a.y_k = m->k;
+    a.y_v = m->v;
+    a.head_dim = c.head_dim;
+    a.theta = c.theta;
+    a.position_dev = m->pos;
+    SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_QKV_ROPE, a, s, true));
+    nl++;
+    if (pend) {
+        h = h_other;
+        h_other = (h == m->h_a) ? m->h_b : m->h_a;
+        pend = nullptr;
+    }
+    // 2. INT8 KV append at the current position
+    SSD_TRY(launch_kv_append(L.kv, m->k, m->v, 0, m->pos, 1, s, true));
+    nl++;
+    // 3. attention over this rank's KV heads
+    AttnArgs at = {};
+    at.k = L.kv->k;
+    at.v = L.kv->v;
+    at.ks = L.kv->k_scale;
+    at.vs = L.kv->v_scale;
+    at.kv_dim = L.kv->kv_dim;
+    at.head_dim = c.head_dim;
+    at.group = c.n_head / c.n_head_kv;
+    at.kv_head0 = m->kv_head0;
+    at.n_kv_local = m->nkv_local;
+    at.q = m->q;
+    at.out = m->attn;
+    at.partial = m->part;
+    at.pos_dev = m->pos;
+    at.max_seq = c.kv_capacity;
+    SSD_TRY(launch_attention(at, s, true));
+    nl += 2;
+    // 4. output projection (+ residual, or partial sum + all-reduce)
+    MvArgs o = mv_plain(L.wo, m->attn, tp ? m->p1 : h_other);
+    if (!tp) o.base = h;
+    SSD_TRY(launch_matvec(m->ctx, c.wtype, tp ? EPI_STORE : EPI_RESID, o, s, true));
+    nl++;
+    if (tp) {
+        SSD_NCCL(ncclAllReduce(m->p1, m->p1, c.n_embd, ncclFloat32, ncclSum, m->comm, s));
+        pend = m->p1;
+    } else {
+        h = h_other;
+        h_other = (h == m->h_a) ? m->h_b : m->h_a;
+    }
+    // 5. gate/up + SwiGLU with the FFN RMSNorm folded in
+    MvArgs g = {};
+    g.qs[0] = L.wg->qs;
+    g.qs[1] = L.wu->qs;
+    g.meta[0] = L.wg->meta;
+    g.meta[1] = L.wu->meta;
+    g.seg_rows[0] = m->ff_local;
+    g.seg_rows[1] = m->ff_local;
+    g.map = MAP_SWIGLU;
+    g.rows = 2 * m->ff_local;
+    g.cols = c.n_embd;
+    g.x = h;
+    if (pend) {
+        g.x_add = pend;
+        g.x_writeback = h_other;
+    }
+    g.norm_w = L.ffn_norm;
+    g.eps = c.eps;
+    g.norm_order = 1;
+    g.y = m->act;
+    SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_SWIGLU, g, s, true));
+    nl++;
+    if (pend) {
+        h = h_other;
+        h_other = (h == m->h_a) ? m->h_b : m->h_a;
+        pend = nullptr;
+    }
+    // 6. down projection (+ residual, or partial sum + all-reduce)
+    MvArgs d = mv_plain(L.wd, m->act, tp ? m->p2 : h_other);
+    if (!tp) d.base = h;
+    SSD_TRY(launch_matvec(m->ctx, c.wtype, tp ? EPI_STORE : EPI_RESID, d, s, true));
+    nl++;
+    if (tp) {
+        SSD_NCCL(ncclAllReduce(m->p2, m->p2, c.n_embd, ncclFloat32, ncclSum, m->comm, s));
+        pend = m->p2;
+    } else {
+        h = h_other;
+    }
+    return SSD_OK;
+}
+
+// Full decode step: embed -> layers -> norm + logits + argmax -> finalize.
+static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl) {
+    const auto& c = m->cfg;
+    SSD_TRY(launch_embed(m->tok_embd, m->token, m->h_a, s, true));
+    nl++;
+    float* h = m->h_a;
+    float* pend = nullptr;
+    for (int l = 0; l < c.n_layers; l++) SSD_TRY(enqueue_layer(m, l, h, pend, s, nl));
+    // logits = output * rmsnorm(h) (eps 1e-5 hard-coded at compute.rs:566), argmax
+    MvArgs a = mv_plain(m->output, h, m->logits);
+    if (pend) a.x_add = pend;
+    a.norm_w = m->out_norm;
+    a.eps = 1e-5f;
+    a.norm_order = 1;
+    a.argmax_key = m->key;
+    a.index_offset = m->vocab0;
+    SSD_TRY(launch_matvec(m->ctx, c.out_type, EPI_ARGMAX, a, s, true));
+    nl++;
+    if (tp_size(m) > 1)
+        SSD_NCCL(ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s));
+    SSD_TRY(launch_finalize(m->key, m->token, m->pos, s, true));
+    nl++;
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_decode_step(ssd_model* m, int use_graph) {
+    SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_TRY(check_weights(m));
+    cudaStream_t s = m->ctx->stream;
+    if (!use_graph) {
+        int nl = 0;
+        SSD_TRY(enqueue_step(m, s, nl));
+        m->launches = nl;
+        return SSD_OK;
+    }
+    if (!m->exec) {
+        int nl = 0;
+        SSD_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        int st = enqueue_step(m, s, nl);
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        SSD_TRY(st);
+        SSD_CK(e);
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        if (e != cudaSuccess) {
+            cudaGraphDestroy(g);
+            SSD_CK(e);
+        }
+        m->graph = g;
+        m->exec = ex;
+        m->launches = nl;
+    }
+    SSD_CK(cudaGraphLaunch(m->exec, s));
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_decode_token(ssd_model* m, int32_t token_in, int32_t* token_out,
+                                      int use_graph) {
+    SSD_REQ(m && token_out, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(token_in >= 0 && token_in < m->cfg.vocab, SSD_ERR_ARG, "token %d outside vocab",
+            token_in);
+    cudaStream_t s = m->ctx->stream;
+    m->pinned[0] = token_in;  // the previous call synchronised: the slot is free
+    SSD_CK(cudaMemcpyAsync(m->token, &m->pinned[0], 4, cudaMemcpyHostToDevice, s));
+    SSD_TRY(ssd_model_decode_step(m, use_graph));
+    SSD_CK(cudaMemcpyAsync(&m->pinned[1], m->token, 4, cudaMemcpyDeviceToHost, s));
+    SSD_CK(cudaStreamSynchronize(s));
+    *token_out = m->pinned[1];
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_layer_step(ssd_model* m, int layer) {
+    SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(layer >= 0 && layer < m->cfg.n_layers, SSD_ERR_ARG, "layer out of range");
+    const Layer& L = m->layers[layer];
+    SSD_REQ(L.wq && L.wk && L.wv && L.wo && L.wg && L.wu && L.wd && L.attn_norm && L.ffn_norm,
+            SSD_ERR_STATE, "layer %d has unset tensors", layer);
+    if (tp_size(m) > 1) SSD_REQ(m->comm != nullptr, SSD_ERR_STATE, "tp_size > 1 needs tp_init");
+    cudaStream_t s = m->ctx->stream;
+    float* h = m->h_a;
+    float* pend = nullptr;
+    int nl = 0;
+    SSD_TRY(enqueue_layer(m, layer, h, pend, s, nl));
+    // leave the layer's output in h_a, with any pending partial sum applied
+    if (pend) {
+        k_add<<<(m->cfg.n_embd + 255) / 256, 256, 0, s>>>(m->h_a, h, pend, m->cfg.n_embd);
+        SSD_CK_LAUNCH();
+    } else if (h != m->h_a) {
+        SSD_CK(cudaMemcpyAsync(m->h_a, h, (size_t)m->cfg.n_embd * 4, cudaMemcpyDeviceToDevice, s));
+    }
+    SSD_CK(cudaStreamSynchronize(s));
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_launches_per_step(ssd_model* m, int* launches) {
+    SSD_REQ(m && launches, SSD_ERR_ARG, "null argument");
+    *launches = m->launches;
+    return SSD_OK;
+}

@@ -1,0 +1,566 @@
+// ops.cu — RMSNorm, softmax, RoPE, SiLU, argmax, INT8 KV cache and split-K decode
+// attention for sm_100a.
+//
+// Reference: MetalCompute::{rmsnorm_f32, softmax_f32, fused_post_attn_norm_f32,
+// flash_attention_f32} (src/metal/compute.rs:193-258, :328-346), their CPU forms
+// (:536-555, :580-645), QuantizedLayerKvCache (src/inference/quantized_kv_cache.rs:23-130),
+// flash_attention_cached (src/inference/flash_attention.rs:40-143) and the greedy
+// argmax of src/inference/sampler.rs:572-578.
+#include <math.h>
+
+#include "ops.cuh"
+
+namespace ssd {
+
+constexpr float kQ80Magic = 8388736.0f;  // 2^23 + 128: (byte ^ 0x80) under 0x4B -> int8 exact
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; w++) t += red[w];
+    return t;
+}
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NT / 32; w++) t = fmaxf(t, red[w]);
+    return t;
+}
+
+// ------------------------------------------------------------ norms
+// rmsnorm_f32_fast_scalar (src/metal/compute.rs:580-588): x *= inv_rms * w.
+__global__ void __launch_bounds__(1024) k_rmsnorm(float* x, const float* w, int n, float eps) {
+    __shared__ float red[32];
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 1024) ss = fmaf(x[i], x[i], ss);
+    ss = block_sum<1024>(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (int i = threadIdx.x; i < n; i += 1024) x[i] = __fmul_rn(x[i], __fmul_rn(inv, w[i]));
+}
+
+// fused_post_attn_norm_f32_cpu (src/metal/compute.rs:536-555): h += a; out = h*inv*w.
+__global__ void __launch_bounds__(1024) k_post_attn_norm(float* h, const float* a, const float* w,
+                                                         int n, float eps, float* out) {
+    __shared__ float red[32];
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const float v = __fadd_rn(h[i], a[i]);
+        h[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum<1024>(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (int i = threadIdx.x; i < n; i += 1024) out[i] = __fmul_rn(__fmul_rn(h[i], inv), w[i]);
+}
+
+// softmax_f32_fast_scalar (src/metal/compute.rs:604-620).
+__global__ void __launch_bounds__(1024) k_softmax(float* x, int n) {
+    __shared__ float red[32];
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += 1024) m = fmaxf(m, x[i]);
+    m = block_max<1024>(m, red);
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const float e = expf(__fsub_rn(x[i], m));
+        x[i] = e;
+        s += e;
+    }
+    s = block_sum<1024>(s, red);
+    if (s > 0.0f) {
+        const float inv = __fdiv_rn(1.0f, s);
+        for (int i = threadIdx.x; i < n; i += 1024) x[i] = __fmul_rn(x[i], inv);
+    }
+}
+
+// rope_f32_multi_head (src/metal/compute.rs:482-506): one thread per adjacent pair.
+__global__ void k_rope(float* x, int len, int head_dim, int n_heads, int pos, float theta) {
+    const int half = head_dim / 2;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n_heads * half) return;
+    const int h = t / half, i = t % half;
+    const int i0 = h * head_dim + 2 * i, i1 = i0 + 1;
+    if (i1 >= len) return;
+    const float e = __fdiv_rn(__fmul_rn(2.0f, (float)i), (float)head_dim);
+    const float freq = __fdiv_rn(1.0f, (float)pow((double)theta, (double)e));
+    const float ang = __fmul_rn((float)pos, freq);
+    double sd, cd;
+    sincos((double)ang, &sd, &cd);
+    const float sn = (float)sd, cs = (float)cd;
+    const float x0 = x[i0], x1 = x[i1];
+    x[i0] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+    x[i1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+}
+
+// silu_f32 (src/metal/compute.rs:641-645): v / (1 + exp(-v)).
+__global__ void k_silu(float* x, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fdiv_rn(x[i], __fadd_rn(1.0f, expf(-x[i])));
+}
+
+__device__ __forceinline__ unsigned long long amax_key(float v, uint32_t idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | idx;
+}
+
+// argmax with the LAST index on ties (Iterator::max_by, src/inference/sampler.rs:572-578).
+__global__ void __launch_bounds__(1024) k_argmax(const float* v, int n, int32_t* idx) {
+    __shared__ unsigned long long red[32];
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const unsigned long long k = amax_key(v[i], (uint32_t)i);
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < 32; w++) b = red[w] > b ? red[w] : b;
+        *idx = (int32_t)(uint32_t)(b & 0xFFFFFFFFull);
+    }
+}
+
+// ------------------------------------------------------------- INT8 KV
+// QuantizedVec::quantize (src/inference/quantized_kv_cache.rs:23-41), bit-exact:
+// absmax = max |v|; zero row -> scale 0; scale = absmax/127; q = clamp(round(v*127/absmax)).
+__global__ void __launch_bounds__(256) k_kv_append(const float* __restrict__ k,
+                                                   const float* __restrict__ v, int8_t* kc,
+                                                   int8_t* vc, float* ksc, float* vsc, int kv_dim,
+                                                   int pos, const int* pos_dev, int capacity) {
+    __shared__ float red[8];
+    pdl_wait();
+    const int base_pos = pos_dev ? *pos_dev : pos;
+    const int r = blockIdx.x, which = blockIdx.y;
+    const int p = base_pos + r;
+    if (p < 0 || p >= capacity) return;  // host checks bounds for the direct API
+    const float* src = (which == 0 ? k : v) + (size_t)r * kv_dim;
+    int8_t* dst = (which == 0 ? kc : vc) + (size_t)p * kv_dim;
+    float am = 0.0f;
+    for (int i = threadIdx.x; i < kv_dim; i += 256) am = fmaxf(am, fabsf(src[i]));
+    am = block_max<256>(am, red);
+    if (am == 0.0f) {
+        for (int i = threadIdx.x; i < kv_dim; i += 256) dst[i] = 0;
+        if (threadIdx.x == 0) (which == 0 ? ksc : vsc)[p] = 0.0f;
+        return;
+    }
+    const float scale = __fdiv_rn(am, 127.0f);
+    const float inv = __fdiv_rn(127.0f, am);
+    for (int i = threadIdx.x; i < kv_dim; i += 256) {
+        float q = roundf(__fmul_rn(src[i], inv));
+        q = fminf(127.0f, fmaxf(-127.0f, q));
+        dst[i] = (int8_t)(int)q;
+    }
+    if (threadIdx.x == 0) (which == 0 ? ksc : vsc)[p] = scale;
+}
+
+// ------------------------------------------------ split-K decode attention
+// CTA (local kv head, chunk of ATT_P positions): scores for the GROUP query heads
+// that share the kv head (GQA kv_h = h / group, flash_attention.rs:79-80), chunk
+// max / exp / sum, then the V-weighted sum; k_attn_combine merges the chunks with
+// the online-softmax rescaling of flash_attention.rs:106-134.
+constexpr int ATT_P = 128;
+
+template <int HD, int G>
+__global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
+    constexpr int DPL = HD / 32;  // dims per lane in the PV phase
+    __shared__ __align__(16) float qs[G][HD];
+    __shared__ float sc[G][ATT_P];
+    __shared__ float ml[G][2];
+    __shared__ __align__(16) float red[4][G][HD];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
+    const int g_kv = a.kv_head0 + gl;
+    pdl_wait();
+    // positions [0, seq); never beyond the cache (max_seq is its capacity on the
+    // graph path), so a position past the end reads nothing out of bounds
+    const int seq = min(a.pos_dev ? (*a.pos_dev + 1) : a.seq_len, a.max_seq);
+    const int p0 = chunk * ATT_P;
+    float* part = a.partial + ((size_t)(gl * G) * nchunks + chunk) * (HD + 2);
+    const size_t head_stride = (size_t)nchunks * (HD + 2);
+    if (p0 >= seq) {
+        if (tid < G) {
+            part[tid * head_stride + 0] = -INFINITY;
+            part[tid * head_stride + 1] = 0.0f;
+        }
+        return;
+    }
+    for (int i = tid; i < G * HD; i += 128) (&qs[0][0])[i] = a.q[(size_t)gl * G * HD + i];
+    __syncthreads();
+
+    // scores: thread -> position; dot = sum_d q[d] * k8[d], score = dot * kscale * 1/sqrt(d)
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    {
+        const int p = p0 + tid;
+        float dot[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) dot[g] = 0.0f;
+        if (p < seq) {
+            const int8_t* kr = a.k + (size_t)p * a.kv_dim + (size_t)g_kv * HD;
+#pragma unroll 2
+            for (int c = 0; c < HD; c += 16) {
+                const uint4 kk = *reinterpret_cast<const uint4*>(kr + c);
+                const uint32_t wv[4] = {kk.x ^ 0x80808080u, kk.y ^ 0x80808080u,
+                                        kk.z ^ 0x80808080u, kk.w ^ 0x80808080u};
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                    const float k0 = magic_byte(wv[m], 0) - kQ80Magic;
+                    const float k1 = magic_byte(wv[m], 1) - kQ80Magic;
+                    const float k2 = magic_byte(wv[m], 2) - kQ80Magic;
+                    const float k3 = magic_byte(wv[m], 3) - kQ80Magic;
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(&qs[g][c + 4 * m]);
+                        float t = dot[g];
+                        t = fmaf(q4.x, k0, t);
+                        t = fmaf(q4.y, k1, t);
+                        t = fmaf(q4.z, k2, t);
+                        t = fmaf(q4.w, k3, t);
+                        dot[g] = t;
+                    }
+                }
+            }
+            const float ksc = a.ks[p];
+#pragma unroll
+            for (int g = 0; g < G; g++) sc[g][tid] = __fmul_rn(__fmul_rn(dot[g], ksc), scale);
+        } else {
+#pragma unroll
+            for (int g = 0; g < G; g++) sc[g][tid] = -INFINITY;
+        }
+    }
+    __syncthreads();
+    // chunk softmax statistics per head
+    for (int g = warp; g < G; g += 4) {
+        float m = -INFINITY;
+        for (int i = lane; i < ATT_P; i += 32) m = fmaxf(m, sc[g][i]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int i = lane; i < ATT_P; i += 32) {
+            const float e = (sc[g][i] == -INFINITY) ? 0.0f : expf(__fsub_rn(sc[g][i], m));
+            sc[g][i] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            ml[g][0] = m;
+            ml[g][1] = l;
+        }
+    }
+    __syncthreads();
+    // PV: lane -> DPL dims, warp -> positions warp, warp+4, ...
+    float acc[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int j = 0; j < DPL; j++) acc[g][j] = 0.0f;
+    const int npos = min(ATT_P, seq - p0);
+    for (int i = warp; i < npos; i += 4) {
+        const int pp = p0 + i;
+        const int8_t* vr = a.v + (size_t)pp * a.kv_dim + (size_t)g_kv * HD + DPL * lane;
+        float vf[DPL];
+        if constexpr (DPL == 4) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(vr) ^ 0x80808080u;
+            vf[0] = magic_byte(w, 0) - kQ80Magic;
+            vf[1] = magic_byte(w, 1) - kQ80Magic;
+            vf[2] = magic_byte(w, 2) - kQ80Magic;
+            vf[3] = magic_byte(w, 3) - kQ80Magic;
+        } else {
+            const uint32_t w = (uint32_t)(*reinterpret_cast<const uint16_t*>(vr)) ^ 0x8080u;
+            vf[0] = magic_byte(w, 0) - kQ80Magic;
+            vf[1] = magic_byte(w, 1) - kQ80Magic;
+        }
+        const float vsc = a.vs[pp];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float wgt = __fmul_rn(sc[g][i], vsc);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) acc[g][j] = fmaf(wgt, vf[j], acc[g][j]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int j = 0; j < DPL; j++) red[warp][g][DPL * lane + j] = acc[g][j];
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += 128) {
+        const int g = i / HD, d = i % HD;
+        const float s = (red[0][g][d] + red[1][g][d]) + (red[2][g][d] + red[3][g][d]);
+        part[g * head_stride + 2 + d] = s;
+    }
+    if (tid < G) {
+        part[tid * head_stride + 0] = ml[tid][0];
+        part[tid * head_stride + 1] = ml[tid][1];
+    }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(HD) k_attn_combine(const AttnArgs a, int nchunks) {
+    const int h = blockIdx.x, d = threadIdx.x;
+    pdl_wait();
+    const float* part = a.partial + (size_t)h * nchunks * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nchunks; c++) M = fmaxf(M, part[(size_t)c * (HD + 2)]);
+    float L = 0.0f, acc = 0.0f;
+    for (int c = 0; c < nchunks; c++) {
+        const float* pc = part + (size_t)c * (HD + 2);
+        const float l = pc[1];
+        if (l == 0.0f) continue;
+        const float f = expf(__fsub_rn(pc[0], M));
+        L = fmaf(l, f, L);
+        acc = fmaf(pc[2 + d], f, acc);
+    }
+    // output_acc[d] * (1 / running_sum)  (flash_attention.rs:126-133)
+    a.out[(size_t)h * HD + d] = L > 0.0f ? __fmul_rn(acc, __fdiv_rn(1.0f, L)) : 0.0f;
+}
+
+size_t attn_partial_floats(int n_heads, int max_seq, int head_dim) {
+    const int nchunks = (max_seq + ATT_P - 1) / ATT_P;
+    return (size_t)n_heads * nchunks * (head_dim + 2);
+}
+
+template <int HD, int G>
+static int launch_attn_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    const int nchunks = (a.max_seq + ATT_P - 1) / ATT_P;
+    SSD_CK(launch_pdl(k_attn_partial<HD, G>, dim3(a.n_kv_local, nchunks), dim3(128), 0, s, pdl, a));
+    SSD_CK(launch_pdl(k_attn_combine<HD>, dim3(a.n_kv_local * G), dim3(HD), 0, s, pdl, a, nchunks));
+    return SSD_OK;
+}
+
+template <int HD>
+static int launch_attn_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    switch (a.group) {
+        case 1: return launch_attn_t<HD, 1>(a, s, pdl);
+        case 2: return launch_attn_t<HD, 2>(a, s, pdl);
+        case 4: return launch_attn_t<HD, 4>(a, s, pdl);
+        case 8: return launch_attn_t<HD, 8>(a, s, pdl);
+        default: set_error("GQA group %d not supported (1, 2, 4, 8)", a.group); return SSD_ERR_SHAPE;
+    }
+}
+
+int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    SSD_REQ(a.max_seq > 0, SSD_ERR_SHAPE, "empty attention");
+    if (a.head_dim == 128) return launch_attn_hd<128>(a, s, pdl);
+    if (a.head_dim == 64) return launch_attn_hd<64>(a, s, pdl);
+    set_error("head_dim %d not supported (64, 128)", a.head_dim);
+    return SSD_ERR_SHAPE;
+}
+
+int launch_kv_append(const ssd_kv_cache* kv, const float* k, const float* v, int pos,
+                     const int* pos_dev, int rows, cudaStream_t s, bool pdl) {
+    SSD_CK(launch_pdl(k_kv_append, dim3(rows, 2), dim3(256), 0, s, pdl, k, v, kv->k, kv->v,
+                      kv->k_scale, kv->v_scale, kv->kv_dim, pos, pos_dev, kv->capacity));
+    return SSD_OK;
+}
+
+// ---------------------------------------------------------- embed / finalize
+__global__ void __launch_bounds__(256) k_embed(const ssd_weight e, const int32_t* token,
+                                               float* hidden) {
+    pdl_wait();
+    int t = *token;
+    t = t < 0 ? 0 : (t >= e.rows ? e.rows - 1 : t);  // out-of-range ids clamp (no OOB read)
+    const int n = e.cols;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        float val;
+        if (e.type == SSD_TYPE_F32) {
+            val = reinterpret_cast<const float*>(e.qs)[(size_t)t * n + i];
+        } else if (e.type == SSD_TYPE_Q4_0) {
+            const size_t blk = (size_t)t * (n / 32) + i / 32;
+            const int j = i % 32;
+            const uint8_t byte = e.qs[blk * 16 + j / 2];
+            const int q = (j & 1) ? (byte >> 4) : (byte & 0x0F);
+            val = __fmul_rn((float)(q - 8), f16_bits_to_f32(reinterpret_cast<const uint16_t*>(e.meta)[blk]));
+        } else {  // Q8_0
+            const size_t blk = (size_t)t * (n / 32) + i / 32;
+            const int8_t q = reinterpret_cast<const int8_t*>(e.qs)[blk * 32 + i % 32];
+            val = __fmul_rn((float)q, f16_bits_to_f32(reinterpret_cast<const uint16_t*>(e.meta)[blk]));
+        }
+        hidden[i] = val;
+    }
+}
+
+__global__ void k_finalize(unsigned long long* key, int32_t* token, int* pos) {
+    pdl_wait();
+    const unsigned long long k = *key;
+    *token = (int32_t)(uint32_t)(k & 0xFFFFFFFFull);
+    *key = 0ull;
+    *pos += 1;
+}
+
+int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
+                 bool pdl) {
+    SSD_REQ(emb->type == SSD_TYPE_F32 || emb->type == SSD_TYPE_Q4_0 || emb->type == SSD_TYPE_Q8_0,
+            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0)", emb->type);
+    SSD_CK(launch_pdl(k_embed, dim3(1), dim3(256), 0, s, pdl, *emb, token_dev, hidden));
+    return SSD_OK;
+}
+
+int launch_finalize(unsigned long long* key, int32_t* token, int* pos, cudaStream_t s, bool pdl) {
+    SSD_CK(launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, pdl, key, token, pos));
+    return SSD_OK;
+}
+
+}  // namespace ssd
+
+using namespace ssd;
+
+// =================================================================== C ABI
+
+extern "C" int ssd_rmsnorm(ssd_ctx* ctx, float* x, const float* w, int n, float eps, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(x && w && n > 0, SSD_ERR_ARG, "bad arguments");
+    k_rmsnorm<<<1, 1024, 0, pick_stream(ctx, s)>>>(x, w, n, eps);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_fused_post_attn_norm(ssd_ctx* ctx, float* h, const float* a, const float* w,
+                                        int n, float eps, float* out, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(h && a && w && out && n > 0, SSD_ERR_ARG, "bad arguments");
+    k_post_attn_norm<<<1, 1024, 0, pick_stream(ctx, s)>>>(h, a, w, n, eps, out);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_softmax(ssd_ctx* ctx, float* x, int n, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(x != nullptr && n >= 0, SSD_ERR_ARG, "bad arguments");
+    if (n == 0) return SSD_OK;  // the reference returns early on empty input
+    k_softmax<<<1, 1024, 0, pick_stream(ctx, s)>>>(x, n);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_rope(ssd_ctx* ctx, float* x, int len, int head_dim, int n_heads, int position,
+                        float theta, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(x && head_dim > 1 && n_heads > 0 && len > 0, SSD_ERR_ARG, "bad arguments");
+    const int pairs = n_heads * (head_dim / 2);
+    k_rope<<<(pairs + 255) / 256, 256, 0, pick_stream(ctx, s)>>>(x, len, head_dim, n_heads,
+                                                                 position, theta);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_silu(ssd_ctx* ctx, float* x, int n, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(x && n > 0, SSD_ERR_ARG, "bad arguments");
+    k_silu<<<(n + 255) / 256, 256, 0, pick_stream(ctx, s)>>>(x, n);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_argmax(ssd_ctx* ctx, const float* v, int n, int32_t* idx, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(v && idx && n > 0, SSD_ERR_ARG, "bad arguments");
+    k_argmax<<<1, 1024, 0, pick_stream(ctx, s)>>>(v, n, idx);
+    SSD_CK_LAUNCH();
+    return SSD_OK;
+}
+
+extern "C" int ssd_kv_create(ssd_ctx* ctx, int capacity, int n_head_kv, int head_dim,
+                             ssd_kv_cache** out) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(out && capacity > 0 && n_head_kv > 0 && head_dim > 0, SSD_ERR_ARG, "bad arguments");
+    SSD_REQ(head_dim % 16 == 0, SSD_ERR_SHAPE, "head_dim %d must be a multiple of 16", head_dim);
+    const int kv_dim = n_head_kv * head_dim;
+    const size_t kb = (size_t)capacity * kv_dim;
+    const size_t kb_pad = (kb + 255) & ~(size_t)255;
+    const size_t sb_pad = ((size_t)capacity * 4 + 255) & ~(size_t)255;
+    const size_t total = 2 * kb_pad + 2 * sb_pad;
+    void* p = nullptr;
+    if (cudaMalloc(&p, total) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("KV cache allocation of %zu bytes failed", total);
+        return SSD_ERR_NOMEM;
+    }
+    SSD_CK(cudaMemset(p, 0, total));
+    ssd_kv_cache* kv = new ssd_kv_cache();
+    kv->ctx = ctx;
+    kv->capacity = capacity;
+    kv->n_head_kv = n_head_kv;
+    kv->head_dim = head_dim;
+    kv->kv_dim = kv_dim;
+    kv->base = p;
+    kv->k = (int8_t*)p;
+    kv->v = (int8_t*)p + kb_pad;
+    kv->k_scale = (float*)((char*)p + 2 * kb_pad);
+    kv->v_scale = (float*)((char*)p + 2 * kb_pad + sb_pad);
+    *out = kv;
+    return SSD_OK;
+}
+
+extern "C" int ssd_kv_free(ssd_kv_cache* kv) {
+    if (!kv) return SSD_OK;
+    cudaSetDevice(kv->ctx->device);
+    cudaFree(kv->base);
+    delete kv;
+    return SSD_OK;
+}
+
+extern "C" int ssd_kv_pointers(ssd_kv_cache* kv, int8_t** k, int8_t** v, float** ks, float** vs) {
+    SSD_REQ(kv != nullptr, SSD_ERR_ARG, "null cache");
+    if (k) *k = kv->k;
+    if (v) *v = kv->v;
+    if (ks) *ks = kv->k_scale;
+    if (vs) *vs = kv->v_scale;
+    return SSD_OK;
+}
+
+extern "C" int ssd_kv_append_rows(ssd_ctx* ctx, ssd_kv_cache* kv, const float* k, const float* v,
+                                  int position, int rows, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(kv && k && v && rows > 0, SSD_ERR_ARG, "bad arguments");
+    SSD_REQ(position >= 0 && position + rows <= kv->capacity, SSD_ERR_SHAPE,
+            "positions [%d, %d) exceed capacity %d", position, position + rows, kv->capacity);
+    return launch_kv_append(kv, k, v, position, nullptr, rows, pick_stream(ctx, s), false);
+}
+
+extern "C" int ssd_kv_append(ssd_ctx* ctx, ssd_kv_cache* kv, const float* k, const float* v,
+                             int position, void* s) {
+    return ssd_kv_append_rows(ctx, kv, k, v, position, 1, s);
+}
+
+extern "C" int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q,
+                                  int n_head, int seq_len, float* out, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(kv && q && out, SSD_ERR_ARG, "null pointer");
+    SSD_REQ(seq_len > 0 && seq_len <= kv->capacity, SSD_ERR_SHAPE, "seq_len %d outside (0, %d]",
+            seq_len, kv->capacity);
+    SSD_REQ(n_head % kv->n_head_kv == 0, SSD_ERR_SHAPE, "n_head %d not a multiple of n_head_kv %d",
+            n_head, kv->n_head_kv);
+    const size_t pf = attn_partial_floats(n_head, seq_len, kv->head_dim);
+    SSD_TRY(ensure_scratch(ctx, pf * 4));
+    AttnArgs a = {};
+    a.k = kv->k;
+    a.v = kv->v;
+    a.ks = kv->k_scale;
+    a.vs = kv->v_scale;
+    a.kv_dim = kv->kv_dim;
+    a.head_dim = kv->head_dim;
+    a.group = n_head / kv->n_head_kv;
+    a.kv_head0 = 0;
+    a.n_kv_local = kv->n_head_kv;
+    a.q = q;
+    a.out = out;
+    a.partial = (float*)ctx->scratch;
+    a.seq_len = seq_len;
+    a.pos_dev = nullptr;
+    a.max_seq = seq_len;
+    return launch_attention(a, pick_stream(ctx, s), false);
+}

@@ -1,0 +1,38 @@
+// ops.cuh — launchers for the non-matvec operators (internal interface).
+#pragma once
+#include "common.cuh"
+
+namespace ssd {
+
+// INT8 KV append of one position (k and v rows of kv_dim floats). The position is
+// read from pos_dev when non-null (graph replay), else `pos`.
+int launch_kv_append(const ssd_kv_cache* kv, const float* k, const float* v, int pos,
+                     const int* pos_dev, int rows, cudaStream_t s, bool pdl);
+
+// Split-K decode attention over the INT8 cache. seq_len = (*pos_dev + 1) when pos_dev
+// is non-null, else seq_len. kv_head0 / n_kv_local select this rank's KV heads;
+// q holds n_kv_local * group heads. partial must hold attn_partial_floats() floats.
+struct AttnArgs {
+    const int8_t* k;
+    const int8_t* v;
+    const float* ks;
+    const float* vs;
+    int kv_dim, head_dim, group, kv_head0, n_kv_local;
+    const float* q;
+    float* out;
+    float* partial;
+    int seq_len;
+    const int* pos_dev;
+    int max_seq;  // grid is sized for max_seq positions (graph-stable)
+};
+size_t attn_partial_floats(int n_heads, int max_seq, int head_dim);
+int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// Embedding row gather (token from *token_dev, or from the argmax key when
+// key_dev is non-null) into hidden.
+int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
+                 bool pdl);
+// token = low 32 bits of *key; *key = 0; *pos += 1.
+int launch_finalize(unsigned long long* key, int32_t* token, int* pos, cudaStream_t s, bool pdl);
+
+}  // namespace ssd

@@ -1,0 +1,520 @@
+"""Python binding of the sm_100a backend (ctypes over include/ssdllm_cuda.h).
+
+`CudaCompute` mirrors the operator surface of ssd-llm's `MetalCompute`
+(src/metal/compute.rs:18-373): same method names and argument meaning, host
+slices in, host results out. The device-pointer functions (`matvec`, `kv_append`,
+`attention_int8`, ...) take torch CUDA tensors and run on torch's current stream.
+Everything runs through libssdllm_cuda.so; there is no CPU fallback: if the
+library or a GPU is missing, loading fails with an error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(HERE, "libssdllm_cuda.so")
+
+F32, F16, Q4_0, Q8_0, Q4_K = 0, 1, 2, 8, 12
+BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), F32: (1, 4)}
+STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported ggml type", 3: "shape mismatch",
+          4: "CUDA error", 5: "device wait timed out", 6: "NCCL error",
+          7: "out of device memory", 8: "invalid state"}
+
+_lib = None
+_vp = ctypes.c_void_p
+
+
+class SsdError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class ModelConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "n_layers", "n_embd", "n_head", "n_head_kv", "head_dim", "n_ff", "vocab", "wtype",
+        "out_type", "embd_type", "kv_capacity")] + [
+        ("theta", ctypes.c_float), ("eps", ctypes.c_float), ("tp_rank", ctypes.c_int),
+        ("tp_size", ctypes.c_int)]
+
+
+# name -> (argtypes, restype); the set is checked against include/ssdllm_cuda.h by tests
+_SIGS = {
+    "ssd_abi_version": ([], ctypes.c_int),
+    "ssd_status_str": ([ctypes.c_int], ctypes.c_char_p),
+    "ssd_last_error": ([], ctypes.c_char_p),
+    "ssd_ctx_create": ([ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_ctx_get": ([ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_ctx_destroy": ([_vp], ctypes.c_int),
+    "ssd_ctx_stream": ([_vp, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_ctx_sync": ([_vp], ctypes.c_int),
+    "ssd_ctx_info": ([_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_size_t],
+                     ctypes.c_int),
+    "ssd_ctx_set_pdl": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_copy_to_device": ([_vp, _vp, _vp, ctypes.c_size_t], ctypes.c_int),
+    "ssd_copy_to_host": ([_vp, _vp, _vp, ctypes.c_size_t], ctypes.c_int),
+    "ssd_weight_upload": ([_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                           ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_weight_upload_device": ([_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, ctypes.POINTER(_vp), _vp], ctypes.c_int),
+    "ssd_weight_download": ([_vp, _vp, _vp, ctypes.c_size_t], ctypes.c_int),
+    "ssd_weight_free": ([_vp], ctypes.c_int),
+    "ssd_weight_info": ([_vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                         ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_size_t)],
+                        ctypes.c_int),
+    "ssd_row_bytes": ([ctypes.c_int, ctypes.c_int64], ctypes.c_size_t),
+    "ssd_weight_synth": ([_vp, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_float,
+                          ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                          ctypes.POINTER(_vp), _vp], ctypes.c_int),
+    "ssd_synth_f32": ([_vp, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_float, ctypes.c_float,
+                       ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                       _vp, _vp], ctypes.c_int),
+    "ssd_quantize": ([_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp],
+                     ctypes.c_int),
+    "ssd_dequantize": ([_vp, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_matvec": ([_vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_matvec_residual": ([_vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_fused_rmsnorm_matvec": ([_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp], ctypes.c_int),
+    "ssd_fused_qkv_rope": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_int,
+                            ctypes.c_int, ctypes.c_float, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_fused_swiglu": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp], ctypes.c_int),
+    "ssd_rmsnorm": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_float, _vp], ctypes.c_int),
+    "ssd_fused_post_attn_norm": ([_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_float, _vp, _vp],
+                                 ctypes.c_int),
+    "ssd_softmax": ([_vp, _vp, ctypes.c_int, _vp], ctypes.c_int),
+    "ssd_rope": ([_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                  ctypes.c_float, _vp], ctypes.c_int),
+    "ssd_silu": ([_vp, _vp, ctypes.c_int, _vp], ctypes.c_int),
+    "ssd_argmax": ([_vp, _vp, ctypes.c_int, _vp, _vp], ctypes.c_int),
+    "ssd_kv_create": ([_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)],
+                      ctypes.c_int),
+    "ssd_kv_free": ([_vp], ctypes.c_int),
+    "ssd_kv_pointers": ([_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                         ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_kv_append": ([_vp, _vp, _vp, _vp, ctypes.c_int, _vp], ctypes.c_int),
+    "ssd_kv_append_rows": ([_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp], ctypes.c_int),
+    "ssd_attention_int8": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp], ctypes.c_int),
+    "ssd_matvec_quantized_host": ([_vp, _vp, ctypes.c_size_t, _vp, _vp, ctypes.c_int,
+                                   ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "ssd_model_create": ([_vp, ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_model_free": ([_vp], ctypes.c_int),
+    "ssd_shard_range": ([ctypes.POINTER(ModelConfig), ctypes.c_char_p, ctypes.c_int,
+                         ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                         ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
+                        ctypes.c_int),
+    "ssd_tp_unique_id": ([ctypes.c_char_p], ctypes.c_int),
+    "ssd_model_tp_init": ([_vp, ctypes.c_char_p], ctypes.c_int),
+    "ssd_model_synth_weights": ([_vp, ctypes.c_uint64, ctypes.c_float], ctypes.c_int),
+    "ssd_model_set_tensor": ([_vp, ctypes.c_char_p, ctypes.c_int, _vp, ctypes.c_size_t],
+                             ctypes.c_int),
+    "ssd_model_synth_kv": ([_vp, ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
+    "ssd_model_set_position": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_model_get_position": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "ssd_model_decode_step": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_model_decode_token": ([_vp, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
+                                ctypes.c_int], ctypes.c_int),
+    "ssd_model_state": ([_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp)],
+                        ctypes.c_int),
+    "ssd_model_weight": ([_vp, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_vp)],
+                         ctypes.c_int),
+    "ssd_model_norm": ([_vp, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_model_kv": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_model_layer_step": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_model_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+}
+
+
+def lib():
+    """Loads libssdllm_cuda.so (raises if it is missing: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} missing: build it with ssd-llm_b200/build.py")
+        try:  # torch first, so its libnccl.so.2 is the one both libraries use
+            import torch  # noqa: F401
+        except ImportError:
+            pass
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def check(status: int):
+    if status != 0:
+        raise SsdError(status, lib().ssd_last_error().decode(errors="replace"))
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def row_bytes(wtype: int, cols: int) -> int:
+    return int(lib().ssd_row_bytes(wtype, cols))
+
+
+class Context:
+    """A device context (MetalCompute::new / MetalGpu::new)."""
+
+    def __init__(self, device: int = 0, cached: bool = True):
+        h = _vp()
+        check((lib().ssd_ctx_get if cached else lib().ssd_ctx_create)(device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+        self.cached = cached
+
+    def sync(self):
+        check(lib().ssd_ctx_sync(self.h))
+
+    def set_pdl(self, on: bool):
+        check(lib().ssd_ctx_set_pdl(self.h, int(on)))
+
+    def info(self):
+        n = ctypes.c_int()
+        buf = ctypes.create_string_buffer(256)
+        check(lib().ssd_ctx_info(self.h, ctypes.byref(n), buf, 256))
+        return n.value, buf.value.decode()
+
+    def close(self):
+        if self.h and not self.cached:
+            lib().ssd_ctx_destroy(self.h)
+        self.h = None
+
+
+class Weight:
+    """HBM-resident quantized tensor (reference block layout in, library layout inside)."""
+
+    def __init__(self, ctx: Context, handle, wtype: int, rows: int, cols: int):
+        self.ctx, self.h, self.type, self.rows, self.cols = ctx, handle, wtype, rows, cols
+
+    @classmethod
+    def upload(cls, ctx: Context, raw: np.ndarray, wtype: int, rows: int, cols: int):
+        raw = np.ascontiguousarray(raw, dtype=np.uint8)
+        h = _vp()
+        check(lib().ssd_weight_upload(ctx.h, raw.ctypes.data, raw.nbytes, wtype, rows, cols,
+                                      ctypes.byref(h)))
+        return cls(ctx, h, wtype, rows, cols)
+
+    @classmethod
+    def upload_device(cls, ctx: Context, raw_dev, wtype: int, rows: int, cols: int):
+        h = _vp()
+        check(lib().ssd_weight_upload_device(ctx.h, _ptr(raw_dev), raw_dev.numel(), wtype, rows,
+                                             cols, ctypes.byref(h), _stream()))
+        return cls(ctx, h, wtype, rows, cols)
+
+    @classmethod
+    def synth(cls, ctx: Context, wtype: int, seed: int, tensor_id: int, std: float,
+              total_cols: int, row0: int, rows: int, col0: int, cols: int):
+        h = _vp()
+        check(lib().ssd_weight_synth(ctx.h, wtype, seed, tensor_id, std, total_cols, row0, rows,
+                                     col0, cols, ctypes.byref(h), _stream()))
+        return cls(ctx, h, wtype, rows, cols)
+
+    def raw_bytes(self) -> int:
+        return row_bytes(self.type, self.cols) * self.rows
+
+    def download(self) -> np.ndarray:
+        out = np.zeros(self.raw_bytes(), dtype=np.uint8)
+        check(lib().ssd_weight_download(self.ctx.h, self.h, out.ctypes.data, out.nbytes))
+        return out
+
+    def free(self):
+        if self.h and not getattr(self, "borrowed", False):
+            lib().ssd_weight_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------- device-pointer ops
+def matvec(ctx, w: Weight, x, y):
+    check(lib().ssd_matvec(ctx.h, w.h, _ptr(x), _ptr(y), _stream()))
+
+
+def matvec_residual(ctx, w: Weight, x, base, y):
+    check(lib().ssd_matvec_residual(ctx.h, w.h, _ptr(x), _ptr(base), _ptr(y), _stream()))
+
+
+def fused_rmsnorm_matvec(ctx, w: Weight, x, norm_w, eps, y):
+    check(lib().ssd_fused_rmsnorm_matvec(ctx.h, w.h, _ptr(x), _ptr(norm_w), eps, _ptr(y),
+                                         _stream()))
+
+
+def fused_qkv_rope(ctx, wq, wk, wv, x, norm_w, eps, head_dim, position, theta, q, k, v):
+    check(lib().ssd_fused_qkv_rope(ctx.h, wq.h, wk.h, wv.h, _ptr(x), _ptr(norm_w), eps, head_dim,
+                                   position, theta, _ptr(q), _ptr(k), _ptr(v), _stream()))
+
+
+def fused_swiglu(ctx, wg, wu, x, norm_w, eps, act):
+    check(lib().ssd_fused_swiglu(ctx.h, wg.h, wu.h, _ptr(x), _ptr(norm_w), eps, _ptr(act),
+                                 _stream()))
+
+
+def quantize(ctx, x, wtype, raw_out):
+    rows, cols = x.shape
+    check(lib().ssd_quantize(ctx.h, _ptr(x), rows, cols, wtype, _ptr(raw_out), _stream()))
+
+
+def dequantize(ctx, w: Weight, out):
+    check(lib().ssd_dequantize(ctx.h, w.h, _ptr(out), _stream()))
+
+
+def synth_f32(ctx, seed, tensor_id, mean, std, total_cols, row0, rows, col0, cols, out):
+    check(lib().ssd_synth_f32(ctx.h, seed, tensor_id, mean, std, total_cols, row0, rows, col0,
+                              cols, _ptr(out), _stream()))
+
+
+def rmsnorm(ctx, x, w, eps=1e-5):
+    check(lib().ssd_rmsnorm(ctx.h, _ptr(x), _ptr(w), x.numel(), eps, _stream()))
+
+
+def fused_post_attn_norm(ctx, h, a, w, eps, out):
+    check(lib().ssd_fused_post_attn_norm(ctx.h, _ptr(h), _ptr(a), _ptr(w), h.numel(), eps,
+                                         _ptr(out), _stream()))
+
+
+def softmax(ctx, x):
+    check(lib().ssd_softmax(ctx.h, _ptr(x), x.numel(), _stream()))
+
+
+def rope(ctx, x, head_dim, n_heads, position, theta):
+    check(lib().ssd_rope(ctx.h, _ptr(x), x.numel(), head_dim, n_heads, position, theta,
+                         _stream()))
+
+
+def silu(ctx, x):
+    check(lib().ssd_silu(ctx.h, _ptr(x), x.numel(), _stream()))
+
+
+def argmax(ctx, v, idx):
+    check(lib().ssd_argmax(ctx.h, _ptr(v), v.numel(), _ptr(idx), _stream()))
+
+
+class KvCache:
+    """Device INT8 KV cache of one layer (QuantizedLayerKvCache)."""
+
+    def __init__(self, ctx: Context, capacity: int, n_head_kv: int, head_dim: int):
+        h = _vp()
+        check(lib().ssd_kv_create(ctx.h, capacity, n_head_kv, head_dim, ctypes.byref(h)))
+        self.ctx, self.h = ctx, h
+        self.capacity, self.n_head_kv, self.head_dim = capacity, n_head_kv, head_dim
+
+    def pointers(self):
+        k, v, ks, vs = _vp(), _vp(), _vp(), _vp()
+        check(lib().ssd_kv_pointers(self.h, ctypes.byref(k), ctypes.byref(v), ctypes.byref(ks),
+                                    ctypes.byref(vs)))
+        return k.value, v.value, ks.value, vs.value
+
+    def append(self, k, v, position: int):
+        check(lib().ssd_kv_append(self.ctx.h, self.h, _ptr(k), _ptr(v), position, _stream()))
+
+    def append_rows(self, k, v, position: int):
+        check(lib().ssd_kv_append_rows(self.ctx.h, self.h, _ptr(k), _ptr(v), position,
+                                       k.shape[0], _stream()))
+
+    def attention(self, q, n_head: int, seq_len: int, out):
+        check(lib().ssd_attention_int8(self.ctx.h, self.h, _ptr(q), n_head, seq_len, _ptr(out),
+                                       _stream()))
+
+    def free(self):
+        if self.h:
+            lib().ssd_kv_free(self.h)
+            self.h = None
+
+
+class Model:
+    """Decode engine (forward_pass / generate's token loop) on HBM-resident weights."""
+
+    def __init__(self, ctx: Context, **cfg):
+        c = ModelConfig(**cfg)
+        h = _vp()
+        check(lib().ssd_model_create(ctx.h, ctypes.byref(c), ctypes.byref(h)))
+        self.ctx, self.h, self.cfg = ctx, h, c
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(lib().ssd_tp_unique_id(buf))
+        return buf.raw
+
+    def tp_init(self, uid: bytes):
+        check(lib().ssd_model_tp_init(self.h, uid))
+
+    def synth_weights(self, seed: int, std: float = 0.02):
+        check(lib().ssd_model_synth_weights(self.h, seed, std))
+
+    def set_tensor(self, name: str, layer: int, raw: np.ndarray):
+        raw = np.ascontiguousarray(raw)
+        check(lib().ssd_model_set_tensor(self.h, name.encode(), layer, raw.ctypes.data,
+                                         raw.nbytes))
+
+    def synth_kv(self, seed: int, n: int):
+        check(lib().ssd_model_synth_kv(self.h, seed, n))
+
+    def set_position(self, pos: int):
+        check(lib().ssd_model_set_position(self.h, pos))
+
+    def position(self) -> int:
+        p = ctypes.c_int()
+        check(lib().ssd_model_get_position(self.h, ctypes.byref(p)))
+        return p.value
+
+    def decode_step(self, use_graph: bool = True):
+        check(lib().ssd_model_decode_step(self.h, int(use_graph)))
+
+    def decode_token(self, token: int, use_graph: bool = True) -> int:
+        out = ctypes.c_int32()
+        check(lib().ssd_model_decode_token(self.h, token, ctypes.byref(out), int(use_graph)))
+        return out.value
+
+    def state_ptrs(self):
+        h, lg, t = _vp(), _vp(), _vp()
+        check(lib().ssd_model_state(self.h, ctypes.byref(h), ctypes.byref(lg), ctypes.byref(t)))
+        return h.value, lg.value, t.value
+
+    def weight(self, name: str, layer: int) -> Weight:
+        """Borrowed handle of this rank's shard (owned by the model; do not free)."""
+        h = _vp()
+        check(lib().ssd_model_weight(self.h, name.encode(), layer, ctypes.byref(h)))
+        t, r, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        check(lib().ssd_weight_info(h, ctypes.byref(t), ctypes.byref(r), ctypes.byref(c), None))
+        w = Weight.__new__(Weight)
+        w.ctx, w.h, w.type, w.rows, w.cols = self.ctx, h, t.value, r.value, c.value
+        w.borrowed = True
+        return w
+
+    def norm(self, name: str, layer: int) -> int:
+        p = _vp()
+        check(lib().ssd_model_norm(self.h, name.encode(), layer, ctypes.byref(p)))
+        return p.value
+
+    def kv(self, layer: int):
+        h = _vp()
+        check(lib().ssd_model_kv(self.h, layer, ctypes.byref(h)))
+        k = KvCache.__new__(KvCache)
+        k.ctx, k.h = self.ctx, h
+        k.capacity, k.n_head_kv, k.head_dim = (self.cfg.kv_capacity, self.cfg.n_head_kv,
+                                               self.cfg.head_dim)
+        return k
+
+    def layer_step(self, layer: int):
+        check(lib().ssd_model_layer_step(self.h, layer))
+
+    def launches_per_step(self) -> int:
+        n = ctypes.c_int()
+        check(lib().ssd_model_launches_per_step(self.h, ctypes.byref(n)))
+        return n.value
+
+    def free(self):
+        if self.h:
+            lib().ssd_model_free(self.h)
+            self.h = None
+
+
+def shard_range(cfg: ModelConfig, name: str, layer: int):
+    """(row0, nrows, col0, ncols) of tensor `name` kept by rank cfg.tp_rank (host only)."""
+    v = [ctypes.c_int() for _ in range(4)]
+    check(lib().ssd_shard_range(ctypes.byref(cfg), name.encode(), layer,
+                                *[ctypes.byref(x) for x in v]))
+    return tuple(x.value for x in v)
+
+
+class CudaCompute:
+    """Host-slice mirror of MetalCompute (src/metal/compute.rs:18-373).
+
+    Same method names and argument meaning as the reference; numpy arrays stand
+    in for Rust slices. Each call copies in, runs the CUDA kernel, copies out.
+    `new()` mirrors MetalCompute::new() -> Option<Self> but raises instead of
+    returning None when no device is usable (no silent CPU fallback).
+    """
+
+    def __init__(self, device: int = 0):
+        import torch
+        self.torch = torch
+        self.ctx = Context(device)
+        self.dev = torch.device("cuda", device)
+
+    @classmethod
+    def new(cls, device: int = 0):
+        return cls(device)
+
+    def _d(self, a):
+        return self.torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.dev)
+
+    def matvec_quantized(self, w_raw, x, out_dim, in_dim, dtype):
+        """compute.rs:157-191"""
+        w_raw = np.ascontiguousarray(w_raw, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(out_dim, dtype=np.float32)
+        check(lib().ssd_matvec_quantized_host(self.ctx.h, w_raw.ctypes.data, w_raw.nbytes,
+                                              x.ctypes.data, y.ctypes.data, out_dim, in_dim,
+                                              dtype))
+        return y
+
+    def rmsnorm_f32(self, x: np.ndarray, weight, eps):
+        """compute.rs:193-202 (in place on x)."""
+        xd, wd = self._d(x), self._d(weight)
+        rmsnorm(self.ctx, xd, wd, eps)
+        x[:] = xd.cpu().numpy()
+
+    def softmax_f32(self, x: np.ndarray):
+        """compute.rs:204-213 (in place)."""
+        xd = self._d(x)
+        softmax(self.ctx, xd)
+        x[:] = xd.cpu().numpy()
+
+    def fused_post_attn_norm_f32(self, hidden: np.ndarray, attn_output, norm_weight, eps):
+        """compute.rs:328-346: hidden += attn; returns rmsnorm(hidden)."""
+        hd, ad, wd = self._d(hidden), self._d(attn_output), self._d(norm_weight)
+        out = self.torch.empty_like(hd)
+        fused_post_attn_norm(self.ctx, hd, ad, wd, eps, out)
+        hidden[:] = hd.cpu().numpy()
+        return out.cpu().numpy()
+
+    def flash_attention_int8(self, q_heads, k_q, k_scale, v_q, v_scale, n_head, n_head_kv,
+                             head_dim, seq_len):
+        """compute.rs:217-258 over the INT8 cache (quantized_kv_cache.rs:107-130)."""
+        kv = KvCache(self.ctx, seq_len, n_head_kv, head_dim)
+        try:
+            kp, vp, ksp, vsp = kv.pointers()
+            self._copy_to(kp, np.ascontiguousarray(k_q, dtype=np.int8))
+            self._copy_to(vp, np.ascontiguousarray(v_q, dtype=np.int8))
+            self._copy_to(ksp, np.ascontiguousarray(k_scale, dtype=np.float32))
+            self._copy_to(vsp, np.ascontiguousarray(v_scale, dtype=np.float32))
+            qd = self._d(q_heads)
+            out = self.torch.empty(n_head * head_dim, device=self.dev)
+            kv.attention(qd, n_head, seq_len, out)
+            return out.cpu().numpy()
+        finally:
+            self.torch.cuda.synchronize()
+            kv.free()
+
+    def _copy_to(self, dev_ptr: int, host: np.ndarray):
+        self.torch.cuda.synchronize()
+        copy_to_device(self.ctx, dev_ptr, host)
+
+
+def copy_to_device(ctx: Context, dev_ptr: int, host: np.ndarray):
+    host = np.ascontiguousarray(host)
+    check(lib().ssd_copy_to_device(ctx.h, dev_ptr, host.ctypes.data, host.nbytes))
+
+
+def copy_to_host(ctx: Context, host: np.ndarray, dev_ptr: int):
+    check(lib().ssd_copy_to_host(ctx.h, host.ctypes.data, dev_ptr, host.nbytes))

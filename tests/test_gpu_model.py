@@ -1,0 +1,170 @@
+"""GPU parity of the decode engine vs the oracle's restatement of forward_pass /
+generate (src/inference/transformer.rs:283-399, :681-770) over an INT8 KV cache."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import ssdllm  # noqa: E402
+from oracle import oracle as ora  # noqa: E402
+
+from _util import rel_err  # noqa: E402
+
+LAYER_NAMES = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return ssdllm.Context(0)
+
+
+def make_weights(rng, E, nh, nkv, hd, F, vocab, n_layers, wtype=ora.Q4_0):
+    shapes = {"attn_q": (nh * hd, E), "attn_k": (nkv * hd, E), "attn_v": (nkv * hd, E),
+              "attn_output": (E, E), "ffn_gate": (F, E), "ffn_up": (F, E), "ffn_down": (E, F)}
+    layers = []
+    for _ in range(n_layers):
+        L = {n: ora.quantize((rng.standard_normal(s) * 0.02).astype(np.float32), wtype)
+             for n, s in shapes.items()}
+        L["attn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+        L["ffn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+        layers.append(L)
+    glob = {"token_embd": ora.quantize(rng.standard_normal((vocab, E)).astype(np.float32),
+                                       ora.Q4_0),
+            "output": ora.quantize((rng.standard_normal((vocab, E)) * 0.05).astype(np.float32),
+                                   ora.Q4_0),
+            "output_norm": (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)}
+    return layers, glob
+
+
+def build_model(ctx, cfg, layers, glob):
+    m = ssdllm.Model(ctx, **cfg)
+    for li, L in enumerate(layers):
+        for n, a in L.items():
+            m.set_tensor(n, li, a)
+    for n, a in glob.items():
+        m.set_tensor(n, -1, a)
+    return m
+
+
+def oracle_layers(cfg, layers):
+    return [ora.Layer(cfg["n_embd"], cfg["n_head"], cfg["n_head_kv"], cfg["head_dim"],
+                      cfg["n_ff"], cfg["wtype"], *(L[n] for n in LAYER_NAMES), L["attn_norm"],
+                      L["ffn_norm"], theta=cfg["theta"], eps=cfg["eps"]) for L in layers]
+
+
+def read_cache(ctx, m, layer, n, kvd):
+    kp, vp, ksp, vsp = m.kv(layer).pointers()
+    out = []
+    for ptr, shape, dt in ((kp, (n, kvd), np.int8), (ksp, (n,), np.float32),
+                           (vp, (n, kvd), np.int8), (vsp, (n,), np.float32)):
+        a = np.zeros(shape, dt)
+        if n:
+            ssdllm.copy_to_host(ctx, a, ptr)
+        out.append(a)
+    return out
+
+
+@pytest.mark.parametrize("shape", ["small_gqa", "llama2_7b"])
+def test_layer_step_matches_oracle(ctx, shape):
+    """One decoder layer at position P over an INT8 cache holding P positions
+    (BASELINE config 2 at full size: hidden 4096, 32 heads, FFN 11008, L = 2048)."""
+    if shape == "small_gqa":
+        E, nh, nkv, hd, F, P, theta = 512, 8, 2, 64, 1024, 77, 5e5
+    else:
+        E, nh, nkv, hd, F, P, theta = 4096, 32, 32, 128, 11008, 2048, 1e4
+    cfg = dict(n_layers=1, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=64,
+               wtype=ora.Q4_0, out_type=ora.Q4_0, embd_type=ora.Q4_0, kv_capacity=P + 1,
+               theta=theta, eps=1e-5, tp_rank=0, tp_size=1)
+    rng = np.random.default_rng(E + P)
+    layers, glob = make_weights(rng, E, nh, nkv, hd, F, 64, 1)
+    m = build_model(ctx, cfg, layers, glob)
+    m.synth_kv(seed=99, n=P)  # K, V ~ N(0, 1), INT8-quantized rows; position = P
+    kvd = nkv * hd
+    kc, ks, vc, vs = read_cache(ctx, m, 0, P, kvd)
+    h0 = rng.standard_normal(E).astype(np.float32)
+    hptr, _, _ = m.state_ptrs()
+    ssdllm.copy_to_device(ctx, hptr, h0)
+    m.layer_step(0)
+    got = np.zeros(E, np.float32)
+    ssdllm.copy_to_host(ctx, got, hptr)
+    # new K/V row as the device quantized it
+    kc1, ks1, vc1, vs1 = read_cache(ctx, m, 0, P + 1, kvd)
+    m.free()
+
+    K = np.zeros((P + 1, kvd), np.int8)
+    V = np.zeros((P + 1, kvd), np.int8)
+    KS = np.zeros(P + 1, np.float32)
+    VS = np.zeros(P + 1, np.float32)
+    K[:P], V[:P], KS[:P], VS[:P] = kc, vc, ks, vs
+    h = h0.copy()
+    oracle_layers(cfg, layers)[0].step(h, P, K, KS, V, VS, mode=0, threads=8)
+    assert rel_err(got, h) <= 1e-3
+    # the appended INT8 row agrees with the oracle's (rounding ties may move a code by 1)
+    assert np.max(np.abs(kc1[P].astype(int) - K[P].astype(int))) <= 1
+    assert abs(ks1[P] - KS[P]) <= 1e-4 * abs(KS[P])
+
+
+def test_greedy_decode_64_steps_identical(ctx):
+    """64 greedy tokens from the decode engine equal the oracle's decode loop
+    (generate without the stop-on-EOS/0 rule, so the runs stay aligned)."""
+    E, nh, nkv, hd, F, vocab, nl = 256, 4, 2, 64, 512, 512, 2
+    cfg = dict(n_layers=nl, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=vocab,
+               wtype=ora.Q4_0, out_type=ora.Q4_0, embd_type=ora.Q4_0, kv_capacity=80,
+               theta=1e4, eps=1e-5, tp_rank=0, tp_size=1)
+    rng = np.random.default_rng(2024)
+    layers, glob = make_weights(rng, E, nh, nkv, hd, F, vocab, nl)
+    m = build_model(ctx, cfg, layers, glob)
+    m.set_position(0)
+    tok0 = 17
+    gpu, t = [], tok0
+    for _ in range(64):
+        t = m.decode_token(t, use_graph=True)
+        gpu.append(t)
+    assert m.position() == 64
+    m.free()
+
+    OL = oracle_layers(cfg, layers)
+    emb = ora.dequantize(glob["token_embd"], ora.Q4_0, vocab * E).reshape(vocab, E)
+    out_w = ora.dequantize(glob["output"], ora.Q4_0, vocab * E).reshape(vocab, E)
+    kvd = nkv * hd
+    caches = [(np.zeros((80, kvd), np.int8), np.zeros(80, np.float32),
+               np.zeros((80, kvd), np.int8), np.zeros(80, np.float32)) for _ in range(nl)]
+    ref, t = [], tok0
+    for pos in range(64):
+        h = emb[t].copy()
+        for li in range(nl):
+            kc, ks, vc, vs = caches[li]
+            OL[li].step(h, pos, kc, ks, vc, vs, mode=0, threads=4)
+        logits = ora.fused_rmsnorm_linear(h, glob["output_norm"], out_w, vocab, E)
+        t = ora.argmax(logits)
+        srt = np.sort(logits)
+        margin = (srt[-1] - srt[-2]) / np.max(np.abs(logits))
+        if gpu[pos] != t:
+            # only a near-tie (below fp32 reordering noise) may differ; stop comparing there
+            assert margin < 1e-4, (pos, gpu[pos], t, margin)
+            return
+        ref.append(t)
+    assert gpu == ref
+
+
+def test_graph_and_eager_steps_agree(ctx):
+    E, nh, nkv, hd, F, vocab = 256, 4, 4, 64, 512, 256
+    cfg = dict(n_layers=2, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=vocab,
+               wtype=ora.Q8_0, out_type=ora.Q4_0, embd_type=ora.Q4_0, kv_capacity=32,
+               theta=1e4, eps=1e-5, tp_rank=0, tp_size=1)
+    m = ssdllm.Model(ctx, **cfg)
+    m.synth_weights(seed=5, std=0.05)
+    toks = {}
+    for g in (False, True):
+        m.set_position(0)
+        t, seq = 3, []
+        for _ in range(12):
+            t = m.decode_token(t, use_graph=g)
+            seq.append(t)
+        toks[g] = seq
+    assert toks[False] == toks[True]
+    assert m.launches_per_step() == 1 + 2 * 7 + 2
+    m.free()
