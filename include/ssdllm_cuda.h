@@ -14,7 +14,8 @@
  *    src/metal/compute.rs:672-675); it returns SSD_ERR_TYPE instead.
  *    ssd_last_error() gives a message for the calling thread's last failure.
  *  - Pointers named *_dev are device pointers; `stream` is a cudaStream_t
- *    (NULL = the context's own stream). Device-pointer calls are stream-ordered
+ *    (NULL = CUDA's default stream, as in every CUDA API; the context's own stream
+ *    is available from ssd_ctx_stream). Device-pointer calls are stream-ordered
  *    and asynchronous; they allocate nothing on the hot path.
  *  - Calls named *_host take host slices, copy in, compute, copy out and
  *    synchronise: they keep the reference's synchronous semantics
@@ -77,6 +78,11 @@ int ssd_ctx_get(int device, ssd_ctx** out);
 int ssd_ctx_destroy(ssd_ctx* ctx);
 int ssd_ctx_stream(ssd_ctx* ctx, void** stream_out);
 int ssd_ctx_sync(ssd_ctx* ctx);
+/* Reads and clears the device status word: SSD_ERR_TIMEOUT if a kernel's bounded
+ * wait (TMA barrier, peer flag) gave up since the last call, else SSD_OK. Synchronises
+ * the device. No reference counterpart (Metal calls block until completion,
+ * src/metal/gpu.rs:531-532). */
+int ssd_ctx_device_status(ssd_ctx* ctx, int* status);
 /* Launch the context's standalone kernels (ssd_matvec and the fused matvecs) with
  * programmatic dependent launch, so a kernel's weight prefetch overlaps the tail
  * of the kernel before it on the same stream (default off). The decode engine

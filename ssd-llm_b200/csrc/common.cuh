@@ -1,6 +1,7 @@
 // common.cuh — shared definitions of the sm_100a backend (internal).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -57,6 +58,7 @@ struct ssd_ctx {
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     unsigned long long* argmax_key = nullptr;  // 8-byte (value, index) slot
+    int* dev_status = nullptr;                 // device status word (bounded waits)
 };
 
 // Device layout of a quantized tensor (library-owned): structure of arrays so that
@@ -93,12 +95,8 @@ __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
     return __half2float(__ushort_as_half(h));
 }
 
-// Byte-granular float construction: byte k of `lo` (which holds 0x80 | q) placed in
-// byte 2 under exponent byte 0x3F gives the float 1 + q/128 exactly.
-__device__ __forceinline__ float biased_nib(uint32_t lo, int k) {
-    return __uint_as_float(__byte_perm(lo, 0x3F000000u, 0x7044u | (k << 8)));
-}
-// 2^23 + byte k of `b` (an unsigned byte), exact.
+// 2^23 + byte k of `b` (an unsigned byte), exact: byte_perm puts the byte in the low
+// mantissa byte under exponent byte 0x4B.
 __device__ __forceinline__ float magic_byte(uint32_t b, int k) {
     return __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7440u | k));
 }
@@ -137,6 +135,53 @@ __device__ __forceinline__ float synth_normal(uint64_t seed, uint32_t tid, uint6
     return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
 }
 
+// ------------------------------------------------------------- TMA / mbarrier
+// Device-side status word (one int per context, ssd_ctx::dev_status): a bounded wait
+// that gives up records SSD_ERR_TIMEOUT there (read and cleared by
+// ssd_ctx_device_status) and the kernel skips the work that depended on it.
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+// Waits for phase `parity` of the barrier with an iteration limit (about a second).
+// Returns false, after recording SSD_ERR_TIMEOUT in *status, if the limit is reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t it = 0; it < (1u << 20); it++) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    if (status) atomicExch(status, SSD_ERR_TIMEOUT);
+    return false;
+}
+// 2-D tiled TMA load (no multicast) of box {c0, c1} into shared memory, completing on bar.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -170,11 +215,21 @@ inline int type_block_bytes(int type) {
     }
 }
 
+// A NULL stream argument is CUDA's default stream (it orders with torch's default
+// stream and every other legacy-stream user); the context's own stream is only used
+// when passed explicitly (ssd_ctx_stream) and by the synchronous host-slice calls.
 inline cudaStream_t pick_stream(ssd_ctx* ctx, void* s) {
-    return s ? (cudaStream_t)s : ctx->stream;
+    (void)ctx;
+    return (cudaStream_t)s;
 }
 
 int check_ctx(ssd_ctx* ctx);
+// Encodes a 2-D fp32 tensor map over a vector of n floats viewed as rows of 32 floats
+// (128 B), box = 32 rows, 128-byte swizzle: chunk c's 16-byte unit u lands at unit
+// u ^ (c & 7) of its row, so the 8 units a lane reads are bank-conflict free across a
+// quarter warp. n must be a multiple of 32 and ptr 16-byte aligned.
+int encode_vec_map(CUtensorMap* map, const float* ptr, int n);
+constexpr int kVecBoxRows = 32;
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out);
 int ensure_scratch(ssd_ctx* ctx, size_t bytes);
 

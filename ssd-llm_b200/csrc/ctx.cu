@@ -14,6 +14,36 @@ namespace ssd {
 
 static thread_local char g_err[1024];
 
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_vec_map(CUtensorMap* map, const float* ptr, int n) {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        SSD_CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q));
+        SSD_REQ(f != nullptr && q == cudaDriverEntryPointSuccess, SSD_ERR_CUDA,
+                "cuTensorMapEncodeTiled unavailable");
+        fn = (EncodeTiledFn)f;
+    }
+    SSD_REQ(ptr && ((uintptr_t)ptr & 15u) == 0 && n > 0 && n % 32 == 0, SSD_ERR_ARG,
+            "tensor map: vector must be 16-byte aligned with a multiple of 32 floats");
+    cuuint64_t dims[2] = {32, (cuuint64_t)(n / 32)};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {32, (cuuint32_t)kVecBoxRows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    SSD_REQ(r == CUDA_SUCCESS, SSD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSD_OK;
+}
+
 void set_error(const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -29,8 +59,8 @@ int check_ctx(ssd_ctx* ctx) {
 
 int ensure_scratch(ssd_ctx* ctx, size_t bytes) {
     if (ctx->scratch_bytes >= bytes) return SSD_OK;
-    if (ctx->scratch) {
-        SSD_CK(cudaStreamSynchronize(ctx->stream));
+    if (ctx->scratch) {  // callers may have work in flight on any stream
+        SSD_CK(cudaDeviceSynchronize());
         SSD_CK(cudaFree(ctx->scratch));
         ctx->scratch = nullptr;
         ctx->scratch_bytes = 0;
@@ -154,11 +184,9 @@ __device__ void quant_block_q4_k(const float* x, uint8_t* meta16, uint8_t* qs128
     __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
     __half mh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
     float d = __half2float(dh), dmin = __half2float(mh);
-    uint16_t db = __half_as_ushort(dh), mb = __half_as_ushort(mh);
-    meta16[0] = db & 0xFF;
-    meta16[1] = db >> 8;
-    meta16[2] = mb & 0xFF;
-    meta16[3] = mb >> 8;
+    // f16 d and dmin, little-endian: aligned 16-bit stores (meta16 is 2-byte aligned)
+    reinterpret_cast<uint16_t*>(meta16)[0] = __half_as_ushort(dh);
+    reinterpret_cast<uint16_t*>(meta16)[1] = __half_as_ushort(mh);
     uint8_t sc6[8], m6[8];
     for (int s = 0; s < 8; s++) {
         sc6[s] = (uint8_t)(d > 0.0f ? min(63, max(0, (int)roundf(__fdiv_rn(scale[s], d)))) : 0);
@@ -194,16 +222,14 @@ __global__ void k_quantize_raw(const float* __restrict__ x, int type, int64_t nb
         uint16_t d;
         uint8_t nib[16];
         quant_block_q4_0(x + i * 32, nib, &d);
-        o[0] = d & 0xFF;
-        o[1] = d >> 8;
+        *reinterpret_cast<uint16_t*>(o) = d;  // 18-byte blocks: 2-byte aligned
         for (int j = 0; j < 16; j++) o[2 + j] = nib[j];
     } else if (type == SSD_TYPE_Q8_0) {
         uint8_t* o = raw + i * 34;
         uint16_t d;
         int8_t q[32];
         quant_block_q8_0(x + i * 32, q, &d);
-        o[0] = d & 0xFF;
-        o[1] = d >> 8;
+        *reinterpret_cast<uint16_t*>(o) = d;  // 34-byte blocks: 2-byte aligned
         for (int j = 0; j < 32; j++) o[2 + j] = (uint8_t)q[j];
     } else {
         uint8_t* o = raw + i * 144;
@@ -350,11 +376,13 @@ extern "C" int ssd_ctx_create(int device, ssd_ctx** out) {
     c->smem_optin = p.sharedMemPerBlockOptin;
     snprintf(c->name, sizeof(c->name), "%s", p.name);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&c->argmax_key, 64) != cudaSuccess) {
+        cudaMalloc(&c->argmax_key, 64) != cudaSuccess ||
+        cudaMemset(c->argmax_key, 0, 64) != cudaSuccess) {
         set_error("context setup failed: %s", cudaGetErrorString(cudaGetLastError()));
         delete c;
         return SSD_ERR_CUDA;
     }
+    c->dev_status = reinterpret_cast<int*>(c->argmax_key + 4);  // same 64-byte allocation
     *out = c;
     return SSD_OK;
 }
@@ -392,6 +420,15 @@ extern "C" int ssd_ctx_stream(ssd_ctx* ctx, void** s) {
 extern "C" int ssd_ctx_sync(ssd_ctx* ctx) {
     SSD_TRY(check_ctx(ctx));
     SSD_CK(cudaStreamSynchronize(ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_ctx_device_status(ssd_ctx* ctx, int* status) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(status != nullptr, SSD_ERR_ARG, "null status");
+    SSD_CK(cudaDeviceSynchronize());
+    SSD_CK(cudaMemcpy(status, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost));
+    SSD_CK(cudaMemset(ctx->dev_status, 0, sizeof(int)));
     return SSD_OK;
 }
 
@@ -526,7 +563,8 @@ extern "C" int ssd_weight_upload(ssd_ctx* ctx, const void* host_raw, size_t byte
         set_error("upload copy failed: %s", cudaGetErrorString(cudaGetLastError()));
         st = SSD_ERR_CUDA;
     }
-    if (st == SSD_OK) st = ssd_weight_upload_device(ctx, staging, bytes, type, rows, cols, out, nullptr);
+    if (st == SSD_OK) st = ssd_weight_upload_device(ctx, staging, bytes, type, rows, cols, out,
+                                            (void*)ctx->stream);
     cudaStreamSynchronize(ctx->stream);
     cudaFree(staging);
     return st;

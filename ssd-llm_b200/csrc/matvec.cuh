@@ -37,6 +37,7 @@ struct MvArgs {
     const int* position_dev;  // if non-null, position is read from device memory
     unsigned long long* argmax_key;
     int index_offset;  // added to row index for ARGMAX (tensor-parallel vocab shards)
+    int* status;       // device status word for bounded waits (default: the context's)
 };
 
 // Launches y = f(W x) with the given epilogue. pdl: launch with programmatic

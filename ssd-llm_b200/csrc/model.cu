@@ -373,10 +373,10 @@ extern "C" int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_de
         if (s.type == SSD_TYPE_F32) {
             SSD_TRY(alloc_weight(m->ctx, SSD_TYPE_F32, s.nrows, s.ncols, &w));
             SSD_TRY(ssd_synth_f32(m->ctx, seed, s.tid, 0.0f, sd, s.cols, s.row0, s.nrows, s.col0,
-                                  s.ncols, (float*)w->qs, nullptr));
+                                  s.ncols, (float*)w->qs, (void*)m->ctx->stream));
         } else {
             SSD_TRY(ssd_weight_synth(m->ctx, s.type, seed, s.tid, sd, s.cols, s.row0, s.nrows,
-                                     s.col0, s.ncols, &w, nullptr));
+                                     s.col0, s.ncols, &w, (void*)m->ctx->stream));
         }
         ssd_weight_free(*slot);
         *slot = w;
@@ -385,7 +385,7 @@ extern "C" int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_de
     auto norm = [&](float** slot, uint32_t tid) -> int {
         if (!*slot) SSD_CK(cudaMalloc(slot, (size_t)c.n_embd * 4));
         return ssd_synth_f32(m->ctx, seed, tid, 1.0f, 0.02f, c.n_embd, 0, 1, 0, c.n_embd, *slot,
-                             nullptr);
+                             (void*)m->ctx->stream);
     };
     for (int l = 0; l < c.n_layers; l++) {
         for (const char* nm : names) SSD_TRY(synth(nm, l, std_dev));
@@ -421,10 +421,10 @@ extern "C" int ssd_model_synth_kv(ssd_model* m, uint64_t seed, int n) {
                 const int rows = n - p0 < chunk ? n - p0 : chunk;
                 // K and V rows N(0, 1): element (pos, i) of tensors 2000000 + 2l (+1)
                 st = ssd_synth_f32(m->ctx, seed, 2000000u + 2u * l, 0.0f, 1.0f, kvd, p0, rows, 0,
-                                   kvd, tmp, nullptr);
+                                   kvd, tmp, (void*)m->ctx->stream);
                 if (st == SSD_OK)
                     st = ssd_synth_f32(m->ctx, seed, 2000001u + 2u * l, 0.0f, 1.0f, kvd, p0, rows,
-                                       0, kvd, tmp + (size_t)chunk * kvd, nullptr);
+                                       0, kvd, tmp + (size_t)chunk * kvd, (void*)m->ctx->stream);
                 if (st == SSD_OK)
                     st = launch_kv_append(m->layers[l].kv, tmp, tmp + (size_t)chunk * kvd, p0,
                                           nullptr, rows, m->ctx->stream, false);

@@ -54,6 +54,7 @@ _SIGS = {
     "ssd_ctx_info": ([_vp, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_size_t],
                      ctypes.c_int),
     "ssd_ctx_set_pdl": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_ctx_device_status": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "ssd_copy_to_device": ([_vp, _vp, _vp, ctypes.c_size_t], ctypes.c_int),
     "ssd_copy_to_host": ([_vp, _vp, _vp, ctypes.c_size_t], ctypes.c_int),
     "ssd_weight_upload": ([_vp, _vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -178,6 +179,11 @@ class Context:
 
     def sync(self):
         check(lib().ssd_ctx_sync(self.h))
+
+    def device_status(self) -> int:
+        st = ctypes.c_int()
+        check(lib().ssd_ctx_device_status(self.h, ctypes.byref(st)))
+        return st.value
 
     def set_pdl(self, on: bool):
         check(lib().ssd_ctx_set_pdl(self.h, int(on)))

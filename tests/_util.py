@@ -25,3 +25,12 @@ def gpu_available() -> bool:
         return torch.cuda.is_available()
     except Exception:
         return False
+
+
+def parity(y, r, exact, tol=1e-3) -> bool:
+    """GPU result y vs oracle r at rel_err <= tol; where the oracle's own fp32 rounding
+    (long sequential sums) is what exceeds tol, an fp64 result arbitrates: y passes if
+    it is no further from `exact` than the oracle is."""
+    if rel_err(y, r) <= tol:
+        return True
+    return rel_err(y, exact) <= max(rel_err(r, exact), tol)
