@@ -14,7 +14,10 @@ Reported on the same JSON line:
              graph, next token out (D2H), synchronised every step
   roofline   the dominant kernel (gate/up dequant-matvec + SwiGLU) timed alone on
              the model's own layer weights, algorithmic bytes / event time
-  kernels    BASELINE config 0: Q4_0 4096x4096 matvec GB/s (32 rotating copies, 302 MB)
+  kernels    BASELINE configs 0-2 one kernel at a time: Q4_0 4096x4096, Q8_0 / Q4_K at
+             11008x4096 and 4096x11008 (rotating weight copies > 2x L2), the INT8-KV
+             attention at the 70B shape, and the Llama-2-7B-shaped layer step (GB/s,
+             fraction of the measured HBM peak); `--case NAME` runs one of them alone
   cpu_baseline  the oracle's restatement of the reference layer step on packed Q4_0
              (src/inference/transformer.rs:283-399 with matvec_quantized_cpu), all host
              cores, one layer timed and extrapolated to 80 layers + logits
@@ -209,46 +212,179 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ CUDA arm
-def time_matvec_config0(ctx, torch, ssdllm, peak):
-    """Q4_0 4096x4096 matvec GB/s over 32 rotating weight copies
-    (302 MB > 2x L2), 64 launches per CUDA graph replay, with and without PDL."""
-    rows = cols = 4096
-    copies = [ssdllm.Weight.synth(ctx, Q4_0, 0, 900 + i, 0.02, cols, 0, rows, 0, cols)
-              for i in range(32)]
+def _graph_time(torch, launches, reps):
+    """Capture `launches` (closures that each enqueue one kernel on torch's current
+    stream) into one CUDA graph and return microseconds per launch over `reps`
+    replays, timed with CUDA events on the replay stream after 3 warm-up replays."""
+    for f in launches[:2]:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in launches:
+            f()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * len(launches))
+
+
+L2_BYTES = 126 * 1024 * 1024
+TYPE_NAMES = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K"}
+
+
+def case_matvec(ctx, torch, ssdllm, peak, wtype, rows, cols, reps=20):
+    """Dequant-matvec y = W x (BASELINE configs 0 and 1) over rotating weight copies
+    whose total exceeds 2x L2, so every launch streams its weights from HBM; with and
+    without programmatic dependent launch (PDL); the faster is reported."""
+    wbytes = rows * ssdllm.row_bytes(wtype, cols)
+    copies = min(64, max(2, -(-int(2.2 * L2_BYTES) // wbytes)))
+    ws = [ssdllm.Weight.synth(ctx, wtype, 0, 900 + i, 0.02, cols, 0, rows, 0, cols)
+          for i in range(copies)]
     x = torch.randn(cols, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
     y = torch.zeros(rows, device="cuda")
+    n = max(copies, 64 // copies * copies)
+    alg = wbytes + cols * 4 + rows * 4
     res = {}
     for pdl in (False, True):
         ctx.set_pdl(pdl)
-        for w in copies[:2]:
-            ssdllm.matvec(ctx, w, x, y)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for i in range(64):
-                ssdllm.matvec(ctx, copies[i % 32], x, y)
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 20
-        e0.record()
-        for _ in range(reps):
-            g.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * 64)
-        alg = rows * cols * Q40_BYTES + cols * 4 + rows * 4
-        res["pdl" if pdl else "plain"] = {"us_per_launch": us, "gbs": alg / us / 1e3,
-                                          "frac_of_peak": alg / us / 1e3 / peak}
-        del g
+        us = _graph_time(torch, [lambda w=ws[i % copies]: ssdllm.matvec(ctx, w, x, y)
+                                 for i in range(n)], reps)
+        res["pdl" if pdl else "plain"] = {"us_per_launch": round(us, 3),
+                                          "gbs": round(alg / us / 1e3, 1),
+                                          "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
     ctx.set_pdl(False)
-    for w in copies:
+    for w in ws:
         w.free()
     best = max(res.values(), key=lambda r: r["gbs"])
-    return {"shape": [rows, cols], "algorithmic_bytes": rows * cols * Q40_BYTES + cols * 8,
-            **{k: round(v, 3) if isinstance(v, float) else v for k, v in best.items()},
-            "variants": res}
+    return {"type": TYPE_NAMES[wtype], "shape": [rows, cols], "algorithmic_bytes": alg,
+            "rotating_copies": copies, **best, "variants": res}
+
+
+def case_attention(ctx, torch, ssdllm, peak, n_head=64, n_head_kv=8, head_dim=128, seq=4096,
+                   reps=20):
+    """Split-K flash-decode over the INT8 KV cache (70B shape: 64 q / 8 kv heads,
+    4096 positions), 8 rotating caches (> 2x L2 of K/V bytes in total)."""
+    kvd = n_head_kv * head_dim
+    gen = torch.Generator("cuda").manual_seed(3)
+    caches = []
+    ncache = max(2, -(-int(2.2 * L2_BYTES) // (2 * seq * kvd)))
+    for _ in range(ncache):
+        kv = ssdllm.KvCache(ctx, seq, n_head_kv, head_dim)
+        k = torch.randn(seq, kvd, device="cuda", generator=gen)
+        v = torch.randn(seq, kvd, device="cuda", generator=gen)
+        kv.append_rows(k, v, 0)
+        caches.append(kv)
+    q = torch.randn(n_head * head_dim, device="cuda", generator=gen)
+    out = torch.zeros_like(q)
+    us = _graph_time(torch, [lambda kv=caches[i % ncache]: kv.attention(q, n_head, seq, out)
+                             for i in range(max(ncache, 16))], reps)
+    for kv in caches:
+        kv.free()
+    alg = 2 * seq * kvd + 8 * seq + 2 * n_head * head_dim * 4
+    return {"shape": {"n_head": n_head, "n_head_kv": n_head_kv, "head_dim": head_dim,
+                      "seq": seq}, "algorithmic_bytes": alg, "rotating_caches": ncache,
+            "us_per_call": round(us, 3), "kernels_per_call": 2,
+            "gbs": round(alg / us / 1e3, 1), "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
+
+
+def case_layer_7b(ctx, torch, ssdllm, peak, n_layers=8, reps=10):
+    """Llama-2-7B-shaped decoder layer decode step (Q4_0, INT8 KV at
+    2048 positions), timed as a CUDA-graph decode step of an n_layers-deep model with a
+    256-token vocab (embed + logits add < 0.1% of the bytes); per layer = step / n_layers."""
+    cfg = dict(n_layers=n_layers, n_embd=4096, n_head=32, n_head_kv=32, head_dim=128,
+               n_ff=11008, vocab=256, wtype=Q4_0, out_type=Q4_0, embd_type=Q4_0,
+               kv_capacity=2048 + 4 * reps + 16, theta=1e4, eps=1e-5, tp_rank=0, tp_size=1)
+    m = ssdllm.Model(ctx, **cfg)
+    try:
+        m.synth_weights(seed=7, std=0.02)
+        m.synth_kv(seed=8, n=2048)
+        stream = torch.cuda.ExternalStream(ssdllm_stream(ctx, ssdllm))
+        m.decode_step(True)
+        for _ in range(3):
+            m.decode_step(True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            m.decode_step(True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us_layer = e0.elapsed_time(e1) * 1e3 / reps / n_layers
+        launches = m.launches_per_step()
+    finally:
+        m.free()
+    E, F = 4096, 11008
+    alg = int((4 * E * E + 3 * F * E) * Q40_BYTES) + 2 * 2049 * E + 8 * 2049 + 2 * E * 4
+    return {"shape": "llama2-7b layer, Q4_0, INT8 KV 2048", "algorithmic_bytes": alg,
+            "us_per_layer": round(us_layer, 3), "gbs": round(alg / us_layer / 1e3, 1),
+            "frac_of_peak": round(alg / us_layer / 1e3 / peak, 4),
+            "launches_per_layer": 6, "model_layers_timed": n_layers, "launches_per_step": launches}
+
+
+def case_swiglu_70b(ctx, torch, ssdllm, peak, reps=10):
+    """The decode step's dominant kernel alone: fused gate/up Q4_0 dequant-matvec with the
+    FFN RMSNorm prologue and SwiGLU epilogue at the Llama-70B shape (2 x 28672 x 8192,
+    264 MB per launch), 2 rotating weight sets."""
+    E, F = 8192, 28672
+    sets = []
+    for i in range(2):
+        wg = ssdllm.Weight.synth(ctx, Q4_0, 0, 700 + 2 * i, 0.02, E, 0, F, 0, E)
+        wu = ssdllm.Weight.synth(ctx, Q4_0, 0, 701 + 2 * i, 0.02, E, 0, F, 0, E)
+        sets.append((wg, wu))
+    gen = torch.Generator("cuda").manual_seed(5)
+    x = torch.randn(E, device="cuda", generator=gen)
+    nw = 1 + 0.1 * torch.randn(E, device="cuda", generator=gen)
+    act = torch.zeros(F, device="cuda")
+    ctx.set_pdl(True)
+    us = _graph_time(torch, [lambda s=sets[i % 2]: ssdllm.fused_swiglu(ctx, s[0], s[1], x, nw,
+                                                                       1e-5, act)
+                             for i in range(8)], reps)
+    ctx.set_pdl(False)
+    for wg, wu in sets:
+        wg.free()
+        wu.free()
+    alg = int(2 * F * E * Q40_BYTES) + 2 * E * 4 + F * 4
+    return {"shape": [2 * F, E], "algorithmic_bytes": alg, "us_per_launch": round(us, 3),
+            "gbs": round(alg / us / 1e3, 1), "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
+
+
+CASES = {
+    "q4_0_4096x4096": lambda c, t, s, p: case_matvec(c, t, s, p, Q4_0, 4096, 4096),
+    "q8_0_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 8, 11008, 4096),
+    "q8_0_4096x11008": lambda c, t, s, p: case_matvec(c, t, s, p, 8, 4096, 11008),
+    "q4_k_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 12, 11008, 4096),
+    "q4_k_4096x11008": lambda c, t, s, p: case_matvec(c, t, s, p, 12, 4096, 11008),
+    "swiglu_q4_0_70b": case_swiglu_70b,
+    "attn_int8_70b_4096": case_attention,
+    "layer_7b_q4_0": case_layer_7b,
+}
+
+
+def run_cases(names, peak):
+    import torch
+    import ssdllm
+    ctx = ssdllm.Context(torch.cuda.current_device())
+    return {n: CASES[n](ctx, torch, ssdllm, peak) for n in names}
+
+
+def run_case_cli(args):
+    """--case NAME[,NAME...]: one kernel configuration alone (parity configs 0-2 and the
+    attention kernel), for profiling and the per-kernel table; prints one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    peak, src = measured_peaks()
+    names = list(CASES) if args.case == "all" else args.case.split(",")
+    res = run_cases(names, peak)
+    print(json.dumps({"cases": res, "peak_gbs": peak, "peak_source": src}), flush=True)
+    return 0
 
 
 def time_dominant_kernel(ctx, model, torch, ssdllm, cfg, world):
@@ -356,7 +492,7 @@ def run_cuda(args):
             tt = torch.tensor([dom_us], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             dom_us = float(tt[0])
-        k0 = time_matvec_config0(ctx, torch, ssdllm, peak) if rank == 0 else None
+        k0 = run_cases(list(CASES), peak) if rank == 0 and not args.no_kernels else None
         clocks = clk.summary() if rank == 0 else None
     finally:
         model.free()  # releases the graph holding NCCL calls before the process group
@@ -402,7 +538,7 @@ def run_cuda(args):
         "cpu_baseline": cpu,
         "gpu_launches": launches * args.steps,
         "clocks": clocks,
-        "kernels": {"q4_0_matvec_4096x4096": k0},
+        "kernels": k0,
         "setup_s": setup_s,
     }
     print(json.dumps(line), flush=True)
@@ -432,11 +568,18 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="override n_layers (debug only; the headline uses 80)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true",
+                    help="skip the per-kernel table (BASELINE configs 0-2)")
+    ap.add_argument("--case", default="",
+                    help="run only kernel configuration(s) NAME[,NAME] or 'all': " +
+                         ", ".join(CASES))
     args = ap.parse_args()
     if args.warmup < 1:
         args.warmup = 1
     if args.impl == "reference":
         return run_reference(args)
+    if args.case:
+        return run_case_cli(args)
     return run_cuda(args)
 
 
