@@ -217,6 +217,21 @@ int ssd_kv_append_rows(ssd_ctx* ctx, ssd_kv_cache* kv, const float* k_dev, const
 int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev, int n_head,
                        int seq_len, float* out_dev, void* stream);
 
+/* ssd_attention_int8 for callers that cannot allocate device memory (code running
+ * beside a CUDA graph capture, hosts whose framework owns the device allocator, loops
+ * that must never block in cudaMalloc/cudaFree). No reference counterpart.
+ * Same arguments and results as ssd_attention_int8, but the split-K partials live in
+ * a fixed 4 MiB device array inside the library (held on every GPU that loads the
+ * library until the process exits) instead of the context's scratch buffer; this
+ * call allocates nothing. Limit: n_head * ceil(seq_len / 128) * (head_dim + 2) must
+ * be at most 1,048,576 floats (e.g. 64 heads x 16,128 positions at head_dim 128);
+ * larger calls return SSD_ERR_SHAPE. The first call on a device looks up the array's
+ * device address, so make that first call before any stream capture. All calls share
+ * the one array: calls whose kernels overlap on the GPU (different streams, or
+ * different threads without ordering) race and must be serialised by the caller. */
+int ssd_attention_int8_noalloc(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev,
+                               int n_head, int seq_len, float* out_dev, void* stream);
+
 /* ------------------------------------------------- host-slice operators */
 /* MetalCompute::matvec_quantized (src/metal/compute.rs:157-191) with its exact
  * signature semantics: raw weight bytes, x and y on the host; uploads, computes,

@@ -8,6 +8,8 @@
 // argmax of src/inference/sampler.rs:572-578.
 #include <math.h>
 
+#include <mutex>
+
 #include "ops.cuh"
 
 namespace ssd {
@@ -559,6 +561,71 @@ extern "C" int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const fl
     a.q = q;
     a.out = out;
     a.partial = (float*)ctx->scratch;
+    a.seq_len = seq_len;
+    a.pos_dev = nullptr;
+    a.max_seq = seq_len;
+    return launch_attention(a, pick_stream(ctx, s), false);
+}
+
+// ============================================ allocation-free attention variant
+// Some callers cannot allocate device memory: code that runs while a CUDA graph is
+// being captured elsewhere in the process, hosts whose allocator is owned by a
+// framework that forbids foreign cudaMalloc/cudaFree (a cudaFree synchronises the
+// whole device), and real-time loops that must not block in the driver. For them,
+// ssd_attention_int8_noalloc keeps the split-K partials in this fixed device array
+// instead of the context's growable scratch buffer. The array is part of the
+// library image: every GPU that loads the library holds its 4 MiB until the process
+// exits. Nothing in it needs to start at zero: k_attn_partial writes every
+// (head, chunk) record that k_attn_combine reads, on every call.
+constexpr size_t kNoAllocPartialFloats = (size_t)1 << 20;  // 4 MiB
+static __device__ __align__(256) float g_noalloc_partial[kNoAllocPartialFloats];
+
+// Device address of g_noalloc_partial on each device, looked up once per device with
+// that device current. In host code the array's name is only a host-side stand-in,
+// never a device address.
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64] = {nullptr};
+
+static int noalloc_partial_ptr(int device, float** out) {
+    SSD_REQ(device >= 0 && device < 64, SSD_ERR_ARG, "device %d out of range", device);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        SSD_CK(cudaGetSymbolAddress(&p, g_noalloc_partial));  // check_ctx made `device` current
+        g_noalloc_ptr[device] = (float*)p;
+    }
+    *out = g_noalloc_ptr[device];
+    return SSD_OK;
+}
+
+extern "C" int ssd_attention_int8_noalloc(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q,
+                                          int n_head, int seq_len, float* out, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(kv && q && out, SSD_ERR_ARG, "null pointer");
+    SSD_REQ(seq_len > 0 && seq_len <= kv->capacity, SSD_ERR_SHAPE, "seq_len %d outside (0, %d]",
+            seq_len, kv->capacity);
+    SSD_REQ(n_head % kv->n_head_kv == 0, SSD_ERR_SHAPE, "n_head %d not a multiple of n_head_kv %d",
+            n_head, kv->n_head_kv);
+    const size_t pf = attn_partial_floats(n_head, seq_len, kv->head_dim);
+    SSD_REQ(pf <= kNoAllocPartialFloats, SSD_ERR_SHAPE,
+            "attention_int8_noalloc: %d heads x %d positions need %zu partial floats; the fixed "
+            "buffer holds %zu (n_head * ceil(seq_len/128) * (head_dim+2) must not exceed it)",
+            n_head, seq_len, pf, kNoAllocPartialFloats);
+    float* partial = nullptr;
+    SSD_TRY(noalloc_partial_ptr(ctx->device, &partial));
+    AttnArgs a = {};
+    a.k = kv->k;
+    a.v = kv->v;
+    a.ks = kv->k_scale;
+    a.vs = kv->v_scale;
+    a.kv_dim = kv->kv_dim;
+    a.head_dim = kv->head_dim;
+    a.group = n_head / kv->n_head_kv;
+    a.kv_head0 = 0;
+    a.n_kv_local = kv->n_head_kv;
+    a.q = q;
+    a.out = out;
+    a.partial = partial;
     a.seq_len = seq_len;
     a.pos_dev = nullptr;
     a.max_seq = seq_len;

@@ -98,6 +98,8 @@ _SIGS = {
     "ssd_kv_append": ([_vp, _vp, _vp, _vp, ctypes.c_int, _vp], ctypes.c_int),
     "ssd_kv_append_rows": ([_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp], ctypes.c_int),
     "ssd_attention_int8": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp], ctypes.c_int),
+    "ssd_attention_int8_noalloc": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp],
+                                   ctypes.c_int),
     "ssd_matvec_quantized_host": ([_vp, _vp, ctypes.c_size_t, _vp, _vp, ctypes.c_int,
                                    ctypes.c_int, ctypes.c_int], ctypes.c_int),
     "ssd_model_create": ([_vp, ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], ctypes.c_int),
@@ -338,6 +340,12 @@ class KvCache:
     def attention(self, q, n_head: int, seq_len: int, out):
         check(lib().ssd_attention_int8(self.ctx.h, self.h, _ptr(q), n_head, seq_len, _ptr(out),
                                        _stream()))
+
+    def attention_noalloc(self, q, n_head: int, seq_len: int, out):
+        """ssd_attention_int8 with the partials in the library's fixed device array
+        (no device allocation; see include/ssdllm_cuda.h for the limit)."""
+        check(lib().ssd_attention_int8_noalloc(self.ctx.h, self.h, _ptr(q), n_head, seq_len,
+                                               _ptr(out), _stream()))
 
     def free(self):
         if self.h:
