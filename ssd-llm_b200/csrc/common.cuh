@@ -50,6 +50,7 @@ struct ssd_ctx {
     int device = 0;
     int num_sms = 0;
     size_t smem_optin = 0;
+    size_t smem_per_sm = 0;  // shared memory per SM usable by resident CTAs
     char name[256] = {0};
     cudaStream_t stream = nullptr;
     bool cached = false;  // owned by the process-wide cache; destroy is a no-op

@@ -374,6 +374,7 @@ extern "C" int ssd_ctx_create(int device, ssd_ctx** out) {
     c->device = device;
     c->num_sms = p.multiProcessorCount;
     c->smem_optin = p.sharedMemPerBlockOptin;
+    c->smem_per_sm = p.sharedMemPerMultiprocessor;
     snprintf(c->name, sizeof(c->name), "%s", p.name);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->argmax_key, 64) != cudaSuccess ||

@@ -8,17 +8,23 @@
 //  * A warp owns R consecutive output rows; lane l owns the 32-wide chunks
 //    c = l, l+32, ... of those rows. Each chunk is one aligned 16-byte (Q4_0, Q4_K)
 //    or 2x16-byte (Q8_0) vector load, so a warp reads 512 contiguous bytes per row.
-//  * Weight loads for the first steps are issued before griddepcontrol.wait: they do
-//    not depend on the previous kernel, so under programmatic dependent launch they
-//    overlap its tail. Loads are double-buffered in registers across chunk steps.
-//  * The kernel is persistent: x is staged once per CTA by TMA into shared memory with
-//    the 128-byte swizzle (chunk c's 16-byte unit u at unit u ^ (c & 7)), so the 8
-//    float4 reads of a chunk are bank-conflict free across a quarter warp; the
+//    Loads run one register stage (U chunks per row) ahead of the arithmetic and
+//    across row-group boundaries; the first stage is issued before
+//    griddepcontrol.wait, so under programmatic dependent launch (PDL) it overlaps
+//    the previous kernel's tail.
+//  * The kernel is persistent: x is staged once per CTA by TMA into shared memory
+//    with the 128-byte swizzle (chunk c's 16-byte unit u at unit u ^ (c & 7)), so
+//    the 8 float4 reads of a chunk are bank-conflict free across a quarter warp; the
 //    residual add and RMSNorm are applied there.
-//  * Quantized values become floats without int->float conversion instructions:
-//    byte_perm places a byte under exponent byte 0x4B, giving 2^23 + b exactly, and one
-//    FADD removes the offset: q - 8 for Q4_0, q for Q4_K, (q+128) - 128 for Q8_0. The
-//    values are exact, so each chunk dot product carries only fp32 FMA rounding.
+//  * Exact decode with one logic op per weight ("denormal decode"): masking a
+//    quantized field in place, w & (0xF << s), and reading the word as an fp32 gives
+//    the denormal q * 2^(s-149) exactly (s <= 16 keeps q * 2^s below 2^23). x is
+//    staged pre-multiplied by 2^(85-s) for each element's field position s, so one
+//    FFMA adds q * x * 2^-64 to the chunk sum, and the epilogue multiplies by 2^64.
+//    All scalings are powers of two, so the arithmetic is the fp32 dot product of the
+//    exact integers q with x; only fp32 FMA rounding remains. Offsets are folded in
+//    by chunk sums of x: sum (q-8) x = sum q x - 8 X (Q4_0), sum q x - 128 X for
+//    Q8_0 read as unsigned q+128, and scale * sum q x - min * X for Q4_K.
 //  * Epilogues fuse what follows the matvec in the decode step: residual add,
 //    SwiGLU, RoPE on Q/K, or argmax (LAST index on ties, sampler.rs:572-578).
 #include <mutex>
@@ -27,7 +33,17 @@
 
 namespace ssd {
 
-constexpr float kQ80Magic = 8388736.0f;  // 2^23 + 128
+// Field positions and the matching power-of-two pre-scale of x. Element k of a
+// 32-bit word sits at bit 4k (nibbles: element 2j = low nibble of byte j,
+// src/metal/compute.rs:693-699) or 8k (Q8_0 bytes). Fields above bit 16 are first
+// shifted down (by 12 for nibbles, 16 for bytes) so that every decoded value is a
+// denormal.
+constexpr int kScaleBias = 85;         // x'' = x * 2^(85 - s); products carry 2^-64
+constexpr float kUnscale = 18446744073709551616.0f;  // 2^64
+__host__ __device__ constexpr int nib_pos(int k) { return k <= 4 ? 4 * k : 4 * k - 12; }
+__host__ __device__ constexpr int byte_pos(int k) { return (k & 1) * 8; }
+
+__device__ __forceinline__ float den(uint32_t bits) { return __uint_as_float(bits); }
 
 template <int FMT>
 struct Chunk;
@@ -47,12 +63,7 @@ struct Chunk<SSD_TYPE_Q4_K> {
     uint4 m;
 };
 
-struct RowPtr {
-    const uint8_t* qs;
-    const uint8_t* meta;
-};
-
-__device__ __forceinline__ void map_row(const MvArgs& a, int v, int& seg, int& lr) {
+__device__ __forceinline__ void map_row(const MvArgs& a, int R, int v, int& seg, int& lr) {
     if (a.map == MAP_PLAIN) {
         seg = 0;
         lr = v;
@@ -67,154 +78,198 @@ __device__ __forceinline__ void map_row(const MvArgs& a, int v, int& seg, int& l
             seg = 2;
             lr = v - a.seg_rows[0] - a.seg_rows[1];
         }
-    } else {  // MAP_SWIGLU: virtual rows 4g..4g+3 = gate 2g, gate 2g+1, up 2g, up 2g+1
-        int g = v >> 2, j = v & 3;
-        seg = j >> 1;
-        lr = 2 * g + (j & 1);
+    } else {  // MAP_SWIGLU: rows R*g .. R*g+R/2-1 are gate rows (R/2)g.., the rest up rows
+        const int h = R >> 1;
+        const int g = v / R, j = v % R;
+        seg = j >= h;
+        lr = h * g + (j - (j >= h ? h : 0));
     }
 }
 
+// Byte pointers of one row of the library layout (see ssd_weight in common.cuh).
 template <int FMT>
-__device__ __forceinline__ RowPtr row_ptr(const MvArgs& a, int v) {
+__device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uint8_t*& qs,
+                                        const uint8_t*& meta) {
     int seg, lr;
-    map_row(a, v, seg, lr);
+    map_row(a, R, v, seg, lr);
     const size_t nc = (size_t)(a.cols >> 5);
-    RowPtr p;
-    const uint8_t* qs = seg == 0 ? a.qs[0] : (seg == 1 ? a.qs[1] : a.qs[2]);
-    const uint8_t* mt = seg == 0 ? a.meta[0] : (seg == 1 ? a.meta[1] : a.meta[2]);
+    const uint8_t* q = seg == 0 ? a.qs[0] : (seg == 1 ? a.qs[1] : a.qs[2]);
+    const uint8_t* m = seg == 0 ? a.meta[0] : (seg == 1 ? a.meta[1] : a.meta[2]);
     if constexpr (FMT == SSD_TYPE_Q4_0) {
-        p.qs = qs + (size_t)lr * nc * 16;
-        p.meta = mt + (size_t)lr * nc * 2;
+        qs = q + (size_t)lr * nc * 16;
+        meta = m + (size_t)lr * nc * 2;
     } else if constexpr (FMT == SSD_TYPE_Q8_0) {
-        p.qs = qs + (size_t)lr * nc * 32;
-        p.meta = mt + (size_t)lr * nc * 2;
+        qs = q + (size_t)lr * nc * 32;
+        meta = m + (size_t)lr * nc * 2;
     } else {
-        p.qs = qs + (size_t)lr * nc * 16;
-        p.meta = mt + (size_t)lr * (nc >> 3) * 16;
+        qs = q + (size_t)lr * nc * 16;
+        meta = m + (size_t)lr * (nc >> 3) * 16;
     }
-    return p;
 }
 
+// ---- cp.async staging of weights. Each lane copies its own chunks of a stage into
+// its own 16-byte slots of the warp's ring and later reads them back, so completion
+// only needs the thread's own cp.async.wait_group (no cross-lane synchronisation).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Ring slot sizes per (row, chunk): payload QB bytes, metadata MB bytes (Q4_0 / Q8_0:
+// the aligned 4-byte word holding the chunk's f16 d; Q4_K: the super-block's 16 bytes).
 template <int FMT>
-__device__ __forceinline__ void load_chunk(Chunk<FMT>& ch, const RowPtr& p, int c, bool valid) {
-    if constexpr (FMT == SSD_TYPE_Q4_0) {
-        auto& k = ch;
-        if (valid) {
-            k.q = ldg_stream(p.qs + (size_t)c * 16);
-            k.d = ldg_u16(p.meta + (size_t)c * 2);
-        } else {
-            k.q = make_uint4(0, 0, 0, 0);
-            k.d = 0;
-        }
-    } else if constexpr (FMT == SSD_TYPE_Q8_0) {
-        auto& k = ch;
-        if (valid) {
-            k.q0 = ldg_stream(p.qs + (size_t)c * 32);
-            k.q1 = ldg_stream(p.qs + (size_t)c * 32 + 16);
-            k.d = ldg_u16(p.meta + (size_t)c * 2);
-        } else {
-            k.q0 = k.q1 = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-            k.d = 0;
-        }
+struct Slot {
+    static constexpr int QB = FMT == SSD_TYPE_Q8_0 ? 32 : 16;
+    static constexpr int MB = FMT == SSD_TYPE_Q4_K ? 16 : 4;
+};
+template <int FMT, int R, int U>
+__host__ __device__ constexpr int stage_bytes() {
+    return R * U * 32 * (Slot<FMT>::QB + Slot<FMT>::MB);
+}
+
+// Issues the copies of chunk step u of a stage for one row. qp / mp point at this
+// lane's chunk of the stage's first step (tail-clamped by the caller).
+template <int FMT>
+__device__ __forceinline__ void issue_chunk(uint8_t* qdst, uint8_t* mdst, const uint8_t* qp,
+                                            const uint8_t* mp) {
+    if constexpr (FMT == SSD_TYPE_Q8_0) {
+        cp_async16(qdst, qp);
+        cp_async16(qdst + 16, qp + 16);
     } else {
-        auto& k = ch;
-        if (valid) {
-            k.q = ldg_stream(p.qs + (size_t)c * 16);
-            k.m = __ldg(reinterpret_cast<const uint4*>(p.meta) + (c >> 3));
-        } else {
-            k.q = make_uint4(0, 0, 0, 0);
-            k.m = make_uint4(0, 0, 0, 0);
-        }
+        cp_async16(qdst, qp);
+    }
+    if constexpr (FMT == SSD_TYPE_Q4_K)
+        cp_async16(mdst, mp);
+    else
+        cp_async4(mdst, reinterpret_cast<const uint8_t*>((uintptr_t)mp & ~(uintptr_t)3));
+}
+
+// Reads one (row, chunk) slot back: qsrc = payload slot, msrc = metadata slot (for
+// Q4_0 / Q8_0 already offset to the f16 d inside the copied 4-byte word).
+template <int FMT>
+__device__ __forceinline__ void read_chunk(Chunk<FMT>& k, const uint8_t* qsrc, const uint8_t* msrc) {
+    if constexpr (FMT == SSD_TYPE_Q4_0) {
+        k.q = *reinterpret_cast<const uint4*>(qsrc);
+        k.d = *reinterpret_cast<const uint16_t*>(msrc);
+    } else if constexpr (FMT == SSD_TYPE_Q8_0) {
+        k.q0 = *reinterpret_cast<const uint4*>(qsrc);
+        k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
+        k.d = *reinterpret_cast<const uint16_t*>(msrc);
+    } else {
+        k.q = *reinterpret_cast<const uint4*>(qsrc);
+        k.m = *reinterpret_cast<const uint4*>(msrc);
     }
 }
+// Bytes by which the stage pointers advance per chunk step of 32 chunks.
+template <int FMT>
+__host__ __device__ constexpr int q_step() { return FMT == SSD_TYPE_Q8_0 ? 1024 : 512; }
+template <int FMT>
+__host__ __device__ constexpr int m_step() { return 64; }
+// Offset of lane l's chunk l within a row (qs, meta).
+template <int FMT>
+__device__ __forceinline__ size_t q_lane(int l) { return (size_t)l * (FMT == SSD_TYPE_Q8_0 ? 32 : 16); }
+template <int FMT>
+__device__ __forceinline__ size_t m_lane(int l) { return FMT == SSD_TYPE_Q4_K ? (size_t)(l >> 3) * 16 : (size_t)l * 2; }
 
 __device__ __forceinline__ uint32_t word_of(const uint4& q, int m) {
     return m == 0 ? q.x : (m == 1 ? q.y : (m == 2 ? q.z : q.w));
 }
 
-// s += sum over the chunk of (q - OFF) * x for a 16-byte nibble chunk (element 2j is
-// the low nibble of byte j, 2j+1 the high nibble: src/metal/compute.rs:693-699).
-// OFF = 8 for Q4_0 (q - 8, compute.rs:696-697), 0 for Q4_K (q, compute.rs:739-740).
-template <int R, int OFF>
-__device__ __forceinline__ void nib_dot(const float4* xc, int c, const uint4 (&q)[R],
-                                        float (&s)[R]) {
-    constexpr float kMagic = 8388608.0f + (float)OFF;  // 2^23 + OFF
+// Two fp32 FMAs in one instruction (sm_100 fma.rn.f32x2): (d0, d1) += (a0, a1) * (b0, b1),
+// each lane rounded exactly as fmaf.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    uint64_t d, a, b;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(d0), "f"(d1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+// (e[r], o[r]) += sum over a 16-byte nibble chunk of q * x'' (x'' pre-scaled per field
+// position, see nib_pos), even elements into e, odd into o. xa / xb are the chunk's
+// elements 8m..8m+3 / 8m+4..8m+7.
+template <int R>
+__device__ __forceinline__ void nib_dot(const float4* xc, int sw, const uint4 (&q)[R],
+                                        float (&e)[R], float (&o)[R]) {
 #pragma unroll
     for (int m = 0; m < 4; m++) {
-        const float4 xa = xc[(2 * m) ^ (c & 7)];
-        const float4 xb = xc[(2 * m + 1) ^ (c & 7)];
+        const float4 xa = xc[(2 * m) ^ sw];
+        const float4 xb = xc[(2 * m + 1) ^ sw];
 #pragma unroll
         for (int r = 0; r < R; r++) {
             const uint32_t w = word_of(q[r], m);
-            const uint32_t lo = w & 0x0F0F0F0Fu;
-            const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;
-            float t = s[r];
-            t = fmaf(magic_byte(lo, 0) - kMagic, xa.x, t);
-            t = fmaf(magic_byte(hi, 0) - kMagic, xa.y, t);
-            t = fmaf(magic_byte(lo, 1) - kMagic, xa.z, t);
-            t = fmaf(magic_byte(hi, 1) - kMagic, xa.w, t);
-            t = fmaf(magic_byte(lo, 2) - kMagic, xb.x, t);
-            t = fmaf(magic_byte(hi, 2) - kMagic, xb.y, t);
-            t = fmaf(magic_byte(lo, 3) - kMagic, xb.z, t);
-            t = fmaf(magic_byte(hi, 3) - kMagic, xb.w, t);
-            s[r] = t;
+            const uint32_t w2 = w >> 12;
+            ffma2(e[r], o[r], den(w & 0x0000000Fu), den(w & 0x000000F0u), xa.x, xa.y);
+            ffma2(e[r], o[r], den(w & 0x00000F00u), den(w & 0x0000F000u), xa.z, xa.w);
+            ffma2(e[r], o[r], den(w & 0x000F0000u), den(w2 & 0x00000F00u), xb.x, xb.y);
+            ffma2(e[r], o[r], den(w2 & 0x0000F000u), den(w2 & 0x000F0000u), xb.z, xb.w);
         }
     }
 }
 
+// Per-chunk data staged next to x'': csum[c] = bias term of the chunk, already scaled
+// by 2^-64: -8 X (Q4_0), -128 X (Q8_0), X (Q4_K), X = sum of the chunk's x.
 template <int FMT, int R>
 __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const float4* xs4,
                                               const float* csum, int c, int lane,
                                               float (&acc)[R]) {
     const float4* xc = xs4 + (size_t)c * 8;
+    const int sw = c & 7;
+    float e[R], o[R];
     if constexpr (FMT == SSD_TYPE_Q4_0) {
         uint4 q[R];
-        float s[R];
+        const float b = csum[c];
 #pragma unroll
         for (int r = 0; r < R; r++) {
             q[r] = ch[r].q;
-            s[r] = 0.0f;
+            e[r] = b;
+            o[r] = 0.0f;
         }
-        nib_dot<R, 8>(xc, c, q, s);
+        nib_dot<R>(xc, sw, q, e, o);
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), e[r] + o[r], acc[r]);
+    } else if constexpr (FMT == SSD_TYPE_Q8_0) {
+        const float b = csum[c];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            const float d = f16_bits_to_f32((uint16_t)ch[r].d);
-            acc[r] = fmaf(d, s[r], acc[r]);
+            e[r] = b;
+            o[r] = 0.0f;
         }
-    } else if constexpr (FMT == SSD_TYPE_Q8_0) {
-        float s[R];
-#pragma unroll
-        for (int r = 0; r < R; r++) s[r] = 0.0f;
 #pragma unroll
         for (int m = 0; m < 8; m++) {
-            const float4 xa = xc[m ^ (c & 7)];
+            const float4 xa = xc[m ^ sw];  // elements 4m..4m+3
 #pragma unroll
             for (int r = 0; r < R; r++) {
-                const auto& k = ch[r];
-                const uint32_t b = word_of(m < 4 ? k.q0 : k.q1, m & 3) ^ 0x80808080u;
-                float t = s[r];
-                t = fmaf(magic_byte(b, 0) - kQ80Magic, xa.x, t);
-                t = fmaf(magic_byte(b, 1) - kQ80Magic, xa.y, t);
-                t = fmaf(magic_byte(b, 2) - kQ80Magic, xa.z, t);
-                t = fmaf(magic_byte(b, 3) - kQ80Magic, xa.w, t);
-                s[r] = t;
+                const uint32_t w = word_of(m < 4 ? ch[r].q0 : ch[r].q1, m & 3) ^ 0x80808080u;
+                const uint32_t w2 = w >> 16;
+                ffma2(e[r], o[r], den(w & 0x000000FFu), den(w & 0x0000FF00u), xa.x, xa.y);
+                ffma2(e[r], o[r], den(w2 & 0x000000FFu), den(w2 & 0x0000FF00u), xa.z, xa.w);
             }
         }
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-            const float d = f16_bits_to_f32((uint16_t)ch[r].d);
-            acc[r] = fmaf(d, s[r], acc[r]);
-        }
+        for (int r = 0; r < R; r++)
+            acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), e[r] + o[r], acc[r]);
     } else {  // Q4_K: this lane's sub-block index is c & 7 == lane & 7
         uint4 q[R];
-        float s[R];
 #pragma unroll
         for (int r = 0; r < R; r++) {
             q[r] = ch[r].q;
-            s[r] = 0.0f;
+            e[r] = 0.0f;
+            o[r] = 0.0f;
         }
-        nib_dot<R, 0>(xc, c, q, s);
-        const float X = csum[c];  // sum of the chunk's x
+        nib_dot<R>(xc, sw, q, e, o);
+        const float X = csum[c];
         const int sb = lane & 7, sh = 8 * (sb & 3);
 #pragma unroll
         for (int r = 0; r < R; r++) {
@@ -234,7 +289,7 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const f
             // sum((scale*q - min) x) = scale * sum(q x) - min * X
             const float scale = __fmul_rn(d, (float)s6);
             const float mn = __fmul_rn(dmin, (float)m6);
-            acc[r] = fmaf(-mn, X, fmaf(scale, s[r], acc[r]));
+            acc[r] = fmaf(-mn, X, fmaf(scale, e[r] + o[r], acc[r]));
         }
     }
 }
@@ -262,46 +317,55 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
     return ((unsigned long long)u << 32) | idx;
 }
 
-// Shared-memory plan of one CTA (offsets from a 1024-byte aligned base).
+// Shared-memory plan of one CTA (offsets from a 1024-byte aligned base): the staged
+// x'' (TMA destination, swizzled), the per-chunk bias sums, reduction scratch, the
+// TMA barrier, and one weight ring of kStages stages per warp.
+constexpr int kStages = 4;
 struct SmemPlan {
-    int nc, xrows;              // chunks, staged rows (multiple of kVecBoxRows)
-    size_t xs, xa, xn, csum, red, bar, total;
+    int nc, xrows;  // chunks, staged rows (multiple of kVecBoxRows)
+    size_t xs, csum, red, bar, ring, total;
 };
-__host__ __device__ inline SmemPlan smem_plan(int cols, bool add, bool norm, bool sums, int nw) {
+__host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_warp) {
     SmemPlan p;
     p.nc = cols >> 5;
     p.xrows = (p.nc + kVecBoxRows - 1) / kVecBoxRows * kVecBoxRows;
-    const size_t vb = (size_t)p.xrows * 128;
     size_t o = 0;
     p.xs = o;
-    o += vb;
-    p.xa = add ? o : 0;
-    o += add ? vb : 0;
-    p.xn = norm ? o : 0;
-    o += norm ? vb : 0;
+    o += (size_t)p.xrows * 128;
     p.csum = o;
-    o += sums ? ((size_t)p.nc * 4 + 15) & ~(size_t)15 : 0;
+    o += ((size_t)p.nc * 4 + 15) & ~(size_t)15;
     p.red = o;
     o += 64 * 4 + (size_t)nw * 8;
     p.bar = o;
     o += 16;
+    o = (o + 127) & ~(size_t)127;
+    p.ring = o;
+    o += (size_t)nw * ring_per_warp;
     p.total = o + 1024;  // alignment slack
     return p;
 }
 
+// Power-of-two pre-scale of element position k (0..7) within a 32-bit word.
+template <int FMT>
+__device__ __forceinline__ float pos_scale(int k) {
+    const int s = FMT == SSD_TYPE_Q8_0 ? byte_pos(k & 3) : nib_pos(k);
+    return __uint_as_float((uint32_t)(127 + kScaleBias - s) << 23);
+}
+
 // Persistent fused dequant-matvec. Grid = resident CTAs (or fewer for small matrices);
 // warp w of the grid owns row-groups (R rows) w, w + W, w + 2W, ... (W = warps in the
-// grid). Weight loads run two register stages ahead across row-group boundaries; the
-// first stage is issued before griddepcontrol.wait. x (and x_add / norm_w) arrive by
-// TMA into 128B-swizzled shared memory; the residual add and RMSNorm are applied there.
+// grid). A "stage" is U chunk steps (32 chunks each) of the R rows of one row-group;
+// each warp keeps kStages - 1 stages of copies in flight in its shared-memory ring,
+// the first ones issued before griddepcontrol.wait.
 template <int FMT, int EPI, int R, int U, int NW>
-__global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
-    k_matvec(const MvArgs a, const __grid_constant__ CUtensorMap tm_x,
-             const __grid_constant__ CUtensorMap tm_add, const __grid_constant__ CUtensorMap tm_norm) {
+__global__ void __launch_bounds__(NW * 32, 1)
+    k_matvec(const MvArgs a, const __grid_constant__ CUtensorMap tm_x) {
+    constexpr int SB = stage_bytes<FMT, R, U>();
+    constexpr int QB = Slot<FMT>::QB, MB = Slot<FMT>::MB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const bool has_add = a.x_add != nullptr, has_norm = a.norm_w != nullptr;
-    const SmemPlan P = smem_plan(a.cols, has_add, has_norm, FMT == SSD_TYPE_Q4_K, NW);
+    const SmemPlan P = smem_plan(a.cols, NW, kStages * SB);
     float4* xs4 = reinterpret_cast<float4*>(base + P.xs);
     float* csum = reinterpret_cast<float*>(base + P.csum);
     float* red = reinterpret_cast<float*>(base + P.red);
@@ -309,70 +373,121 @@ __global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
     uint64_t* bar = reinterpret_cast<uint64_t*>(base + P.bar);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint8_t* ring = base + P.ring + (size_t)warp * (kStages * SB);
     const int nc = P.nc;
-    const int iters = (nc + 31) >> 5;               // chunk iterations per lane per row
-    const int spr = (iters + U - 1) / U;            // register steps per row-group
+    const int iters = (nc + 31) >> 5;     // chunk iterations per lane per row
+    const int spr = (iters + U - 1) / U;  // stages per row-group
     const int n_rg = (a.rows + R - 1) / R;
     const int W = gridDim.x * NW;
     const int wg = blockIdx.x * NW + warp;
     const int my_rg = wg < n_rg ? (n_rg - 1 - wg) / W + 1 : 0;
-    const int total = my_rg * spr;
+    const int total = my_rg * spr;  // stages this warp computes
 
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
     }
 
-    Chunk<FMT> A[U][R], B[U][R];
-    auto load_step = [&](Chunk<FMT>(&buf)[U][R], int s) {
-        const int rg = wg + (s / spr) * W, st = s % spr;
-        const int v0 = rg * R;
+    // ---- issue cursor: row-group lrg, stage lst; lq / lm = this lane's chunk of the
+    // stage in each row (rows past the end alias the last row; their sums are dropped).
+    // Steps whose chunks run past the row (the tail of a row whose chunk count is not a
+    // multiple of 32*U) re-read the lane's last chunk; compute skips those chunks.
+    int lrg = wg, lst = 0, issued = 0;
+    const uint8_t* lq[R];
+    const uint8_t* lm[R];
+    // largest c < nc with c = lane (mod 32); lanes with no chunk at all (nc < 32) use 0
+    const int last_c = lane < nc ? nc - 1 - ((nc - 1 - lane) & 31) : 0;
+    auto set_rows = [&]() {
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            const bool rv = v0 + r < a.rows;
-            const RowPtr rp = rv ? row_ptr<FMT>(a, v0 + r) : RowPtr{nullptr, nullptr};
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int c = lane + 32 * (st * U + u);
-                load_chunk<FMT>(buf[u][r], rp, c, rv && c < nc);
-            }
+            const int v = min(lrg * R + r, a.rows - 1);
+            const uint8_t *q0, *m0;
+            row_ptr<FMT>(a, R, v, q0, m0);
+            lq[r] = q0 + q_lane<FMT>(lane < nc ? lane : 0);
+            lm[r] = m0 + m_lane<FMT>(lane < nc ? lane : 0);
         }
     };
-    // Weights never depend on the previous kernel: issue the first stage before waiting.
-    if (total > 0) load_step(A, 0);
+    if (lrg < n_rg) set_rows();
+    const bool any_tail = nc % (32 * U) != 0 || nc < 32;
+    // this lane's slots: payload at ring_q + stage + (r*U+u)*32*QB, metadata at
+    // ring_m + stage + (r*U+u)*32*MB (compile-time offsets from two lane pointers)
+    uint8_t* const ring_q = ring + (size_t)lane * QB;
+    uint8_t* const ring_m = ring + (size_t)R * U * 32 * QB + (size_t)lane * MB;
+    int ist = 0;  // byte offset of the stage being issued
+    auto issue = [&]() {  // the next stage into the ring, then commit
+        if (issued < total) {
+            if (!any_tail || (lst + 1) * U * 32 <= nc) {
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+#pragma unroll
+                    for (int u = 0; u < U; u++)
+                        issue_chunk<FMT>(ring_q + ist + (r * U + u) * 32 * QB,
+                                         ring_m + ist + (r * U + u) * 32 * MB,
+                                         lq[r] + u * q_step<FMT>(), lm[r] + u * m_step<FMT>());
+                }
+            } else {  // tail stage: chunks past the row end re-read the lane's last chunk
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int cu = lane + 32 * (lst * U + u);
+                    const int cp = (lane < nc ? lane : 0) + 32 * (lst * U + u);
+                    // chunk-index step back to last_c: the same stride per chunk index in
+                    // qs (16 or 32 B) and 2 B in meta (Q4_K: 16 B per 8 chunks, dc a
+                    // multiple of 32)
+                    const long long dc = cu < nc ? 0 : (long long)(last_c - cp);
+#pragma unroll
+                    for (int r = 0; r < R; r++)
+                        issue_chunk<FMT>(ring_q + ist + (r * U + u) * 32 * QB,
+                                         ring_m + ist + (r * U + u) * 32 * MB,
+                                         lq[r] + u * q_step<FMT>() + dc * (q_step<FMT>() / 32),
+                                         lm[r] + u * m_step<FMT>() + dc * 2);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                lq[r] += U * q_step<FMT>();
+                lm[r] += U * m_step<FMT>();
+            }
+            issued++;
+            ist = ist + SB == kStages * SB ? 0 : ist + SB;
+            if (++lst == spr) {
+                lst = 0;
+                lrg += W;
+                if (lrg < n_rg) set_rows();
+            }
+        }
+        cp_commit();  // one group per call, empty or not: wait_group counts stay uniform
+    };
+    // Weights never depend on the previous kernel: fill the ring before waiting.
+#pragma unroll
+    for (int k = 0; k < kStages - 1; k++) issue();
     __syncthreads();  // barrier initialised
     pdl_wait();
 
     if (tid == 0) {
         const int nbox = P.xrows / kVecBoxRows;
-        const uint32_t vbytes = (uint32_t)P.xrows * 128u;
-        mbar_expect_tx(bar, vbytes * (1u + (has_add ? 1u : 0u) + (has_norm ? 1u : 0u)));
-        for (int b = 0; b < nbox; b++) {
+        mbar_expect_tx(bar, (uint32_t)P.xrows * 128u);
+        for (int b = 0; b < nbox; b++)
             tma_load_2d(base + P.xs + (size_t)b * kVecBoxRows * 128, &tm_x, 0, b * kVecBoxRows, bar);
-            if (has_add)
-                tma_load_2d(base + P.xa + (size_t)b * kVecBoxRows * 128, &tm_add, 0,
-                            b * kVecBoxRows, bar);
-            if (has_norm)
-                tma_load_2d(base + P.xn + (size_t)b * kVecBoxRows * 128, &tm_norm, 0,
-                            b * kVecBoxRows, bar);
-        }
     }
     const bool ok = mbar_wait(bar, 0, a.status);
-    if (__syncthreads_or(!ok)) return;  // timed out: status recorded, nothing computed
+    if (__syncthreads_or(!ok)) {  // timed out: status recorded, nothing computed
+        cp_wait<0>();
+        return;
+    }
 
-    // prologue in shared memory: x_eff = x (+ x_add); optional RMSNorm; chunk sums
+    // ---- prologue in shared memory: x_eff = x (+ x_add) [written back by CTA 0];
+    // optional RMSNorm; chunk bias sums; per-position power-of-two pre-scale.
     const int nunits = nc * 8;  // 16-byte units
     const unsigned gmask = 0xFFu << (lane & 24);
+    float inv = 1.0f;
     if (has_add || has_norm) {
-        const float4* xa4 = reinterpret_cast<const float4*>(base + P.xa);
-        const float4* xn4 = reinterpret_cast<const float4*>(base + P.xn);
         const bool wb = a.x_writeback != nullptr && blockIdx.x == 0;
         float ss = 0.0f;
         for (int i = tid; i < nunits; i += NW * 32) {
             const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
             float4 v = xs4[ph];
             if (has_add) {  // hidden[i] += attn_output[i] (src/metal/compute.rs:547-549)
-                const float4 r = xa4[ph];
+                const float4 r = __ldg(reinterpret_cast<const float4*>(a.x_add) + i);
                 v.x = __fadd_rn(v.x, r.x);
                 v.y = __fadd_rn(v.y, r.y);
                 v.z = __fadd_rn(v.z, r.z);
@@ -393,12 +508,16 @@ __global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
 #pragma unroll
             for (int w = 0; w < NW; w++) tot += red[w];
             // inv_rms = 1 / sqrt(sum_sq / n + eps)   (src/metal/compute.rs:583-584)
-            const float inv =
-                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.cols), a.eps)));
-            for (int i = tid; i < nunits; i += NW * 32) {
-                const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
-                float4 v = xs4[ph];
-                const float4 w = xn4[ph];
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.cols), a.eps)));
+        }
+    }
+    {
+        const float4* nw4 = reinterpret_cast<const float4*>(a.norm_w);
+        for (int i = tid; i < nunits; i += NW * 32) {
+            const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
+            float4 v = xs4[ph];
+            if (has_norm) {
+                const float4 w = __ldg(nw4 + i);
                 if (a.norm_order == 0) {  // x * (inv_rms * w)
                     v.x = __fmul_rn(v.x, __fmul_rn(inv, w.x));
                     v.y = __fmul_rn(v.y, __fmul_rn(inv, w.y));
@@ -410,19 +529,22 @@ __global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
                     v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
                     v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
                 }
-                xs4[ph] = v;
             }
-        }
-    }
-    if constexpr (FMT == SSD_TYPE_Q4_K) {  // chunk sums of x for the min term
-        for (int i = tid; i < nunits; i += NW * 32) {
-            const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
-            const float4 v = xs4[ph];
+            // chunk sum of x (8 consecutive threads hold one chunk's 8 units)
             float t = (v.x + v.y) + (v.z + v.w);
             t += __shfl_xor_sync(gmask, t, 1);
             t += __shfl_xor_sync(gmask, t, 2);
             t += __shfl_xor_sync(gmask, t, 4);
-            if ((i & 7) == 0) csum[c] = t;
+            if ((i & 7) == 0) {
+                const float X = __fmul_rn(t, 1.0f / kUnscale);
+                csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X : (FMT == SSD_TYPE_Q8_0 ? -128.0f * X : X);
+            }
+            const int k0 = (FMT == SSD_TYPE_Q8_0) ? 0 : 4 * (i & 1);  // word position of v.x
+            v.x = __fmul_rn(v.x, pos_scale<FMT>(k0 + 0));
+            v.y = __fmul_rn(v.y, pos_scale<FMT>(k0 + 1));
+            v.z = __fmul_rn(v.z, pos_scale<FMT>(k0 + 2));
+            v.w = __fmul_rn(v.w, pos_scale<FMT>(k0 + 3));
+            xs4[ph] = v;
         }
     }
     __syncthreads();
@@ -432,21 +554,53 @@ __global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
 #pragma unroll
     for (int r = 0; r < R; r++) acc[r] = 0.0f;
     unsigned long long best = 0ull;
-
-    auto compute_step = [&](const Chunk<FMT>(&buf)[U][R], int s) {
-        const int st = s % spr;
+    int crg = wg, cst = 0;  // compute cursor
+    // byte offset of the f16 d inside its copied aligned 4-byte word: the half of
+    // byte offset 2 * (row * nc + c) in the segment, c = lane (mod 2)
+    int doff[R];
+    auto set_doff = [&]() {
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int c = lane + 32 * (st * U + u);
-            if (c < nc) compute_chunk<FMT, R>(buf[u], xs4, csum, c, lane, acc);
+        for (int r = 0; r < R; r++) {
+            int seg, lr;
+            map_row(a, R, min(crg * R + r, a.rows - 1), seg, lr);
+            doff[r] = (((lr & 1) * (nc & 1) + lane) & 1) * 2;
         }
-        if (st != spr - 1) return;
+    };
+    if (FMT != SSD_TYPE_Q4_K && crg < n_rg) set_doff();
+    int cst_off = 0;  // byte offset of the stage being computed
+
+    for (int k = 0; k < total; k++) {
+        cp_wait<kStages - 2>();  // this thread's copies of stage k have landed
+        const uint8_t* sq = ring_q + cst_off;
+        const uint8_t* sm = ring_m + cst_off;
+        auto do_u = [&](int u) {
+            Chunk<FMT> ch[R];
+#pragma unroll
+            for (int r = 0; r < R; r++)
+                read_chunk<FMT>(ch[r], sq + (r * U + u) * 32 * QB,
+                                sm + (r * U + u) * 32 * MB + (FMT == SSD_TYPE_Q4_K ? 0 : doff[r]));
+            compute_chunk<FMT, R>(ch, xs4, csum, lane + 32 * (cst * U + u), lane, acc);
+        };
+        if (!any_tail || (cst + 1) * U * 32 <= nc) {
+#pragma unroll
+            for (int u = 0; u < U; u++) do_u(u);
+        } else {
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (lane + 32 * (cst * U + u) < nc) do_u(u);
+        }
+        cst_off = cst_off + SB == kStages * SB ? 0 : cst_off + SB;
+        issue();  // refill the buffer of stage k - 1 (this thread is done reading it)
+        if (++cst != spr) continue;
         // row-group finished: reduce across the warp and run the epilogue
-        const int v0 = (wg + (s / spr) * W) * R;
+        cst = 0;
+        const int v0 = crg * R;
+        crg += W;
+        if (FMT != SSD_TYPE_Q4_K && crg < n_rg) set_doff();
         float res[R];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            res[r] = warp_sum(acc[r]);
+            res[r] = __fmul_rn(warp_sum(acc[r]), kUnscale);
             acc[r] = 0.0f;
         }
         if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
@@ -456,22 +610,33 @@ __global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
                 if (lane == r && row < a.rows)
                     a.y[row] = (EPI == EPI_RESID) ? __fadd_rn(a.base[row], res[r]) : res[r];
             }
-        } else if constexpr (EPI == EPI_SWIGLU) {  // rows (gate 2g, gate 2g+1, up 2g, up 2g+1)
-            if (lane < 2 && v0 < a.rows) {
-                const float g = lane == 0 ? res[0] : res[1];
-                const float up = lane == 0 ? res[2] : res[3];
+        } else if constexpr (EPI == EPI_SWIGLU) {  // rows: R/2 gate rows, then R/2 up rows
+            constexpr int H = R / 2;
+            if (lane < H && v0 < a.rows) {
+                float g = res[0], up = res[H];
+#pragma unroll
+                for (int j = 1; j < H; j++)
+                    if (lane == j) {
+                        g = res[j];
+                        up = res[H + j];
+                    }
                 // silu(v) = v / (1 + exp(-v)), then gate *= up (feed_forward.rs:31-39,
                 // compute.rs:641-645)
                 const float si = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-                a.y[(v0 >> 1) + lane] = __fmul_rn(si, up);
+                a.y[(v0 / R) * H + lane] = __fmul_rn(si, up);
             }
         } else if constexpr (EPI == EPI_QKV_ROPE) {  // adjacent pairs (v0+2p, v0+2p+1)
             if (lane < R / 2 && v0 < a.rows) {
                 const int pos = a.position_dev ? *a.position_dev : a.position;
                 int seg, lr;
-                map_row(a, v0 + 2 * lane, seg, lr);
-                float x0 = lane == 0 ? res[0] : res[2];
-                float x1 = lane == 0 ? res[1] : res[3];
+                map_row(a, R, v0 + 2 * lane, seg, lr);
+                float x0 = res[0], x1 = res[1];
+#pragma unroll
+                for (int p = 1; p < R / 2; p++)
+                    if (lane == p) {
+                        x0 = res[2 * p];
+                        x1 = res[2 * p + 1];
+                    }
                 if (seg < 2) rope_pair(x0, x1, lr, a.head_dim, a.theta, pos);
                 float* dst = seg == 0 ? a.y : (seg == 1 ? a.y_k : a.y_v);
                 dst[lr] = x0;
@@ -483,19 +648,13 @@ __global__ void __launch_bounds__(NW * 32, (NW == 8 ? 2 : 4))
                 const int row = v0 + r;
                 if (row < a.rows) {
                     if (a.y && lane == r) a.y[row] = res[r];
-                    const unsigned long long k = argmax_key(res[r], (uint32_t)(row + a.index_offset));
-                    best = k > best ? k : best;
+                    const unsigned long long kk = argmax_key(res[r], (uint32_t)(row + a.index_offset));
+                    best = kk > best ? kk : best;
                 }
             }
         }
-    };
-
-    for (int s = 0; s < total; s += 2) {
-        if (s + 1 < total) load_step(B, s + 1);
-        compute_step(A, s);
-        if (s + 2 < total) load_step(A, s + 2);
-        if (s + 1 < total) compute_step(B, s + 1);
     }
+    cp_wait<0>();
 
     if constexpr (EPI == EPI_ARGMAX) {
         if (lane == 0) keys[warp] = best;
@@ -514,6 +673,8 @@ struct Cfg {
     int R, U, NW;
 };
 
+// SSD_MV_CONFIG="R,U,NW" selects a tiling of the instantiated set for every matvec
+// (tuning sweeps); unset, launch_fmt_epi picks one by shape.
 static Cfg env_cfg() {
     static Cfg c = [] {
         Cfg d{0, 0, 0};
@@ -537,7 +698,7 @@ static int occupancy(ssd_ctx* ctx, K kern, int threads, size_t smem, int* out) {
         size_t smem;
         int blocks;
     };
-    static Entry cache[256];
+    static Entry cache[512];
     static int n = 0;
     static std::mutex mu;
     std::lock_guard<std::mutex> lk(mu);
@@ -557,7 +718,7 @@ static int occupancy(ssd_ctx* ctx, K kern, int threads, size_t smem, int* out) {
     int nb = 0;
     SSD_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem));
     SSD_REQ(nb > 0, SSD_ERR_SHAPE, "matvec kernel does not fit on an SM (%zu B smem)", smem);
-    if (n < 256) cache[n++] = Entry{fn, ctx->device, smem, nb};
+    if (n < 512) cache[n++] = Entry{fn, ctx->device, smem, nb};
     *out = nb;
     return SSD_OK;
 }
@@ -565,8 +726,7 @@ static int occupancy(ssd_ctx* ctx, K kern, int threads, size_t smem, int* out) {
 template <int FMT, int EPI, int R, int U, int NW>
 static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     auto kern = k_matvec<FMT, EPI, R, U, NW>;
-    const SmemPlan P =
-        smem_plan(a.cols, a.x_add != nullptr, a.norm_w != nullptr, FMT == SSD_TYPE_Q4_K, NW);
+    const SmemPlan P = smem_plan(a.cols, NW, kStages * stage_bytes<FMT, R, U>());
     SSD_REQ(P.total <= ctx->smem_optin, SSD_ERR_SHAPE,
             "cols %d too large for shared-memory staging (%zu bytes)", a.cols, P.total);
     int nb = 0;
@@ -574,51 +734,41 @@ static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     const int n_rg = (a.rows + R - 1) / R;
     const int need = (n_rg + NW - 1) / NW;
     const int grid = need < ctx->num_sms * nb ? need : ctx->num_sms * nb;
-    CUtensorMap mx, madd, mnorm;
+    CUtensorMap mx;
     SSD_TRY(encode_vec_map(&mx, a.x, a.cols));
-    madd = mx;
-    mnorm = mx;
-    if (a.x_add) SSD_TRY(encode_vec_map(&madd, a.x_add, a.cols));
-    if (a.norm_w) SSD_TRY(encode_vec_map(&mnorm, a.norm_w, a.cols));
-    SSD_CK(launch_pdl(kern, dim3(grid), dim3(NW * 32), P.total, s, pdl, a, mx, madd, mnorm));
+    SSD_CK(launch_pdl(kern, dim3(grid), dim3(NW * 32), P.total, s, pdl, a, mx));
     return SSD_OK;
 }
 
-// Active warps per SM the launch would get with NW warps per CTA.
-template <int FMT, int EPI, int R, int U, int NW>
-static int active_warps(ssd_ctx* ctx, const MvArgs& a, int* warps) {
-    const SmemPlan P =
-        smem_plan(a.cols, a.x_add != nullptr, a.norm_w != nullptr, FMT == SSD_TYPE_Q4_K, NW);
-    *warps = 0;
-    if (P.total > ctx->smem_optin) return SSD_OK;
-    int nb = 0;
-    SSD_TRY(occupancy(ctx, k_matvec<FMT, EPI, R, U, NW>, NW * 32, P.total, &nb));
-    const int n_rg = (a.rows + R - 1) / R;
-    const int ctas = (n_rg + NW - 1) / NW;
-    const int resident = ctx->num_sms * nb;
-    const long long w = (long long)(ctas < resident ? ctas : resident) * NW;
-    *warps = (int)(w / ctx->num_sms);
-    return SSD_OK;
-}
-
-// Tiling: R = 4 rows per warp; 4 or 8 warps per CTA, whichever keeps more warps
-// resident per SM for this width and prologue (ties go to 8: fewer x stagings).
-// Q4_0 keeps two chunk steps per register stage (128 registers, no spill), Q8_0 / Q4_K
-// one. SSD_MV_CONFIG="R,U,NW" selects another instantiation of the plain matvec.
+// Tiling by shape. Rows per warp R = 4 (x reads from shared memory shared by 4 rows)
+// unless that leaves fewer than ~16 warps per SM, then R = 2. Q4_0 keeps two chunk
+// steps per register stage (U = 2); Q8_0 (32-byte chunks) and Q4_K (16 more bytes of
+// super-block metadata per chunk) one, which keeps them spill-free. 8 warps per CTA
+// while two CTAs' x staging fits in shared memory, else 16 (one CTA per SM).
+// Tiling by shape: R = 2 rows per warp, U = 2 chunk steps per stage (Q4_0; one for the
+// wider Q8_0 / Q4_K slots), kStages = 4 ring stages per warp. 16 warps per CTA (one
+// CTA per SM, one copy of x'' per SM) when their rings fit beside x'' in shared
+// memory, else 8.
 template <int FMT, int EPI>
 static int launch_fmt_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
-    if constexpr (EPI == EPI_STORE) {
-        const Cfg c = env_cfg();
-        if (c.R == 4 && c.U == 1 && c.NW == 4) return launch_t<FMT, EPI, 4, 1, 4>(ctx, a, s, pdl);
-        if (c.R == 4 && c.U == 1 && c.NW == 8) return launch_t<FMT, EPI, 4, 1, 8>(ctx, a, s, pdl);
-        if (c.R == 2 && c.U == 2 && c.NW == 4) return launch_t<FMT, EPI, 2, 2, 4>(ctx, a, s, pdl);
-    }
     constexpr int U = FMT == SSD_TYPE_Q4_0 ? 2 : 1;
-    int w4 = 0, w8 = 0;
-    SSD_TRY((active_warps<FMT, EPI, 4, U, 4>(ctx, a, &w4)));
-    SSD_TRY((active_warps<FMT, EPI, 4, U, 8>(ctx, a, &w8)));
-    if (w8 >= w4 && w8 > 0) return launch_t<FMT, EPI, 4, U, 8>(ctx, a, s, pdl);
-    return launch_t<FMT, EPI, 4, U, 4>(ctx, a, s, pdl);
+    const Cfg c = env_cfg();
+    if (c.R) {  // tuning: any instantiated (R, U, NW)
+        if (c.U == U && c.NW == 8 && c.R == 2) return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);
+        if (c.U == U && c.NW == 8 && c.R == 4) return launch_t<FMT, EPI, 4, U, 8>(ctx, a, s, pdl);
+        if (c.U == U && c.NW == 16 && c.R == 2) return launch_t<FMT, EPI, 2, U, 16>(ctx, a, s, pdl);
+        if (c.U == U && c.NW == 16 && c.R == 4) return launch_t<FMT, EPI, 4, U, 16>(ctx, a, s, pdl);
+        if constexpr (U == 2) {
+            if (c.U == 1 && c.NW == 8 && c.R == 4) return launch_t<FMT, EPI, 4, 1, 8>(ctx, a, s, pdl);
+            if (c.U == 1 && c.NW == 16 && c.R == 4) return launch_t<FMT, EPI, 4, 1, 16>(ctx, a, s, pdl);
+        }
+        set_error("SSD_MV_CONFIG=%d,%d,%d is not an instantiated tiling", c.R, c.U, c.NW);
+        return SSD_ERR_ARG;
+    }
+    const size_t ring = (size_t)kStages * stage_bytes<FMT, 2, U>();
+    if (smem_plan(a.cols, 16, (int)ring).total <= ctx->smem_optin)
+        return launch_t<FMT, EPI, 2, U, 16>(ctx, a, s, pdl);
+    return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);
 }
 
 template <int FMT>
