@@ -294,21 +294,22 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const f
     }
 }
 
-// RoPE of one adjacent pair (src/metal/compute.rs:494-503). The angle's powf /
-// sin / cos are evaluated in double and rounded once to float.
-__device__ __forceinline__ void rope_pair(float& x0, float& x1, int lr, int head_dim, float theta,
-                                          int pos) {
-    const int i = (lr % head_dim) >> 1;
+// RoPE angle of pair i at `pos` (src/metal/compute.rs:494-503): freq = 1 / theta^(2i/d),
+// angle = pos * freq, rotation by (cos, sin). powf / sin / cos are evaluated in double
+// and rounded once to float. Computed once per CTA for the head_dim/2 pairs.
+__device__ __forceinline__ float2 rope_cs(int i, int head_dim, float theta, int pos) {
     const float e = __fdiv_rn(__fmul_rn(2.0f, (float)i), (float)head_dim);
     const float p = (float)pow((double)theta, (double)e);
     const float freq = __fdiv_rn(1.0f, p);
     const float ang = __fmul_rn((float)pos, freq);
     double sd, cd;
     sincos((double)ang, &sd, &cd);
-    const float sn = (float)sd, cs = (float)cd;
+    return make_float2((float)cd, (float)sd);
+}
+__device__ __forceinline__ void rope_apply(float& x0, float& x1, float2 cs) {
     const float a0 = x0, a1 = x1;
-    x0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
-    x1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+    x0 = __fsub_rn(__fmul_rn(a0, cs.x), __fmul_rn(a1, cs.y));
+    x1 = __fadd_rn(__fmul_rn(a0, cs.y), __fmul_rn(a1, cs.x));
 }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
@@ -323,8 +324,9 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 constexpr int kStages = 4;
 struct SmemPlan {
     int nc, xrows;  // chunks, staged rows (multiple of kVecBoxRows)
-    size_t xs, csum, red, bar, ring, total;
+    size_t xs, csum, red, bar, rope, ring, total;
 };
+constexpr int kMaxRopePairs = 256;  // head_dim <= 512
 __host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_warp) {
     SmemPlan p;
     p.nc = cols >> 5;
@@ -338,6 +340,8 @@ __host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_war
     o += 64 * 4 + (size_t)nw * 8;
     p.bar = o;
     o += 16;
+    p.rope = o;
+    o += (size_t)kMaxRopePairs * 8;
     o = (o + 127) & ~(size_t)127;
     p.ring = o;
     o += (size_t)nw * ring_per_warp;
@@ -463,6 +467,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
     __syncthreads();  // barrier initialised
     pdl_wait();
 
+    float2* rope_tab = reinterpret_cast<float2*>(base + P.rope);
+    if constexpr (EPI == EPI_QKV_ROPE) {  // (cos, sin) of every pair at this position
+        const int pos = a.position_dev ? *a.position_dev : a.position;
+        for (int i = tid; i < (a.head_dim >> 1); i += NW * 32)
+            rope_tab[i] = rope_cs(i, a.head_dim, a.theta, pos);
+    }
     if (tid == 0) {
         const int nbox = P.xrows / kVecBoxRows;
         mbar_expect_tx(bar, (uint32_t)P.xrows * 128u);
@@ -627,7 +637,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
             }
         } else if constexpr (EPI == EPI_QKV_ROPE) {  // adjacent pairs (v0+2p, v0+2p+1)
             if (lane < R / 2 && v0 < a.rows) {
-                const int pos = a.position_dev ? *a.position_dev : a.position;
                 int seg, lr;
                 map_row(a, R, v0 + 2 * lane, seg, lr);
                 float x0 = res[0], x1 = res[1];
@@ -637,7 +646,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
                         x0 = res[2 * p];
                         x1 = res[2 * p + 1];
                     }
-                if (seg < 2) rope_pair(x0, x1, lr, a.head_dim, a.theta, pos);
+                if (seg < 2) rope_apply(x0, x1, rope_tab[(lr % a.head_dim) >> 1]);
                 float* dst = seg == 0 ? a.y : (seg == 1 ? a.y_k : a.y_v);
                 dst[lr] = x0;
                 dst[lr + 1] = x1;
@@ -748,7 +757,8 @@ static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
 // Tiling by shape: R = 2 rows per warp, U = 2 chunk steps per stage (Q4_0; one for the
 // wider Q8_0 / Q4_K slots), kStages = 4 ring stages per warp. 16 warps per CTA (one
 // CTA per SM, one copy of x'' per SM) when their rings fit beside x'' in shared
-// memory, else 8.
+// memory; for very wide rows Q4_0 first halves its stage (U = 1) to keep 16 warps;
+// else 8 warps.
 template <int FMT, int EPI>
 static int launch_fmt_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     constexpr int U = FMT == SSD_TYPE_Q4_0 ? 2 : 1;
@@ -761,13 +771,18 @@ static int launch_fmt_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pd
         if constexpr (U == 2) {
             if (c.U == 1 && c.NW == 8 && c.R == 4) return launch_t<FMT, EPI, 4, 1, 8>(ctx, a, s, pdl);
             if (c.U == 1 && c.NW == 16 && c.R == 4) return launch_t<FMT, EPI, 4, 1, 16>(ctx, a, s, pdl);
+            if (c.U == 1 && c.NW == 16 && c.R == 2) return launch_t<FMT, EPI, 2, 1, 16>(ctx, a, s, pdl);
         }
         set_error("SSD_MV_CONFIG=%d,%d,%d is not an instantiated tiling", c.R, c.U, c.NW);
         return SSD_ERR_ARG;
     }
-    const size_t ring = (size_t)kStages * stage_bytes<FMT, 2, U>();
-    if (smem_plan(a.cols, 16, (int)ring).total <= ctx->smem_optin)
+    const int ring = kStages * stage_bytes<FMT, 2, U>();
+    if (smem_plan(a.cols, 16, ring).total <= ctx->smem_optin)
         return launch_t<FMT, EPI, 2, U, 16>(ctx, a, s, pdl);
+    if constexpr (U == 2) {  // wide rows (x'' over 100 KB): halve the stage, keep 16 warps
+        if (smem_plan(a.cols, 16, kStages * stage_bytes<FMT, 2, 1>()).total <= ctx->smem_optin)
+            return launch_t<FMT, EPI, 2, 1, 16>(ctx, a, s, pdl);
+    }
     return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);
 }
 
@@ -797,6 +812,8 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
             "null output");
     SSD_REQ(epi != EPI_RESID || a.base != nullptr, SSD_ERR_ARG, "null residual base");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.y_k && a.y_v), SSD_ERR_ARG, "null K/V output");
+    SSD_REQ(epi != EPI_QKV_ROPE || (a.head_dim > 0 && a.head_dim / 2 <= kMaxRopePairs),
+            SSD_ERR_SHAPE, "head_dim %d outside (0, %d]", a.head_dim, 2 * kMaxRopePairs);
     switch (type) {
         case SSD_TYPE_Q4_0: return launch_fmt<SSD_TYPE_Q4_0>(ctx, epi, a, s, pdl);
         case SSD_TYPE_Q8_0: return launch_fmt<SSD_TYPE_Q8_0>(ctx, epi, a, s, pdl);

@@ -172,19 +172,50 @@ __global__ void __launch_bounds__(256) k_kv_append(const float* __restrict__ k,
 }
 
 // ------------------------------------------------ split-K decode attention
-// CTA (local kv head, chunk of ATT_P positions): scores for the GROUP query heads
-// that share the kv head (GQA kv_h = h / group, flash_attention.rs:79-80), chunk
-// max / exp / sum, then the V-weighted sum; k_attn_combine merges the chunks with
-// the online-softmax rescaling of flash_attention.rs:106-134.
+// CTA (local kv head, chunk of ATT_P = 128 positions), 4 warps of 32 positions. The
+// GROUP query heads that share the kv head (GQA kv_h = h / group,
+// flash_attention.rs:79-80) are processed together:
+//  * scores: lane = position. Each lane streams its own int8 K row (16-byte loads) and
+//    dots it with the group's q, broadcast from shared memory. The int8 values are
+//    decoded exactly with the denormal trick of the matvec (byte b of a word read as
+//    the fp32 (k+128) * 2^(s-149), q pre-scaled by 2^(85-s), the +128 removed by a
+//    per-head bias), two FMAs per instruction (fma.rn.f32x2);
+//    score = (q . k) * k_scale * 1/sqrt(d) (flash_attention.rs:87-95 over the
+//    INT8 rows of quantized_kv_cache.rs:118-130);
+//  * warp softmax statistics per head: max, sum of exp (flash_attention.rs:96-118);
+//  * P V: lane = head dimensions; weights exp(s - m) * v_scale broadcast from shared
+//    memory, V decoded exactly as signed integers;
+//  * the 4 warps' (m, l, acc) are merged with the online-softmax rescaling into one
+//    partial per (head, chunk); k_attn_combine merges the chunks (:106-134).
 constexpr int ATT_P = 128;
+constexpr int ATT_NW = ATT_P / 32;
+constexpr float kAttUnscale = 18446744073709551616.0f;  // 2^64
+constexpr float kAttS0 = 38685626227668133590597632.0f;  // 2^85: byte at bit 0
+constexpr float kAttS8 = 151115727451828646838272.0f;    // 2^77: byte at bit 8
+
+__device__ __forceinline__ float att_den(uint32_t bits) { return __uint_as_float(bits); }
+__device__ __forceinline__ void att_ffma2(float& d0, float& d1, float a0, float a1, float b0,
+                                          float b1) {
+    uint64_t d, a, b;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(d0), "f"(d1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+__device__ __forceinline__ uint32_t att_word(const uint4& q, int m) {
+    return m == 0 ? q.x : (m == 1 ? q.y : (m == 2 ? q.z : q.w));
+}
 
 template <int HD, int G>
 __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
-    constexpr int DPL = HD / 32;  // dims per lane in the PV phase
-    __shared__ __align__(16) float qs[G][HD];
-    __shared__ float sc[G][ATT_P];
-    __shared__ float ml[G][2];
-    __shared__ __align__(16) float red[4][G][HD];
+    constexpr int DPL = HD / 32;  // dims per lane in the P V phase
+    __shared__ __align__(16) float qs[G][HD];         // q * 2^85 / 2^77 by byte position
+    __shared__ __align__(16) float2 pw[ATT_NW][G][32];  // (weight, weight)
+    __shared__ __align__(16) float red[ATT_NW][G][HD];
+    __shared__ float mlw[ATT_NW][G][2];  // warp max, sum exp
+    __shared__ float fac[ATT_NW][G];
+    __shared__ float qbias[G];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
     const int g_kv = a.kv_head0 + gl;
@@ -202,130 +233,181 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
         }
         return;
     }
-    for (int i = tid; i < G * HD; i += 128) (&qs[0][0])[i] = a.q[(size_t)gl * G * HD + i];
+    const float* qg = a.q + (size_t)gl * G * HD;
+    for (int i = tid; i < G * HD; i += 128)
+        (&qs[0][0])[i] = __fmul_rn(qg[i], (i & 1) ? kAttS8 : kAttS0);
+    for (int i = warp; i < G; i += ATT_NW) {  // -128 * sum_d q[d], scaled by 2^-64
+        float t = 0.0f;
+        for (int d = lane; d < HD; d += 32) t += qg[(size_t)i * HD + d];
+        t = warp_sum(t);
+        if (lane == 0) qbias[i] = __fmul_rn(-128.0f, __fmul_rn(t, 1.0f / kAttUnscale));
+    }
     __syncthreads();
 
-    // scores: thread -> position; dot = sum_d q[d] * k8[d], score = dot * kscale * 1/sqrt(d)
+    // ---- scores: lane = position
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    const int p = p0 + 32 * warp + lane;
+    float sc[G];
     {
-        const int p = p0 + tid;
-        float dot[G];
+        float e[G], o[G];
 #pragma unroll
-        for (int g = 0; g < G; g++) dot[g] = 0.0f;
+        for (int i = 0; i < G; i++) {
+            e[i] = qbias[i];
+            o[i] = 0.0f;
+        }
         if (p < seq) {
-            const int8_t* kr = a.k + (size_t)p * a.kv_dim + (size_t)g_kv * HD;
-#pragma unroll 2
-            for (int c = 0; c < HD; c += 16) {
-                const uint4 kk = *reinterpret_cast<const uint4*>(kr + c);
-                const uint32_t wv[4] = {kk.x ^ 0x80808080u, kk.y ^ 0x80808080u,
-                                        kk.z ^ 0x80808080u, kk.w ^ 0x80808080u};
+            const uint4* kr =
+                reinterpret_cast<const uint4*>(a.k + (size_t)p * a.kv_dim + (size_t)g_kv * HD);
+            uint4 krow[HD / 16];  // the whole row in flight at once
+#pragma unroll
+            for (int j = 0; j < HD / 16; j++) krow[j] = __ldg(kr + j);
+#pragma unroll
+            for (int j = 0; j < HD / 16; j++) {
+                const uint4 kk = krow[j];  // dims 16j .. 16j+15
 #pragma unroll
                 for (int m = 0; m < 4; m++) {
-                    const float k0 = magic_byte(wv[m], 0) - kQ80Magic;
-                    const float k1 = magic_byte(wv[m], 1) - kQ80Magic;
-                    const float k2 = magic_byte(wv[m], 2) - kQ80Magic;
-                    const float k3 = magic_byte(wv[m], 3) - kQ80Magic;
+                    const uint32_t w = att_word(kk, m) ^ 0x80808080u, w2 = w >> 16;
+                    const float f0 = att_den(w & 0xFFu), f1 = att_den(w & 0xFF00u);
+                    const float f2 = att_den(w2 & 0xFFu), f3 = att_den(w2 & 0xFF00u);
 #pragma unroll
-                    for (int g = 0; g < G; g++) {
-                        const float4 q4 = *reinterpret_cast<const float4*>(&qs[g][c + 4 * m]);
-                        float t = dot[g];
-                        t = fmaf(q4.x, k0, t);
-                        t = fmaf(q4.y, k1, t);
-                        t = fmaf(q4.z, k2, t);
-                        t = fmaf(q4.w, k3, t);
-                        dot[g] = t;
+                    for (int i = 0; i < G; i++) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(&qs[i][16 * j + 4 * m]);
+                        att_ffma2(e[i], o[i], f0, f1, q4.x, q4.y);
+                        att_ffma2(e[i], o[i], f2, f3, q4.z, q4.w);
                     }
                 }
             }
             const float ksc = a.ks[p];
 #pragma unroll
-            for (int g = 0; g < G; g++) sc[g][tid] = __fmul_rn(__fmul_rn(dot[g], ksc), scale);
+            for (int i = 0; i < G; i++)
+                sc[i] = __fmul_rn(__fmul_rn(__fmul_rn(e[i] + o[i], kAttUnscale), ksc), scale);
         } else {
 #pragma unroll
-            for (int g = 0; g < G; g++) sc[g][tid] = -INFINITY;
+            for (int i = 0; i < G; i++) sc[i] = -INFINITY;
         }
     }
-    __syncthreads();
-    // chunk softmax statistics per head
-    for (int g = warp; g < G; g += 4) {
-        float m = -INFINITY;
-        for (int i = lane; i < ATT_P; i += 32) m = fmaxf(m, sc[g][i]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int i = lane; i < ATT_P; i += 32) {
-            const float e = (sc[g][i] == -INFINITY) ? 0.0f : expf(__fsub_rn(sc[g][i], m));
-            sc[g][i] = e;
-            l += e;
-        }
-        l = warp_sum(l);
+    // ---- warp softmax statistics; weights exp(s - m) * v_scale for P V
+    const float vsc = p < seq ? a.vs[p] : 0.0f;
+#pragma unroll
+    for (int i = 0; i < G; i++) {
+        const float m = warp_max(sc[i]);
+        const float ex = sc[i] == -INFINITY ? 0.0f : expf(__fsub_rn(sc[i], m));
+        const float wgt = __fmul_rn(ex, vsc);
+        const float l = warp_sum(ex);
+        pw[warp][i][lane] = make_float2(wgt, wgt);
         if (lane == 0) {
-            ml[g][0] = m;
-            ml[g][1] = l;
+            mlw[warp][i][0] = m;
+            mlw[warp][i][1] = l;
         }
     }
-    __syncthreads();
-    // PV: lane -> DPL dims, warp -> positions warp, warp+4, ...
+    __syncwarp();
+
+    // ---- P V over this warp's 32 positions: lane = dims DPL*lane ..; V values decoded
+    // exactly as signed integers (byte ^ 0x80 under exponent 0x4B, minus 2^23 + 128):
+    // the weights are all positive, so an offset decode would not cancel.
     float acc[G][DPL];
 #pragma unroll
-    for (int g = 0; g < G; g++)
+    for (int i = 0; i < G; i++)
 #pragma unroll
-        for (int j = 0; j < DPL; j++) acc[g][j] = 0.0f;
-    const int npos = min(ATT_P, seq - p0);
-    for (int i = warp; i < npos; i += 4) {
-        const int pp = p0 + i;
-        const int8_t* vr = a.v + (size_t)pp * a.kv_dim + (size_t)g_kv * HD + DPL * lane;
-        float vf[DPL];
-        if constexpr (DPL == 4) {
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(vr) ^ 0x80808080u;
-            vf[0] = magic_byte(w, 0) - kQ80Magic;
-            vf[1] = magic_byte(w, 1) - kQ80Magic;
-            vf[2] = magic_byte(w, 2) - kQ80Magic;
-            vf[3] = magic_byte(w, 3) - kQ80Magic;
-        } else {
-            const uint32_t w = (uint32_t)(*reinterpret_cast<const uint16_t*>(vr)) ^ 0x8080u;
-            vf[0] = magic_byte(w, 0) - kQ80Magic;
-            vf[1] = magic_byte(w, 1) - kQ80Magic;
-        }
-        const float vsc = a.vs[pp];
+        for (int j = 0; j < DPL; j++) acc[i][j] = 0.0f;
+    const int pw0 = p0 + 32 * warp;
+    const int npos = min(32, seq - pw0);
+    const int8_t* vbase = a.v + (size_t)g_kv * HD + DPL * lane + (size_t)pw0 * a.kv_dim;
+    uint32_t vw[32];  // this lane's bytes of the warp's 32 V rows, all loads in flight
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float wgt = __fmul_rn(sc[g][i], vsc);
-#pragma unroll
-            for (int j = 0; j < DPL; j++) acc[g][j] = fmaf(wgt, vf[j], acc[g][j]);
+    for (int t = 0; t < 32; t++) {
+        vw[t] = 0x80808080u;
+        if (t < npos) {
+            const int8_t* vr = vbase + (size_t)t * a.kv_dim;
+            if constexpr (DPL == 4)
+                vw[t] = __ldg(reinterpret_cast<const uint32_t*>(vr));
+            else
+                vw[t] = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(vr));
         }
     }
 #pragma unroll
-    for (int g = 0; g < G; g++)
+    for (int t = 0; t < 32; t++) {
+        if (t >= npos) break;
+        float f[DPL];
+        const uint32_t w = vw[t] ^ 0x80808080u;
 #pragma unroll
-        for (int j = 0; j < DPL; j++) red[warp][g][DPL * lane + j] = acc[g][j];
+        for (int j = 0; j < DPL; j++) f[j] = magic_byte(w, j) - kQ80Magic;
+#pragma unroll
+        for (int i = 0; i < G; i++) {
+            const float2 wp = pw[warp][i][t];
+#pragma unroll
+            for (int j = 0; j < DPL; j += 2) att_ffma2(acc[i][j], acc[i][j + 1], f[j], f[j + 1], wp.x, wp.y);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < G; i++)
+#pragma unroll
+        for (int j = 0; j < DPL; j++) red[warp][i][DPL * lane + j] = acc[i][j];
     __syncthreads();
-    for (int i = tid; i < G * HD; i += 128) {
-        const int g = i / HD, d = i % HD;
-        const float s = (red[0][g][d] + red[1][g][d]) + (red[2][g][d] + red[3][g][d]);
-        part[g * head_stride + 2 + d] = s;
+    // ---- merge the 4 warps: M = max m_w, factor exp(m_w - M) (0 for empty warps)
+    if (tid < ATT_NW * G) {
+        const int w = tid / G, i = tid % G;
+        float M = -INFINITY;
+#pragma unroll
+        for (int v = 0; v < ATT_NW; v++) M = fmaxf(M, mlw[v][i][0]);
+        fac[w][i] = mlw[w][i][1] == 0.0f ? 0.0f : expf(__fsub_rn(mlw[w][i][0], M));
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * HD; idx += 128) {
+        const int i = idx / HD, d = idx % HD;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < ATT_NW; w++) s = fmaf(red[w][i][d], fac[w][i], s);
+        part[i * head_stride + 2 + d] = s;
     }
     if (tid < G) {
-        part[tid * head_stride + 0] = ml[tid][0];
-        part[tid * head_stride + 1] = ml[tid][1];
+        float M = -INFINITY, L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < ATT_NW; w++) M = fmaxf(M, mlw[w][tid][0]);
+#pragma unroll
+        for (int w = 0; w < ATT_NW; w++) L = fmaf(mlw[w][tid][1], fac[w][tid], L);
+        part[tid * head_stride + 0] = M;
+        part[tid * head_stride + 1] = L;
     }
 }
 
+// Merges the chunk partials of one query head (flash_attention.rs:106-134): the chunk
+// statistics are loaded in parallel, the rescale factors exp(m_c - M) shared through
+// shared memory, then thread d sums its dimension over the chunks.
 template <int HD>
 __global__ void __launch_bounds__(HD) k_attn_combine(const AttnArgs a, int nchunks) {
-    const int h = blockIdx.x, d = threadIdx.x;
+    __shared__ float fac[1024];
+    __shared__ float red[HD / 32];
+    __shared__ float lsum[HD / 32];
+    const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     pdl_wait();
     const float* part = a.partial + (size_t)h * nchunks * (HD + 2);
+    float m = -INFINITY;
+    for (int c = d; c < nchunks; c += HD) m = fmaxf(m, part[(size_t)c * (HD + 2)]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
     float M = -INFINITY;
-    for (int c = 0; c < nchunks; c++) M = fmaxf(M, part[(size_t)c * (HD + 2)]);
-    float L = 0.0f, acc = 0.0f;
-    for (int c = 0; c < nchunks; c++) {
+#pragma unroll
+    for (int w = 0; w < HD / 32; w++) M = fmaxf(M, red[w]);
+    float L = 0.0f;
+    for (int c = d; c < nchunks; c += HD) {
         const float* pc = part + (size_t)c * (HD + 2);
         const float l = pc[1];
-        if (l == 0.0f) continue;
-        const float f = expf(__fsub_rn(pc[0], M));
+        const float f = l == 0.0f ? 0.0f : expf(__fsub_rn(pc[0], M));
+        fac[c] = f;
         L = fmaf(l, f, L);
-        acc = fmaf(pc[2 + d], f, acc);
     }
+    L = warp_sum(L);
+    if (lane == 0) lsum[warp] = L;
+    __syncthreads();
+    L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < HD / 32; w++) L += lsum[w];
+    float acc = 0.0f;  // chunks past the sequence (factor 0) hold no data: skip them
+#pragma unroll 8
+    for (int c = 0; c < nchunks; c++)
+        if (fac[c] != 0.0f) acc = fmaf(part[(size_t)c * (HD + 2) + 2 + d], fac[c], acc);
     // output_acc[d] * (1 / running_sum)  (flash_attention.rs:126-133)
     a.out[(size_t)h * HD + d] = L > 0.0f ? __fmul_rn(acc, __fdiv_rn(1.0f, L)) : 0.0f;
 }
@@ -356,6 +438,8 @@ static int launch_attn_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     SSD_REQ(a.max_seq > 0, SSD_ERR_SHAPE, "empty attention");
+    SSD_REQ((a.max_seq + ATT_P - 1) / ATT_P <= 1024, SSD_ERR_SHAPE,
+            "attention over %d positions exceeds %d", a.max_seq, 1024 * ATT_P);
     if (a.head_dim == 128) return launch_attn_hd<128>(a, s, pdl);
     if (a.head_dim == 64) return launch_attn_hd<64>(a, s, pdl);
     set_error("head_dim %d not supported (64, 128)", a.head_dim);

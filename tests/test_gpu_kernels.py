@@ -312,5 +312,22 @@ def test_attention_int8_matches_oracle(ctx, n_head, n_kv, hd, seq):
     k, ks = ora.kv_quantize_rows(kf)
     v, vs = ora.kv_quantize_rows(vf)
     ref = ora.attention_int8(q, k, ks, v, vs, seq, n_head, n_kv, hd)
-    assert rel_err(out.cpu().numpy(), ref) <= TOL
+    exact = attention_fp64(q, k, ks, v, vs, n_head, n_kv, hd)
+    got = out.cpu().numpy()
+    assert parity(got, ref, exact), (rel_err(got, ref), rel_err(ref, exact), rel_err(got, exact))
     kv.free()
+
+
+def attention_fp64(q, k, ks, v, vs, n_head, n_kv, hd):
+    """fp64 arbiter: the reference's fp32-dequantized K/V rows (key_at / value_at,
+    src/inference/quantized_kv_cache.rs:118-130), everything after in float64."""
+    kd = (k.astype(np.float32) * ks[:, None]).astype(np.float64)
+    vd = (v.astype(np.float32) * vs[:, None]).astype(np.float64)
+    g = n_head // n_kv
+    out = np.zeros(n_head * hd)
+    for h in range(n_head):
+        c = (h // g) * hd
+        sc = kd[:, c:c + hd] @ q[h * hd:(h + 1) * hd].astype(np.float64) / np.sqrt(hd)
+        p = np.exp(sc - sc.max())
+        out[h * hd:(h + 1) * hd] = (p / p.sum()) @ vd[:, c:c + hd]
+    return out
