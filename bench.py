@@ -356,6 +356,35 @@ def case_swiglu_70b(ctx, torch, ssdllm, peak, reps=10):
             "gbs": round(alg / us / 1e3, 1), "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
 
 
+def case_layer_70b(ctx, torch, ssdllm, peak, n_layers=4, reps=10):
+    """One Llama-70B-shaped decoder layer at TP1 (Q4_0, INT8 KV at 4096 positions), timed
+    as a CUDA-graph decode step of an n_layers-deep model with a 256-token vocab; per
+    layer = step / n_layers (481 MB of weights + 8.4 MB of KV per layer)."""
+    cfg = dict(CFG70B, n_layers=n_layers, vocab=256, kv_capacity=4096, tp_rank=0, tp_size=1)
+    m = ssdllm.Model(ctx, **cfg)
+    try:
+        m.synth_weights(seed=7, std=0.02)
+        m.synth_kv(seed=8, n=4096 - 4 * reps - 16)
+        stream = torch.cuda.ExternalStream(ssdllm_stream(ctx, ssdllm))
+        for _ in range(4):
+            m.decode_step(True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            m.decode_step(True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us_layer = e0.elapsed_time(e1) * 1e3 / reps / n_layers
+    finally:
+        m.free()
+    E, F, kvd = 8192, 28672, 1024
+    alg = int((2 * E * E + 2 * kvd * E + 3 * F * E) * Q40_BYTES) + 2 * 4096 * (kvd + 4) + 2 * E * 4
+    return {"shape": "llama-70b layer, Q4_0, INT8 KV ~4040, TP1", "algorithmic_bytes": alg,
+            "us_per_layer": round(us_layer, 3), "gbs": round(alg / us_layer / 1e3, 1),
+            "frac_of_peak": round(alg / us_layer / 1e3 / peak, 4), "model_layers_timed": n_layers}
+
+
 CASES = {
     "q4_0_4096x4096": lambda c, t, s, p: case_matvec(c, t, s, p, Q4_0, 4096, 4096),
     "q8_0_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 8, 11008, 4096),
@@ -365,6 +394,7 @@ CASES = {
     "swiglu_q4_0_70b": case_swiglu_70b,
     "attn_int8_70b_4096": case_attention,
     "layer_7b_q4_0": case_layer_7b,
+    "layer_70b_q4_0": case_layer_70b,
 }
 
 

@@ -233,20 +233,40 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
         }
         return;
     }
-    const float* qg = a.q + (size_t)gl * G * HD;
-    for (int i = tid; i < G * HD; i += 128)
-        (&qs[0][0])[i] = __fmul_rn(qg[i], (i & 1) ? kAttS8 : kAttS0);
-    for (int i = warp; i < G; i += ATT_NW) {  // -128 * sum_d q[d], scaled by 2^-64
+    // q of the group: all float4 loads issued at once; each HD/4 consecutive float4 are
+    // one head, so sub-groups of HD/4 lanes reduce that head's sum for the decode bias
+    const int p = p0 + 32 * warp + lane;
+    const float4* qg4 = reinterpret_cast<const float4*>(a.q + (size_t)gl * G * HD);
+    constexpr int QV = G * HD / 4 / 128 > 0 ? G * HD / 4 / 128 : 1;  // float4 per thread
+    float4 qv[QV];
+#pragma unroll
+    for (int j = 0; j < QV; j++)
+        if (tid + 128 * j < G * HD / 4) qv[j] = __ldg(qg4 + tid + 128 * j);
+    // this lane's position scales, in flight with the q loads
+    const float ksc = p < seq ? __ldg(a.ks + p) : 0.0f;
+    const float vsc = p < seq ? __ldg(a.vs + p) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < QV; j++) {
+        const int u = tid + 128 * j;  // float4 index
+        const bool in = u < G * HD / 4;
         float t = 0.0f;
-        for (int d = lane; d < HD; d += 32) t += qg[(size_t)i * HD + d];
-        t = warp_sum(t);
-        if (lane == 0) qbias[i] = __fmul_rn(-128.0f, __fmul_rn(t, 1.0f / kAttUnscale));
+        if (in) {
+            const float4 v = qv[j];
+            reinterpret_cast<float4*>(&qs[0][0])[u] =
+                make_float4(__fmul_rn(v.x, kAttS0), __fmul_rn(v.y, kAttS8),
+                            __fmul_rn(v.z, kAttS0), __fmul_rn(v.w, kAttS8));
+            t = (v.x + v.y) + (v.z + v.w);
+        }
+        // every lane shuffles (uniform control flow); groups of HD/4 lanes = one head
+#pragma unroll
+        for (int o = 1; o < HD / 4 && o < 32; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (in && (u % (HD / 4)) == 0)  // -128 * sum_d q[d], scaled by 2^-64
+            qbias[u / (HD / 4)] = __fmul_rn(-128.0f, __fmul_rn(t, 1.0f / kAttUnscale));
     }
     __syncthreads();
 
     // ---- scores: lane = position
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-    const int p = p0 + 32 * warp + lane;
     float sc[G];
     {
         float e[G], o[G];
@@ -277,7 +297,6 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
                     }
                 }
             }
-            const float ksc = a.ks[p];
 #pragma unroll
             for (int i = 0; i < G; i++)
                 sc[i] = __fmul_rn(__fmul_rn(__fmul_rn(e[i] + o[i], kAttUnscale), ksc), scale);
@@ -287,7 +306,6 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
         }
     }
     // ---- warp softmax statistics; weights exp(s - m) * v_scale for P V
-    const float vsc = p < seq ? a.vs[p] : 0.0f;
 #pragma unroll
     for (int i = 0; i < G; i++) {
         const float m = warp_max(sc[i]);
@@ -404,10 +422,25 @@ __global__ void __launch_bounds__(HD) k_attn_combine(const AttnArgs a, int nchun
     L = 0.0f;
 #pragma unroll
     for (int w = 0; w < HD / 32; w++) L += lsum[w];
-    float acc = 0.0f;  // chunks past the sequence (factor 0) hold no data: skip them
-#pragma unroll 8
-    for (int c = 0; c < nchunks; c++)
-        if (fac[c] != 0.0f) acc = fmaf(part[(size_t)c * (HD + 2) + 2 + d], fac[c], acc);
+    // chunks past the sequence (factor 0) hold stale data: their values are loaded (the
+    // buffer holds all nchunks records) but not used
+    float acc = 0.0f;
+    const float* pd = part + 2 + d;
+    int c = 0;
+    for (; c + 8 <= nchunks; c += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = pd[(size_t)(c + j) * (HD + 2)];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float f = fac[c + j];
+            acc = f != 0.0f ? fmaf(v[j], f, acc) : acc;
+        }
+    }
+    for (; c < nchunks; c++) {
+        const float v = pd[(size_t)c * (HD + 2)], f = fac[c];
+        acc = f != 0.0f ? fmaf(v, f, acc) : acc;
+    }
     // output_acc[d] * (1 / running_sum)  (flash_attention.rs:126-133)
     a.out[(size_t)h * HD + d] = L > 0.0f ? __fmul_rn(acc, __fdiv_rn(1.0f, L)) : 0.0f;
 }
