@@ -4,7 +4,8 @@
 One step = one generated token (batch 1) through the whole model: token embedding,
 80 decoder layers (fused Q4_0 dequant-matvecs, INT8-KV flash-decode attention),
 final RMSNorm + vocab matvec + greedy argmax, tensor-parallel over N GPUs with an
-NCCL all-reduce after o_proj and down_proj. Weights (39 GB) are synthetic
+all-reduce after o_proj and down_proj (in the kernels over NVLink peer memory; NCCL with
+--allreduce nccl). Weights (39 GB) are synthetic
 N(0, 0.02), quantized to Q4_0 on the device; the INT8 KV cache is filled with
 N(0, 1) rows to ~3968 positions of a 4096 capacity, so decode runs at ~4K context.
 
@@ -473,6 +474,10 @@ def run_cuda(args):
             obj = [ssdllm.Model.unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
             model.tp_init(obj[0])
+            if args.allreduce == "p2p":  # partial sums over NVLink peer memory
+                hs = [None] * world
+                dist.all_gather_object(hs, model.p2p_handle())
+                model.p2p_open(hs)
         t0 = time.perf_counter()
         model.synth_weights(seed=0, std=0.02)
         total = args.warmup + 2 * args.steps + 1
@@ -555,6 +560,7 @@ def run_cuda(args):
         "config": {"workload": "llama70b_q4_0_decode_b1", "n_layers": cfg["n_layers"],
                    "hidden": 8192, "heads": 64, "kv_heads": 8, "ffn": 28672,
                    "vocab": 128256, "context": prompt, "kv": "int8", "tp": world,
+                   "allreduce": args.allreduce if world > 1 else None,
                    "l2": "not flushed: 39 GB of weights per token >> 126 MB L2",
                    "weights_gb_per_gpu": round(weight_bytes(cfg) / world / 1e9, 2)},
         "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
@@ -598,6 +604,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="override n_layers (debug only; the headline uses 80)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
+                    help="TP partial sums: in-kernel over NVLink peer memory, or ncclAllReduce")
     ap.add_argument("--no-kernels", action="store_true",
                     help="skip the per-kernel table (BASELINE configs 0-2)")
     ap.add_argument("--case", default="",

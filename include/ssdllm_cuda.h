@@ -268,6 +268,17 @@ int ssd_model_free(ssd_model* m);
  * thread spawn/join of src/inference/tensor_parallel.rs:69-103 (one process per GPU). */
 int ssd_tp_unique_id(uint8_t out[128]);
 int ssd_model_tp_init(ssd_model* m, const uint8_t unique_id[128]);
+/* Peer-memory all-reduce for tensor parallelism. No reference counterpart: the
+ * reference's "tensor parallelism" is a thread row-split with no reduction
+ * (src/inference/tensor_parallel.rs:33-105). After ssd_model_tp_init, each rank calls
+ * ssd_model_p2p_handle (allocates its receive buffer and returns the 64-byte CUDA IPC
+ * handle), the handles are exchanged out of band, and each rank calls ssd_model_p2p_open
+ * with all tp_size handles in rank order. From then on the decode step sums the o_proj
+ * and down partials over NVLink peer memory inside its own kernels (bounded waits;
+ * a peer that never arrives is reported as SSD_ERR_TIMEOUT by ssd_ctx_device_status)
+ * instead of calling ncclAllReduce. One process per GPU, GPUs with peer access. */
+int ssd_model_p2p_handle(ssd_model* m, uint8_t out[64]);
+int ssd_model_p2p_open(ssd_model* m, const uint8_t* handles);
 /* Fill every weight with ssd_weight_synth (this rank's shard of the global tensors).
  * No reference counterpart (benchmark inputs; the reference loads GGUF files). */
 int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_dev);

@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     constexpr int QB = Slot<FMT>::QB, MB = Slot<FMT>::MB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    const bool has_add = a.x_add != nullptr, has_norm = a.norm_w != nullptr;
+    const bool has_add = a.x_add != nullptr || a.ar_in_n > 0, has_norm = a.norm_w != nullptr;
     const SmemPlan P = smem_plan(a.cols, NW, kStages * SB);
     float4* xs4 = reinterpret_cast<float4*>(base + P.xs);
     float* csum = reinterpret_cast<float*>(base + P.csum);
@@ -479,6 +479,24 @@ __global__ void __launch_bounds__(NW * 32, 1)
         for (int b = 0; b < nbox; b++)
             tma_load_2d(base + P.xs + (size_t)b * kVecBoxRows * 128, &tm_x, 0, b * kVecBoxRows, bar);
     }
+    if (a.ar_in_n > 0) {  // wait for every rank's partial of this call (bounded)
+        // fail fast: once any wait of this context has timed out, later ones do not wait
+        if (warp == 0 && lane < a.ar_in_n && *(volatile int*)a.status == SSD_OK) {
+            const unsigned long long ep = *a.ar_epoch + (unsigned long long)a.ar_call + 1ull;
+            bool done = false;
+            for (uint32_t it = 0; it < (1u << 21) && !done; it++) {
+                unsigned long long f;
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];"
+                             : "=l"(f)
+                             : "l"(a.ar_in_flag + lane)
+                             : "memory");
+                done = f >= ep;
+                if (!done) __nanosleep(100);
+            }
+            if (!done) atomicExch(a.status, SSD_ERR_TIMEOUT);  // data below is then stale
+        }
+        __syncthreads();
+    }
     const bool ok = mbar_wait(bar, 0, a.status);
     if (__syncthreads_or(!ok)) {  // timed out: status recorded, nothing computed
         cp_wait<0>();
@@ -497,7 +515,20 @@ __global__ void __launch_bounds__(NW * 32, 1)
             const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
             float4 v = xs4[ph];
             if (has_add) {  // hidden[i] += attn_output[i] (src/metal/compute.rs:547-549)
-                const float4 r = __ldg(reinterpret_cast<const float4*>(a.x_add) + i);
+                float4 r;
+                if (a.ar_in_n > 0) {  // the ranks' partials, summed in rank order (L2 reads)
+                    r = __ldcg(reinterpret_cast<const float4*>(a.ar_in) + i);
+                    for (int p = 1; p < a.ar_in_n; p++) {
+                        const float4 t =
+                            __ldcg(reinterpret_cast<const float4*>(a.ar_in + (size_t)p * a.cols) + i);
+                        r.x = __fadd_rn(r.x, t.x);
+                        r.y = __fadd_rn(r.y, t.y);
+                        r.z = __fadd_rn(r.z, t.z);
+                        r.w = __fadd_rn(r.w, t.w);
+                    }
+                } else {
+                    r = __ldg(reinterpret_cast<const float4*>(a.x_add) + i);
+                }
                 v.x = __fadd_rn(v.x, r.x);
                 v.y = __fadd_rn(v.y, r.y);
                 v.z = __fadd_rn(v.z, r.z);
@@ -620,6 +651,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
                 if (lane == r && row < a.rows)
                     a.y[row] = (EPI == EPI_RESID) ? __fadd_rn(a.base[row], res[r]) : res[r];
             }
+        } else if constexpr (EPI == EPI_PEERS) {  // partial row -> every rank's buffer
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int row = v0 + r;
+                if (lane < a.ar_out_n && row < a.rows) a.ar_out[lane][row] = res[r];
+            }
         } else if constexpr (EPI == EPI_SWIGLU) {  // rows: R/2 gate rows, then R/2 up rows
             constexpr int H = R / 2;
             if (lane < H && v0 < a.rows) {
@@ -664,6 +701,25 @@ __global__ void __launch_bounds__(NW * 32, 1)
         }
     }
     cp_wait<0>();
+
+    if constexpr (EPI == EPI_PEERS) {
+        // publish: every thread's peer stores are made visible system-wide, then the
+        // last CTA to finish raises this call's flag on every rank
+        __threadfence_system();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned prev = atomicAdd(a.ar_counter, 1u);
+            if (prev == gridDim.x - 1) {
+                __threadfence_system();
+                *a.ar_counter = 0u;  // zero for the next launch (stream-ordered)
+                const unsigned long long ep = *a.ar_epoch + (unsigned long long)a.ar_call + 1ull;
+                for (int p = 0; p < a.ar_out_n; p++)
+                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.ar_out_flag[p]),
+                                 "l"(ep)
+                                 : "memory");
+            }
+        }
+    }
 
     if constexpr (EPI == EPI_ARGMAX) {
         if (lane == 0) keys[warp] = best;
@@ -794,6 +850,7 @@ static int launch_fmt(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bo
         case EPI_SWIGLU: return launch_fmt_epi<FMT, EPI_SWIGLU>(ctx, a, s, pdl);
         case EPI_QKV_ROPE: return launch_fmt_epi<FMT, EPI_QKV_ROPE>(ctx, a, s, pdl);
         case EPI_ARGMAX: return launch_fmt_epi<FMT, EPI_ARGMAX>(ctx, a, s, pdl);
+        case EPI_PEERS: return launch_fmt_epi<FMT, EPI_PEERS>(ctx, a, s, pdl);
         default: set_error("bad epilogue %d", epi); return SSD_ERR_ARG;
     }
 }
@@ -808,8 +865,20 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
     // x, x_add, x_writeback and norm_w are read by TMA / written as float4
     SSD_REQ(a.x && al16(a.x) && al16(a.x_add) && al16(a.x_writeback) && al16(a.norm_w),
             SSD_ERR_ARG, "vector inputs must be non-null and 16-byte aligned");
-    SSD_REQ(epi == EPI_ARGMAX ? a.argmax_key != nullptr : a.y != nullptr, SSD_ERR_ARG,
-            "null output");
+    SSD_REQ(epi == EPI_ARGMAX ? a.argmax_key != nullptr
+                              : (epi == EPI_PEERS ? a.ar_out_n > 0 : a.y != nullptr),
+            SSD_ERR_ARG, "null output");
+    SSD_REQ(a.ar_in_n >= 0 && a.ar_in_n <= kMaxPeers && a.ar_out_n >= 0 &&
+                a.ar_out_n <= kMaxPeers,
+            SSD_ERR_ARG, "peer count outside [0, %d]", kMaxPeers);
+    SSD_REQ(a.ar_in_n == 0 || (a.ar_in && a.ar_in_flag && a.ar_epoch && al16(a.ar_in) &&
+                               a.x_add == nullptr),
+            SSD_ERR_ARG, "peer all-reduce input incomplete");
+    SSD_REQ(epi != EPI_PEERS || (a.ar_counter && a.ar_epoch), SSD_ERR_ARG,
+            "peer all-reduce output incomplete");
+    if (epi == EPI_PEERS)
+        for (int p = 0; p < a.ar_out_n; p++)
+            SSD_REQ(a.ar_out[p] && a.ar_out_flag[p], SSD_ERR_ARG, "null peer buffer %d", p);
     SSD_REQ(epi != EPI_RESID || a.base != nullptr, SSD_ERR_ARG, "null residual base");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.y_k && a.y_v), SSD_ERR_ARG, "null K/V output");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.head_dim > 0 && a.head_dim / 2 <= kMaxRopePairs),

@@ -7,7 +7,15 @@ namespace ssd {
 // How virtual rows map onto up to three weight tensors of the same type and width.
 enum MapMode { MAP_PLAIN = 0, MAP_QKV = 1, MAP_SWIGLU = 2 };
 // What the kernel does with each finished row.
-enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV_ROPE = 3, EPI_ARGMAX = 4 };
+enum EpiMode {
+    EPI_STORE = 0,
+    EPI_RESID = 1,
+    EPI_SWIGLU = 2,
+    EPI_QKV_ROPE = 3,
+    EPI_ARGMAX = 4,
+    EPI_PEERS = 5  // partial rows stored into every tensor-parallel rank's buffer
+};
+constexpr int kMaxPeers = 8;
 
 struct MvArgs {
     // weights (library layout); all segments share type and cols
@@ -38,6 +46,21 @@ struct MvArgs {
     unsigned long long* argmax_key;
     int index_offset;  // added to row index for ARGMAX (tensor-parallel vocab shards)
     int* status;       // device status word for bounded waits (default: the context's)
+    // Peer-memory all-reduce of tensor parallelism (model.cu). Epochs: the producer of
+    // call `ar_call` of a step raises flags to *ar_epoch + ar_call + 1.
+    // Input side (any epilogue): x_add = sum over r < ar_in_n, in rank order, of the
+    // partials at ar_in + r * cols, read after ar_in_flag[r] reaches the epoch.
+    const float* ar_in;
+    const unsigned long long* ar_in_flag;
+    int ar_in_n;
+    // Output side (EPI_PEERS): row values go to ar_out[r] + row for every rank r; the
+    // last CTA to finish (ar_counter, zero between launches) raises ar_out_flag[r].
+    float* ar_out[kMaxPeers];
+    unsigned long long* ar_out_flag[kMaxPeers];
+    int ar_out_n;
+    unsigned int* ar_counter;
+    const unsigned long long* ar_epoch;
+    int ar_call;
 };
 
 // Launches y = f(W x) with the given epilogue. pdl: launch with programmatic

@@ -13,8 +13,14 @@
 //
 // Kernel sequence per layer (TP = 1): QKV+RoPE (norm folded) -> KV append ->
 // attention (2 kernels) -> Wo + residual -> gate/up + SwiGLU (norm folded) ->
-// down + residual. With TP = N, Wo and down write partial sums that an NCCL
-// all-reduce completes; the residual add is folded into the next kernel's prologue.
+// down + residual. With TP = N, Wo and down produce partial sums of the hidden state
+// and the residual add is folded into the next kernel's prologue. The partials are
+// summed either by an NCCL all-reduce or, once the ranks have exchanged CUDA IPC
+// handles (ssd_model_p2p_*), by the kernels themselves over peer memory: Wo / down
+// store their rows straight into every rank's receive buffer (plain NVLink stores) and
+// the last CTA raises a per-call flag on every rank; the next kernel waits for the
+// flags (bounded) and sums the N partials in rank order, so every rank computes the
+// same bits. No collective library call sits between the two kernels.
 #include <nccl.h>
 #include <string.h>
 
@@ -73,6 +79,15 @@ struct ssd_model {
     int32_t* pinned = nullptr;  // 2 pinned ints: token in / token out
     // tensor parallel
     ncclComm_t comm = nullptr;
+    // peer-memory all-reduce: this rank's exported buffer ([kArSlots][tp][n_embd] floats,
+    // then [kArSlots][tp] u64 flags) and every rank's buffer as mapped here
+    void* p2p_buf = nullptr;
+    float* p2p_rbuf[kMaxPeers] = {};
+    unsigned long long* p2p_flag[kMaxPeers] = {};
+    void* p2p_mapped[kMaxPeers] = {};
+    bool p2p = false;
+    unsigned long long* ar_epoch = nullptr;  // advanced by 2 * n_layers per step
+    unsigned int* ar_counter = nullptr;      // CTA completion counter of the producers
     // graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -159,6 +174,8 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     m->key = reinterpret_cast<unsigned long long*>(S + o_misc);
     m->token = reinterpret_cast<int32_t*>(S + o_misc + 4);
     m->pos = reinterpret_cast<int*>(S + o_misc + 8);
+    m->ar_epoch = reinterpret_cast<unsigned long long*>(S + o_misc + 16);
+    m->ar_counter = reinterpret_cast<unsigned int*>(S + o_misc + 20);
     if (cudaHostAlloc(&m->pinned, 16, cudaHostAllocDefault) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->state);
@@ -199,6 +216,9 @@ extern "C" int ssd_model_free(ssd_model* m) {
     ssd_weight_free(m->output);
     if (m->out_norm) cudaFree(m->out_norm);
     if (m->comm) ncclCommDestroy(m->comm);
+    for (int r = 0; r < kMaxPeers; r++)
+        if (m->p2p_mapped[r]) cudaIpcCloseMemHandle(m->p2p_mapped[r]);
+    if (m->p2p_buf) cudaFree(m->p2p_buf);
     if (m->state) cudaFree(m->state);
     if (m->pinned) cudaFreeHost(m->pinned);
     delete m;
@@ -222,6 +242,122 @@ extern "C" int ssd_model_tp_init(ssd_model* m, const uint8_t uid[128]) {
     ncclUniqueId id;
     memcpy(&id, uid, 128);
     SSD_NCCL(ncclCommInitRank(&m->comm, tp_size(m), id, m->cfg.tp_rank));
+    return SSD_OK;
+}
+
+// ------------------------------------------------------ peer-memory all-reduce
+constexpr int kArSlots = 4;  // receive slots, used round robin by the producer calls
+
+static size_t p2p_floats(const ssd_model* m) {
+    return (size_t)kArSlots * tp_size(m) * m->cfg.n_embd;
+}
+
+extern "C" int ssd_model_p2p_handle(ssd_model* m, uint8_t out[64]) {
+    SSD_REQ(m && out, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(tp_size(m) > 1 && tp_size(m) <= kMaxPeers, SSD_ERR_STATE,
+            "peer all-reduce needs 2..%d ranks", kMaxPeers);
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t size");
+    if (!m->p2p_buf) {
+        const size_t fl = (p2p_floats(m) * 4 + 255) & ~(size_t)255;
+        const size_t bytes = fl + (size_t)kArSlots * tp_size(m) * 8;
+        if (cudaMalloc(&m->p2p_buf, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            m->p2p_buf = nullptr;
+            set_error("peer all-reduce buffer allocation (%zu bytes) failed", bytes);
+            return SSD_ERR_NOMEM;
+        }
+        SSD_CK(cudaMemset(m->p2p_buf, 0, bytes));
+        SSD_CK(cudaDeviceSynchronize());
+    }
+    cudaIpcMemHandle_t h;
+    SSD_CK(cudaIpcGetMemHandle(&h, m->p2p_buf));
+    memcpy(out, &h, 64);
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_p2p_open(ssd_model* m, const uint8_t* handles) {
+    SSD_REQ(m && handles, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(m->p2p_buf != nullptr, SSD_ERR_STATE, "call ssd_model_p2p_handle first");
+    SSD_REQ(!m->p2p, SSD_ERR_STATE, "peer buffers already open");
+    const int N = tp_size(m), me = m->cfg.tp_rank;
+    const size_t fl = (p2p_floats(m) * 4 + 255) & ~(size_t)255;
+    for (int r = 0; r < N; r++) {
+        void* p = nullptr;
+        if (r == me) {
+            p = m->p2p_buf;
+        } else {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, handles + (size_t)r * 64, 64);
+            cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                set_error("opening rank %d's buffer: %s", r, cudaGetErrorString(e));
+                return SSD_ERR_CUDA;
+            }
+            m->p2p_mapped[r] = p;
+        }
+        m->p2p_rbuf[r] = (float*)p;
+        m->p2p_flag[r] = (unsigned long long*)((char*)p + fl);
+    }
+    m->p2p = true;
+    if (m->exec) {  // re-capture with the peer path
+        cudaGraphExecDestroy(m->exec);
+        cudaGraphDestroy(m->graph);
+        m->exec = nullptr;
+        m->graph = nullptr;
+    }
+    return SSD_OK;
+}
+
+// A partial sum of the hidden state waiting to be added by the next kernel's prologue:
+// an NCCL-reduced buffer, or the peer-memory slot of producer call `call`.
+struct Pending {
+    bool on = false;
+    bool p2p = false;
+    float* buf = nullptr;
+    int call = 0;
+};
+
+static void take_pending(ssd_model* m, MvArgs& a, Pending& p) {
+    if (!p.on) return;
+    if (p.p2p) {
+        const int N = tp_size(m), slot = p.call % kArSlots;
+        a.ar_in = m->p2p_rbuf[m->cfg.tp_rank] + (size_t)slot * N * m->cfg.n_embd;
+        a.ar_in_flag = m->p2p_flag[m->cfg.tp_rank] + (size_t)slot * N;
+        a.ar_in_n = N;
+        a.ar_epoch = m->ar_epoch;
+        a.ar_call = p.call;
+    } else {
+        a.x_add = p.buf;
+    }
+    p = Pending{};
+}
+
+// Launches a partial-sum producer (Wo or down at TP > 1) and leaves the pending sum.
+static int produce_partial(ssd_model* m, MvArgs a, float* nccl_buf, bool use_p2p, int call,
+                           Pending& p, cudaStream_t s) {
+    const auto& c = m->cfg;
+    if (use_p2p) {
+        const int N = tp_size(m), me = c.tp_rank, slot = call % kArSlots;
+        a.y = nullptr;
+        a.ar_out_n = N;
+        for (int r = 0; r < N; r++) {
+            a.ar_out[r] = m->p2p_rbuf[r] + ((size_t)slot * N + me) * c.n_embd;
+            a.ar_out_flag[r] = m->p2p_flag[r] + (size_t)slot * N + me;
+        }
+        a.ar_counter = m->ar_counter;
+        a.ar_epoch = m->ar_epoch;
+        a.ar_call = call;
+        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_PEERS, a, s, true));
+        p = Pending{true, true, nullptr, call};
+    } else {
+        a.y = nccl_buf;
+        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_STORE, a, s, true));
+        SSD_NCCL(ncclAllReduce(nccl_buf, nccl_buf, c.n_embd, ncclFloat32, ncclSum, m->comm, s));
+        p = Pending{true, false, nccl_buf, call};
+    }
     return SSD_OK;
 }
 
@@ -510,9 +646,11 @@ static int check_weights(ssd_model* m) {
 }
 
 // Enqueues one layer on stream s. `h` is the residual stream on entry; `pend` a
-// pending partial sum (TP) to add first, or null. On return `h`/`pend` describe
-// the new residual stream.
-static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStream_t s, int& nl) {
+// pending partial sum (TP) to add first. On return `h` / `pend` describe the new
+// residual stream. Producer calls of the step are numbered 2*layer (Wo) and
+// 2*layer + 1 (down).
+static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use_p2p,
+                         cudaStream_t s, int& nl) {
     const auto& c = m->cfg;
     const Layer& L = m->layers[l];
     const bool tp = tp_size(m) > 1;
@@ -532,8 +670,9 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStrea
     a.rows = m->q_rows + 2 * m->kv_rows;
     a.cols = c.n_embd;
     a.x = h;
-    if (pend) {  // hidden += partial (all-reduced), written back for the residual path
-        a.x_add = pend;
+    const bool had_pend = pend.on;
+    if (had_pend) {  // hidden += partial (all-reduced), written back for the residual path
+        take_pending(m, a, pend);
         a.x_writeback = h_other;
     }
     a.norm_w = L.attn_norm;
@@ -547,10 +686,9 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStrea
     a.position_dev = m->pos;
     SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_QKV_ROPE, a, s, true));
     nl++;
-    if (pend) {
+    if (had_pend) {
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
-        pend = nullptr;
     }
     // 2. INT8 KV append at the current position
     SSD_TRY(launch_kv_append(L.kv, m->k, m->v, 0, m->pos, 1, s, true));
@@ -573,18 +711,17 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStrea
     at.max_seq = c.kv_capacity;
     SSD_TRY(launch_attention(at, s, true));
     nl += 2;
-    // 4. output projection (+ residual, or partial sum + all-reduce)
-    MvArgs o = mv_plain(L.wo, m->attn, tp ? m->p1 : h_other);
-    if (!tp) o.base = h;
-    SSD_TRY(launch_matvec(m->ctx, c.wtype, tp ? EPI_STORE : EPI_RESID, o, s, true));
-    nl++;
+    // 4. output projection (+ residual, or a partial sum for the all-reduce)
+    MvArgs o = mv_plain(L.wo, m->attn, h_other);
     if (tp) {
-        SSD_NCCL(ncclAllReduce(m->p1, m->p1, c.n_embd, ncclFloat32, ncclSum, m->comm, s));
-        pend = m->p1;
+        SSD_TRY(produce_partial(m, o, m->p1, use_p2p, 2 * l, pend, s));
     } else {
+        o.base = h;
+        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_RESID, o, s, true));
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
     }
+    nl++;
     // 5. gate/up + SwiGLU with the FFN RMSNorm folded in
     MvArgs g = {};
     g.qs[0] = L.wg->qs;
@@ -597,8 +734,9 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStrea
     g.rows = 2 * m->ff_local;
     g.cols = c.n_embd;
     g.x = h;
-    if (pend) {
-        g.x_add = pend;
+    const bool had_pend2 = pend.on;
+    if (had_pend2) {
+        take_pending(m, g, pend);
         g.x_writeback = h_other;
     }
     g.norm_w = L.ffn_norm;
@@ -607,22 +745,20 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, float*& pend, cudaStrea
     g.y = m->act;
     SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_SWIGLU, g, s, true));
     nl++;
-    if (pend) {
+    if (had_pend2) {
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
-        pend = nullptr;
     }
-    // 6. down projection (+ residual, or partial sum + all-reduce)
-    MvArgs d = mv_plain(L.wd, m->act, tp ? m->p2 : h_other);
-    if (!tp) d.base = h;
-    SSD_TRY(launch_matvec(m->ctx, c.wtype, tp ? EPI_STORE : EPI_RESID, d, s, true));
-    nl++;
+    // 6. down projection (+ residual, or a partial sum for the all-reduce)
+    MvArgs d = mv_plain(L.wd, m->act, h_other);
     if (tp) {
-        SSD_NCCL(ncclAllReduce(m->p2, m->p2, c.n_embd, ncclFloat32, ncclSum, m->comm, s));
-        pend = m->p2;
+        SSD_TRY(produce_partial(m, d, m->p2, use_p2p, 2 * l + 1, pend, s));
     } else {
+        d.base = h;
+        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_RESID, d, s, true));
         h = h_other;
     }
+    nl++;
     return SSD_OK;
 }
 
@@ -632,11 +768,12 @@ static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl) {
     SSD_TRY(launch_embed(m->tok_embd, m->token, m->h_a, s, true));
     nl++;
     float* h = m->h_a;
-    float* pend = nullptr;
-    for (int l = 0; l < c.n_layers; l++) SSD_TRY(enqueue_layer(m, l, h, pend, s, nl));
+    Pending pend;
+    const bool use_p2p = m->p2p && tp_size(m) > 1;
+    for (int l = 0; l < c.n_layers; l++) SSD_TRY(enqueue_layer(m, l, h, pend, use_p2p, s, nl));
     // logits = output * rmsnorm(h) (eps 1e-5 hard-coded at compute.rs:566), argmax
     MvArgs a = mv_plain(m->output, h, m->logits);
-    if (pend) a.x_add = pend;
+    take_pending(m, a, pend);
     a.norm_w = m->out_norm;
     a.eps = 1e-5f;
     a.norm_order = 1;
@@ -646,7 +783,8 @@ static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl) {
     nl++;
     if (tp_size(m) > 1)
         SSD_NCCL(ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s));
-    SSD_TRY(launch_finalize(m->key, m->token, m->pos, s, true));
+    SSD_TRY(launch_finalize(m->key, m->token, m->pos, use_p2p ? m->ar_epoch : nullptr,
+                            2 * c.n_layers, s, true));
     nl++;
     return SSD_OK;
 }
@@ -710,12 +848,12 @@ extern "C" int ssd_model_layer_step(ssd_model* m, int layer) {
     if (tp_size(m) > 1) SSD_REQ(m->comm != nullptr, SSD_ERR_STATE, "tp_size > 1 needs tp_init");
     cudaStream_t s = m->ctx->stream;
     float* h = m->h_a;
-    float* pend = nullptr;
+    Pending pend;
     int nl = 0;
-    SSD_TRY(enqueue_layer(m, layer, h, pend, s, nl));
+    SSD_TRY(enqueue_layer(m, layer, h, pend, false, s, nl));  // NCCL path for partials
     // leave the layer's output in h_a, with any pending partial sum applied
-    if (pend) {
-        k_add<<<(m->cfg.n_embd + 255) / 256, 256, 0, s>>>(m->h_a, h, pend, m->cfg.n_embd);
+    if (pend.on) {
+        k_add<<<(m->cfg.n_embd + 255) / 256, 256, 0, s>>>(m->h_a, h, pend.buf, m->cfg.n_embd);
         SSD_CK_LAUNCH();
     } else if (h != m->h_a) {
         SSD_CK(cudaMemcpyAsync(m->h_a, h, (size_t)m->cfg.n_embd * 4, cudaMemcpyDeviceToDevice, s));

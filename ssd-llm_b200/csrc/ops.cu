@@ -512,12 +512,14 @@ __global__ void __launch_bounds__(256) k_embed(const ssd_weight e, const int32_t
     }
 }
 
-__global__ void k_finalize(unsigned long long* key, int32_t* token, int* pos) {
+__global__ void k_finalize(unsigned long long* key, int32_t* token, int* pos,
+                           unsigned long long* epoch, int epoch_inc) {
     pdl_wait();
     const unsigned long long k = *key;
     *token = (int32_t)(uint32_t)(k & 0xFFFFFFFFull);
     *key = 0ull;
     *pos += 1;
+    if (epoch) *epoch += (unsigned long long)epoch_inc;
 }
 
 int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
@@ -528,8 +530,9 @@ int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden,
     return SSD_OK;
 }
 
-int launch_finalize(unsigned long long* key, int32_t* token, int* pos, cudaStream_t s, bool pdl) {
-    SSD_CK(launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, pdl, key, token, pos));
+int launch_finalize(unsigned long long* key, int32_t* token, int* pos, unsigned long long* epoch,
+                    int epoch_inc, cudaStream_t s, bool pdl) {
+    SSD_CK(launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, pdl, key, token, pos, epoch, epoch_inc));
     return SSD_OK;
 }
 

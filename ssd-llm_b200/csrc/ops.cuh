@@ -32,7 +32,8 @@ int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 // key_dev is non-null) into hidden.
 int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
                  bool pdl);
-// token = low 32 bits of *key; *key = 0; *pos += 1.
-int launch_finalize(unsigned long long* key, int32_t* token, int* pos, cudaStream_t s, bool pdl);
+// token = low 32 bits of *key; *key = 0; *pos += 1; *epoch += epoch_inc (if epoch).
+int launch_finalize(unsigned long long* key, int32_t* token, int* pos, unsigned long long* epoch,
+                    int epoch_inc, cudaStream_t s, bool pdl);
 
 }  // namespace ssd

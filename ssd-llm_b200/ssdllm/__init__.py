@@ -126,6 +126,8 @@ _SIGS = {
     "ssd_model_norm": ([_vp, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
     "ssd_model_kv": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
     "ssd_model_layer_step": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_model_p2p_handle": ([_vp, ctypes.c_char_p], ctypes.c_int),
+    "ssd_model_p2p_open": ([_vp, ctypes.c_char_p], ctypes.c_int),
     "ssd_model_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
 
@@ -370,6 +372,17 @@ class Model:
 
     def tp_init(self, uid: bytes):
         check(lib().ssd_model_tp_init(self.h, uid))
+
+    def p2p_handle(self) -> bytes:
+        """This rank's 64-byte CUDA IPC handle of its all-reduce receive buffer."""
+        buf = ctypes.create_string_buffer(64)
+        check(lib().ssd_model_p2p_handle(self.h, buf))
+        return buf.raw
+
+    def p2p_open(self, handles):
+        """Maps every rank's buffer (handles in rank order): partial sums then travel
+        over peer memory inside the decode kernels instead of ncclAllReduce."""
+        check(lib().ssd_model_p2p_open(self.h, b"".join(handles)))
 
     def synth_weights(self, seed: int, std: float = 0.02):
         check(lib().ssd_model_synth_weights(self.h, seed, std))
