@@ -144,6 +144,16 @@ int ssd_quantize(ssd_ctx* ctx, const float* x_dev, int rows, int cols, int ggml_
  * matvec_q4_k_cpu (src/metal/compute.rs:718-744). */
 int ssd_dequantize(ssd_ctx* ctx, const ssd_weight* w, float* out_dev, void* stream);
 
+/* ------------------------------------------------------- batch prefill */
+/* y[t] = W x[t] for n_tokens prompt tokens at once (x [n_tokens][cols], y
+ * [n_tokens][rows], row-major device arrays): the per-token matvec_quantized calls of the
+ * layer-major batch_prefill_lora loop (src/inference/transformer.rs:120-250) as one
+ * tensor-core GEMM (tcgen05, fp16 hi/lo operand splits, three passes, fp32 accumulation in
+ * TMEM). n_tokens and rows multiples of 128, cols a multiple of 64. Uses the context's
+ * scratch buffer (4 bytes per weight + 4 per activation). */
+int ssd_prefill_matmul(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev, int n_tokens,
+                       float* y_dev, void* stream);
+
 /* ------------------------------------------------------------- matvecs */
 /* y = W x. Replaces MetalCompute::matvec_quantized (src/metal/compute.rs:157-191)
  * and the matvec_q4_0 / matvec_q8_0 / matvec_q4_k Metal kernels

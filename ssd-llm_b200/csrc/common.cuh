@@ -136,6 +136,51 @@ __device__ __forceinline__ float synth_normal(uint64_t seed, uint32_t tid, uint6
     return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
 }
 
+// Elements e0 .. e0+7 (e0 a multiple of 8) of a weight in the library layout, flat
+// row-major index, dequantized exactly as dequantize_to_f32 (src/ssd/streamer.rs:93-180)
+// and the Q4_K element formula of matvec_q4_k_cpu (src/metal/compute.rs:718-744).
+__device__ __forceinline__ void dequant8(const ssd_weight& w, int64_t e0, float (&v)[8]) {
+    if (w.type == SSD_TYPE_F32) {
+        for (int t = 0; t < 8; t++) v[t] = reinterpret_cast<const float*>(w.qs)[e0 + t];
+    } else if (w.type == SSD_TYPE_Q4_0) {
+        const int64_t blk = e0 / 32;
+        const int j0 = (int)(e0 % 32) / 2;  // byte index
+        const float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
+        const uint8_t* q = w.qs + blk * 16 + j0;
+        for (int t = 0; t < 4; t++) {
+            v[2 * t] = __fmul_rn((float)((int)(q[t] & 0x0F) - 8), s);
+            v[2 * t + 1] = __fmul_rn((float)((int)(q[t] >> 4) - 8), s);
+        }
+    } else if (w.type == SSD_TYPE_Q8_0) {
+        const int64_t blk = e0 / 32;
+        const float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
+        const int8_t* q = reinterpret_cast<const int8_t*>(w.qs) + e0;
+        for (int t = 0; t < 8; t++) v[t] = __fmul_rn((float)q[t], s);
+    } else {  // Q4_K
+        const int64_t sbk = e0 / 256;
+        const int within = (int)(e0 % 256);
+        const int sb = within / 32, j0 = (within % 32) / 2;
+        const uint8_t* m = w.meta + sbk * 16;
+        const float d = f16_bits_to_f32((uint16_t)(m[0] | (m[1] << 8)));
+        const float dmin = f16_bits_to_f32((uint16_t)(m[2] | (m[3] << 8)));
+        const uint8_t* sc = m + 4;
+        int s6, m6;
+        if (sb < 4) {
+            s6 = sc[sb] & 0x3F;
+            m6 = sc[sb + 4] & 0x3F;
+        } else {
+            s6 = (sc[sb - 4] >> 6) | ((sc[sb + 4] & 0x0F) << 2);
+            m6 = (sc[sb] >> 6) | ((sc[sb + 4] >> 4) << 2);
+        }
+        const float scale = __fmul_rn(d, (float)s6), mn = __fmul_rn(dmin, (float)m6);
+        const uint8_t* q = w.qs + sbk * 128 + sb * 16 + j0;
+        for (int t = 0; t < 4; t++) {
+            v[2 * t] = __fsub_rn(__fmul_rn(scale, (float)(q[t] & 0x0F)), mn);
+            v[2 * t + 1] = __fsub_rn(__fmul_rn(scale, (float)(q[t] >> 4)), mn);
+        }
+    }
+}
+
 // ------------------------------------------------------------- TMA / mbarrier
 // Device-side status word (one int per context, ssd_ctx::dev_status): a bounded wait
 // that gives up records SSD_ERR_TIMEOUT there (read and cleared by
@@ -155,6 +200,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)
                  : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // Waits for phase `parity` of the barrier with an iteration limit (about a second).
 // Returns false, after recording SSD_ERR_TIMEOUT in *status, if the limit is reached.

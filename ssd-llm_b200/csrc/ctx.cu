@@ -290,45 +290,7 @@ __global__ void k_dequant(const ssd_weight w, float* __restrict__ out) {
     int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;  // 8 elements
     if (e0 >= n) return;
     float v[8];
-    if (w.type == SSD_TYPE_F32) {
-        for (int t = 0; t < 8; t++) v[t] = reinterpret_cast<const float*>(w.qs)[e0 + t];
-    } else if (w.type == SSD_TYPE_Q4_0) {
-        int64_t blk = e0 / 32;
-        int j0 = (int)(e0 % 32) / 2;  // byte index
-        float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
-        const uint8_t* q = w.qs + blk * 16 + j0;
-        for (int t = 0; t < 4; t++) {
-            v[2 * t] = __fmul_rn((float)((int)(q[t] & 0x0F) - 8), s);
-            v[2 * t + 1] = __fmul_rn((float)((int)(q[t] >> 4) - 8), s);
-        }
-    } else if (w.type == SSD_TYPE_Q8_0) {
-        int64_t blk = e0 / 32;
-        float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
-        const int8_t* q = reinterpret_cast<const int8_t*>(w.qs) + e0;
-        for (int t = 0; t < 8; t++) v[t] = __fmul_rn((float)q[t], s);
-    } else {  // Q4_K
-        int64_t sbk = e0 / 256;
-        int within = (int)(e0 % 256);
-        int sb = within / 32, j0 = (within % 32) / 2;
-        const uint8_t* m = w.meta + sbk * 16;
-        float d = f16_bits_to_f32((uint16_t)(m[0] | (m[1] << 8)));
-        float dmin = f16_bits_to_f32((uint16_t)(m[2] | (m[3] << 8)));
-        const uint8_t* sc = m + 4;
-        int s6, m6;
-        if (sb < 4) {
-            s6 = sc[sb] & 0x3F;
-            m6 = sc[sb + 4] & 0x3F;
-        } else {
-            s6 = (sc[sb - 4] >> 6) | ((sc[sb + 4] & 0x0F) << 2);
-            m6 = (sc[sb] >> 6) | ((sc[sb + 4] >> 4) << 2);
-        }
-        float scale = __fmul_rn(d, (float)s6), mn = __fmul_rn(dmin, (float)m6);
-        const uint8_t* q = w.qs + sbk * 128 + sb * 16 + j0;
-        for (int t = 0; t < 4; t++) {
-            v[2 * t] = __fsub_rn(__fmul_rn(scale, (float)(q[t] & 0x0F)), mn);
-            v[2 * t + 1] = __fsub_rn(__fmul_rn(scale, (float)(q[t] >> 4)), mn);
-        }
-    }
+    dequant8(w, e0, v);
     for (int t = 0; t < 8; t++) out[e0 + t] = v[t];
 }
 

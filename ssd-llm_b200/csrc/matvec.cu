@@ -320,8 +320,11 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 
 // Shared-memory plan of one CTA (offsets from a 1024-byte aligned base): the staged
 // x'' (TMA destination, swizzled), the per-chunk bias sums, reduction scratch, the
-// TMA barrier, and one weight ring of kStages stages per warp.
-constexpr int kStages = 4;
+// TMA barrier, and one weight ring of n_stages stages per warp: 4 for the 16-warp CTAs
+// that own an SM, 3 for the 8-warp CTAs sized so that two CTAs fit on an SM (the next
+// kernel's CTAs can then start their weight prefetch beside the previous kernel's).
+template <int NW>
+__host__ __device__ constexpr int n_stages() { return NW >= 16 ? 4 : 3; }
 struct SmemPlan {
     int nc, xrows;  // chunks, staged rows (multiple of kVecBoxRows)
     size_t xs, csum, red, bar, rope, ring, total;
@@ -362,8 +365,9 @@ __device__ __forceinline__ float pos_scale(int k) {
 // each warp keeps kStages - 1 stages of copies in flight in its shared-memory ring,
 // the first ones issued before griddepcontrol.wait.
 template <int FMT, int EPI, int R, int U, int NW>
-__global__ void __launch_bounds__(NW * 32, 1)
+__global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     k_matvec(const MvArgs a, const __grid_constant__ CUtensorMap tm_x) {
+    constexpr int kStages = n_stages<NW>();
     constexpr int SB = stage_bytes<FMT, R, U>();
     constexpr int QB = Slot<FMT>::QB, MB = Slot<FMT>::MB;
     extern __shared__ uint8_t smem_raw[];
@@ -791,7 +795,7 @@ static int occupancy(ssd_ctx* ctx, K kern, int threads, size_t smem, int* out) {
 template <int FMT, int EPI, int R, int U, int NW>
 static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     auto kern = k_matvec<FMT, EPI, R, U, NW>;
-    const SmemPlan P = smem_plan(a.cols, NW, kStages * stage_bytes<FMT, R, U>());
+    const SmemPlan P = smem_plan(a.cols, NW, n_stages<NW>() * stage_bytes<FMT, R, U>());
     SSD_REQ(P.total <= ctx->smem_optin, SSD_ERR_SHAPE,
             "cols %d too large for shared-memory staging (%zu bytes)", a.cols, P.total);
     int nb = 0;
@@ -832,11 +836,20 @@ static int launch_fmt_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pd
         set_error("SSD_MV_CONFIG=%d,%d,%d is not an instantiated tiling", c.R, c.U, c.NW);
         return SSD_ERR_ARG;
     }
-    const int ring = kStages * stage_bytes<FMT, 2, U>();
+    static const bool coresident = [] {
+        const char* e = getenv("SSD_MV_COAL");
+        return e && e[0] == '1';
+    }();
+    if (coresident &&
+        2 * (smem_plan(a.cols, 8, n_stages<8>() * stage_bytes<FMT, 2, U>()).total + 1024) <=
+            ctx->smem_per_sm)
+        return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);
+    const int ring = n_stages<16>() * stage_bytes<FMT, 2, U>();
     if (smem_plan(a.cols, 16, ring).total <= ctx->smem_optin)
         return launch_t<FMT, EPI, 2, U, 16>(ctx, a, s, pdl);
     if constexpr (U == 2) {  // wide rows (x'' over 100 KB): halve the stage, keep 16 warps
-        if (smem_plan(a.cols, 16, kStages * stage_bytes<FMT, 2, 1>()).total <= ctx->smem_optin)
+        if (smem_plan(a.cols, 16, n_stages<16>() * stage_bytes<FMT, 2, 1>()).total <=
+            ctx->smem_optin)
             return launch_t<FMT, EPI, 2, 1, 16>(ctx, a, s, pdl);
     }
     return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);

@@ -100,6 +100,7 @@ _SIGS = {
     "ssd_attention_int8": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp], ctypes.c_int),
     "ssd_attention_int8_noalloc": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp],
                                    ctypes.c_int),
+    "ssd_prefill_matmul": ([_vp, _vp, _vp, ctypes.c_int, _vp, _vp], ctypes.c_int),
     "ssd_matvec_quantized_host": ([_vp, _vp, ctypes.c_size_t, _vp, _vp, ctypes.c_int,
                                    ctypes.c_int, ctypes.c_int], ctypes.c_int),
     "ssd_model_create": ([_vp, ctypes.POINTER(ModelConfig), ctypes.POINTER(_vp)], ctypes.c_int),
@@ -256,6 +257,11 @@ class Weight:
 # ------------------------------------------------------- device-pointer ops
 def matvec(ctx, w: Weight, x, y):
     check(lib().ssd_matvec(ctx.h, w.h, _ptr(x), _ptr(y), _stream()))
+
+
+def prefill_matmul(ctx, w: Weight, x, y):
+    """y[t] = W x[t] for every row t of x (torch [n_tokens][cols] -> [n_tokens][rows])."""
+    check(lib().ssd_prefill_matmul(ctx.h, w.h, _ptr(x), x.shape[0], _ptr(y), _stream()))
 
 
 def matvec_residual(ctx, w: Weight, x, base, y):
