@@ -386,6 +386,54 @@ def case_layer_70b(ctx, torch, ssdllm, peak, n_layers=4, reps=10):
             "frac_of_peak": round(alg / us_layer / 1e3 / peak, 4), "model_layers_timed": n_layers}
 
 
+def case_prefill_l3_8b(ctx, torch, ssdllm, peak, reps=3):
+    """layer-major batch prefill of 512 tokens through Llama-3-8B-shaped
+    layers (hidden 4096, 32 q / 8 kv heads, FFN 14336, Q4_K weights, RoPE theta 5e5, causal
+    attention over the INT8 cache), then the vocab matvec (128256) and argmax of the last
+    token. Models of 1 and 3 layers are timed (weight splits prepared by an untimed first
+    call); per layer = difference / 2. Useful FLOPs per layer = the GEMMs' 2 M N K + the
+    causal attention's QK^T and PV; the tensor-core GEMMs execute 3 fp16 passes of each
+    product (hi/lo operand splits) for fp32-level accuracy."""
+    M, E, F, nh, nkv, hd, V = 512, 4096, 14336, 32, 8, 128, 128256
+    toks = torch.randint(0, V, (M,), generator=torch.Generator().manual_seed(9)).numpy()
+    times = {}
+    for L in (1, 3):
+        cfg = dict(n_layers=L, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=V,
+                   wtype=12, out_type=12, embd_type=0, kv_capacity=M, theta=5e5, eps=1e-5,
+                   tp_rank=0, tp_size=1)
+        m = ssdllm.Model(ctx, **cfg)
+        try:
+            m.synth_weights(seed=21, std=0.02)
+            m.set_position(0)
+            m.prefill(toks)  # prepares the weight splits
+            ts = []
+            for _ in range(reps):
+                m.set_position(0)
+                t0 = time.perf_counter()
+                m.prefill(toks)
+                ts.append(time.perf_counter() - t0)
+            times[L] = min(ts)
+        finally:
+            m.free()
+    per_layer = (times[3] - times[1]) / 2
+    gemm_flops = 2 * M * ((nh * hd + 2 * nkv * hd) * E + E * E + 2 * F * E + F * E)
+    attn_flops = 2 * 2 * nh * hd * (M * (M + 1) // 2)
+    tflops = (gemm_flops + attn_flops) / per_layer / 1e12
+    tpk, _ = measured_tensor_peak()
+    return {"shape": "llama3-8b layer, Q4_K, 512 tokens", "useful_flops_per_layer":
+            gemm_flops + attn_flops, "ms_per_layer": round(per_layer * 1e3, 3),
+            "prefill_ms_1_layer_incl_logits": round(times[1] * 1e3, 3),
+            "tokens_per_s_per_layer": round(M / per_layer, 1), "tflops": round(tflops, 1),
+            "frac_of_bf16_peak": round(tflops / tpk, 4), "mma_passes": 3}
+
+
+def measured_tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured bf16_tflops"
+    return 1590.0, "fallback 1.59 PFLOP/s"
+
+
 CASES = {
     "q4_0_4096x4096": lambda c, t, s, p: case_matvec(c, t, s, p, Q4_0, 4096, 4096),
     "q8_0_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 8, 11008, 4096),
@@ -396,6 +444,7 @@ CASES = {
     "attn_int8_70b_4096": case_attention,
     "layer_7b_q4_0": case_layer_7b,
     "layer_70b_q4_0": case_layer_70b,
+    "prefill_l3_8b_q4_k": case_prefill_l3_8b,
 }
 
 

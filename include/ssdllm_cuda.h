@@ -314,6 +314,15 @@ int ssd_model_decode_step(ssd_model* m, int use_graph);
 /* Host token in, host token out: ssd_model_decode_step with the H2D and D2H copies
  * (generate's embed -> forward_pass -> sample, src/inference/transformer.rs:732-770). */
 int ssd_model_decode_token(ssd_model* m, int32_t token_in, int32_t* token_out, int use_graph);
+/* Layer-major batch prefill of n prompt tokens (host array) at the current position:
+ * batch_prefill_lora (src/inference/transformer.rs:120-250) followed by the logits and
+ * greedy argmax of the last token (generate, :681-741). Every layer's projections run as
+ * tensor-core GEMMs over the n token rows, attention is causal over the INT8 cache (the
+ * tokens' K/V rows are appended first); the first call prepares fp16 hi/lo splits of the
+ * layer weights (4 bytes per weight, kept by the model). Leaves the decode state as after
+ * n decode steps: position += n, the next token in the token slot and *next_token.
+ * tp_size 1; n a multiple of 128; n_embd, n_ff and the QKV rows multiples of 128. */
+int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int32_t* next_token);
 /* Device pointers of the decode state: hidden [n_embd] (generate's hidden_state,
  * src/inference/transformer.rs:637), logits [vocab/tp], token. */
 int ssd_model_state(ssd_model* m, float** hidden_dev, float** logits_dev, int32_t** token_dev);

@@ -181,6 +181,18 @@ __device__ __forceinline__ void dequant8(const ssd_weight& w, int64_t e0, float 
     }
 }
 
+// RoPE angle of pair i at `pos` (src/metal/compute.rs:494-503): freq = 1 / theta^(2i/d),
+// angle = pos * freq, rotation by (cos, sin). powf / sin / cos are evaluated in double
+// and rounded once to float. Computed once per CTA for the head_dim/2 pairs.
+__device__ __forceinline__ float2 rope_cs(int i, int head_dim, float theta, int pos) {
+    const float e = __fdiv_rn(__fmul_rn(2.0f, (float)i), (float)head_dim);
+    const float p = (float)pow((double)theta, (double)e);
+    const float freq = __fdiv_rn(1.0f, p);
+    const float ang = __fmul_rn((float)pos, freq);
+    double sd, cd;
+    sincos((double)ang, &sd, &cd);
+    return make_float2((float)cd, (float)sd);
+}
 // ------------------------------------------------------------- TMA / mbarrier
 // Device-side status word (one int per context, ssd_ctx::dev_status): a bounded wait
 // that gives up records SSD_ERR_TIMEOUT there (read and cleared by

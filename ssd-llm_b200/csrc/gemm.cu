@@ -257,10 +257,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // dst row = row_map(src row): plain, or the SwiGLU tiling (gate rows and up rows of the same
 // output columns side by side in one BN-wide tile).
 __global__ void __launch_bounds__(256) k_wsplit(const ssd_weight w, int map_mode, int half_tile,
-                                                int seg, __half* hi, __half* lo, float* rscale) {
+                                                int seg, int dst0, __half* hi, __half* lo,
+                                                float* rscale) {
     __shared__ float red[8];
     const int r = blockIdx.x, K = w.cols;
-    int dst = r;
+    int dst = dst0 + r;
     if (map_mode == 1) dst = (r / half_tile) * 2 * half_tile + seg * half_tile + (r % half_tile);
     float mx = 0.0f;
     for (int e = threadIdx.x * 8; e < K; e += 256 * 8) {
@@ -351,9 +352,9 @@ static int encode_f16_map(CUtensorMap* map, const __half* ptr, int rows, int K, 
 }
 
 int prepare_weight_split(ssd_ctx* ctx, const ssd_weight* w, int map_mode, int half_tile, int seg,
-                         __half* hi, __half* lo, float* rscale, cudaStream_t s) {
+                         int dst0, __half* hi, __half* lo, float* rscale, cudaStream_t s) {
     SSD_REQ(w->cols % 64 == 0, SSD_ERR_SHAPE, "prefill GEMM needs K %% 64 == 0 (K = %d)", w->cols);
-    k_wsplit<<<w->rows, 256, 0, s>>>(*w, map_mode, half_tile, seg, hi, lo, rscale);
+    k_wsplit<<<w->rows, 256, 0, s>>>(*w, map_mode, half_tile, seg, dst0, hi, lo, rscale);
     SSD_CK_LAUNCH();
     (void)ctx;
     return SSD_OK;
@@ -429,7 +430,7 @@ extern "C" int ssd_prefill_matmul(ssd_ctx* ctx, const ssd_weight* w, const float
     __half* ahi = wlo + N * K;
     __half* alo = ahi + M * K;
     float* rs = (float*)(alo + M * K);
-    SSD_TRY(prepare_weight_split(ctx, w, 0, 0, 0, whi, wlo, rs, s));
+    SSD_TRY(prepare_weight_split(ctx, w, 0, 0, 0, 0, whi, wlo, rs, s));
     SSD_TRY(prepare_act_split(x_dev, (int)M, (int)K, nullptr, 0.0f, 0, ahi, alo, s, false));
     GemmOperands op{ahi, alo, whi, wlo};
     GemmArgs g = {};

@@ -28,9 +28,10 @@ struct GemmOperands {
 };
 
 // Weight -> fp16 hi / lo rows with power-of-two row scales (rscale = 1 / scale).
-// map_mode 1 places row r of segment seg (0 gate, 1 up) at (r / half) * 2 half + seg half + r % half.
+// map_mode 0 places row r at dst0 + r; map_mode 1 places row r of segment seg (0 gate,
+// 1 up) at (r / half) * 2 half + seg half + r % half.
 int prepare_weight_split(ssd_ctx* ctx, const ssd_weight* w, int map_mode, int half_tile, int seg,
-                         __half* hi, __half* lo, float* rscale, cudaStream_t s);
+                         int dst0, __half* hi, __half* lo, float* rscale, cudaStream_t s);
 // Activations [M][K] f32 -> fp16 hi / lo, with an optional per-row RMSNorm first.
 int prepare_act_split(const float* x, int M, int K, const float* norm_w, float eps, int norm_order,
                       __half* hi, __half* lo, cudaStream_t s, bool pdl);

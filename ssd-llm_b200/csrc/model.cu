@@ -27,6 +27,7 @@
 #include <string>
 #include <vector>
 
+#include "gemm.cuh"
 #include "matvec.cuh"
 #include "ops.cuh"
 
@@ -48,6 +49,41 @@ struct Layer {
     float* ffn_norm = nullptr;
     ssd_kv_cache* kv = nullptr;
 };
+
+// Prefill weights of one layer as fp16 hi / lo splits for the tensor-core GEMMs: QKV
+// concatenated ([Wq; Wk; Wv] rows), Wo, gate/up interleaved in 64-row halves of each
+// 128-row tile (the SwiGLU epilogue pairs them), down; r* = per-row inverse scales.
+struct PfLayer {
+    __half *qkv_h = nullptr, *qkv_l = nullptr, *o_h = nullptr, *o_l = nullptr;
+    __half *gu_h = nullptr, *gu_l = nullptr, *d_h = nullptr, *d_l = nullptr;
+    float *qkv_r = nullptr, *o_r = nullptr, *gu_r = nullptr, *d_r = nullptr;
+};
+
+// Prefill RoPE: QKV rows [n][q_rows + 2 kv_rows] of tokens at positions pos0 + t ->
+// contiguous Q (rotated), K (rotated), V; pairs (2i, 2i+1) within each head
+// (rope_f32_multi_head, src/metal/compute.rs:482-506).
+__global__ void __launch_bounds__(256) k_prefill_rope(const float* qkv, int q_rows, int kv_rows,
+                                                      int head_dim, float theta, int pos0, float* q,
+                                                      float* k, float* v) {
+    __shared__ float2 cs[256];
+    const int t = blockIdx.x, N = q_rows + 2 * kv_rows;
+    pdl_wait();
+    for (int i = threadIdx.x; i < head_dim / 2; i += 256) cs[i] = rope_cs(i, head_dim, theta, pos0 + t);
+    __syncthreads();
+    const float* row = qkv + (size_t)t * N;
+    for (int j = 2 * threadIdx.x; j < q_rows + kv_rows; j += 512) {
+        float x0 = row[j], x1 = row[j + 1];
+        const float2 c = cs[(j % head_dim) >> 1];
+        const float a0 = x0, a1 = x1;
+        x0 = __fsub_rn(__fmul_rn(a0, c.x), __fmul_rn(a1, c.y));
+        x1 = __fadd_rn(__fmul_rn(a0, c.y), __fmul_rn(a1, c.x));
+        float* dst = j < q_rows ? q + (size_t)t * q_rows + j : k + (size_t)t * kv_rows + (j - q_rows);
+        dst[0] = x0;
+        dst[1] = x1;
+    }
+    for (int j = threadIdx.x; j < kv_rows; j += 256)
+        v[(size_t)t * kv_rows + j] = row[q_rows + kv_rows + j];
+}
 
 __global__ void k_add(float* out, const float* a, const float* b, int n) {
     pdl_wait();
@@ -88,6 +124,11 @@ struct ssd_model {
     bool p2p = false;
     unsigned long long* ar_epoch = nullptr;  // advanced by 2 * n_layers per step
     unsigned int* ar_counter = nullptr;      // CTA completion counter of the producers
+    // batch prefill: weight splits (prepared on first use) and work buffers
+    void* pf_walloc = nullptr;
+    std::vector<PfLayer> pf;
+    void* pf_buf = nullptr;
+    size_t pf_buf_bytes = 0;
     // graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -219,6 +260,8 @@ extern "C" int ssd_model_free(ssd_model* m) {
     for (int r = 0; r < kMaxPeers; r++)
         if (m->p2p_mapped[r]) cudaIpcCloseMemHandle(m->p2p_mapped[r]);
     if (m->p2p_buf) cudaFree(m->p2p_buf);
+    if (m->pf_walloc) cudaFree(m->pf_walloc);
+    if (m->pf_buf) cudaFree(m->pf_buf);
     if (m->state) cudaFree(m->state);
     if (m->pinned) cudaFreeHost(m->pinned);
     delete m;
@@ -867,3 +910,220 @@ extern "C" int ssd_model_launches_per_step(ssd_model* m, int* launches) {
     *launches = m->launches;
     return SSD_OK;
 }
+
+// ================================================================ batch prefill
+// Layer-major batch prefill (batch_prefill_lora, src/inference/transformer.rs:120-250):
+// the n prompt tokens go through each layer together, every projection one tensor-core
+// GEMM over the n token rows (gemm.cu), attention causal over the INT8 cache.
+
+static int prepare_prefill_weights(ssd_model* m, cudaStream_t s) {
+    if (m->pf_walloc) return SSD_OK;
+    const auto& c = m->cfg;
+    const size_t E = c.n_embd, F = m->ff_local, NQ = (size_t)m->q_rows + 2 * m->kv_rows;
+    auto pad = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t per = pad(NQ * E * 2) * 2 + pad(NQ * 4) + pad(E * E * 2) * 2 + pad(E * 4) +
+                       pad(2 * F * E * 2) * 2 + pad(2 * F * 4) + pad(E * F * 2) * 2 + pad(E * 4);
+    const size_t total = per * c.n_layers;
+    if (cudaMalloc(&m->pf_walloc, total) != cudaSuccess) {
+        cudaGetLastError();
+        m->pf_walloc = nullptr;
+        set_error("prefill weight splits (%zu bytes) do not fit", total);
+        return SSD_ERR_NOMEM;
+    }
+    m->pf.assign(c.n_layers, PfLayer{});
+    char* p = (char*)m->pf_walloc;
+    auto take = [&](size_t b) {
+        char* r = p;
+        p += pad(b);
+        return r;
+    };
+    for (int l = 0; l < c.n_layers; l++) {
+        PfLayer& P = m->pf[l];
+        const Layer& L = m->layers[l];
+        P.qkv_h = (__half*)take(NQ * E * 2);
+        P.qkv_l = (__half*)take(NQ * E * 2);
+        P.qkv_r = (float*)take(NQ * 4);
+        P.o_h = (__half*)take(E * E * 2);
+        P.o_l = (__half*)take(E * E * 2);
+        P.o_r = (float*)take(E * 4);
+        P.gu_h = (__half*)take(2 * F * E * 2);
+        P.gu_l = (__half*)take(2 * F * E * 2);
+        P.gu_r = (float*)take(2 * F * 4);
+        P.d_h = (__half*)take(E * F * 2);
+        P.d_l = (__half*)take(E * F * 2);
+        P.d_r = (float*)take(E * 4);
+        SSD_TRY(prepare_weight_split(m->ctx, L.wq, 0, 0, 0, 0, P.qkv_h, P.qkv_l, P.qkv_r, s));
+        SSD_TRY(prepare_weight_split(m->ctx, L.wk, 0, 0, 0, m->q_rows, P.qkv_h, P.qkv_l, P.qkv_r, s));
+        SSD_TRY(prepare_weight_split(m->ctx, L.wv, 0, 0, 0, m->q_rows + m->kv_rows, P.qkv_h,
+                                     P.qkv_l, P.qkv_r, s));
+        SSD_TRY(prepare_weight_split(m->ctx, L.wo, 0, 0, 0, 0, P.o_h, P.o_l, P.o_r, s));
+        SSD_TRY(prepare_weight_split(m->ctx, L.wg, 1, 64, 0, 0, P.gu_h, P.gu_l, P.gu_r, s));
+        SSD_TRY(prepare_weight_split(m->ctx, L.wu, 1, 64, 1, 0, P.gu_h, P.gu_l, P.gu_r, s));
+        SSD_TRY(prepare_weight_split(m->ctx, L.wd, 0, 0, 0, 0, P.d_h, P.d_l, P.d_r, s));
+    }
+    return SSD_OK;
+}
+
+extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int32_t* next_token) {
+    SSD_REQ(m && tokens && next_token, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_TRY(check_weights(m));
+    const auto& c = m->cfg;
+    SSD_REQ(tp_size(m) == 1, SSD_ERR_STATE, "batch prefill runs at tp_size 1");
+    SSD_REQ(n > 0 && n % 128 == 0, SSD_ERR_SHAPE, "prefill of %d tokens: a multiple of 128", n);
+    const int E = c.n_embd, F = m->ff_local, NQ = m->q_rows + 2 * m->kv_rows;
+    SSD_REQ(E % 128 == 0 && F % 128 == 0 && NQ % 128 == 0 && m->q_rows == E, SSD_ERR_SHAPE,
+            "prefill needs n_embd, n_ff and the QKV rows in multiples of 128");
+    for (int i = 0; i < n; i++)
+        SSD_REQ(tokens[i] >= 0 && tokens[i] < c.vocab, SSD_ERR_ARG, "token %d outside vocab",
+                tokens[i]);
+    cudaStream_t s = m->ctx->stream;
+    int pos0 = 0;
+    SSD_CK(cudaMemcpy(&pos0, m->pos, 4, cudaMemcpyDeviceToHost));
+    SSD_REQ(pos0 + n <= c.kv_capacity, SSD_ERR_SHAPE, "positions [%d, %d) exceed capacity %d", pos0,
+            pos0 + n, c.kv_capacity);
+    SSD_TRY(prepare_prefill_weights(m, s));
+
+    // work buffers
+    const size_t KM = (size_t)(F > E ? F : E);
+    const size_t pf = (size_t)n * attn_partial_floats(m->nq_local, pos0 + n, c.head_dim);
+    auto pad = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t bytes = pad((size_t)n * E * 4) + 2 * pad((size_t)n * KM * 2) +
+                         pad((size_t)n * NQ * 4) + pad((size_t)n * m->q_rows * 4) +
+                         2 * pad((size_t)n * m->kv_rows * 4) + pad((size_t)n * m->q_rows * 4) +
+                         pad((size_t)n * F * 4) + pad(pf * 4) + pad((size_t)n * 4);
+    if (bytes > m->pf_buf_bytes) {
+        if (m->pf_buf) {
+            SSD_CK(cudaStreamSynchronize(s));
+            cudaFree(m->pf_buf);
+        }
+        m->pf_buf = nullptr;
+        m->pf_buf_bytes = 0;
+        if (cudaMalloc(&m->pf_buf, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            m->pf_buf = nullptr;
+            set_error("prefill buffers (%zu bytes) do not fit", bytes);
+            return SSD_ERR_NOMEM;
+        }
+        m->pf_buf_bytes = bytes;
+    }
+    char* p = (char*)m->pf_buf;
+    auto take = [&](size_t b) {
+        char* r = p;
+        p += pad(b);
+        return r;
+    };
+    float* H = (float*)take((size_t)n * E * 4);
+    __half* Ah = (__half*)take((size_t)n * KM * 2);
+    __half* Al = (__half*)take((size_t)n * KM * 2);
+    float* QKV = (float*)take((size_t)n * NQ * 4);
+    float* Q = (float*)take((size_t)n * m->q_rows * 4);
+    float* Kr = (float*)take((size_t)n * m->kv_rows * 4);
+    float* Vr = (float*)take((size_t)n * m->kv_rows * 4);
+    float* AO = (float*)take((size_t)n * m->q_rows * 4);
+    float* ACT = (float*)take((size_t)n * F * 4);
+    float* PART = (float*)take(pf * 4);
+    int32_t* TOK = (int32_t*)take((size_t)n * 4);
+
+    SSD_CK(cudaMemcpyAsync(TOK, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    SSD_TRY(launch_embed_rows(m->tok_embd, TOK, n, H, s));
+    GemmOperands op{Ah, Al, nullptr, nullptr};
+    for (int l = 0; l < c.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        const PfLayer& P = m->pf[l];
+        // attn_in = rms_norm(h) (transformer.rs:323-326); q, k, v = W attn_in
+        SSD_TRY(prepare_act_split(H, n, E, L.attn_norm, c.eps, 0, Ah, Al, s, false));
+        GemmArgs g = {};
+        g.M = n;
+        g.K = E;
+        g.N = NQ;
+        g.C = QKV;
+        g.ldc = NQ;
+        g.rscale = P.qkv_r;
+        g.epi = GEMM_STORE;
+        op.w_hi = P.qkv_h;
+        op.w_lo = P.qkv_l;
+        SSD_TRY(launch_gemm(m->ctx, op, g, s, false));
+        k_prefill_rope<<<n, 256, 0, s>>>(QKV, m->q_rows, m->kv_rows, c.head_dim, c.theta, pos0, Q,
+                                         Kr, Vr);
+        SSD_CK_LAUNCH();
+        // the tokens' K / V rows into the INT8 cache, then causal attention over it
+        SSD_TRY(launch_kv_append(L.kv, Kr, Vr, pos0, nullptr, n, s, false));
+        AttnArgs at = {};
+        at.k = L.kv->k;
+        at.v = L.kv->v;
+        at.ks = L.kv->k_scale;
+        at.vs = L.kv->v_scale;
+        at.kv_dim = L.kv->kv_dim;
+        at.head_dim = c.head_dim;
+        at.group = c.n_head / c.n_head_kv;
+        at.kv_head0 = 0;
+        at.n_kv_local = m->nkv_local;
+        at.q = Q;
+        at.out = AO;
+        at.partial = PART;
+        at.max_seq = pos0 + n;
+        at.n_q = n;
+        at.q_stride = m->q_rows;
+        at.out_stride = m->q_rows;
+        at.seq0 = pos0;
+        SSD_TRY(launch_attention(at, s, false));
+        // h += Wo attn (transformer.rs:350-352)
+        SSD_TRY(prepare_act_split(AO, n, m->q_rows, nullptr, 0.0f, 0, Ah, Al, s, false));
+        g.K = m->q_rows;
+        g.N = E;
+        g.C = H;
+        g.ldc = E;
+        g.base = H;
+        g.ldb = E;
+        g.rscale = P.o_r;
+        g.epi = GEMM_RESID;
+        op.w_hi = P.o_h;
+        op.w_lo = P.o_l;
+        SSD_TRY(launch_gemm(m->ctx, op, g, s, false));
+        // ffn_in = h * inv_rms * w (fused_post_attn_norm, compute.rs:536-555); SwiGLU
+        SSD_TRY(prepare_act_split(H, n, E, L.ffn_norm, c.eps, 1, Ah, Al, s, false));
+        g.K = E;
+        g.N = 2 * F;
+        g.C = ACT;
+        g.ldc = F;
+        g.base = nullptr;
+        g.rscale = P.gu_r;
+        g.epi = GEMM_SWIGLU;
+        op.w_hi = P.gu_h;
+        op.w_lo = P.gu_l;
+        SSD_TRY(launch_gemm(m->ctx, op, g, s, false));
+        // h += down(act) (feed_forward.rs:40-43, transformer.rs:392)
+        SSD_TRY(prepare_act_split(ACT, n, F, nullptr, 0.0f, 0, Ah, Al, s, false));
+        g.K = F;
+        g.N = E;
+        g.C = H;
+        g.ldc = E;
+        g.base = H;
+        g.ldb = E;
+        g.rscale = P.d_r;
+        g.epi = GEMM_RESID;
+        op.w_hi = P.d_h;
+        op.w_lo = P.d_l;
+        SSD_TRY(launch_gemm(m->ctx, op, g, s, false));
+    }
+    // the last token's hidden state is the decode state; logits, greedy argmax, position
+    SSD_CK(cudaMemcpyAsync(m->h_a, H + (size_t)(n - 1) * E, (size_t)E * 4, cudaMemcpyDeviceToDevice,
+                           s));
+    const int last = pos0 + n - 1;
+    m->pinned[2] = last;
+    SSD_CK(cudaMemcpyAsync(m->pos, &m->pinned[2], 4, cudaMemcpyHostToDevice, s));
+    MvArgs a = mv_plain(m->output, m->h_a, m->logits);
+    a.norm_w = m->out_norm;
+    a.eps = 1e-5f;  // compute.rs:566
+    a.norm_order = 1;
+    a.argmax_key = m->key;
+    a.index_offset = m->vocab0;
+    SSD_TRY(launch_matvec(m->ctx, c.out_type, EPI_ARGMAX, a, s, false));
+    SSD_TRY(launch_finalize(m->key, m->token, m->pos, nullptr, 0, s, false));
+    SSD_CK(cudaMemcpyAsync(&m->pinned[1], m->token, 4, cudaMemcpyDeviceToHost, s));
+    SSD_CK(cudaStreamSynchronize(s));
+    *next_token = m->pinned[1];
+    return SSD_OK;
+}
+

@@ -217,14 +217,17 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
     __shared__ float fac[ATT_NW][G];
     __shared__ float qbias[G];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
+    const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y, qi = blockIdx.z;
     const int g_kv = a.kv_head0 + gl;
     pdl_wait();
     // positions [0, seq); never beyond the cache (max_seq is its capacity on the
-    // graph path), so a position past the end reads nothing out of bounds
-    const int seq = min(a.pos_dev ? (*a.pos_dev + 1) : a.seq_len, a.max_seq);
+    // graph path), so a position past the end reads nothing out of bounds. A batch of
+    // causal queries (prefill): query qi sees positions [0, seq0 + qi].
+    const int seq = min(a.n_q > 1 ? a.seq0 + qi + 1 : (a.pos_dev ? (*a.pos_dev + 1) : a.seq_len),
+                        a.max_seq);
     const int p0 = chunk * ATT_P;
-    float* part = a.partial + ((size_t)(gl * G) * nchunks + chunk) * (HD + 2);
+    const size_t qpart = (size_t)a.n_kv_local * G * nchunks * (HD + 2);
+    float* part = a.partial + qpart * qi + ((size_t)(gl * G) * nchunks + chunk) * (HD + 2);
     const size_t head_stride = (size_t)nchunks * (HD + 2);
     if (p0 >= seq) {
         if (tid < G) {
@@ -236,7 +239,8 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
     // q of the group: all float4 loads issued at once; each HD/4 consecutive float4 are
     // one head, so sub-groups of HD/4 lanes reduce that head's sum for the decode bias
     const int p = p0 + 32 * warp + lane;
-    const float4* qg4 = reinterpret_cast<const float4*>(a.q + (size_t)gl * G * HD);
+    const float4* qg4 =
+        reinterpret_cast<const float4*>(a.q + (size_t)qi * a.q_stride + (size_t)gl * G * HD);
     constexpr int QV = G * HD / 4 / 128 > 0 ? G * HD / 4 / 128 : 1;  // float4 per thread
     float4 qv[QV];
 #pragma unroll
@@ -397,9 +401,10 @@ __global__ void __launch_bounds__(HD) k_attn_combine(const AttnArgs a, int nchun
     __shared__ float fac[1024];
     __shared__ float red[HD / 32];
     __shared__ float lsum[HD / 32];
-    const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5, qi = blockIdx.y;
     pdl_wait();
-    const float* part = a.partial + (size_t)h * nchunks * (HD + 2);
+    const float* part = a.partial + (size_t)qi * gridDim.x * nchunks * (HD + 2) +
+                        (size_t)h * nchunks * (HD + 2);
     float m = -INFINITY;
     for (int c = d; c < nchunks; c += HD) m = fmaxf(m, part[(size_t)c * (HD + 2)]);
     m = warp_max(m);
@@ -442,7 +447,8 @@ __global__ void __launch_bounds__(HD) k_attn_combine(const AttnArgs a, int nchun
         acc = f != 0.0f ? fmaf(v, f, acc) : acc;
     }
     // output_acc[d] * (1 / running_sum)  (flash_attention.rs:126-133)
-    a.out[(size_t)h * HD + d] = L > 0.0f ? __fmul_rn(acc, __fdiv_rn(1.0f, L)) : 0.0f;
+    a.out[(size_t)qi * a.out_stride + (size_t)h * HD + d] =
+        L > 0.0f ? __fmul_rn(acc, __fdiv_rn(1.0f, L)) : 0.0f;
 }
 
 size_t attn_partial_floats(int n_heads, int max_seq, int head_dim) {
@@ -453,8 +459,11 @@ size_t attn_partial_floats(int n_heads, int max_seq, int head_dim) {
 template <int HD, int G>
 static int launch_attn_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const int nchunks = (a.max_seq + ATT_P - 1) / ATT_P;
-    SSD_CK(launch_pdl(k_attn_partial<HD, G>, dim3(a.n_kv_local, nchunks), dim3(128), 0, s, pdl, a));
-    SSD_CK(launch_pdl(k_attn_combine<HD>, dim3(a.n_kv_local * G), dim3(HD), 0, s, pdl, a, nchunks));
+    const int nq = a.n_q > 1 ? a.n_q : 1;
+    SSD_CK(launch_pdl(k_attn_partial<HD, G>, dim3(a.n_kv_local, nchunks, nq), dim3(128), 0, s, pdl,
+                      a));
+    SSD_CK(launch_pdl(k_attn_combine<HD>, dim3(a.n_kv_local * G, nq), dim3(HD), 0, s, pdl, a,
+                      nchunks));
     return SSD_OK;
 }
 
@@ -490,7 +499,8 @@ int launch_kv_append(const ssd_kv_cache* kv, const float* k, const float* v, int
 __global__ void __launch_bounds__(256) k_embed(const ssd_weight e, const int32_t* token,
                                                float* hidden) {
     pdl_wait();
-    int t = *token;
+    int t = token[blockIdx.x];  // one row per block (one block on the decode path)
+    hidden += (size_t)blockIdx.x * e.cols;
     t = t < 0 ? 0 : (t >= e.rows ? e.rows - 1 : t);  // out-of-range ids clamp (no OOB read)
     const int n = e.cols;
     for (int i = threadIdx.x; i < n; i += 256) {
@@ -527,6 +537,14 @@ int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden,
     SSD_REQ(emb->type == SSD_TYPE_F32 || emb->type == SSD_TYPE_Q4_0 || emb->type == SSD_TYPE_Q8_0,
             SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0)", emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(1), dim3(256), 0, s, pdl, *emb, token_dev, hidden));
+    return SSD_OK;
+}
+
+int launch_embed_rows(const ssd_weight* emb, const int32_t* tokens_dev, int n, float* hidden,
+                      cudaStream_t s) {
+    SSD_REQ(emb->type == SSD_TYPE_F32 || emb->type == SSD_TYPE_Q4_0 || emb->type == SSD_TYPE_Q8_0,
+            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0)", emb->type);
+    SSD_CK(launch_pdl(k_embed, dim3(n), dim3(256), 0, s, false, *emb, tokens_dev, hidden));
     return SSD_OK;
 }
 

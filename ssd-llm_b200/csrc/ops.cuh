@@ -24,6 +24,12 @@ struct AttnArgs {
     int seq_len;
     const int* pos_dev;
     int max_seq;  // grid is sized for max_seq positions (graph-stable)
+    // Batch of causal queries (prefill): when n_q > 1, query i (q + i * q_stride, out +
+    // i * out_stride) attends to positions [0, seq0 + i], its partials at
+    // partial + i * attn_partial_floats(heads, max_seq, head_dim).
+    int n_q;
+    int q_stride, out_stride;
+    int seq0;
 };
 size_t attn_partial_floats(int n_heads, int max_seq, int head_dim);
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
@@ -32,6 +38,9 @@ int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 // key_dev is non-null) into hidden.
 int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
                  bool pdl);
+// Embedding rows of n tokens (tokens_dev[n]) into hidden [n][n_embd].
+int launch_embed_rows(const ssd_weight* emb, const int32_t* tokens_dev, int n, float* hidden,
+                      cudaStream_t s);
 // token = low 32 bits of *key; *key = 0; *pos += 1; *epoch += epoch_inc (if epoch).
 int launch_finalize(unsigned long long* key, int32_t* token, int* pos, unsigned long long* epoch,
                     int epoch_inc, cudaStream_t s, bool pdl);

@@ -128,6 +128,7 @@ _SIGS = {
     "ssd_model_kv": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
     "ssd_model_layer_step": ([_vp, ctypes.c_int], ctypes.c_int),
     "ssd_model_p2p_handle": ([_vp, ctypes.c_char_p], ctypes.c_int),
+    "ssd_model_prefill": ([_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "ssd_model_p2p_open": ([_vp, ctypes.c_char_p], ctypes.c_int),
     "ssd_model_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
@@ -415,6 +416,14 @@ class Model:
     def decode_token(self, token: int, use_graph: bool = True) -> int:
         out = ctypes.c_int32()
         check(lib().ssd_model_decode_token(self.h, token, ctypes.byref(out), int(use_graph)))
+        return out.value
+
+    def prefill(self, tokens) -> int:
+        """Batch prefill of the prompt tokens at the current position (batch_prefill_lora
+        + the last token's greedy argmax); returns the next token."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = ctypes.c_int32()
+        check(lib().ssd_model_prefill(self.h, t.ctypes.data, t.size, ctypes.byref(out)))
         return out.value
 
     def state_ptrs(self):
