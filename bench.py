@@ -434,6 +434,70 @@ def measured_tensor_peak():
     return 1590.0, "fallback 1.59 PFLOP/s"
 
 
+def case_mv_shapes(ctx, torch, ssdllm, peak, reps=10):
+    """Every decode-step matvec of the Llama-70B shape (QKV + RoPE, o_proj + residual,
+    gate/up + SwiGLU, down + residual) at the row/column shards of TP = 1, 2, 4, 8, timed
+    with each of the library's two matvec kernels: the integer tensor-core kernel
+    (default where it covers the shape) and the FMA kernel (SSD_MV_IMPL=fma). Weights
+    rotate over copies totalling more than 2x L2; launches are graph-captured with PDL."""
+    import os
+    E, F, HQ, HKV = 8192, 28672, 8192, 1024
+    gen = torch.Generator("cuda").manual_seed(9)
+    out = {}
+    tid = [2000]
+
+    def synth(rows, cols):
+        tid[0] += 1
+        return ssdllm.Weight.synth(ctx, Q4_0, 0, tid[0], 0.02, cols, 0, rows, 0, cols)
+
+    for tp in (1, 2, 4, 8):
+        hq, ff, ecol, fcol = HQ // tp, F // tp, E // tp, F // tp
+        kinds = {
+            "qkv": (hq + 2 * HKV) * E, "o_proj": E * ecol, "gate_up": 2 * ff * E, "down": E * fcol,
+        }
+        for kind, nw in kinds.items():
+            wbytes = nw * Q40_BYTES
+            copies = min(16, max(2, -(-int(2.2 * L2_BYTES) // int(wbytes))))
+            x = torch.randn(E if kind in ("qkv", "gate_up") else (ecol if kind == "o_proj" else fcol),
+                            device="cuda", generator=gen)
+            nw_ = 1 + 0.1 * torch.randn(E, device="cuda", generator=gen)
+            if kind == "qkv":
+                ws = [(synth(hq, E), synth(HKV, E), synth(HKV, E)) for _ in range(copies)]
+                q, k, v = (torch.zeros(n, device="cuda") for n in (hq, HKV, HKV))
+                mk = lambda w: (lambda: ssdllm.fused_qkv_rope(ctx, *w, x, nw_, 1e-5, 128, 77, 5e5,
+                                                              q, k, v))
+                alg = wbytes + E * 4 + (hq + 2 * HKV) * 4
+            elif kind == "gate_up":
+                ws = [(synth(ff, E), synth(ff, E)) for _ in range(copies)]
+                act = torch.zeros(ff, device="cuda")
+                mk = lambda w: (lambda: ssdllm.fused_swiglu(ctx, w[0], w[1], x, nw_, 1e-5, act))
+                alg = wbytes + E * 4 + ff * 4
+            else:
+                cols = ecol if kind == "o_proj" else fcol
+                ws = [(synth(E, cols),) for _ in range(copies)]
+                base = torch.randn(E, device="cuda", generator=gen)
+                y = torch.zeros(E, device="cuda")
+                mk = lambda w: (lambda: ssdllm.matvec_residual(ctx, w[0], x, base, y))
+                alg = wbytes + cols * 4 + 2 * E * 4
+            res = {}
+            ctx.set_pdl(True)
+            for impl in ("tc", "fma"):
+                if impl == "fma":
+                    os.environ["SSD_MV_IMPL"] = "fma"
+                else:
+                    os.environ.pop("SSD_MV_IMPL", None)
+                n = max(copies, 32 // copies * copies)
+                us = _graph_time(torch, [mk(ws[i % copies]) for i in range(n)], reps)
+                res[impl] = {"us": round(us, 3), "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
+            os.environ.pop("SSD_MV_IMPL", None)
+            ctx.set_pdl(False)
+            for w in ws:
+                for t in w:
+                    t.free()
+            out[f"tp{tp}_{kind}"] = {"bytes": int(alg), **res}
+    return out
+
+
 CASES = {
     "q4_0_4096x4096": lambda c, t, s, p: case_matvec(c, t, s, p, Q4_0, 4096, 4096),
     "q8_0_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 8, 11008, 4096),
@@ -445,7 +509,10 @@ CASES = {
     "layer_7b_q4_0": case_layer_7b,
     "layer_70b_q4_0": case_layer_70b,
     "prefill_l3_8b_q4_k": case_prefill_l3_8b,
+    "mv_shapes_70b": case_mv_shapes,
 }
+# measured on every default run (mv_shapes_70b, a kernel-selection study, only by --case)
+DEFAULT_CASES = [n for n in CASES if n != "mv_shapes_70b"]
 
 
 def run_cases(names, peak):
@@ -461,7 +528,7 @@ def run_case_cli(args):
     import torch
     torch.cuda.set_device(0)
     peak, src = measured_peaks()
-    names = list(CASES) if args.case == "all" else args.case.split(",")
+    names = DEFAULT_CASES if args.case == "all" else args.case.split(",")
     res = run_cases(names, peak)
     print(json.dumps({"cases": res, "peak_gbs": peak, "peak_source": src}), flush=True)
     return 0
@@ -576,7 +643,7 @@ def run_cuda(args):
             tt = torch.tensor([dom_us], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             dom_us = float(tt[0])
-        k0 = run_cases(list(CASES), peak) if rank == 0 and not args.no_kernels else None
+        k0 = run_cases(DEFAULT_CASES, peak) if rank == 0 and not args.no_kernels else None
         clocks = clk.summary() if rank == 0 else None
     finally:
         model.free()  # releases the graph holding NCCL calls before the process group

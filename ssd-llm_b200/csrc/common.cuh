@@ -243,6 +243,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// 3-D tiled TMA load (no multicast) of box {c0, c1, c2} into shared memory.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -290,6 +300,16 @@ int check_ctx(ssd_ctx* ctx);
 // u ^ (c & 7) of its row, so the 8 units a lane reads are bank-conflict free across a
 // quarter warp. n must be a multiple of 32 and ptr 16-byte aligned.
 int encode_vec_map(CUtensorMap* map, const float* ptr, int n);
+// 2-D byte tensor map over `rows` rows of row_bytes (16-byte multiple, >= 128) at ptr
+// (16-byte aligned): box = 128 bytes x box_rows rows, 128-byte swizzle (16-byte unit u
+// of box row r lands at unit u ^ (r & 7)); out-of-range rows and bytes read as zero.
+int encode_rows_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
+                    uint32_t box_rows);
+// 3-D view of the same rows as 128-byte blocks: box = box_blocks blocks x box_rows rows,
+// landing in shared memory as [block][row][128 B] with the 128-byte swizzle (unit u of
+// shared row r at u ^ (r & 7) when box_rows is 8). row_bytes must be a multiple of 128.
+int encode_blocks_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
+                      uint32_t box_rows, uint32_t box_blocks);
 constexpr int kVecBoxRows = 32;
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out);
 int ensure_scratch(ssd_ctx* ctx, size_t bytes);

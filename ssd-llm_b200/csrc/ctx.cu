@@ -21,7 +21,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-int encode_vec_map(CUtensorMap* map, const float* ptr, int n) {
+static int tensor_map_fn(EncodeTiledFn* out) {
     static EncodeTiledFn fn = nullptr;
     if (!fn) {
         void* f = nullptr;
@@ -31,6 +31,13 @@ int encode_vec_map(CUtensorMap* map, const float* ptr, int n) {
                 "cuTensorMapEncodeTiled unavailable");
         fn = (EncodeTiledFn)f;
     }
+    *out = fn;
+    return SSD_OK;
+}
+
+int encode_vec_map(CUtensorMap* map, const float* ptr, int n) {
+    EncodeTiledFn fn;
+    SSD_TRY(tensor_map_fn(&fn));
     SSD_REQ(ptr && ((uintptr_t)ptr & 15u) == 0 && n > 0 && n % 32 == 0, SSD_ERR_ARG,
             "tensor map: vector must be 16-byte aligned with a multiple of 32 floats");
     cuuint64_t dims[2] = {32, (cuuint64_t)(n / 32)};
@@ -40,6 +47,46 @@ int encode_vec_map(CUtensorMap* map, const float* ptr, int n) {
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)ptr, dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    SSD_REQ(r == CUDA_SUCCESS, SSD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSD_OK;
+}
+
+int encode_rows_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
+                    uint32_t box_rows) {
+    EncodeTiledFn fn;
+    SSD_TRY(tensor_map_fn(&fn));
+    SSD_REQ(ptr && ((uintptr_t)ptr & 15u) == 0 && row_bytes % 16 == 0 && row_bytes >= 128 &&
+                rows >= box_rows && box_rows >= 1 && box_rows <= 256,
+            SSD_ERR_ARG, "tensor map: rows of %llu bytes x %llu not tileable",
+            (unsigned long long)row_bytes, (unsigned long long)rows);
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    SSD_REQ(r == CUDA_SUCCESS, SSD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSD_OK;
+}
+
+int encode_blocks_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
+                      uint32_t box_rows, uint32_t box_blocks) {
+    EncodeTiledFn fn;
+    SSD_TRY(tensor_map_fn(&fn));
+    SSD_REQ(ptr && ((uintptr_t)ptr & 15u) == 0 && row_bytes % 128 == 0 && row_bytes >= 128 &&
+                rows >= box_rows && box_rows >= 1 && box_rows <= 256 && box_blocks >= 1 &&
+                box_blocks <= 256,
+            SSD_ERR_ARG, "tensor map: rows of %llu bytes x %llu not tileable in 128-byte blocks",
+            (unsigned long long)row_bytes, (unsigned long long)rows);
+    // dims: byte within a 128-byte block, row, block; the box lands as [block][row][128 B]
+    cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(row_bytes / 128)};
+    cuuint64_t strides[2] = {(cuuint64_t)row_bytes, 128};
+    cuuint32_t box[3] = {128, box_rows, box_blocks};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     SSD_REQ(r == CUDA_SUCCESS, SSD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return SSD_OK;
 }

@@ -27,9 +27,9 @@
 //    Q8_0 read as unsigned q+128, and scale * sum q x - min * X for Q4_K.
 //  * Epilogues fuse what follows the matvec in the decode step: residual add,
 //    SwiGLU, RoPE on Q/K, or argmax (LAST index on ties, sampler.rs:572-578).
-#include <mutex>
+#include <cstring>
 
-#include "matvec.cuh"
+#include "matvec_dev.cuh"
 
 namespace ssd {
 
@@ -63,29 +63,6 @@ struct Chunk<SSD_TYPE_Q4_K> {
     uint4 m;
 };
 
-__device__ __forceinline__ void map_row(const MvArgs& a, int R, int v, int& seg, int& lr) {
-    if (a.map == MAP_PLAIN) {
-        seg = 0;
-        lr = v;
-    } else if (a.map == MAP_QKV) {
-        if (v < a.seg_rows[0]) {
-            seg = 0;
-            lr = v;
-        } else if (v < a.seg_rows[0] + a.seg_rows[1]) {
-            seg = 1;
-            lr = v - a.seg_rows[0];
-        } else {
-            seg = 2;
-            lr = v - a.seg_rows[0] - a.seg_rows[1];
-        }
-    } else {  // MAP_SWIGLU: rows R*g .. R*g+R/2-1 are gate rows (R/2)g.., the rest up rows
-        const int h = R >> 1;
-        const int g = v / R, j = v % R;
-        seg = j >= h;
-        lr = h * g + (j - (j >= h ? h : 0));
-    }
-}
-
 // Byte pointers of one row of the library layout (see ssd_weight in common.cuh).
 template <int FMT>
 __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uint8_t*& qs,
@@ -110,20 +87,6 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
 // ---- cp.async staging of weights. Each lane copies its own chunks of a stage into
 // its own 16-byte slots of the warp's ring and later reads them back, so completion
 // only needs the thread's own cp.async.wait_group (no cross-lane synchronisation).
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Ring slot sizes per (row, chunk): payload QB bytes, metadata MB bytes (Q4_0 / Q8_0:
 // the aligned 4-byte word holding the chunk's f16 d; Q4_K: the super-block's 16 bytes).
 template <int FMT>
@@ -294,18 +257,6 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const f
     }
 }
 
-__device__ __forceinline__ void rope_apply(float& x0, float& x1, float2 cs) {
-    const float a0 = x0, a1 = x1;
-    x0 = __fsub_rn(__fmul_rn(a0, cs.x), __fmul_rn(a1, cs.y));
-    x1 = __fadd_rn(__fmul_rn(a0, cs.y), __fmul_rn(a1, cs.x));
-}
-
-__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
-    uint32_t u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | idx;
-}
-
 // Shared-memory plan of one CTA (offsets from a 1024-byte aligned base): the staged
 // x'' (TMA destination, swizzled), the per-chunk bias sums, reduction scratch, the
 // TMA barrier, and one weight ring of n_stages stages per warp: 4 for the 16-warp CTAs
@@ -317,7 +268,6 @@ struct SmemPlan {
     int nc, xrows;  // chunks, staged rows (multiple of kVecBoxRows)
     size_t xs, csum, red, bar, rope, ring, total;
 };
-constexpr int kMaxRopePairs = 256;  // head_dim <= 512
 __host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_warp) {
     SmemPlan p;
     p.nc = cols >> 5;
@@ -360,7 +310,6 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     constexpr int QB = Slot<FMT>::QB, MB = Slot<FMT>::MB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    const bool has_add = a.x_add != nullptr || a.ar_in_n > 0, has_norm = a.norm_w != nullptr;
     const SmemPlan P = smem_plan(a.cols, NW, kStages * SB);
     float4* xs4 = reinterpret_cast<float4*>(base + P.xs);
     float* csum = reinterpret_cast<float*>(base + P.csum);
@@ -457,131 +406,29 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
 #pragma unroll
     for (int k = 0; k < kStages - 1; k++) issue();
     __syncthreads();  // barrier initialised
-    pdl_wait();
-
     float2* rope_tab = reinterpret_cast<float2*>(base + P.rope);
-    if constexpr (EPI == EPI_QKV_ROPE) {  // (cos, sin) of every pair at this position
-        const int pos = a.position_dev ? *a.position_dev : a.position;
-        for (int i = tid; i < (a.head_dim >> 1); i += NW * 32)
-            rope_tab[i] = rope_cs(i, a.head_dim, a.theta, pos);
-    }
-    if (tid == 0) {
-        const int nbox = P.xrows / kVecBoxRows;
-        mbar_expect_tx(bar, (uint32_t)P.xrows * 128u);
-        for (int b = 0; b < nbox; b++)
-            tma_load_2d(base + P.xs + (size_t)b * kVecBoxRows * 128, &tm_x, 0, b * kVecBoxRows, bar);
-    }
-    if (a.ar_in_n > 0) {  // wait for every rank's partial of this call (bounded)
-        // fail fast: once any wait of this context has timed out, later ones do not wait
-        if (warp == 0 && lane < a.ar_in_n && *(volatile int*)a.status == SSD_OK) {
-            const unsigned long long ep = *a.ar_epoch + (unsigned long long)a.ar_call + 1ull;
-            bool done = false;
-            for (uint32_t it = 0; it < (1u << 21) && !done; it++) {
-                unsigned long long f;
-                asm volatile("ld.acquire.sys.global.u64 %0, [%1];"
-                             : "=l"(f)
-                             : "l"(a.ar_in_flag + lane)
-                             : "memory");
-                done = f >= ep;
-                if (!done) __nanosleep(100);
-            }
-            if (!done) atomicExch(a.status, SSD_ERR_TIMEOUT);  // data below is then stale
+    // finish: chunk bias sum (8 consecutive threads hold one chunk's 8 units) and the
+    // per-position power-of-two pre-scale, in place
+    auto finish = [&](int i, int c, int ph, float4 v, unsigned gmask) {
+        float t = (v.x + v.y) + (v.z + v.w);
+        t += __shfl_xor_sync(gmask, t, 1);
+        t += __shfl_xor_sync(gmask, t, 2);
+        t += __shfl_xor_sync(gmask, t, 4);
+        if ((i & 7) == 0) {
+            const float X = __fmul_rn(t, 1.0f / kUnscale);
+            csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X : (FMT == SSD_TYPE_Q8_0 ? -128.0f * X : X);
         }
-        __syncthreads();
-    }
-    const bool ok = mbar_wait(bar, 0, a.status);
-    if (__syncthreads_or(!ok)) {  // timed out: status recorded, nothing computed
+        const int k0 = (FMT == SSD_TYPE_Q8_0) ? 0 : 4 * (i & 1);  // word position of v.x
+        v.x = __fmul_rn(v.x, pos_scale<FMT>(k0 + 0));
+        v.y = __fmul_rn(v.y, pos_scale<FMT>(k0 + 1));
+        v.z = __fmul_rn(v.z, pos_scale<FMT>(k0 + 2));
+        v.w = __fmul_rn(v.w, pos_scale<FMT>(k0 + 3));
+        xs4[ph] = v;
+    };
+    if (!mv_prologue<NW * 32, EPI>(a, &tm_x, base + P.xs, nc, P.xrows, red, bar, rope_tab, finish)) {
         cp_wait<0>();
         return;
     }
-
-    // ---- prologue in shared memory: x_eff = x (+ x_add) [written back by CTA 0];
-    // optional RMSNorm; chunk bias sums; per-position power-of-two pre-scale.
-    const int nunits = nc * 8;  // 16-byte units
-    const unsigned gmask = 0xFFu << (lane & 24);
-    float inv = 1.0f;
-    if (has_add || has_norm) {
-        const bool wb = a.x_writeback != nullptr && blockIdx.x == 0;
-        float ss = 0.0f;
-        for (int i = tid; i < nunits; i += NW * 32) {
-            const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
-            float4 v = xs4[ph];
-            if (has_add) {  // hidden[i] += attn_output[i] (src/metal/compute.rs:547-549)
-                float4 r;
-                if (a.ar_in_n > 0) {  // the ranks' partials, summed in rank order (L2 reads)
-                    r = __ldcg(reinterpret_cast<const float4*>(a.ar_in) + i);
-                    for (int p = 1; p < a.ar_in_n; p++) {
-                        const float4 t =
-                            __ldcg(reinterpret_cast<const float4*>(a.ar_in + (size_t)p * a.cols) + i);
-                        r.x = __fadd_rn(r.x, t.x);
-                        r.y = __fadd_rn(r.y, t.y);
-                        r.z = __fadd_rn(r.z, t.z);
-                        r.w = __fadd_rn(r.w, t.w);
-                    }
-                } else {
-                    r = __ldg(reinterpret_cast<const float4*>(a.x_add) + i);
-                }
-                v.x = __fadd_rn(v.x, r.x);
-                v.y = __fadd_rn(v.y, r.y);
-                v.z = __fadd_rn(v.z, r.z);
-                v.w = __fadd_rn(v.w, r.w);
-                xs4[ph] = v;
-                if (wb) reinterpret_cast<float4*>(a.x_writeback)[i] = v;
-            }
-            ss = fmaf(v.x, v.x, ss);
-            ss = fmaf(v.y, v.y, ss);
-            ss = fmaf(v.z, v.z, ss);
-            ss = fmaf(v.w, v.w, ss);
-        }
-        if (has_norm) {
-            ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
-            __syncthreads();
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < NW; w++) tot += red[w];
-            // inv_rms = 1 / sqrt(sum_sq / n + eps)   (src/metal/compute.rs:583-584)
-            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.cols), a.eps)));
-        }
-    }
-    {
-        const float4* nw4 = reinterpret_cast<const float4*>(a.norm_w);
-        for (int i = tid; i < nunits; i += NW * 32) {
-            const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
-            float4 v = xs4[ph];
-            if (has_norm) {
-                const float4 w = __ldg(nw4 + i);
-                if (a.norm_order == 0) {  // x * (inv_rms * w)
-                    v.x = __fmul_rn(v.x, __fmul_rn(inv, w.x));
-                    v.y = __fmul_rn(v.y, __fmul_rn(inv, w.y));
-                    v.z = __fmul_rn(v.z, __fmul_rn(inv, w.z));
-                    v.w = __fmul_rn(v.w, __fmul_rn(inv, w.w));
-                } else {  // (x * inv_rms) * w
-                    v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
-                    v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
-                    v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
-                    v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
-                }
-            }
-            // chunk sum of x (8 consecutive threads hold one chunk's 8 units)
-            float t = (v.x + v.y) + (v.z + v.w);
-            t += __shfl_xor_sync(gmask, t, 1);
-            t += __shfl_xor_sync(gmask, t, 2);
-            t += __shfl_xor_sync(gmask, t, 4);
-            if ((i & 7) == 0) {
-                const float X = __fmul_rn(t, 1.0f / kUnscale);
-                csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X : (FMT == SSD_TYPE_Q8_0 ? -128.0f * X : X);
-            }
-            const int k0 = (FMT == SSD_TYPE_Q8_0) ? 0 : 4 * (i & 1);  // word position of v.x
-            v.x = __fmul_rn(v.x, pos_scale<FMT>(k0 + 0));
-            v.y = __fmul_rn(v.y, pos_scale<FMT>(k0 + 1));
-            v.z = __fmul_rn(v.z, pos_scale<FMT>(k0 + 2));
-            v.w = __fmul_rn(v.w, pos_scale<FMT>(k0 + 3));
-            xs4[ph] = v;
-        }
-    }
-    __syncthreads();
-    pdl_trigger();
 
     float acc[R];
 #pragma unroll
@@ -745,41 +592,6 @@ static Cfg env_cfg() {
     return c;
 }
 
-// Resident CTAs per SM of one kernel at a given dynamic shared-memory size, cached
-// per (kernel, device, size); sets the shared-memory opt-in attribute on first use.
-template <typename K>
-static int occupancy(ssd_ctx* ctx, K kern, int threads, size_t smem, int* out) {
-    struct Entry {
-        const void* fn;
-        int dev;
-        size_t smem;
-        int blocks;
-    };
-    static Entry cache[512];
-    static int n = 0;
-    static std::mutex mu;
-    std::lock_guard<std::mutex> lk(mu);
-    const void* fn = reinterpret_cast<const void*>(kern);
-    bool attr_set = false;
-    for (int i = 0; i < n; i++) {
-        if (cache[i].fn != fn || cache[i].dev != ctx->device) continue;
-        attr_set = true;
-        if (cache[i].smem == smem) {
-            *out = cache[i].blocks;
-            return SSD_OK;
-        }
-    }
-    if (!attr_set)
-        SSD_CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)ctx->smem_optin));
-    int nb = 0;
-    SSD_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem));
-    SSD_REQ(nb > 0, SSD_ERR_SHAPE, "matvec kernel does not fit on an SM (%zu B smem)", smem);
-    if (n < 512) cache[n++] = Entry{fn, ctx->device, smem, nb};
-    *out = nb;
-    return SSD_OK;
-}
-
 template <int FMT, int EPI, int R, int U, int NW>
 static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     auto kern = k_matvec<FMT, EPI, R, U, NW>;
@@ -884,6 +696,22 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
     SSD_REQ(epi != EPI_QKV_ROPE || (a.y_k && a.y_v), SSD_ERR_ARG, "null K/V output");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.head_dim > 0 && a.head_dim / 2 <= kMaxRopePairs),
             SSD_ERR_SHAPE, "head_dim %d outside (0, %d]", a.head_dim, 2 * kMaxRopePairs);
+    // Kernel choice. The integer tensor-core kernel (matvec_tc.cu) beats this FMA kernel
+    // only on the largest matrices: measured per decode shape of the 70B model (bench.py
+    // --case mv_shapes_70b), it wins on the fused gate/up of >= 28672 virtual rows and
+    // loses elsewhere to its fixed cost per launch (one CTA per SM, x converted to limbs
+    // in every CTA, no overlap with the previous kernel's tail). SSD_MV_IMPL=tc / fma
+    // forces either kernel (tc where it covers the shape); read per call so that one
+    // process can compare them.
+    const char* impl = getenv("SSD_MV_IMPL");
+    const bool force_tc = impl && strcmp(impl, "tc") == 0;
+    const bool force_fma = impl && strcmp(impl, "fma") == 0;
+    const bool want_tc = force_tc || (!force_fma && epi == EPI_SWIGLU && a.rows >= 28672);
+    if (want_tc && (type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 ||
+                    (type == SSD_TYPE_Q4_K && a.cols % 256 == 0))) {
+        const int st = launch_matvec_tc(ctx, type, epi, a, s, pdl);
+        if (st != kTcNotCovered) return st;
+    }
     switch (type) {
         case SSD_TYPE_Q4_0: return launch_fmt<SSD_TYPE_Q4_0>(ctx, epi, a, s, pdl);
         case SSD_TYPE_Q8_0: return launch_fmt<SSD_TYPE_Q8_0>(ctx, epi, a, s, pdl);
