@@ -327,7 +327,7 @@ def case_layer_7b(ctx, torch, ssdllm, peak, n_layers=8, reps=10):
     return {"shape": "llama2-7b layer, Q4_0, INT8 KV 2048", "algorithmic_bytes": alg,
             "us_per_layer": round(us_layer, 3), "gbs": round(alg / us_layer / 1e3, 1),
             "frac_of_peak": round(alg / us_layer / 1e3 / peak, 4),
-            "launches_per_layer": 6, "model_layers_timed": n_layers, "launches_per_step": launches}
+            "launches_per_layer": 5, "model_layers_timed": n_layers, "launches_per_step": launches}
 
 
 def case_swiglu_70b(ctx, torch, ssdllm, peak, reps=10):

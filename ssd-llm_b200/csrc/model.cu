@@ -733,11 +733,11 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
     }
-    // 2. INT8 KV append at the current position
-    SSD_TRY(launch_kv_append(L.kv, m->k, m->v, 0, m->pos, 1, s, true));
-    nl++;
-    // 3. attention over this rank's KV heads
+    // 2-3. INT8 KV append at the current position (fused) and attention over this rank's
+    // KV heads
     AttnArgs at = {};
+    at.k_new = m->k;
+    at.v_new = m->v;
     at.k = L.kv->k;
     at.v = L.kv->v;
     at.ks = L.kv->k_scale;

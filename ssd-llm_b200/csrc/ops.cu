@@ -216,19 +216,63 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
     __shared__ float mlw[ATT_NW][G][2];  // warp max, sum exp
     __shared__ float fac[ATT_NW][G];
     __shared__ float qbias[G];
+    __shared__ float amred[2][ATT_NW];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y, qi = blockIdx.z;
     const int g_kv = a.kv_head0 + gl;
-    pdl_wait();
+    // Decode with the append fused (k_new set): the new K/V row is quantized and written
+    // by the CTAs of its chunk. No kernel before this one writes the cache then, so the
+    // old rows are loaded before griddepcontrol.wait, overlapping the previous kernel; the
+    // position itself was written by the previous step's last kernel, long complete.
+    const bool fused = a.k_new != nullptr;
+    int pnew = -1;
+    if (!fused) pdl_wait();
     // positions [0, seq); never beyond the cache (max_seq is its capacity on the
     // graph path), so a position past the end reads nothing out of bounds. A batch of
     // causal queries (prefill): query qi sees positions [0, seq0 + qi].
-    const int seq = min(a.n_q > 1 ? a.seq0 + qi + 1 : (a.pos_dev ? (*a.pos_dev + 1) : a.seq_len),
-                        a.max_seq);
+    int seq;
+    if (fused) {
+        pnew = *a.pos_dev;
+        seq = min(pnew + 1, a.max_seq);
+    } else {
+        seq = min(a.n_q > 1 ? a.seq0 + qi + 1 : (a.pos_dev ? (*a.pos_dev + 1) : a.seq_len),
+                  a.max_seq);
+    }
     const int p0 = chunk * ATT_P;
     const size_t qpart = (size_t)a.n_kv_local * G * nchunks * (HD + 2);
     float* part = a.partial + qpart * qi + ((size_t)(gl * G) * nchunks + chunk) * (HD + 2);
     const size_t head_stride = (size_t)nchunks * (HD + 2);
+    const int p = p0 + 32 * warp + lane;
+    // this lane's K row and position scales, and its bytes of the warp's 32 V rows: all in
+    // flight at once (the new row, if in this chunk, is loaded once written below)
+    const int pw0 = p0 + 32 * warp;
+    const int npos = max(0, min(32, seq - pw0));
+    uint4 krow[HD / 16];
+    uint32_t vw[32];
+    float ksc = 0.0f, vsc = 0.0f;
+    const int8_t* vbase = a.v + (size_t)g_kv * HD + DPL * lane + (size_t)pw0 * a.kv_dim;
+    if (p0 < seq) {
+        if (p < seq && p != pnew) {
+            const uint4* kr =
+                reinterpret_cast<const uint4*>(a.k + (size_t)p * a.kv_dim + (size_t)g_kv * HD);
+#pragma unroll
+            for (int j = 0; j < HD / 16; j++) krow[j] = __ldg(kr + j);
+            ksc = __ldg(a.ks + p);
+            vsc = __ldg(a.vs + p);
+        }
+#pragma unroll
+        for (int t = 0; t < 32; t++) {
+            vw[t] = 0x80808080u;
+            if (t < npos && pw0 + t != pnew) {
+                const int8_t* vr = vbase + (size_t)t * a.kv_dim;
+                if constexpr (DPL == 4)
+                    vw[t] = __ldg(reinterpret_cast<const uint32_t*>(vr));
+                else
+                    vw[t] = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(vr));
+            }
+        }
+    }
+    if (fused) pdl_wait();
     if (p0 >= seq) {
         if (tid < G) {
             part[tid * head_stride + 0] = -INFINITY;
@@ -238,7 +282,6 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
     }
     // q of the group: all float4 loads issued at once; each HD/4 consecutive float4 are
     // one head, so sub-groups of HD/4 lanes reduce that head's sum for the decode bias
-    const int p = p0 + 32 * warp + lane;
     const float4* qg4 =
         reinterpret_cast<const float4*>(a.q + (size_t)qi * a.q_stride + (size_t)gl * G * HD);
     constexpr int QV = G * HD / 4 / 128 > 0 ? G * HD / 4 / 128 : 1;  // float4 per thread
@@ -246,9 +289,6 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
 #pragma unroll
     for (int j = 0; j < QV; j++)
         if (tid + 128 * j < G * HD / 4) qv[j] = __ldg(qg4 + tid + 128 * j);
-    // this lane's position scales, in flight with the q loads
-    const float ksc = p < seq ? __ldg(a.ks + p) : 0.0f;
-    const float vsc = p < seq ? __ldg(a.vs + p) : 0.0f;
 #pragma unroll
     for (int j = 0; j < QV; j++) {
         const int u = tid + 128 * j;  // float4 index
@@ -267,6 +307,65 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
         if (in && (u % (HD / 4)) == 0)  // -128 * sum_d q[d], scaled by 2^-64
             qbias[u / (HD / 4)] = __fmul_rn(-128.0f, __fmul_rn(t, 1.0f / kAttUnscale));
     }
+    if (fused && pnew >= p0 && pnew < p0 + ATT_P && pnew < a.max_seq) {
+        // ---- the new position is in this chunk: quantize its K and V rows exactly as
+        // k_kv_append (QuantizedVec::quantize, quantized_kv_cache.rs:23-41; the scale spans
+        // every KV head), write this head's bytes (the CTA of local head 0 the scales), and
+        // load them back
+        float amk = 0.0f, amv = 0.0f;
+        for (int i = tid; i < a.kv_dim; i += 128) {
+            amk = fmaxf(amk, fabsf(a.k_new[i]));
+            amv = fmaxf(amv, fabsf(a.v_new[i]));
+        }
+        amk = warp_max(amk);
+        amv = warp_max(amv);
+        if (lane == 0) {
+            amred[0][warp] = amk;
+            amred[1][warp] = amv;
+        }
+        __syncthreads();
+        amk = 0.0f;
+        amv = 0.0f;
+#pragma unroll
+        for (int w = 0; w < ATT_NW; w++) {
+            amk = fmaxf(amk, amred[0][w]);
+            amv = fmaxf(amv, amred[1][w]);
+        }
+        const float sk = amk == 0.0f ? 0.0f : __fdiv_rn(amk, 127.0f);
+        const float sv = amv == 0.0f ? 0.0f : __fdiv_rn(amv, 127.0f);
+        const float ik = amk == 0.0f ? 0.0f : __fdiv_rn(127.0f, amk);
+        const float iv = amv == 0.0f ? 0.0f : __fdiv_rn(127.0f, amv);
+        int8_t* kc = const_cast<int8_t*>(a.k) + (size_t)pnew * a.kv_dim + (size_t)g_kv * HD;
+        int8_t* vc = const_cast<int8_t*>(a.v) + (size_t)pnew * a.kv_dim + (size_t)g_kv * HD;
+        for (int d = tid; d < HD; d += 128) {
+            const float fk = fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(a.k_new[g_kv * HD + d], ik))));
+            const float fv = fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(a.v_new[g_kv * HD + d], iv))));
+            kc[d] = (int8_t)(int)fk;
+            vc[d] = (int8_t)(int)fv;
+        }
+        if (gl == 0 && tid == 0) {
+            const_cast<float*>(a.ks)[pnew] = sk;
+            const_cast<float*>(a.vs)[pnew] = sv;
+        }
+        __syncthreads();  // the row's bytes are visible to the whole CTA
+        if (p == pnew) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kc);
+#pragma unroll
+            for (int j = 0; j < HD / 16; j++) krow[j] = kr[j];
+            ksc = sk;
+            vsc = sv;
+        }
+#pragma unroll
+        for (int t = 0; t < 32; t++) {
+            if (pw0 + t == pnew) {
+                const int8_t* vr = vc + DPL * lane;
+                if constexpr (DPL == 4)
+                    vw[t] = *reinterpret_cast<const uint32_t*>(vr);
+                else
+                    vw[t] = (uint32_t)*reinterpret_cast<const uint16_t*>(vr);
+            }
+        }
+    }
     __syncthreads();
 
     // ---- scores: lane = position
@@ -280,11 +379,6 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
             o[i] = 0.0f;
         }
         if (p < seq) {
-            const uint4* kr =
-                reinterpret_cast<const uint4*>(a.k + (size_t)p * a.kv_dim + (size_t)g_kv * HD);
-            uint4 krow[HD / 16];  // the whole row in flight at once
-#pragma unroll
-            for (int j = 0; j < HD / 16; j++) krow[j] = __ldg(kr + j);
 #pragma unroll
             for (int j = 0; j < HD / 16; j++) {
                 const uint4 kk = krow[j];  // dims 16j .. 16j+15
@@ -332,21 +426,6 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
     for (int i = 0; i < G; i++)
 #pragma unroll
         for (int j = 0; j < DPL; j++) acc[i][j] = 0.0f;
-    const int pw0 = p0 + 32 * warp;
-    const int npos = min(32, seq - pw0);
-    const int8_t* vbase = a.v + (size_t)g_kv * HD + DPL * lane + (size_t)pw0 * a.kv_dim;
-    uint32_t vw[32];  // this lane's bytes of the warp's 32 V rows, all loads in flight
-#pragma unroll
-    for (int t = 0; t < 32; t++) {
-        vw[t] = 0x80808080u;
-        if (t < npos) {
-            const int8_t* vr = vbase + (size_t)t * a.kv_dim;
-            if constexpr (DPL == 4)
-                vw[t] = __ldg(reinterpret_cast<const uint32_t*>(vr));
-            else
-                vw[t] = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(vr));
-        }
-    }
 #pragma unroll
     for (int t = 0; t < 32; t++) {
         if (t >= npos) break;
@@ -480,6 +559,8 @@ static int launch_attn_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     SSD_REQ(a.max_seq > 0, SSD_ERR_SHAPE, "empty attention");
+    SSD_REQ(!a.k_new || (a.v_new && a.pos_dev && a.n_q <= 1), SSD_ERR_ARG,
+            "fused KV append needs v_new, pos_dev and a single query");
     SSD_REQ((a.max_seq + ATT_P - 1) / ATT_P <= 1024, SSD_ERR_SHAPE,
             "attention over %d positions exceeds %d", a.max_seq, 1024 * ATT_P);
     if (a.head_dim == 128) return launch_attn_hd<128>(a, s, pdl);

@@ -30,6 +30,11 @@ struct AttnArgs {
     int n_q;
     int q_stride, out_stride;
     int seq0;
+    // Decode with the KV append fused (n_q 1, pos_dev set): when k_new is non-null the
+    // CTAs of the new position's chunk quantize k_new / v_new (kv_dim floats each) into the
+    // cache at *pos_dev (their own heads' bytes; local head 0 also the scales) first.
+    const float* k_new;
+    const float* v_new;
 };
 size_t attn_partial_floats(int n_heads, int max_seq, int head_dim);
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
