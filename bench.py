@@ -437,8 +437,8 @@ def measured_tensor_peak():
 def case_mv_shapes(ctx, torch, ssdllm, peak, reps=10):
     """Every decode-step matvec of the Llama-70B shape (QKV + RoPE, o_proj + residual,
     gate/up + SwiGLU, down + residual) at the row/column shards of TP = 1, 2, 4, 8, timed
-    with each of the library's two matvec kernels: the integer tensor-core kernel
-    (default where it covers the shape) and the FMA kernel (SSD_MV_IMPL=fma). Weights
+    with each of the library's two matvec kernels: the FMA kernel (the default) and the
+    integer tensor-core kernel (SSD_MV_IMPL=tc, where it covers the shape). Weights
     rotate over copies totalling more than 2x L2; launches are graph-captured with PDL."""
     import os
     E, F, HQ, HKV = 8192, 28672, 8192, 1024
@@ -482,10 +482,7 @@ def case_mv_shapes(ctx, torch, ssdllm, peak, reps=10):
             res = {}
             ctx.set_pdl(True)
             for impl in ("tc", "fma"):
-                if impl == "fma":
-                    os.environ["SSD_MV_IMPL"] = "fma"
-                else:
-                    os.environ.pop("SSD_MV_IMPL", None)
+                os.environ["SSD_MV_IMPL"] = impl
                 n = max(copies, 32 // copies * copies)
                 us = _graph_time(torch, [mk(ws[i % copies]) for i in range(n)], reps)
                 res[impl] = {"us": round(us, 3), "frac_of_peak": round(alg / us / 1e3 / peak, 4)}

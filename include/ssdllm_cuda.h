@@ -341,6 +341,46 @@ int ssd_model_layer_step(ssd_model* m, int layer);
 /* Kernel launches issued by one decode step. No reference counterpart (reports). */
 int ssd_model_launches_per_step(ssd_model* m, int* launches);
 
+/* ------------------------------------------------------------ GGUF files */
+typedef struct ssd_gguf ssd_gguf;
+/* GgufFile::open (src/model/gguf.rs:233-315): parses the header, metadata and tensor
+ * infos (magic "GGUF", version 2-3, strings <= 1 MiB, data at the next multiple of
+ * general.alignment, default 32). Host only. Bad files fail with SSD_ERR_ARG. */
+int ssd_gguf_open(const char* path, ssd_gguf** out);
+/* Frees the parsed file (the GgufFile value of src/model/gguf.rs:224-231 going out of
+ * scope). */
+int ssd_gguf_close(ssd_gguf* g);
+/* GgufHeader fields and GgufFile::data_offset (src/model/gguf.rs:139-143, :224-231). */
+int ssd_gguf_info(const ssd_gguf* g, uint32_t* version, uint64_t* n_tensors, uint64_t* n_kv,
+                  uint64_t* data_offset);
+/* TensorInfo i (src/model/gguf.rs:216-222): name (NUL-terminated, truncated to cap),
+ * dims (ne0 = columns first), ggml type, offset in the data section, size in bytes. */
+int ssd_gguf_tensor(const ssd_gguf* g, uint64_t i, char* name, size_t cap, uint32_t* n_dims,
+                    uint64_t dims[8], uint32_t* type, uint64_t* offset, uint64_t* size_bytes);
+/* GgufFile::find_tensor (src/model/gguf.rs:405-407): index, or -1 if absent. */
+int ssd_gguf_find(const ssd_gguf* g, const char* name, int64_t* index);
+/* GgufFile::get_u32 / get_f32 and MetadataValue::as_u32 / as_f32 / as_string
+ * (src/model/gguf.rs:427-435, :183-212): *found = 0 when the key is absent or of another
+ * type. The array length is what vocab_size reads from tokenizer.ggml.tokens
+ * (src/model/gguf.rs:371-379). */
+int ssd_gguf_get_u32(const ssd_gguf* g, const char* key, int* found, uint32_t* value);
+int ssd_gguf_get_f32(const ssd_gguf* g, const char* key, int* found, float* value);
+int ssd_gguf_get_str(const ssd_gguf* g, const char* key, int* found, char* out, size_t cap);
+int ssd_gguf_array_len(const ssd_gguf* g, const char* key, int* found, uint64_t* n);
+/* Raw bytes of tensor i in the file's block format (what the layer streamer reads,
+ * src/ssd/streamer.rs:34-91); bytes must equal its size. */
+int ssd_gguf_read(const ssd_gguf* g, uint64_t i, void* dst, size_t bytes);
+/* Decode-engine config from the file's {arch}.* metadata (GgufFile::architecture ..
+ * vocab_size, src/model/gguf.rs:318-379; RoPE base default 10000 as
+ * src/inference/transformer.rs:20-21; eps default 1e-5), the layer / output / embedding
+ * types from blk.0.attn_q, output (or token_embd) and token_embd. */
+int ssd_gguf_model_config(const ssd_gguf* g, int kv_capacity, int tp_rank, int tp_size,
+                          ssd_model_config* cfg);
+/* Loads every tensor of the first n_layers layers plus token_embd, output_norm and
+ * output (token_embd if absent, src/inference/transformer.rs:690-700) into the model:
+ * this rank's shard, HBM-resident (the layer lookups of transformer.rs:171-180, :557). */
+int ssd_model_load_gguf(ssd_model* m, const ssd_gguf* g, int n_layers);
+
 #ifdef __cplusplus
 }
 #endif

@@ -696,17 +696,15 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
     SSD_REQ(epi != EPI_QKV_ROPE || (a.y_k && a.y_v), SSD_ERR_ARG, "null K/V output");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.head_dim > 0 && a.head_dim / 2 <= kMaxRopePairs),
             SSD_ERR_SHAPE, "head_dim %d outside (0, %d]", a.head_dim, 2 * kMaxRopePairs);
-    // Kernel choice. The integer tensor-core kernel (matvec_tc.cu) beats this FMA kernel
-    // only on the largest matrices: measured per decode shape of the 70B model (bench.py
-    // --case mv_shapes_70b), it wins on the fused gate/up of >= 28672 virtual rows and
-    // loses elsewhere to its fixed cost per launch (one CTA per SM, x converted to limbs
-    // in every CTA, no overlap with the previous kernel's tail). SSD_MV_IMPL=tc / fma
-    // forces either kernel (tc where it covers the shape); read per call so that one
-    // process can compare them.
+    // Kernel choice: this FMA kernel (nibbles and scales unpacked in registers) for every
+    // shape. The integer tensor-core kernel (matvec_tc.cu) is an opt-in study
+    // (SSD_MV_IMPL=tc, where it covers the shape): measured per decode shape of the 70B
+    // model (bench.py --case mv_shapes_70b) it is faster only on the fused gate/up of
+    // >= 28672 rows (6 % at TP1), and tensor cores are kept for the prefill contractions.
+    // Read per call so that one process can compare the two.
     const char* impl = getenv("SSD_MV_IMPL");
     const bool force_tc = impl && strcmp(impl, "tc") == 0;
-    const bool force_fma = impl && strcmp(impl, "fma") == 0;
-    const bool want_tc = force_tc || (!force_fma && epi == EPI_SWIGLU && a.rows >= 28672);
+    const bool want_tc = force_tc;
     if (want_tc && (type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 ||
                     (type == SSD_TYPE_Q4_K && a.cols % 256 == 0))) {
         const int st = launch_matvec_tc(ctx, type, epi, a, s, pdl);

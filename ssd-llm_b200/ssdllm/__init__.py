@@ -41,6 +41,10 @@ class ModelConfig(ctypes.Structure):
         ("tp_size", ctypes.c_int)]
 
 
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_ip = ctypes.POINTER(ctypes.c_int)
+
 # name -> (argtypes, restype); the set is checked against include/ssdllm_cuda.h by tests
 _SIGS = {
     "ssd_abi_version": ([], ctypes.c_int),
@@ -131,6 +135,22 @@ _SIGS = {
     "ssd_model_prefill": ([_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "ssd_model_p2p_open": ([_vp, ctypes.c_char_p], ctypes.c_int),
     "ssd_model_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "ssd_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_gguf_close": ([_vp], ctypes.c_int),
+    "ssd_gguf_info": ([_vp, _u32p, _u64p, _u64p, _u64p], ctypes.c_int),
+    "ssd_gguf_tensor": ([_vp, ctypes.c_uint64, ctypes.c_char_p, ctypes.c_size_t, _u32p, _u64p,
+                         _u32p, _u64p, _u64p], ctypes.c_int),
+    "ssd_gguf_find": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
+    "ssd_gguf_get_u32": ([_vp, ctypes.c_char_p, _ip, _u32p], ctypes.c_int),
+    "ssd_gguf_get_f32": ([_vp, ctypes.c_char_p, _ip, ctypes.POINTER(ctypes.c_float)],
+                         ctypes.c_int),
+    "ssd_gguf_get_str": ([_vp, ctypes.c_char_p, _ip, ctypes.c_char_p, ctypes.c_size_t],
+                         ctypes.c_int),
+    "ssd_gguf_array_len": ([_vp, ctypes.c_char_p, _ip, _u64p], ctypes.c_int),
+    "ssd_gguf_read": ([_vp, ctypes.c_uint64, _vp, ctypes.c_size_t], ctypes.c_int),
+    "ssd_gguf_model_config": ([_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                               ctypes.POINTER(ModelConfig)], ctypes.c_int),
+    "ssd_model_load_gguf": ([_vp, _vp, ctypes.c_int], ctypes.c_int),
 }
 
 
@@ -362,6 +382,85 @@ class KvCache:
             self.h = None
 
 
+class GgufFile:
+    """A parsed GGUF file (GgufFile, src/model/gguf.rs:224-441): header fields, tensor
+    infos and metadata lookups, read through the C ABI (host only, no GPU needed)."""
+
+    def __init__(self, path: str):
+        self.h = None
+        h = _vp()
+        check(lib().ssd_gguf_open(os.fsencode(path), ctypes.byref(h)))
+        self.h, self.path = h, path
+        v, nt, nk, off = ctypes.c_uint32(), ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        check(lib().ssd_gguf_info(h, ctypes.byref(v), ctypes.byref(nt), ctypes.byref(nk),
+                                  ctypes.byref(off)))
+        self.version, self.n_tensors, self.n_kv = v.value, nt.value, nk.value
+        self.data_offset = off.value
+        self.tensors = [self._tensor(i) for i in range(self.n_tensors)]
+
+    def _tensor(self, i):
+        name = ctypes.create_string_buffer(4096)
+        nd, ty = ctypes.c_uint32(), ctypes.c_uint32()
+        off, size = ctypes.c_uint64(), ctypes.c_uint64()
+        dims = (ctypes.c_uint64 * 8)()
+        check(lib().ssd_gguf_tensor(self.h, i, name, 4096, ctypes.byref(nd), dims,
+                                    ctypes.byref(ty), ctypes.byref(off), ctypes.byref(size)))
+        return {"name": name.value.decode(), "dims": [dims[d] for d in range(nd.value)],
+                "type": ty.value, "offset": off.value, "size": size.value}
+
+    def find_tensor(self, name: str):
+        idx = ctypes.c_int64()
+        check(lib().ssd_gguf_find(self.h, name.encode(), ctypes.byref(idx)))
+        return None if idx.value < 0 else self.tensors[idx.value]
+
+    def get_u32(self, key: str):
+        f, v = ctypes.c_int(), ctypes.c_uint32()
+        check(lib().ssd_gguf_get_u32(self.h, key.encode(), ctypes.byref(f), ctypes.byref(v)))
+        return v.value if f.value else None
+
+    def get_f32(self, key: str):
+        f, v = ctypes.c_int(), ctypes.c_float()
+        check(lib().ssd_gguf_get_f32(self.h, key.encode(), ctypes.byref(f), ctypes.byref(v)))
+        return v.value if f.value else None
+
+    def get_str(self, key: str):
+        f, buf = ctypes.c_int(), ctypes.create_string_buffer(65536)
+        check(lib().ssd_gguf_get_str(self.h, key.encode(), ctypes.byref(f), buf, 65536))
+        return buf.value.decode() if f.value else None
+
+    def array_len(self, key: str):
+        f, n = ctypes.c_int(), ctypes.c_uint64()
+        check(lib().ssd_gguf_array_len(self.h, key.encode(), ctypes.byref(f), ctypes.byref(n)))
+        return n.value if f.value else None
+
+    def read(self, name: str) -> np.ndarray:
+        """Raw bytes of a tensor in its block format."""
+        idx = ctypes.c_int64()
+        check(lib().ssd_gguf_find(self.h, name.encode(), ctypes.byref(idx)))
+        if idx.value < 0:
+            raise KeyError(name)
+        out = np.empty(self.tensors[idx.value]["size"], np.uint8)
+        check(lib().ssd_gguf_read(self.h, idx.value, out.ctypes.data, out.nbytes))
+        return out
+
+    def model_config(self, kv_capacity: int, tp_rank: int = 0, tp_size: int = 1) -> dict:
+        c = ModelConfig()
+        check(lib().ssd_gguf_model_config(self.h, kv_capacity, tp_rank, tp_size,
+                                          ctypes.byref(c)))
+        return {n: getattr(c, n) for n, _ in ModelConfig._fields_}
+
+    def close(self):
+        if self.h:
+            lib().ssd_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Model:
     """Decode engine (forward_pass / generate's token loop) on HBM-resident weights."""
 
@@ -390,6 +489,22 @@ class Model:
         """Maps every rank's buffer (handles in rank order): partial sums then travel
         over peer memory inside the decode kernels instead of ncclAllReduce."""
         check(lib().ssd_model_p2p_open(self.h, b"".join(handles)))
+
+    @classmethod
+    def from_gguf(cls, ctx: Context, path: str, kv_capacity: int, tp_rank: int = 0,
+                  tp_size: int = 1, uid: bytes = None):
+        """The decode engine built from a GGUF file: config from its metadata, every
+        tensor streamed into HBM (this rank's shard). TP needs the NCCL id (uid)."""
+        g = GgufFile(path)
+        try:
+            cfg = g.model_config(kv_capacity, tp_rank, tp_size)
+            m = cls(ctx, **cfg)
+            if tp_size > 1:
+                m.tp_init(uid)
+            check(lib().ssd_model_load_gguf(m.h, g.h, cfg["n_layers"]))
+        finally:
+            g.close()
+        return m
 
     def synth_weights(self, seed: int, std: float = 0.02):
         check(lib().ssd_model_synth_weights(self.h, seed, std))

@@ -1,5 +1,5 @@
 """GPU parity of the two matvec kernels: the integer tensor-core kernel (matvec_tc.cu,
-covering cols % 256 == 0, cols >= 2048; the default only for the largest fused gate/up)
+covering cols % 256 == 0, cols >= 2048; opt-in with SSD_MV_IMPL=tc)
 and the FMA kernel (matvec.cu, every shape), each forced in turn with SSD_MV_IMPL=tc /
 fma, which the library reads on each call.
 
