@@ -242,6 +242,16 @@ int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev,
 int ssd_attention_int8_noalloc(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev,
                                int n_head, int seq_len, float* out_dev, void* stream);
 
+/* Causal attention of a prompt batch: n_q queries (rows of q_dev, q_stride floats apart,
+ * n_head x head_dim each, RoPE applied) at positions pos0 .. pos0 + n_q - 1, each over
+ * the cache positions 0 .. its own (already appended). Replaces the per-token attention
+ * of batch_prefill_lora (src/inference/transformer.rs:120-250, attention.rs:172-240)
+ * with one call; runs on the tcgen05 tensor cores when head_dim is 128 and n_q a
+ * multiple of 128. */
+int ssd_attention_prefill(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev, int n_q,
+                          int q_stride, int pos0, int n_head, float* out_dev, int out_stride,
+                          void* stream);
+
 /* ------------------------------------------------- host-slice operators */
 /* MetalCompute::matvec_quantized (src/metal/compute.rs:157-191) with its exact
  * signature semantics: raw weight bytes, x and y on the host; uploads, computes,

@@ -1067,7 +1067,7 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
         at.q_stride = m->q_rows;
         at.out_stride = m->q_rows;
         at.seq0 = pos0;
-        SSD_TRY(launch_attention(at, s, false));
+        SSD_TRY(launch_prefill_attention(m->ctx, at, s, false));
         // h += Wo attn (transformer.rs:350-352)
         SSD_TRY(prepare_act_split(AO, n, m->q_rows, nullptr, 0.0f, 0, Ah, Al, s, false));
         g.K = m->q_rows;

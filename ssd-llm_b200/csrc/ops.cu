@@ -10,6 +10,8 @@
 
 #include <mutex>
 
+#include <cstring>
+
 #include "ops.cuh"
 
 namespace ssd {
@@ -784,6 +786,56 @@ extern "C" int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const fl
     a.pos_dev = nullptr;
     a.max_seq = seq_len;
     return launch_attention(a, pick_stream(ctx, s), false);
+}
+
+// Causal attention of n_q consecutive queries (a prompt batch) at positions pos0 .. over
+// the cache rows [0, pos0 + n_q): on the tcgen05 tensor cores when head_dim is 128 and n_q
+// a multiple of 128 (SSD_PREFILL_ATTN=decode forces the per-query kernels), else the
+// batched split-K decode kernels.
+int ssd::launch_prefill_attention(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s, bool pdl) {
+    const char* e = getenv("SSD_PREFILL_ATTN");
+    const bool per_query = e && strcmp(e, "decode") == 0;
+    if (!per_query && a.head_dim == 128 && a.n_q % 128 == 0 && a.q_stride % 4 == 0 &&
+        a.out_stride % 4 == 0 && a.kv_dim % 16 == 0)
+        return launch_attention_prefill_tc(ctx, a, s, pdl);
+    return launch_attention(a, s, pdl);
+}
+
+extern "C" int ssd_attention_prefill(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q,
+                                     int n_q, int q_stride, int pos0, int n_head, float* out,
+                                     int out_stride, void* s) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_REQ(kv && q && out, SSD_ERR_ARG, "null pointer");
+    SSD_REQ(n_q > 0 && pos0 >= 0 && pos0 + n_q <= kv->capacity, SSD_ERR_SHAPE,
+            "queries [%d, %d) outside the cache of %d", pos0, pos0 + n_q, kv->capacity);
+    SSD_REQ(n_head % kv->n_head_kv == 0, SSD_ERR_SHAPE, "n_head %d not a multiple of n_head_kv %d",
+            n_head, kv->n_head_kv);
+    SSD_REQ(q_stride >= n_head * kv->head_dim && out_stride >= n_head * kv->head_dim, SSD_ERR_SHAPE,
+            "row strides shorter than n_head * head_dim");
+    AttnArgs a = {};
+    a.k = kv->k;
+    a.v = kv->v;
+    a.ks = kv->k_scale;
+    a.vs = kv->v_scale;
+    a.kv_dim = kv->kv_dim;
+    a.head_dim = kv->head_dim;
+    a.group = n_head / kv->n_head_kv;
+    a.kv_head0 = 0;
+    a.n_kv_local = kv->n_head_kv;
+    a.q = q;
+    a.out = out;
+    a.max_seq = pos0 + n_q;
+    a.n_q = n_q;
+    a.q_stride = q_stride;
+    a.out_stride = out_stride;
+    a.seq0 = pos0;
+    const size_t pf = (size_t)n_q * attn_partial_floats(n_head, pos0 + n_q, kv->head_dim);
+    const char* e = getenv("SSD_PREFILL_ATTN");
+    if (kv->head_dim != 128 || n_q % 128 != 0 || (e && strcmp(e, "decode") == 0)) {
+        SSD_TRY(ensure_scratch(ctx, pf * 4));  // partials of the per-query kernels
+        a.partial = (float*)ctx->scratch;
+    }
+    return launch_prefill_attention(ctx, a, pick_stream(ctx, s), false);
 }
 
 // ============================================ allocation-free attention variant

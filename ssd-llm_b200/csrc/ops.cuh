@@ -35,7 +35,15 @@ struct AttnArgs {
     // cache at *pos_dev (their own heads' bytes; local head 0 also the scales) first.
     const float* k_new;
     const float* v_new;
+    int* status;  // device status word for bounded waits (default: the context's)
 };
+// Causal attention of a prompt batch on the tcgen05 tensor cores (attn_tc.cu): n_q
+// queries (a multiple of 128, head_dim 128) at positions seq0 .., over the cache rows
+// [0, seq0 + n_q) already appended. Same arguments as the batched launch_attention.
+int launch_attention_prefill_tc(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s, bool pdl);
+// The prompt-batch attention: the tensor-core kernel where it covers the shape, else
+// launch_attention's batched per-query kernels (which need a.partial).
+int launch_prefill_attention(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s, bool pdl);
 size_t attn_partial_floats(int n_heads, int max_seq, int head_dim);
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 

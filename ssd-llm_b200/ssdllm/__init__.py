@@ -135,6 +135,8 @@ _SIGS = {
     "ssd_model_prefill": ([_vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "ssd_model_p2p_open": ([_vp, ctypes.c_char_p], ctypes.c_int),
     "ssd_model_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "ssd_attention_prefill": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_int, _vp, ctypes.c_int, _vp], ctypes.c_int),
     "ssd_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], ctypes.c_int),
     "ssd_gguf_close": ([_vp], ctypes.c_int),
     "ssd_gguf_info": ([_vp, _u32p, _u64p, _u64p, _u64p], ctypes.c_int),
@@ -369,6 +371,13 @@ class KvCache:
     def attention(self, q, n_head: int, seq_len: int, out):
         check(lib().ssd_attention_int8(self.ctx.h, self.h, _ptr(q), n_head, seq_len, _ptr(out),
                                        _stream()))
+
+    def attention_prefill(self, q, n_head: int, pos0: int, out):
+        """Causal attention of the rows of q (n_q x n_head*head_dim) at positions pos0..
+        over this cache (their K/V rows already appended)."""
+        n_q = q.shape[0]
+        check(lib().ssd_attention_prefill(self.ctx.h, self.h, _ptr(q), n_q, q.shape[1], pos0,
+                                          n_head, _ptr(out), out.shape[1], _stream()))
 
     def attention_noalloc(self, q, n_head: int, seq_len: int, out):
         """ssd_attention_int8 with the partials in the library's fixed device array

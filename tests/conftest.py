@@ -15,3 +15,4 @@ for p in (ROOT, os.path.join(ROOT, "ssd-llm_b200")):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+    config.addinivalue_line("markers", "tc_only: a case run on the tensor-core kernel only")
