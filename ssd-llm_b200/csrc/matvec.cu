@@ -28,6 +28,7 @@
 //  * Epilogues fuse what follows the matvec in the decode step: residual add,
 //    SwiGLU, RoPE on Q/K, or argmax (LAST index on ties, sampler.rs:572-578).
 #include <cstring>
+#include <type_traits>
 
 #include "matvec_dev.cuh"
 
@@ -64,11 +65,11 @@ struct Chunk<SSD_TYPE_Q4_K> {
 };
 
 // Byte pointers of one row of the library layout (see ssd_weight in common.cuh).
-template <int FMT>
+template <int FMT, int MAP>
 __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uint8_t*& qs,
                                         const uint8_t*& meta) {
     int seg, lr;
-    map_row(a, R, v, seg, lr);
+    map_row<MAP>(a, R, v, seg, lr);
     const size_t nc = (size_t)(a.cols >> 5);
     const uint8_t* q = seg == 0 ? a.qs[0] : (seg == 1 ? a.qs[1] : a.qs[2]);
     const uint8_t* m = seg == 0 ? a.meta[0] : (seg == 1 ? a.meta[1] : a.meta[2]);
@@ -99,21 +100,25 @@ __host__ __device__ constexpr int stage_bytes() {
     return R * U * 32 * (Slot<FMT>::QB + Slot<FMT>::MB);
 }
 
-// Issues the copies of chunk step u of a stage for one row. qp / mp point at this
-// lane's chunk of the stage's first step (tail-clamped by the caller).
+// Issues the copies of chunk step u of a stage for one row into the shared addresses
+// qdst / mdst. qp / mp point at this lane's chunk of the stage's first step
+// (tail-clamped by the caller); for Q4_0 / Q8_0 mp is the aligned 4-byte word holding
+// the chunk's f16 d.
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4_s(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
 template <int FMT>
-__device__ __forceinline__ void issue_chunk(uint8_t* qdst, uint8_t* mdst, const uint8_t* qp,
+__device__ __forceinline__ void issue_chunk(uint32_t qdst, uint32_t mdst, const uint8_t* qp,
                                             const uint8_t* mp) {
-    if constexpr (FMT == SSD_TYPE_Q8_0) {
-        cp_async16(qdst, qp);
-        cp_async16(qdst + 16, qp + 16);
-    } else {
-        cp_async16(qdst, qp);
-    }
+    cp_async16_s(qdst, qp);
+    if constexpr (FMT == SSD_TYPE_Q8_0) cp_async16_s(qdst + 16, qp + 16);
     if constexpr (FMT == SSD_TYPE_Q4_K)
-        cp_async16(mdst, mp);
+        cp_async16_s(mdst, mp);
     else
-        cp_async4(mdst, reinterpret_cast<const uint8_t*>((uintptr_t)mp & ~(uintptr_t)3));
+        cp_async4_s(mdst, mp);
 }
 
 // Reads one (row, chunk) slot back: qsrc = payload slot, msrc = metadata slot (for
@@ -147,92 +152,175 @@ __device__ __forceinline__ uint32_t word_of(const uint4& q, int m) {
     return m == 0 ? q.x : (m == 1 ? q.y : (m == 2 ? q.z : q.w));
 }
 
-// Two fp32 FMAs in one instruction (sm_100 fma.rn.f32x2): (d0, d1) += (a0, a1) * (b0, b1),
-// each lane rounded exactly as fmaf.
-__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    uint64_t d, a, b;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(d0), "f"(d1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+// Two x'' units of 16 bytes as four fp32 pairs {a01, a23} at shared address addr + OFF.
+template <int OFF>
+__device__ __forceinline__ void lds_x(uint32_t addr, uint64_t& a01, uint64_t& a23) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2+%3];" : "=l"(a01), "=l"(a23) : "r"(addr), "n"(OFF));
+}
+__device__ __forceinline__ float sum_f2(uint64_t p) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(p));
+    return lo + hi;
 }
 
-// (e[r], o[r]) += sum over a 16-byte nibble chunk of q * x'' (x'' pre-scaled per field
-// position, see nib_pos), even elements into e, odd into o. xa / xb are the chunk's
-// elements 8m..8m+3 / 8m+4..8m+7.
-template <int R>
-__device__ __forceinline__ void nib_dot(const float4* xc, int sw, const uint4 (&q)[R],
-                                        float (&e)[R], float (&o)[R]) {
+// acc (an fp32 pair: even, odd elements) += the 8 nibbles of word w times x'' elements
+// 0..7 of the word, given as pairs (0,1) (2,3) (4,5) (6,7). Each nibble is masked in
+// place and read as a denormal; nibbles 5-7 come from w >> 12. Two fp32 FMAs per
+// fma.rn.f32x2, each rounded exactly as fmaf; denormal operands are not flushed. FIRST:
+// the chunk's first word starts the pair (multiply, no accumulate).
+template <bool FIRST>
+__device__ __forceinline__ void nib_word(uint64_t& acc, uint32_t w, uint64_t x01, uint64_t x23,
+                                         uint64_t x45, uint64_t x67) {
+    if constexpr (FIRST)
+        asm(
+            "{\n\t"
+            ".reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, w2;\n\t"
+            ".reg .b64 p0, p1, p2, p3;\n\t"
+            "and.b32 t0, %1, 0x0000000F;\n\t"
+            "and.b32 t1, %1, 0x000000F0;\n\t"
+            "mov.b64 p0, {t0, t1};\n\t"
+            "mul.rn.f32x2 %0, p0, %2;\n\t"
+            "and.b32 t2, %1, 0x00000F00;\n\t"
+            "and.b32 t3, %1, 0x0000F000;\n\t"
+            "mov.b64 p1, {t2, t3};\n\t"
+            "fma.rn.f32x2 %0, p1, %3, %0;\n\t"
+            "shr.u32 w2, %1, 12;\n\t"
+            "and.b32 t4, %1, 0x000F0000;\n\t"
+            "and.b32 t5, w2, 0x00000F00;\n\t"
+            "mov.b64 p2, {t4, t5};\n\t"
+            "fma.rn.f32x2 %0, p2, %4, %0;\n\t"
+            "and.b32 t6, w2, 0x0000F000;\n\t"
+            "and.b32 t7, w2, 0x000F0000;\n\t"
+            "mov.b64 p3, {t6, t7};\n\t"
+            "fma.rn.f32x2 %0, p3, %5, %0;\n\t"
+            "}"
+            : "=&l"(acc)
+            : "r"(w), "l"(x01), "l"(x23), "l"(x45), "l"(x67));
+    else
+        asm(
+            "{\n\t"
+            ".reg .b32 t0, t1, t2, t3, t4, t5, t6, t7, w2;\n\t"
+            ".reg .b64 p0, p1, p2, p3;\n\t"
+            "and.b32 t0, %1, 0x0000000F;\n\t"
+            "and.b32 t1, %1, 0x000000F0;\n\t"
+            "mov.b64 p0, {t0, t1};\n\t"
+            "fma.rn.f32x2 %0, p0, %2, %0;\n\t"
+            "and.b32 t2, %1, 0x00000F00;\n\t"
+            "and.b32 t3, %1, 0x0000F000;\n\t"
+            "mov.b64 p1, {t2, t3};\n\t"
+            "fma.rn.f32x2 %0, p1, %3, %0;\n\t"
+            "shr.u32 w2, %1, 12;\n\t"
+            "and.b32 t4, %1, 0x000F0000;\n\t"
+            "and.b32 t5, w2, 0x00000F00;\n\t"
+            "mov.b64 p2, {t4, t5};\n\t"
+            "fma.rn.f32x2 %0, p2, %4, %0;\n\t"
+            "and.b32 t6, w2, 0x0000F000;\n\t"
+            "and.b32 t7, w2, 0x000F0000;\n\t"
+            "mov.b64 p3, {t6, t7};\n\t"
+            "fma.rn.f32x2 %0, p3, %5, %0;\n\t"
+            "}"
+            : "+l"(acc)
+            : "r"(w), "l"(x01), "l"(x23), "l"(x45), "l"(x67));
+}
+
+// acc += the 4 signed bytes of word w (read as unsigned q + 128: one LOP3 per byte does
+// the mask and the sign flip) times x'' pairs (0,1) (2,3); bytes 2-3 via w >> 16.
+template <bool FIRST>
+__device__ __forceinline__ void byte_word(uint64_t& acc, uint32_t w, uint64_t x01, uint64_t x23) {
+    if constexpr (FIRST)
+        asm(
+            "{\n\t"
+            ".reg .b32 t0, t1, t2, t3, w2;\n\t"
+            ".reg .b64 p0, p1;\n\t"
+            "lop3.b32 t0, %1, 0x000000FF, 0x00000080, 0x6A;\n\t"
+            "lop3.b32 t1, %1, 0x0000FF00, 0x00008000, 0x6A;\n\t"
+            "mov.b64 p0, {t0, t1};\n\t"
+            "mul.rn.f32x2 %0, p0, %2;\n\t"
+            "shr.u32 w2, %1, 16;\n\t"
+            "lop3.b32 t2, w2, 0x000000FF, 0x00000080, 0x6A;\n\t"
+            "lop3.b32 t3, w2, 0x0000FF00, 0x00008000, 0x6A;\n\t"
+            "mov.b64 p1, {t2, t3};\n\t"
+            "fma.rn.f32x2 %0, p1, %3, %0;\n\t"
+            "}"
+            : "=&l"(acc)
+            : "r"(w), "l"(x01), "l"(x23));
+    else
+        asm(
+            "{\n\t"
+            ".reg .b32 t0, t1, t2, t3, w2;\n\t"
+            ".reg .b64 p0, p1;\n\t"
+            "lop3.b32 t0, %1, 0x000000FF, 0x00000080, 0x6A;\n\t"
+            "lop3.b32 t1, %1, 0x0000FF00, 0x00008000, 0x6A;\n\t"
+            "mov.b64 p0, {t0, t1};\n\t"
+            "fma.rn.f32x2 %0, p0, %2, %0;\n\t"
+            "shr.u32 w2, %1, 16;\n\t"
+            "lop3.b32 t2, w2, 0x000000FF, 0x00000080, 0x6A;\n\t"
+            "lop3.b32 t3, w2, 0x0000FF00, 0x00008000, 0x6A;\n\t"
+            "mov.b64 p1, {t2, t3};\n\t"
+            "fma.rn.f32x2 %0, p1, %3, %0;\n\t"
+            "}"
+            : "+l"(acc)
+            : "r"(w), "l"(x01), "l"(x23));
+}
+
+// acc[r] = sum over a 16-byte nibble chunk of q * x''. The chunk's x'' unit u is at
+// shared address xq[u] + XOFF (x'' pre-scaled per field position, see nib_pos).
+template <int R, int XOFF>
+__device__ __forceinline__ void nib_dot(const uint32_t (&xq)[8], const uint4 (&q)[R],
+                                        uint64_t (&acc)[R]) {
 #pragma unroll
     for (int m = 0; m < 4; m++) {
-        const float4 xa = xc[(2 * m) ^ sw];
-        const float4 xb = xc[(2 * m + 1) ^ sw];
+        uint64_t x01, x23, x45, x67;
+        lds_x<XOFF>(xq[2 * m], x01, x23);
+        lds_x<XOFF>(xq[2 * m + 1], x45, x67);
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            const uint32_t w = word_of(q[r], m);
-            const uint32_t w2 = w >> 12;
-            ffma2(e[r], o[r], den(w & 0x0000000Fu), den(w & 0x000000F0u), xa.x, xa.y);
-            ffma2(e[r], o[r], den(w & 0x00000F00u), den(w & 0x0000F000u), xa.z, xa.w);
-            ffma2(e[r], o[r], den(w & 0x000F0000u), den(w2 & 0x00000F00u), xb.x, xb.y);
-            ffma2(e[r], o[r], den(w2 & 0x0000F000u), den(w2 & 0x000F0000u), xb.z, xb.w);
+            if (m == 0)
+                nib_word<true>(acc[r], word_of(q[r], m), x01, x23, x45, x67);
+            else
+                nib_word<false>(acc[r], word_of(q[r], m), x01, x23, x45, x67);
         }
     }
 }
 
 // Per-chunk data staged next to x'': csum[c] = bias term of the chunk, already scaled
-// by 2^-64: -8 X (Q4_0), -128 X (Q8_0), X (Q4_K), X = sum of the chunk's x.
-template <int FMT, int R>
-__device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const float4* xs4,
-                                              const float* csum, int c, int lane,
-                                              float (&acc)[R]) {
-    const float4* xc = xs4 + (size_t)c * 8;
-    const int sw = c & 7;
-    float e[R], o[R];
+// by 2^-64: -8 X (Q4_0), -128 X (Q8_0), X (Q4_K), X = sum of the chunk's x. b = csum of
+// this chunk; the chunk's x'' unit u is at shared address xq[u] + XOFF.
+template <int FMT, int R, int XOFF>
+__device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const uint32_t (&xq)[8],
+                                              float b, int lane, float (&acc)[R]) {
+    uint64_t eo[R];
     if constexpr (FMT == SSD_TYPE_Q4_0) {
         uint4 q[R];
-        const float b = csum[c];
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-            q[r] = ch[r].q;
-            e[r] = b;
-            o[r] = 0.0f;
-        }
-        nib_dot<R>(xc, sw, q, e, o);
+        for (int r = 0; r < R; r++) q[r] = ch[r].q;
+        nib_dot<R, XOFF>(xq, q, eo);
 #pragma unroll
         for (int r = 0; r < R; r++)
-            acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), e[r] + o[r], acc[r]);
+            acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), sum_f2(eo[r]) + b, acc[r]);
     } else if constexpr (FMT == SSD_TYPE_Q8_0) {
-        const float b = csum[c];
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-            e[r] = b;
-            o[r] = 0.0f;
-        }
-#pragma unroll
-        for (int m = 0; m < 8; m++) {
-            const float4 xa = xc[m ^ sw];  // elements 4m..4m+3
+        for (int m = 0; m < 8; m++) {  // unit m = elements 4m..4m+3
+            uint64_t x01, x23;
+            lds_x<XOFF>(xq[m], x01, x23);
 #pragma unroll
             for (int r = 0; r < R; r++) {
-                const uint32_t w = word_of(m < 4 ? ch[r].q0 : ch[r].q1, m & 3) ^ 0x80808080u;
-                const uint32_t w2 = w >> 16;
-                ffma2(e[r], o[r], den(w & 0x000000FFu), den(w & 0x0000FF00u), xa.x, xa.y);
-                ffma2(e[r], o[r], den(w2 & 0x000000FFu), den(w2 & 0x0000FF00u), xa.z, xa.w);
+                const uint32_t w = word_of(m < 4 ? ch[r].q0 : ch[r].q1, m & 3);
+                if (m == 0)
+                    byte_word<true>(eo[r], w, x01, x23);
+                else
+                    byte_word<false>(eo[r], w, x01, x23);
             }
         }
 #pragma unroll
         for (int r = 0; r < R; r++)
-            acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), e[r] + o[r], acc[r]);
+            acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), sum_f2(eo[r]) + b, acc[r]);
     } else {  // Q4_K: this lane's sub-block index is c & 7 == lane & 7
         uint4 q[R];
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-            q[r] = ch[r].q;
-            e[r] = 0.0f;
-            o[r] = 0.0f;
-        }
-        nib_dot<R>(xc, sw, q, e, o);
-        const float X = csum[c];
+        for (int r = 0; r < R; r++) q[r] = ch[r].q;
+        nib_dot<R, XOFF>(xq, q, eo);
+        const float X = b;
         const int sb = lane & 7, sh = 8 * (sb & 3);
 #pragma unroll
         for (int r = 0; r < R; r++) {
@@ -252,7 +340,7 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const f
             // sum((scale*q - min) x) = scale * sum(q x) - min * X
             const float scale = __fmul_rn(d, (float)s6);
             const float mn = __fmul_rn(dmin, (float)m6);
-            acc[r] = fmaf(-mn, X, fmaf(scale, e[r] + o[r], acc[r]));
+            acc[r] = fmaf(-mn, X, fmaf(scale, sum_f2(eo[r]), acc[r]));
         }
     }
 }
@@ -308,6 +396,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     constexpr int kStages = n_stages<NW>();
     constexpr int SB = stage_bytes<FMT, R, U>();
     constexpr int QB = Slot<FMT>::QB, MB = Slot<FMT>::MB;
+    static_assert(U == 1 || U == 2, "chunk steps per stage");
+    constexpr int kMap = epi_map(EPI);  // launch_matvec checks a.map against it
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const SmemPlan P = smem_plan(a.cols, NW, kStages * SB);
@@ -347,9 +437,13 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
         for (int r = 0; r < R; r++) {
             const int v = min(lrg * R + r, a.rows - 1);
             const uint8_t *q0, *m0;
-            row_ptr<FMT>(a, R, v, q0, m0);
+            row_ptr<FMT, kMap>(a, R, v, q0, m0);
             lq[r] = q0 + q_lane<FMT>(lane < nc ? lane : 0);
             lm[r] = m0 + m_lane<FMT>(lane < nc ? lane : 0);
+            // Q4_0 / Q8_0: the aligned 4-byte word holding the d (stays aligned: the
+            // pointer advances by multiples of 64 bytes)
+            if constexpr (FMT != SSD_TYPE_Q4_K)
+                lm[r] = reinterpret_cast<const uint8_t*>((uintptr_t)lm[r] & ~(uintptr_t)3);
         }
     };
     if (lrg < n_rg) set_rows();
@@ -358,6 +452,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     // ring_m + stage + (r*U+u)*32*MB (compile-time offsets from two lane pointers)
     uint8_t* const ring_q = ring + (size_t)lane * QB;
     uint8_t* const ring_m = ring + (size_t)R * U * 32 * QB + (size_t)lane * MB;
+    const uint32_t ring_qs = smem_u32(ring_q), ring_ms = smem_u32(ring_m);  // copy targets
     int ist = 0;  // byte offset of the stage being issued
     auto issue = [&]() {  // the next stage into the ring, then commit
         if (issued < total) {
@@ -366,8 +461,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
                 for (int r = 0; r < R; r++) {
 #pragma unroll
                     for (int u = 0; u < U; u++)
-                        issue_chunk<FMT>(ring_q + ist + (r * U + u) * 32 * QB,
-                                         ring_m + ist + (r * U + u) * 32 * MB,
+                        issue_chunk<FMT>(ring_qs + ist + (r * U + u) * 32 * QB,
+                                         ring_ms + ist + (r * U + u) * 32 * MB,
                                          lq[r] + u * q_step<FMT>(), lm[r] + u * m_step<FMT>());
                 }
             } else {  // tail stage: chunks past the row end re-read the lane's last chunk
@@ -381,8 +476,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
                     const long long dc = cu < nc ? 0 : (long long)(last_c - cp);
 #pragma unroll
                     for (int r = 0; r < R; r++)
-                        issue_chunk<FMT>(ring_q + ist + (r * U + u) * 32 * QB,
-                                         ring_m + ist + (r * U + u) * 32 * MB,
+                        issue_chunk<FMT>(ring_qs + ist + (r * U + u) * 32 * QB,
+                                         ring_ms + ist + (r * U + u) * 32 * MB,
                                          lq[r] + u * q_step<FMT>() + dc * (q_step<FMT>() / 32),
                                          lm[r] + u * m_step<FMT>() + dc * 2);
                 }
@@ -442,32 +537,45 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
 #pragma unroll
         for (int r = 0; r < R; r++) {
             int seg, lr;
-            map_row(a, R, min(crg * R + r, a.rows - 1), seg, lr);
+            map_row<kMap>(a, R, min(crg * R + r, a.rows - 1), seg, lr);
             doff[r] = (((lr & 1) * (nc & 1) + lane) & 1) * 2;
         }
     };
     if (FMT != SSD_TYPE_Q4_K && crg < n_rg) set_doff();
     int cst_off = 0;  // byte offset of the stage being computed
+    // this lane's shared address of x'' unit u of its chunk c = lane (mod 32): row c of
+    // 128 bytes, unit u at slot u ^ (c & 7) = u ^ (lane & 7); chunk c + 32 t is 4096 t
+    // bytes further
+    uint32_t xp[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) xp[u] = smem_u32(xs4) + lane * 128 + ((u ^ (lane & 7)) << 4);
 
     for (int k = 0; k < total; k++) {
         cp_wait<kStages - 2>();  // this thread's copies of stage k have landed
         const uint8_t* sq = ring_q + cst_off;
         const uint8_t* sm = ring_m + cst_off;
-        auto do_u = [&](int u) {
+        uint32_t xst[8];  // x'' units of this stage's first chunk step
+#pragma unroll
+        for (int u = 0; u < 8; u++) xst[u] = xp[u] + (uint32_t)cst * (U * 4096);
+        const float* cs = csum + lane + 32 * U * cst;
+        auto do_u = [&](auto uc) {  // chunk step u (a compile-time constant)
+            constexpr int u = decltype(uc)::value;
             Chunk<FMT> ch[R];
 #pragma unroll
             for (int r = 0; r < R; r++)
                 read_chunk<FMT>(ch[r], sq + (r * U + u) * 32 * QB,
                                 sm + (r * U + u) * 32 * MB + (FMT == SSD_TYPE_Q4_K ? 0 : doff[r]));
-            compute_chunk<FMT, R>(ch, xs4, csum, lane + 32 * (cst * U + u), lane, acc);
+            compute_chunk<FMT, R, u * 4096>(ch, xst, cs[32 * u], lane, acc);
         };
+        using U0 = std::integral_constant<int, 0>;
+        using U1 = std::integral_constant<int, (U > 1 ? 1 : 0)>;
         if (!any_tail || (cst + 1) * U * 32 <= nc) {
-#pragma unroll
-            for (int u = 0; u < U; u++) do_u(u);
+            do_u(U0{});
+            if constexpr (U > 1) do_u(U1{});
         } else {
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (lane + 32 * (cst * U + u) < nc) do_u(u);
+            if (lane + 32 * (cst * U) < nc) do_u(U0{});
+            if constexpr (U > 1)
+                if (lane + 32 * (cst * U + 1) < nc) do_u(U1{});
         }
         cst_off = cst_off + SB == kStages * SB ? 0 : cst_off + SB;
         issue();  // refill the buffer of stage k - 1 (this thread is done reading it)
@@ -514,7 +622,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
         } else if constexpr (EPI == EPI_QKV_ROPE) {  // adjacent pairs (v0+2p, v0+2p+1)
             if (lane < R / 2 && v0 < a.rows) {
                 int seg, lr;
-                map_row(a, R, v0 + 2 * lane, seg, lr);
+                map_row<kMap>(a, R, v0 + 2 * lane, seg, lr);
                 float x0 = res[0], x1 = res[1];
 #pragma unroll
                 for (int p = 1; p < R / 2; p++)
@@ -692,6 +800,8 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
     if (epi == EPI_PEERS)
         for (int p = 0; p < a.ar_out_n; p++)
             SSD_REQ(a.ar_out[p] && a.ar_out_flag[p], SSD_ERR_ARG, "null peer buffer %d", p);
+    SSD_REQ(a.map == epi_map(epi), SSD_ERR_ARG, "row map %d does not match epilogue %d", a.map,
+            epi);
     SSD_REQ(epi != EPI_RESID || a.base != nullptr, SSD_ERR_ARG, "null residual base");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.y_k && a.y_v), SSD_ERR_ARG, "null K/V output");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.head_dim > 0 && a.head_dim / 2 <= kMaxRopePairs),

@@ -10,14 +10,22 @@ namespace ssd {
 
 constexpr int kMaxRopePairs = 256;  // head_dim <= 512
 
+// The row map each epilogue is launched with: QKV + RoPE reads the three projections,
+// SwiGLU interleaves gate and up rows, every other epilogue reads one matrix.
+__host__ __device__ constexpr int epi_map(int epi) {
+    return epi == EPI_QKV_ROPE ? MAP_QKV : (epi == EPI_SWIGLU ? MAP_SWIGLU : MAP_PLAIN);
+}
+
 // Virtual row v -> (segment, row within the segment). R is the number of rows a warp
 // computes together; MAP_SWIGLU puts R/2 gate rows then the R/2 matching up rows in
-// each group of R.
+// each group of R. MAP >= 0 fixes the map at compile time (it must equal a.map).
+template <int MAP = -1>
 __device__ __forceinline__ void map_row(const MvArgs& a, int R, int v, int& seg, int& lr) {
-    if (a.map == MAP_PLAIN) {
+    const int map = MAP >= 0 ? MAP : a.map;
+    if (map == MAP_PLAIN) {
         seg = 0;
         lr = v;
-    } else if (a.map == MAP_QKV) {
+    } else if (map == MAP_QKV) {
         if (v < a.seg_rows[0]) {
             seg = 0;
             lr = v;
