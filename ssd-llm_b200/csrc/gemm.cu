@@ -64,7 +64,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* acc_free = acc_full + 2;  // [2]: buffer b drained by the 4 epilogue warps
     uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_free + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.y * 128, n0 = blockIdx.x * BN;
+    // blockIdx.x = M tile (fastest): the M / 128 CTAs that read one weight tile are launched
+    // together, so the weights stream from HBM once and the other reads hit L2
+    const int m0 = blockIdx.x * 128, n0 = blockIdx.y * BN;
     const int KB = g.K / 64, NW = KB / SM::kWin;
 
     if (tid == 0) {
@@ -322,7 +324,7 @@ static int launch_gemm_t(ssd_ctx* ctx, const GemmOperands& op, const GemmArgs& g
     SSD_TRY(encode_f16_map(&mal, op.a_lo, g.M, g.K, 128));
     SSD_TRY(encode_f16_map(&mbh, op.w_hi, g.N, g.K, kGemmBN));
     SSD_TRY(encode_f16_map(&mbl, op.w_lo, g.N, g.K, kGemmBN));
-    SSD_CK(launch_pdl(kern, dim3(g.N / kGemmBN, g.M / 128), dim3(kGemmThreads), SM::kTotal, s, pdl,
+    SSD_CK(launch_pdl(kern, dim3(g.M / 128, g.N / kGemmBN), dim3(kGemmThreads), SM::kTotal, s, pdl,
                       g, mah, mal, mbh, mbl));
     return SSD_OK;
 }
