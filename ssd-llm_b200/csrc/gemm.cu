@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int row = m0 + 32 * warp + lane;
         if constexpr (EPI == GEMM_SWIGLU) {  // tile columns [0, 64) gate, [64, 128) up
             constexpr int H = BN / 2;
-            float* out = g.C + (size_t)row * g.ldc + (n0 / 2);
+            const size_t o0 = (size_t)row * g.ldc + (n0 / 2);
 #pragma unroll
             for (int j = 0; j < H; j += 4) {
                 float4 o;
@@ -164,7 +164,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     // silu(v) = v / (1 + exp(-v)), then gate *= up (feed_forward.rs:31-39)
                     op[t] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
                 }
-                *reinterpret_cast<float4*>(out + j) = o;
+                if (g.c_hi) {  // the down GEMM's A operand, split as k_asplit splits it
+                    __align__(8) __half h[4], l[4];
+#pragma unroll
+                    for (int t = 0; t < 4; t++) {
+                        h[t] = __float2half_rn(op[t]);
+                        l[t] = __float2half_rn(op[t] - __half2float(h[t]));
+                    }
+                    *reinterpret_cast<uint2*>(g.c_hi + o0 + j) = *reinterpret_cast<const uint2*>(h);
+                    *reinterpret_cast<uint2*>(g.c_lo + o0 + j) = *reinterpret_cast<const uint2*>(l);
+                } else {
+                    *reinterpret_cast<float4*>(g.C + o0 + j) = o;
+                }
             }
         } else {
             float* out = g.C + (size_t)row * g.ldc + n0;
@@ -336,8 +347,11 @@ int launch_gemm(ssd_ctx* ctx, const GemmOperands& op, GemmArgs g, cudaStream_t s
             "GEMM K %d not a multiple of %d", g.K, 64 * GemmSmem::kWin);
     SSD_REQ(g.N > 0 && g.N % kGemmBN == 0, SSD_ERR_SHAPE, "GEMM N %d not a multiple of %d", g.N,
             kGemmBN);
-    SSD_REQ(g.C && g.rscale && op.a_hi && op.a_lo && op.w_hi && op.w_lo, SSD_ERR_ARG,
-            "null GEMM operand");
+    SSD_REQ((g.C || (g.epi == GEMM_SWIGLU && g.c_hi && g.c_lo)) && g.rscale && op.a_hi && op.a_lo &&
+                op.w_hi && op.w_lo,
+            SSD_ERR_ARG, "null GEMM operand");
+    SSD_REQ(!g.c_hi || (g.epi == GEMM_SWIGLU && g.c_lo && g.ldc % 4 == 0), SSD_ERR_ARG,
+            "fp16 split output needs the SwiGLU epilogue and ldc a multiple of 4");
     SSD_REQ(g.epi != GEMM_RESID || g.base, SSD_ERR_ARG, "null residual base");
     if (g.epi == GEMM_STORE) return launch_gemm_t<GEMM_STORE>(ctx, op, g, s, pdl);
     if (g.epi == GEMM_RESID) return launch_gemm_t<GEMM_RESID>(ctx, op, g, s, pdl);

@@ -19,6 +19,11 @@ struct GemmArgs {
     const float* rscale;
     int epi;
     int* status;
+    // GEMM_SWIGLU only: when set, the outputs are written as fp16 hi / lo splits
+    // (hi = fp16(y), lo = fp16(y - hi), the A-operand form of the next GEMM, ld = ldc)
+    // instead of fp32 C (C may then be null).
+    __half* c_hi;
+    __half* c_lo;
 };
 struct GemmOperands {
     const __half* a_hi;

@@ -991,7 +991,7 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
     const size_t bytes = pad((size_t)n * E * 4) + 2 * pad((size_t)n * KM * 2) +
                          pad((size_t)n * NQ * 4) + pad((size_t)n * m->q_rows * 4) +
                          2 * pad((size_t)n * m->kv_rows * 4) + pad((size_t)n * m->q_rows * 4) +
-                         pad((size_t)n * F * 4) + pad(pf * 4) + pad((size_t)n * 4);
+                         2 * pad((size_t)n * F * 2) + pad(pf * 4) + pad((size_t)n * 4);
     if (bytes > m->pf_buf_bytes) {
         if (m->pf_buf) {
             SSD_CK(cudaStreamSynchronize(s));
@@ -1021,7 +1021,8 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
     float* Kr = (float*)take((size_t)n * m->kv_rows * 4);
     float* Vr = (float*)take((size_t)n * m->kv_rows * 4);
     float* AO = (float*)take((size_t)n * m->q_rows * 4);
-    float* ACT = (float*)take((size_t)n * F * 4);
+    __half* ACTh = (__half*)take((size_t)n * F * 2);  // SwiGLU output, split for the down GEMM
+    __half* ACTl = (__half*)take((size_t)n * F * 2);
     float* PART = (float*)take(pf * 4);
     int32_t* TOK = (int32_t*)take((size_t)n * 4);
 
@@ -1085,7 +1086,9 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
         SSD_TRY(prepare_act_split(H, n, E, L.ffn_norm, c.eps, 1, Ah, Al, s, false));
         g.K = E;
         g.N = 2 * F;
-        g.C = ACT;
+        g.C = nullptr;
+        g.c_hi = ACTh;  // the epilogue writes act as the down GEMM's hi / lo operand
+        g.c_lo = ACTl;
         g.ldc = F;
         g.base = nullptr;
         g.rscale = P.gu_r;
@@ -1094,7 +1097,9 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
         op.w_lo = P.gu_l;
         SSD_TRY(launch_gemm(m->ctx, op, g, s, false));
         // h += down(act) (feed_forward.rs:40-43, transformer.rs:392)
-        SSD_TRY(prepare_act_split(ACT, n, F, nullptr, 0.0f, 0, Ah, Al, s, false));
+        g.c_hi = g.c_lo = nullptr;
+        op.a_hi = ACTh;
+        op.a_lo = ACTl;
         g.K = F;
         g.N = E;
         g.C = H;
@@ -1106,6 +1111,8 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
         op.w_hi = P.d_h;
         op.w_lo = P.d_l;
         SSD_TRY(launch_gemm(m->ctx, op, g, s, false));
+        op.a_hi = Ah;
+        op.a_lo = Al;
     }
     // the last token's hidden state is the decode state; logits, greedy argmax, position
     SSD_CK(cudaMemcpyAsync(m->h_a, H + (size_t)(n - 1) * E, (size_t)E * 4, cudaMemcpyDeviceToDevice,
