@@ -288,12 +288,28 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill_tc(const AttnArgs a) {
         if (half == 0) linv_s[r] = __fdiv_rn(1.0f, l);
         __syncthreads();
         const float inv = linv_s[r];
-        float* orow = a.out + (size_t)qi * a.out_stride + (size_t)h * kAtHD + 64 * half;
+        const size_t o0 = (size_t)qi * a.out_stride + (size_t)h * kAtHD + 64 * half;
+        if (a.out_hi) {  // the output projection's A operand, split as k_asplit splits it
 #pragma unroll
-        for (int d = 0; d < 64; d += 4)
-            *reinterpret_cast<float4*>(orow + d) =
-                make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
-                            __fmul_rn(o[d + 3], inv));
+            for (int d = 0; d < 64; d += 4) {
+                __align__(8) __half hh[4], ll[4];
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const float v = __fmul_rn(o[d + t], inv);
+                    hh[t] = __float2half_rn(v);
+                    ll[t] = __float2half_rn(v - __half2float(hh[t]));
+                }
+                *reinterpret_cast<uint2*>(a.out_hi + o0 + d) = *reinterpret_cast<const uint2*>(hh);
+                *reinterpret_cast<uint2*>(a.out_lo + o0 + d) = *reinterpret_cast<const uint2*>(ll);
+            }
+        } else {
+            float* orow = a.out + o0;
+#pragma unroll
+            for (int d = 0; d < 64; d += 4)
+                *reinterpret_cast<float4*>(orow + d) =
+                    make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv),
+                                __fmul_rn(o[d + 2], inv), __fmul_rn(o[d + 3], inv));
+        }
     }
     pdl_trigger();
     tc_fence_before();

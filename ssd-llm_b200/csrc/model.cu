@@ -1068,9 +1068,16 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
         at.q_stride = m->q_rows;
         at.out_stride = m->q_rows;
         at.seq0 = pos0;
+        // the tensor-core kernel writes the output as the Wo GEMM's hi / lo operand (the
+        // QKV GEMM, the last reader of Ah / Al, precedes it on the stream)
+        const bool ao_split = prefill_attention_uses_tc(at);
+        if (ao_split) {
+            at.out_hi = Ah;
+            at.out_lo = Al;
+        }
         SSD_TRY(launch_prefill_attention(m->ctx, at, s, false));
         // h += Wo attn (transformer.rs:350-352)
-        SSD_TRY(prepare_act_split(AO, n, m->q_rows, nullptr, 0.0f, 0, Ah, Al, s, false));
+        if (!ao_split) SSD_TRY(prepare_act_split(AO, n, m->q_rows, nullptr, 0.0f, 0, Ah, Al, s, false));
         g.K = m->q_rows;
         g.N = E;
         g.C = H;

@@ -792,12 +792,16 @@ extern "C" int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const fl
 // the cache rows [0, pos0 + n_q): on the tcgen05 tensor cores when head_dim is 128 and n_q
 // a multiple of 128 (SSD_PREFILL_ATTN=decode forces the per-query kernels), else the
 // batched split-K decode kernels.
-int ssd::launch_prefill_attention(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s, bool pdl) {
+bool ssd::prefill_attention_uses_tc(const AttnArgs& a) {
     const char* e = getenv("SSD_PREFILL_ATTN");
     const bool per_query = e && strcmp(e, "decode") == 0;
-    if (!per_query && a.head_dim == 128 && a.n_q % 128 == 0 && a.q_stride % 4 == 0 &&
-        a.out_stride % 4 == 0 && a.kv_dim % 16 == 0)
-        return launch_attention_prefill_tc(ctx, a, s, pdl);
+    return !per_query && a.head_dim == 128 && a.n_q % 128 == 0 && a.q_stride % 4 == 0 &&
+           a.out_stride % 4 == 0 && a.kv_dim % 16 == 0;
+}
+
+int ssd::launch_prefill_attention(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s, bool pdl) {
+    if (prefill_attention_uses_tc(a)) return launch_attention_prefill_tc(ctx, a, s, pdl);
+    SSD_REQ(!a.out_hi, SSD_ERR_ARG, "fp16 split output needs the tensor-core prefill attention");
     return launch_attention(a, s, pdl);
 }
 

@@ -36,6 +36,11 @@ struct AttnArgs {
     const float* k_new;
     const float* v_new;
     int* status;  // device status word for bounded waits (default: the context's)
+    // Tensor-core prefill kernel only: when set, the output rows are written as fp16 hi /
+    // lo splits (hi = fp16(o), lo = fp16(o - hi), row stride out_stride: the A operand of
+    // the output-projection GEMM) instead of fp32 out.
+    __half* out_hi;
+    __half* out_lo;
 };
 // Causal attention of a prompt batch on the tcgen05 tensor cores (attn_tc.cu): n_q
 // queries (a multiple of 128, head_dim 128) at positions seq0 .., over the cache rows
@@ -44,6 +49,8 @@ int launch_attention_prefill_tc(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s,
 // The prompt-batch attention: the tensor-core kernel where it covers the shape, else
 // launch_attention's batched per-query kernels (which need a.partial).
 int launch_prefill_attention(ssd_ctx* ctx, const AttnArgs& a, cudaStream_t s, bool pdl);
+// Whether launch_prefill_attention takes the tensor-core kernel for these arguments.
+bool prefill_attention_uses_tc(const AttnArgs& a);
 size_t attn_partial_floats(int n_heads, int max_seq, int head_dim);
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 
