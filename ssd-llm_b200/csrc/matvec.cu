@@ -321,22 +321,20 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const u
         for (int r = 0; r < R; r++) q[r] = ch[r].q;
         nib_dot<R, XOFF>(xq, q, eo);
         const float X = b;
+        // 6-bit scale / min of sub-block sb (src/metal/compute.rs:725-733): sb < 4 takes the
+        // low 6 bits of header bytes 4 + sb / 8 + sb; sb >= 4 their top 2 bits joined with
+        // the low / high nibble of byte 12 + sb - 4. Branch-free with lane-constant shifts
+        // and masks (sb = lane & 7 differs within each group of 8 lanes).
         const int sb = lane & 7, sh = 8 * (sb & 3);
+        const uint32_t sa = sb < 4 ? 0u : 6u, ma = sb < 4 ? 63u : 3u, m8 = sb < 4 ? 0u : 15u;
 #pragma unroll
         for (int r = 0; r < R; r++) {
             const uint4 m = ch[r].m;
             const float d = f16_bits_to_f32((uint16_t)(m.x & 0xFFFF));
             const float dmin = f16_bits_to_f32((uint16_t)(m.x >> 16));
-            const uint32_t b0 = (m.y >> sh) & 0xFF, b4 = (m.z >> sh) & 0xFF,
-                           b8 = (m.w >> sh) & 0xFF;
-            uint32_t s6, m6;  // src/metal/compute.rs:725-733
-            if (sb < 4) {
-                s6 = b0 & 0x3F;
-                m6 = b4 & 0x3F;
-            } else {
-                s6 = (b0 >> 6) | ((b8 & 0x0F) << 2);
-                m6 = (b4 >> 6) | ((b8 >> 4) << 2);
-            }
+            const uint32_t yb = m.y >> sh, zb = m.z >> sh, wb = m.w >> sh;
+            const uint32_t s6 = ((yb >> sa) & ma) | ((wb & m8) << 2);
+            const uint32_t m6 = ((zb >> sa) & ma) | (((wb >> 4) & m8) << 2);
             // sum((scale*q - min) x) = scale * sum(q x) - min * X
             const float scale = __fmul_rn(d, (float)s6);
             const float mn = __fmul_rn(dmin, (float)m6);
