@@ -21,7 +21,9 @@ Reported on the same JSON line:
              fraction of the measured HBM peak); `--case NAME` runs one of them alone
   cpu_baseline  the oracle's restatement of the reference layer step on packed Q4_0
              (src/inference/transformer.rs:283-399 with matvec_quantized_cpu), all host
-             cores, one layer timed and extrapolated to 80 layers + logits
+             cores, one layer timed and extrapolated to 80 layers + logits; each of the
+             configs 0-2 kernel cases also carries its own cpu_baseline (the restated
+             matvec or layer step on its shape, 1 thread and all host threads)
 `--impl reference` times that CPU restatement alone (rank 0) and prints its line.
 """
 from __future__ import annotations
@@ -164,6 +166,56 @@ def cpu_token_time(cfg, layer_samples, threads):
     t_logits = (time.perf_counter() - t0) * (cfg["vocab"] / vocab_rows)
     t_layer = statistics.median(t_layers)
     return cfg["n_layers"] * t_layer + t_logits, t_layers, t_logits
+
+
+def cpu_case_baselines(threads):
+    """CPU baselines of the per-kernel cases: the oracle's C
+    restatement of the reference CPU paths on this host, 1 thread (the reference's own CPU
+    paths are single-threaded) and all threads (its row split). Matvec configs: the
+    restated matvec_quantized_cpu (src/metal/compute.rs:680-750, :904-925) on the case's
+    shape; the 7B layer: the restated layer step (transformer.rs:283-399) on packed Q4_0 at
+    2048 cached positions. Median of 3 timed calls after one untimed."""
+    import numpy as np
+    from oracle import oracle as ora
+
+    def timed(fn, reps=3):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    out = {}
+    rng = np.random.default_rng(3)
+    for name, wtype, rows, cols in (("q4_0_4096x4096", Q4_0, 4096, 4096),
+                                    ("q8_0_11008x4096", 8, 11008, 4096),
+                                    ("q8_0_4096x11008", 8, 4096, 11008),
+                                    ("q4_k_11008x4096", 12, 11008, 4096),
+                                    ("q4_k_4096x11008", 12, 4096, 11008)):
+        w = rng.standard_normal((rows, cols), dtype=np.float32)
+        w *= np.float32(0.02)
+        packed = ora.quantize(w, wtype)
+        del w
+        x = rng.standard_normal(cols, dtype=np.float32)
+        t1 = timed(lambda: ora.matvec_quantized(packed, x, rows, cols, wtype, threads=1))
+        tn = timed(lambda: ora.matvec_quantized(packed, x, rows, cols, wtype, threads=threads))
+        out[name] = {"us_1thread": round(t1 * 1e6, 1), "us_all_threads": round(tn * 1e6, 1),
+                     "cores": threads, "kind": "port", "cpu": cpu_model_name(),
+                     "sample": "the whole matvec, median of 3 calls"}
+    cfg = dict(n_embd=4096, n_head=32, n_head_kv=32, head_dim=128, n_ff=11008,
+               kv_capacity=2049, theta=1e4, eps=1e-5)
+    layer, (kc, ks, vc, vs), h = cpu_layer_inputs(cfg, seed=5)
+    res = {}
+    for t in (1, threads):
+        res[t] = timed(lambda: layer.step(h.copy(), 2048, kc, ks, vc, vs, mode=1, threads=t))
+    out["layer_7b_q4_0"] = {"us_1thread": round(res[1] * 1e6, 1),
+                            "us_all_threads": round(res[threads] * 1e6, 1), "cores": threads,
+                            "kind": "port", "cpu": cpu_model_name(),
+                            "sample": "one 7B-shape layer step (packed Q4_0, INT8 KV at 2048), "
+                                      "median of 3"}
+    return out
 
 
 def cpu_model_name():
@@ -327,7 +379,7 @@ def case_layer_7b(ctx, torch, ssdllm, peak, n_layers=8, reps=10):
     return {"shape": "llama2-7b layer, Q4_0, INT8 KV 2048", "algorithmic_bytes": alg,
             "us_per_layer": round(us_layer, 3), "gbs": round(alg / us_layer / 1e3, 1),
             "frac_of_peak": round(alg / us_layer / 1e3 / peak, 4),
-            "launches_per_layer": 5, "model_layers_timed": n_layers, "launches_per_step": launches}
+            "launches_per_layer": 6, "model_layers_timed": n_layers, "launches_per_step": launches}
 
 
 def case_swiglu_70b(ctx, torch, ssdllm, peak, reps=10):
@@ -654,6 +706,10 @@ def run_cuda(args):
                "cpu": cpu_model_name(),
                "sample": f"{len(t_layers)} timed 70B-shape layer steps (packed Q4_0, INT8 KV "
                          f"at {PROMPT}) x 80 layers + vocab matvec; extrapolated"}
+        if k0:  # the per-kernel cases' own CPU baselines
+            for name, v in cpu_case_baselines(threads).items():
+                if name in k0:
+                    k0[name]["cpu_baseline"] = v
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
