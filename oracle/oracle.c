@@ -85,6 +85,7 @@ size_t ora_row_bytes(int type, int64_t n) {
         case ORA_Q4_0: return (size_t)(n / 32) * 18;
         case ORA_Q8_0: return (size_t)(n / 32) * 34;
         case ORA_Q4_K: return (size_t)(n / 256) * 144;
+        case ORA_Q6_K: return (size_t)(n / 256) * 210;
         default: return 0;
     }
 }
@@ -215,6 +216,17 @@ static inline void q4k_scale_min(const uint8_t* sc, int sb, uint8_t* s, uint8_t*
 
 /* ---------------------------------------------------------- dequantize */
 
+/* Q6_K super-block (256 weights, 210 bytes) as matvec_q6_k_cpu reads it
+ * (src/metal/compute.rs:752-790): ql[128] low nibbles (element idx: byte idx / 2, high
+ * nibble when idx is odd), qh[64] 2-bit high parts (byte idx / 4, bits 2 (idx % 4)),
+ * 16 int8 scales (one per 16 elements), f16 d at byte 208. q = (high2 << 4 | low4) - 32. */
+static int q6k_q(const uint8_t* blk, int idx) {
+    const uint8_t ql_byte = blk[idx / 2];
+    const int low4 = (idx & 1) ? (ql_byte >> 4) & 0x0F : ql_byte & 0x0F;
+    const int high2 = (blk[128 + idx / 4] >> ((idx % 4) * 2)) & 0x03;
+    return ((high2 << 4) | low4) - 32;
+}
+
 int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
     switch (type) {
         case ORA_F32: memcpy(out, w, (size_t)n * 4); return 0;
@@ -238,6 +250,17 @@ int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
                     int hi = (int)((byte >> 4) & 0x0F) - 8;
                     out[b * 32 + 2 * j] = (float)lo * scale;
                     out[b * 32 + 2 * j + 1] = (float)hi * scale;
+                }
+            }
+            return 0;
+        case ORA_Q6_K: /* element value of matvec_q6_k_cpu src/metal/compute.rs:768-785 */
+            for (int64_t b = 0; b < n / 256; b++) {
+                const uint8_t* blk = w + b * 210;
+                const float d = rd_f16(blk + 208);
+                for (int sb = 0; sb < 16; sb++) {
+                    const float sc = d * (float)(int8_t)blk[192 + sb];
+                    for (int j = 0; j < 16; j++)
+                        out[b * 256 + sb * 16 + j] = sc * (float)q6k_q(blk, sb * 16 + j);
                 }
             }
             return 0;
@@ -329,6 +352,26 @@ static float row_q4_k(const uint8_t* w, const float* x, int in_dim, int row) {
     return sum;
 }
 
+/* matvec_q6_k_cpu src/metal/compute.rs:752-790, one row: sum += (d * scale) * q * x in
+ * element order. */
+static float row_q6_k(const uint8_t* w, const float* x, int in_dim, int row) {
+    int bpr = in_dim / 256;
+    const uint8_t* r = w + (size_t)row * bpr * 210;
+    float sum = 0.0f;
+    for (int b = 0; b < bpr; b++) {
+        const uint8_t* blk = r + (size_t)b * 210;
+        const float d = rd_f16(blk + 208);
+        for (int sb = 0; sb < 16; sb++) {
+            const float sc = d * (float)(int8_t)blk[192 + sb];
+            for (int j = 0; j < 16; j++) {
+                const int idx = sb * 16 + j;
+                sum += sc * (float)q6k_q(blk, idx) * x[b * 256 + idx];
+            }
+        }
+    }
+    return sum;
+}
+
 /* f16 matvec src/metal/compute.rs:2272-2285, one row. */
 static float row_f16(const uint8_t* w, const float* x, int in_dim, int row) {
     const uint8_t* r = w + (size_t)row * in_dim * 2;
@@ -365,6 +408,7 @@ static row_fn pick_row(int type) {
         case ORA_Q4_0: return row_q4_0;
         case ORA_Q8_0: return row_q8_0;
         case ORA_Q4_K: return row_q4_k;
+        case ORA_Q6_K: return row_q6_k;
         case ORA_F16: return row_f16;
         default: return NULL;
     }
