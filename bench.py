@@ -321,6 +321,40 @@ def case_matvec(ctx, torch, ssdllm, peak, wtype, rows, cols, reps=20):
             "rotating_copies": copies, **best, "variants": res}
 
 
+def case_matvec_q6k(ctx, torch, ssdllm, peak, rows=11008, cols=4096, reps=20):
+    """Q6_K dequant-matvec at a config-1 shape. No device quantizer exists for Q6_K, so the
+    rotating copies are random reference blocks (every bit pattern is a valid block; d
+    set in a typical range) uploaded through ssd_weight_upload."""
+    import numpy as np
+    Q6_K = 14
+    nb = cols // 256
+    raw_bytes = rows * nb * 210
+    copies = min(16, max(2, -(-int(2.2 * L2_BYTES) // raw_bytes)))
+    rng = np.random.default_rng(11)
+    ws = []
+    for _ in range(copies):
+        raw = rng.integers(0, 256, (rows, nb * 210), dtype=np.uint8)
+        dv = rng.uniform(2e-5, 2e-4, (rows, nb)).astype(np.float16).view(np.uint16)
+        raw[:, 208::210] = (dv & 0xFF).astype(np.uint8)
+        raw[:, 209::210] = (dv >> 8).astype(np.uint8)
+        ws.append(ssdllm.Weight.upload(ctx, raw, Q6_K, rows, cols))
+    x = torch.randn(cols, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+    y = torch.zeros(rows, device="cuda")
+    n = max(copies, 64 // copies * copies)
+    # bytes the kernel streams: 32 B of signed q per 32 weights + a 4-byte scale word
+    alg = rows * (cols // 32) * 36 + cols * 4 + rows * 4
+    ctx.set_pdl(True)
+    us = _graph_time(torch, [lambda w=ws[i % copies]: ssdllm.matvec(ctx, w, x, y)
+                             for i in range(n)], reps)
+    ctx.set_pdl(False)
+    for w in ws:
+        w.free()
+    return {"type": "Q6_K", "shape": [rows, cols], "algorithmic_bytes": alg,
+            "reference_block_bytes": rows * nb * 210, "rotating_copies": copies,
+            "us_per_launch": round(us, 3), "gbs": round(alg / us / 1e3, 1),
+            "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
+
+
 def case_attention(ctx, torch, ssdllm, peak, n_head=64, n_head_kv=8, head_dim=128, seq=4096,
                    reps=20):
     """Split-K flash-decode over the INT8 KV cache (70B shape: 64 q / 8 kv heads,
@@ -553,6 +587,7 @@ CASES = {
     "q8_0_4096x11008": lambda c, t, s, p: case_matvec(c, t, s, p, 8, 4096, 11008),
     "q4_k_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 12, 11008, 4096),
     "q4_k_4096x11008": lambda c, t, s, p: case_matvec(c, t, s, p, 12, 4096, 11008),
+    "q6_k_11008x4096": case_matvec_q6k,
     "swiglu_q4_0_70b": case_swiglu_70b,
     "attn_int8_70b_4096": case_attention,
     "layer_7b_q4_0": case_layer_7b,

@@ -55,6 +55,11 @@ extern "C" {
 #define SSD_TYPE_Q4_0 2
 #define SSD_TYPE_Q8_0 8
 #define SSD_TYPE_Q4_K 12
+/* Q6_K in the reference's own block layout (matvec_q6_k_cpu, src/metal/compute.rs:752-790):
+ * 256 weights in 210 bytes, ql[128] low nibbles, qh[64] 2-bit high parts, 16 int8 scales,
+ * f16 d; weight = (d * scale) * ((high2 << 4 | low4) - 32). Accepted by ssd_weight_upload,
+ * ssd_dequantize, the matvec entry points and the prefill matmul. */
+#define SSD_TYPE_Q6_K 14
 
 typedef struct ssd_ctx ssd_ctx;
 typedef struct ssd_weight ssd_weight;

@@ -143,6 +143,22 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int64_t nblo
         for (int j = 0; j < 32; j++) d[j] = s[2 + j];
         meta[2 * i] = s[0];
         meta[2 * i + 1] = s[1];
+    } else if (type == SSD_TYPE_Q6_K) {  // one signed byte per weight + a word per 32
+        const uint8_t* s = raw + i * 210;
+        int8_t* d = reinterpret_cast<int8_t*>(qs) + i * 256;
+        for (int idx = 0; idx < 256; idx++) {  // compute.rs:771-780
+            const uint8_t qlb = s[idx / 2];
+            const int low4 = (idx & 1) ? (qlb >> 4) & 0x0F : qlb & 0x0F;
+            const int high2 = (s[128 + idx / 4] >> ((idx % 4) * 2)) & 0x03;
+            d[idx] = (int8_t)(((high2 << 4) | low4) - 32);
+        }
+        for (int c = 0; c < 8; c++) {
+            uint8_t* m = meta + (i * 8 + c) * 4;
+            m[0] = s[192 + 2 * c];
+            m[1] = s[192 + 2 * c + 1];
+            m[2] = s[208];
+            m[3] = s[209];
+        }
     } else {  // Q4_K
         const uint8_t* s = raw + i * 144;
         uint8_t* d = qs + i * 128;
@@ -167,6 +183,21 @@ __global__ void k_unpack(const uint8_t* __restrict__ qs, const uint8_t* __restri
         d[0] = meta[2 * i];
         d[1] = meta[2 * i + 1];
         for (int j = 0; j < 32; j++) d[2 + j] = qs[i * 32 + j];
+    } else if (type == SSD_TYPE_Q6_K) {  // exact inverse of k_repack
+        uint8_t* d = raw + i * 210;
+        for (int j = 0; j < 192; j++) d[j] = 0;
+        const int8_t* q = reinterpret_cast<const int8_t*>(qs) + i * 256;
+        for (int idx = 0; idx < 256; idx++) {
+            const int v = q[idx] + 32;
+            d[idx / 2] |= (uint8_t)((v & 0x0F) << (4 * (idx & 1)));
+            d[128 + idx / 4] |= (uint8_t)(((v >> 4) & 0x03) << (2 * (idx % 4)));
+        }
+        for (int c = 0; c < 8; c++) {
+            d[192 + 2 * c] = meta[(i * 8 + c) * 4];
+            d[192 + 2 * c + 1] = meta[(i * 8 + c) * 4 + 1];
+        }
+        d[208] = meta[i * 32 + 2];
+        d[209] = meta[i * 32 + 3];
     } else {
         uint8_t* d = raw + i * 144;
         for (int j = 0; j < 16; j++) d[j] = meta[i * 16 + j];
@@ -481,8 +512,9 @@ namespace ssd {
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
-                type == SSD_TYPE_F32,
-            SSD_ERR_TYPE, "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, F32=0)", type);
+                type == SSD_TYPE_Q6_K || type == SSD_TYPE_F32,
+            SSD_ERR_TYPE, "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q6_K=14, F32=0)",
+            type);
     SSD_REQ(rows > 0 && cols > 0, SSD_ERR_SHAPE, "empty tensor %dx%d", rows, cols);
     int bs = type_block(type);
     SSD_REQ(cols % bs == 0, SSD_ERR_SHAPE, "cols %d not a multiple of block %d", cols, bs);
@@ -497,6 +529,9 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     } else if (type == SSD_TYPE_Q4_K) {
         qs_bytes = nb * 128;
         meta_bytes = nb * 16;
+    } else if (type == SSD_TYPE_Q6_K) {
+        qs_bytes = nb * 256;
+        meta_bytes = nb * 32;
     } else {
         qs_bytes = (size_t)rows * cols * 4;
         meta_bytes = 0;

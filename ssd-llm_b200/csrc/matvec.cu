@@ -63,6 +63,11 @@ struct Chunk<SSD_TYPE_Q4_K> {
     uint4 q;
     uint4 m;
 };
+template <>
+struct Chunk<SSD_TYPE_Q6_K> {
+    uint4 q0, q1;  // 32 signed bytes q - 32
+    uint32_t m;    // int8 scale of elements 0-15, of 16-31, f16 d
+};
 
 // Byte pointers of one row of the library layout (see ssd_weight in common.cuh).
 template <int FMT, int MAP>
@@ -79,6 +84,9 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
     } else if constexpr (FMT == SSD_TYPE_Q8_0) {
         qs = q + (size_t)lr * nc * 32;
         meta = m + (size_t)lr * nc * 2;
+    } else if constexpr (FMT == SSD_TYPE_Q6_K) {
+        qs = q + (size_t)lr * nc * 32;
+        meta = m + (size_t)lr * nc * 4;
     } else {
         qs = q + (size_t)lr * nc * 16;
         meta = m + (size_t)lr * (nc >> 3) * 16;
@@ -92,7 +100,7 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
 // the aligned 4-byte word holding the chunk's f16 d; Q4_K: the super-block's 16 bytes).
 template <int FMT>
 struct Slot {
-    static constexpr int QB = FMT == SSD_TYPE_Q8_0 ? 32 : 16;
+    static constexpr int QB = FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K ? 32 : 16;
     static constexpr int MB = FMT == SSD_TYPE_Q4_K ? 16 : 4;
 };
 template <int FMT, int R, int U>
@@ -114,7 +122,7 @@ template <int FMT>
 __device__ __forceinline__ void issue_chunk(uint32_t qdst, uint32_t mdst, const uint8_t* qp,
                                             const uint8_t* mp) {
     cp_async16_s(qdst, qp);
-    if constexpr (FMT == SSD_TYPE_Q8_0) cp_async16_s(qdst + 16, qp + 16);
+    if constexpr (FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K) cp_async16_s(qdst + 16, qp + 16);
     if constexpr (FMT == SSD_TYPE_Q4_K)
         cp_async16_s(mdst, mp);
     else
@@ -132,6 +140,10 @@ __device__ __forceinline__ void read_chunk(Chunk<FMT>& k, const uint8_t* qsrc, c
         k.q0 = *reinterpret_cast<const uint4*>(qsrc);
         k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
         k.d = *reinterpret_cast<const uint16_t*>(msrc);
+    } else if constexpr (FMT == SSD_TYPE_Q6_K) {
+        k.q0 = *reinterpret_cast<const uint4*>(qsrc);
+        k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
+        k.m = *reinterpret_cast<const uint32_t*>(msrc);
     } else {
         k.q = *reinterpret_cast<const uint4*>(qsrc);
         k.m = *reinterpret_cast<const uint4*>(msrc);
@@ -139,14 +151,27 @@ __device__ __forceinline__ void read_chunk(Chunk<FMT>& k, const uint8_t* qsrc, c
 }
 // Bytes by which the stage pointers advance per chunk step of 32 chunks.
 template <int FMT>
-__host__ __device__ constexpr int q_step() { return FMT == SSD_TYPE_Q8_0 ? 1024 : 512; }
+__host__ __device__ constexpr int q_step() {
+    return FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K ? 1024 : 512;
+}
+// Scale bytes per chunk (Q4_K: 16 B per 8 chunks) and per chunk step of 32 chunks.
 template <int FMT>
-__host__ __device__ constexpr int m_step() { return 64; }
+__host__ __device__ constexpr int m_chunk() { return FMT == SSD_TYPE_Q6_K ? 4 : 2; }
+template <int FMT>
+__host__ __device__ constexpr int m_step() { return 32 * m_chunk<FMT>(); }
+// Q4_0 / Q8_0 copy the aligned word holding a chunk's 2-byte d: the half to read varies.
+template <int FMT>
+__host__ __device__ constexpr bool has_doff() { return FMT == SSD_TYPE_Q4_0 || FMT == SSD_TYPE_Q8_0; }
+// Per-chunk bias sums staged beside x'': one per chunk, Q6_K one per 16-element half.
+template <int FMT>
+__host__ __device__ constexpr int csum_per_chunk() { return FMT == SSD_TYPE_Q6_K ? 2 : 1; }
 // Offset of lane l's chunk l within a row (qs, meta).
 template <int FMT>
-__device__ __forceinline__ size_t q_lane(int l) { return (size_t)l * (FMT == SSD_TYPE_Q8_0 ? 32 : 16); }
+__device__ __forceinline__ size_t q_lane(int l) { return (size_t)l * Slot<FMT>::QB; }
 template <int FMT>
-__device__ __forceinline__ size_t m_lane(int l) { return FMT == SSD_TYPE_Q4_K ? (size_t)(l >> 3) * 16 : (size_t)l * 2; }
+__device__ __forceinline__ size_t m_lane(int l) {
+    return FMT == SSD_TYPE_Q4_K ? (size_t)(l >> 3) * 16 : (size_t)l * m_chunk<FMT>();
+}
 
 __device__ __forceinline__ uint32_t word_of(const uint4& q, int m) {
     return m == 0 ? q.x : (m == 1 ? q.y : (m == 2 ? q.z : q.w));
@@ -288,7 +313,7 @@ __device__ __forceinline__ void nib_dot(const uint32_t (&xq)[8], const uint4 (&q
 // this chunk; the chunk's x'' unit u is at shared address xq[u] + XOFF.
 template <int FMT, int R, int XOFF>
 __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const uint32_t (&xq)[8],
-                                              float b, int lane, float (&acc)[R]) {
+                                              float b, float b2, int lane, float (&acc)[R]) {
     uint64_t eo[R];
     if constexpr (FMT == SSD_TYPE_Q4_0) {
         uint4 q[R];
@@ -315,6 +340,36 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const u
 #pragma unroll
         for (int r = 0; r < R; r++)
             acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), sum_f2(eo[r]) + b, acc[r]);
+    } else if constexpr (FMT == SSD_TYPE_Q6_K) {
+        // signed bytes q - 32 decoded as Q8_0's (q + 128 read unsigned); elements 0-15 and
+        // 16-31 have their own scale, so each half has its own pair and bias (b, b2):
+        // sum (d * sc_h) * q * x = (d * sc_h) * (sum q x) per half (compute.rs:768-785)
+        uint64_t eh[R];
+#pragma unroll
+        for (int m = 0; m < 8; m++) {  // unit m = elements 4m..4m+3
+            uint64_t x01, x23;
+            lds_x<XOFF>(xq[m], x01, x23);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const uint32_t w = word_of(m < 4 ? ch[r].q0 : ch[r].q1, m & 3);
+                if (m == 0)
+                    byte_word<true>(eo[r], w, x01, x23);
+                else if (m < 4)
+                    byte_word<false>(eo[r], w, x01, x23);
+                else if (m == 4)
+                    byte_word<true>(eh[r], w, x01, x23);
+                else
+                    byte_word<false>(eh[r], w, x01, x23);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const uint32_t mw = ch[r].m;
+            const float d = f16_bits_to_f32((uint16_t)(mw >> 16));
+            const float s0 = __fmul_rn(d, (float)(int)(int8_t)(mw & 0xFF));
+            const float s1 = __fmul_rn(d, (float)(int)(int8_t)((mw >> 8) & 0xFF));
+            acc[r] = fmaf(s1, sum_f2(eh[r]) + b2, fmaf(s0, sum_f2(eo[r]) + b, acc[r]));
+        }
     } else {  // Q4_K: this lane's sub-block index is c & 7 == lane & 7
         uint4 q[R];
 #pragma unroll
@@ -354,7 +409,8 @@ struct SmemPlan {
     int nc, xrows;  // chunks, staged rows (multiple of kVecBoxRows)
     size_t xs, csum, red, bar, rope, ring, total;
 };
-__host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_warp) {
+__host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_warp,
+                                              int csum_per_chunk = 1) {
     SmemPlan p;
     p.nc = cols >> 5;
     p.xrows = (p.nc + kVecBoxRows - 1) / kVecBoxRows * kVecBoxRows;
@@ -362,7 +418,7 @@ __host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_war
     p.xs = o;
     o += (size_t)p.xrows * 128;
     p.csum = o;
-    o += ((size_t)p.nc * 4 + 15) & ~(size_t)15;
+    o += ((size_t)p.nc * 4 * csum_per_chunk + 15) & ~(size_t)15;
     p.red = o;
     o += 64 * 4 + (size_t)nw * 8;
     p.bar = o;
@@ -379,7 +435,7 @@ __host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_war
 // Power-of-two pre-scale of element position k (0..7) within a 32-bit word.
 template <int FMT>
 __device__ __forceinline__ float pos_scale(int k) {
-    const int s = FMT == SSD_TYPE_Q8_0 ? byte_pos(k & 3) : nib_pos(k);
+    const int s = FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K ? byte_pos(k & 3) : nib_pos(k);
     return __uint_as_float((uint32_t)(127 + kScaleBias - s) << 23);
 }
 
@@ -398,7 +454,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     constexpr int kMap = epi_map(EPI);  // launch_matvec checks a.map against it
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    const SmemPlan P = smem_plan(a.cols, NW, kStages * SB);
+    const SmemPlan P = smem_plan(a.cols, NW, kStages * SB, csum_per_chunk<FMT>());
     float4* xs4 = reinterpret_cast<float4*>(base + P.xs);
     float* csum = reinterpret_cast<float*>(base + P.csum);
     float* red = reinterpret_cast<float*>(base + P.red);
@@ -477,7 +533,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
                         issue_chunk<FMT>(ring_qs + ist + (r * U + u) * 32 * QB,
                                          ring_ms + ist + (r * U + u) * 32 * MB,
                                          lq[r] + u * q_step<FMT>() + dc * (q_step<FMT>() / 32),
-                                         lm[r] + u * m_step<FMT>() + dc * 2);
+                                         lm[r] + u * m_step<FMT>() + dc * m_chunk<FMT>());
                 }
             }
 #pragma unroll
@@ -506,12 +562,17 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
         float t = (v.x + v.y) + (v.z + v.w);
         t += __shfl_xor_sync(gmask, t, 1);
         t += __shfl_xor_sync(gmask, t, 2);
-        t += __shfl_xor_sync(gmask, t, 4);
-        if ((i & 7) == 0) {
-            const float X = __fmul_rn(t, 1.0f / kUnscale);
-            csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X : (FMT == SSD_TYPE_Q8_0 ? -128.0f * X : X);
+        if constexpr (FMT == SSD_TYPE_Q6_K) {  // per 16-element half: units 0-3, 4-7
+            if ((i & 3) == 0) csum[2 * c + ((i >> 2) & 1)] = -128.0f * __fmul_rn(t, 1.0f / kUnscale);
+        } else {
+            t += __shfl_xor_sync(gmask, t, 4);
+            if ((i & 7) == 0) {
+                const float X = __fmul_rn(t, 1.0f / kUnscale);
+                csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X : (FMT == SSD_TYPE_Q8_0 ? -128.0f * X : X);
+            }
         }
-        const int k0 = (FMT == SSD_TYPE_Q8_0) ? 0 : 4 * (i & 1);  // word position of v.x
+        // word position of v.x
+        const int k0 = (FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K) ? 0 : 4 * (i & 1);
         v.x = __fmul_rn(v.x, pos_scale<FMT>(k0 + 0));
         v.y = __fmul_rn(v.y, pos_scale<FMT>(k0 + 1));
         v.z = __fmul_rn(v.z, pos_scale<FMT>(k0 + 2));
@@ -539,7 +600,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             doff[r] = (((lr & 1) * (nc & 1) + lane) & 1) * 2;
         }
     };
-    if (FMT != SSD_TYPE_Q4_K && crg < n_rg) set_doff();
+    if (has_doff<FMT>() && crg < n_rg) set_doff();
     int cst_off = 0;  // byte offset of the stage being computed
     // this lane's shared address of x'' unit u of its chunk c = lane (mod 32): row c of
     // 128 bytes, unit u at slot u ^ (c & 7) = u ^ (lane & 7); chunk c + 32 t is 4096 t
@@ -555,15 +616,17 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
         uint32_t xst[8];  // x'' units of this stage's first chunk step
 #pragma unroll
         for (int u = 0; u < 8; u++) xst[u] = xp[u] + (uint32_t)cst * (U * 4096);
-        const float* cs = csum + lane + 32 * U * cst;
+        const float* cs = csum + (lane + 32 * U * cst) * csum_per_chunk<FMT>();
         auto do_u = [&](auto uc) {  // chunk step u (a compile-time constant)
             constexpr int u = decltype(uc)::value;
             Chunk<FMT> ch[R];
 #pragma unroll
             for (int r = 0; r < R; r++)
                 read_chunk<FMT>(ch[r], sq + (r * U + u) * 32 * QB,
-                                sm + (r * U + u) * 32 * MB + (FMT == SSD_TYPE_Q4_K ? 0 : doff[r]));
-            compute_chunk<FMT, R, u * 4096>(ch, xst, cs[32 * u], lane, acc);
+                                sm + (r * U + u) * 32 * MB + (has_doff<FMT>() ? doff[r] : 0));
+            constexpr int CPC = csum_per_chunk<FMT>();
+            compute_chunk<FMT, R, u * 4096>(ch, xst, cs[32 * u * CPC], CPC == 2 ? cs[32 * u * CPC + 1] : 0.0f,
+                                            lane, acc);
         };
         using U0 = std::integral_constant<int, 0>;
         using U1 = std::integral_constant<int, (U > 1 ? 1 : 0)>;
@@ -582,7 +645,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
         cst = 0;
         const int v0 = crg * R;
         crg += W;
-        if (FMT != SSD_TYPE_Q4_K && crg < n_rg) set_doff();
+        if (has_doff<FMT>() && crg < n_rg) set_doff();
         float res[R];
 #pragma unroll
         for (int r = 0; r < R; r++) {
@@ -701,7 +764,8 @@ static Cfg env_cfg() {
 template <int FMT, int EPI, int R, int U, int NW>
 static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     auto kern = k_matvec<FMT, EPI, R, U, NW>;
-    const SmemPlan P = smem_plan(a.cols, NW, n_stages<NW>() * stage_bytes<FMT, R, U>());
+    const SmemPlan P =
+        smem_plan(a.cols, NW, n_stages<NW>() * stage_bytes<FMT, R, U>(), csum_per_chunk<FMT>());
     SSD_REQ(P.total <= ctx->smem_optin, SSD_ERR_SHAPE,
             "cols %d too large for shared-memory staging (%zu bytes)", a.cols, P.total);
     int nb = 0;
@@ -747,11 +811,13 @@ static int launch_fmt_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pd
         return e && e[0] == '1';
     }();
     if (coresident &&
-        2 * (smem_plan(a.cols, 8, n_stages<8>() * stage_bytes<FMT, 2, U>()).total + 1024) <=
+        2 * (smem_plan(a.cols, 8, n_stages<8>() * stage_bytes<FMT, 2, U>(), csum_per_chunk<FMT>())
+                 .total +
+             1024) <=
             ctx->smem_per_sm)
         return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);
     const int ring = n_stages<16>() * stage_bytes<FMT, 2, U>();
-    if (smem_plan(a.cols, 16, ring).total <= ctx->smem_optin)
+    if (smem_plan(a.cols, 16, ring, csum_per_chunk<FMT>()).total <= ctx->smem_optin)
         return launch_t<FMT, EPI, 2, U, 16>(ctx, a, s, pdl);
     if constexpr (U == 2) {  // wide rows (x'' over 100 KB): halve the stage, keep 16 warps
         if (smem_plan(a.cols, 16, n_stages<16>() * stage_bytes<FMT, 2, 1>()).total <=
@@ -824,8 +890,11 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
         case SSD_TYPE_Q4_K:
             SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q4_K cols %d not a multiple of 256", a.cols);
             return launch_fmt<SSD_TYPE_Q4_K>(ctx, epi, a, s, pdl);
+        case SSD_TYPE_Q6_K:
+            SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q6_K cols %d not a multiple of 256", a.cols);
+            return launch_fmt<SSD_TYPE_Q6_K>(ctx, epi, a, s, pdl);
         default:
-            set_error("matvec: ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12)", type);
+            set_error("matvec: ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q6_K=14)", type);
             return SSD_ERR_TYPE;
     }
 }
@@ -836,7 +905,8 @@ using namespace ssd;
 
 static int check_w(const ssd_weight* w) {
     SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
-    SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K,
+    SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
+                w->type == SSD_TYPE_Q6_K,
             SSD_ERR_TYPE, "matvec: ggml type %d not supported", w->type);
     return SSD_OK;
 }
@@ -946,8 +1016,9 @@ extern "C" int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, siz
                                          int type) {
     SSD_TRY(check_ctx(ctx));
     SSD_REQ(w_raw && x && y, SSD_ERR_ARG, "null pointer");
-    SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K, SSD_ERR_TYPE,
-            "matvec_quantized: ggml type %d not supported", type);
+    SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
+                type == SSD_TYPE_Q6_K,
+            SSD_ERR_TYPE, "matvec_quantized: ggml type %d not supported", type);
     ssd_weight* w = nullptr;
     SSD_TRY(ssd_weight_upload(ctx, w_raw, w_bytes, type, out_dim, in_dim, &w));
     size_t xb = (size_t)in_dim * 4, yb = (size_t)out_dim * 4;

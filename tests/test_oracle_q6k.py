@@ -115,3 +115,11 @@ def test_dequant_agrees_with_matvec():
     w = ora.dequantize(raw, ora.Q6_K, 1024)
     y = ora.matvec_quantized(raw, x, 1, 1024, ora.Q6_K)
     assert abs(float(y[0]) - float(np.dot(w.astype(np.float64), x))) <= 1e-4 * np.abs(w * x).sum()
+
+
+def test_library_row_bytes_matches_oracle():
+    """The library's host-side size rule (no GPU needed) agrees with the oracle's."""
+    import ssdllm
+    for cols in (256, 4096, 11008 // 256 * 256):
+        assert ssdllm.row_bytes(ora.Q6_K, cols) == ora.row_bytes(ora.Q6_K, cols)
+    assert ssdllm.row_bytes(ora.Q6_K, 128) == 0  # not a whole super-block
