@@ -157,7 +157,8 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     SSD_REQ((c->n_embd / N) % bs == 0 && (c->n_ff / N) % bs == 0, SSD_ERR_SHAPE,
             "column shards must be whole %d-wide blocks", bs);
     SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
-                c->embd_type == SSD_TYPE_Q8_0,
+                c->embd_type == SSD_TYPE_Q8_0 || c->embd_type == SSD_TYPE_Q4_K ||
+                c->embd_type == SSD_TYPE_Q6_K,
             SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
     SSD_REQ(type_block(c->out_type) == 32 || type_block(c->out_type) == 256, SSD_ERR_TYPE,
             "output type %d not supported", c->out_type);

@@ -586,22 +586,12 @@ __global__ void __launch_bounds__(256) k_embed(const ssd_weight e, const int32_t
     hidden += (size_t)blockIdx.x * e.cols;
     t = t < 0 ? 0 : (t >= e.rows ? e.rows - 1 : t);  // out-of-range ids clamp (no OOB read)
     const int n = e.cols;
-    for (int i = threadIdx.x; i < n; i += 256) {
-        float val;
-        if (e.type == SSD_TYPE_F32) {
-            val = reinterpret_cast<const float*>(e.qs)[(size_t)t * n + i];
-        } else if (e.type == SSD_TYPE_Q4_0) {
-            const size_t blk = (size_t)t * (n / 32) + i / 32;
-            const int j = i % 32;
-            const uint8_t byte = e.qs[blk * 16 + j / 2];
-            const int q = (j & 1) ? (byte >> 4) : (byte & 0x0F);
-            val = __fmul_rn((float)(q - 8), f16_bits_to_f32(reinterpret_cast<const uint16_t*>(e.meta)[blk]));
-        } else {  // Q8_0
-            const size_t blk = (size_t)t * (n / 32) + i / 32;
-            const int8_t q = reinterpret_cast<const int8_t*>(e.qs)[blk * 32 + i % 32];
-            val = __fmul_rn((float)q, f16_bits_to_f32(reinterpret_cast<const uint16_t*>(e.meta)[blk]));
-        }
-        hidden[i] = val;
+    // dequant8: the element values of the matvec decoders (bit-exact dequantization)
+    for (int i = 8 * threadIdx.x; i < n; i += 8 * 256) {
+        float v[8];
+        dequant8(e, (int64_t)t * n + i, v);
+#pragma unroll
+        for (int j = 0; j < 8; j++) hidden[i + j] = v[j];
     }
 }
 
@@ -617,16 +607,18 @@ __global__ void k_finalize(unsigned long long* key, int32_t* token, int* pos,
 
 int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
                  bool pdl) {
-    SSD_REQ(emb->type == SSD_TYPE_F32 || emb->type == SSD_TYPE_Q4_0 || emb->type == SSD_TYPE_Q8_0,
-            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0)", emb->type);
+    SSD_REQ(type_block(emb->type) != 0 && emb->type != SSD_TYPE_F16 && emb->cols % 8 == 0,
+            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0, Q4_K, Q6_K)",
+            emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(1), dim3(256), 0, s, pdl, *emb, token_dev, hidden));
     return SSD_OK;
 }
 
 int launch_embed_rows(const ssd_weight* emb, const int32_t* tokens_dev, int n, float* hidden,
                       cudaStream_t s) {
-    SSD_REQ(emb->type == SSD_TYPE_F32 || emb->type == SSD_TYPE_Q4_0 || emb->type == SSD_TYPE_Q8_0,
-            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0)", emb->type);
+    SSD_REQ(type_block(emb->type) != 0 && emb->type != SSD_TYPE_F16 && emb->cols % 8 == 0,
+            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0, Q4_K, Q6_K)",
+            emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(n), dim3(256), 0, s, false, *emb, tokens_dev, hidden));
     return SSD_OK;
 }

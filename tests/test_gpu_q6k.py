@@ -117,3 +117,52 @@ def test_rejects_cols_not_multiple_of_256(ctx):
     rng = np.random.default_rng(73)
     with pytest.raises(ssdllm.SsdError):
         ssdllm.Weight.upload(ctx, rng.integers(0, 256, 210, dtype=np.uint8), Q6_K, 1, 128)
+
+
+def test_q6k_model_greedy_decode_matches_oracle(ctx):
+    """A model whose layer weights, output head and token embedding are all Q6_K (as in a
+    Q6_K GGUF file): 32 greedy tokens equal the oracle's decode loop (a near-tie below
+    fp32 reordering noise may end the comparison early)."""
+    from test_gpu_model import LAYER_NAMES, build_model, oracle_layers
+    E, nh, nkv, hd, F, vocab, nl = 256, 4, 2, 64, 512, 512, 2
+    cfg = dict(n_layers=nl, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=vocab,
+               wtype=Q6_K, out_type=Q6_K, embd_type=Q6_K, kv_capacity=48, theta=1e4, eps=1e-5,
+               tp_rank=0, tp_size=1)
+    rng = np.random.default_rng(74)
+    shapes = {"attn_q": (nh * hd, E), "attn_k": (nkv * hd, E), "attn_v": (nkv * hd, E),
+              "attn_output": (E, E), "ffn_gate": (F, E), "ffn_up": (F, E), "ffn_down": (E, F)}
+    layers = []
+    for _ in range(nl):
+        L = {n: raw_q6k(rng, *s) for n, s in shapes.items()}
+        L["attn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+        L["ffn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+        layers.append(L)
+    glob = {"token_embd": raw_q6k(rng, vocab, E), "output": raw_q6k(rng, vocab, E),
+            "output_norm": (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)}
+    assert set(LAYER_NAMES) <= set(layers[0])
+    m = build_model(ctx, cfg, layers, glob)
+    m.set_position(0)
+    gpu, t = [], 5
+    for _ in range(32):
+        t = m.decode_token(t, use_graph=True)
+        gpu.append(t)
+    m.free()
+
+    OL = oracle_layers(cfg, layers)
+    emb = ora.dequantize(glob["token_embd"], Q6_K, vocab * E).reshape(vocab, E)
+    out_w = ora.dequantize(glob["output"], Q6_K, vocab * E).reshape(vocab, E)
+    kvd = nkv * hd
+    caches = [(np.zeros((48, kvd), np.int8), np.zeros(48, np.float32),
+               np.zeros((48, kvd), np.int8), np.zeros(48, np.float32)) for _ in range(nl)]
+    t = 5
+    for pos in range(32):
+        h = emb[t].copy()
+        for li in range(nl):
+            kc, ks, vc, vs = caches[li]
+            OL[li].step(h, pos, kc, ks, vc, vs, mode=0, threads=4)
+        logits = ora.fused_rmsnorm_linear(h, glob["output_norm"], out_w, vocab, E)
+        t = ora.argmax(logits)
+        if gpu[pos] != t:
+            srt = np.sort(logits)
+            assert (srt[-1] - srt[-2]) / np.max(np.abs(logits)) < 1e-4, (pos, gpu[pos], t)
+            return
