@@ -313,6 +313,13 @@ int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_dev);
  * output_norm, output (layer = -1): the GGUF names of src/model/gguf.rs:410-416. */
 int ssd_model_set_tensor(ssd_model* m, const char* name, int layer, const void* host_raw,
                          size_t bytes);
+/* Same, with the tensor's own ggml type (-1: the type the model config gives that name).
+ * A file may mix types per tensor; the reference reads each tensor's dtype from its GGUF
+ * tensor info (src/model/gguf.rs:284-291) and dispatches the matvec on it
+ * (src/metal/compute.rs:648-675). attn_q / attn_k and ffn_gate / ffn_up must share a type
+ * (each pair is one fused launch); an attn_v of another type gets a launch of its own. */
+int ssd_model_set_tensor_typed(ssd_model* m, const char* name, int layer, const void* host_raw,
+                               size_t bytes, int ggml_type);
 /* Fill the KV cache of every layer at positions [0, n) (both K and V rows drawn
  * N(0,1) by the synthetic generator, then INT8-quantized) and set the position.
  * No reference counterpart (benchmark inputs). */

@@ -707,12 +707,18 @@ static void layer_matvec(const uint8_t* w, int wtype, const float* x, int out_di
         for (int t = 0; t < threads; t++) pthread_join(th[t], NULL);
 }
 
+static int layer_wtype(const ora_layer* L, int i) {
+    return L->wtypes[i] >= 0 ? L->wtypes[i] : L->wtype;
+}
+
 int ora_layer_step(const ora_layer* L, float* hidden, int position, int8_t* k_cache,
                    float* k_scales, int8_t* v_cache, float* v_scales, int matvec_mode,
                    int threads) {
     int n = L->n_embd, hd = L->head_dim;
     int q_dim = L->n_head * hd, kv_dim = L->n_head_kv * hd, ff = L->n_ff;
-    if (q_dim != n || !pick_row(L->wtype)) return -1;
+    if (q_dim != n) return -1;
+    for (int i = 0; i < 7; i++)
+        if (!pick_row(layer_wtype(L, i))) return -1;
     float* attn_in = (float*)malloc(sizeof(float) * (size_t)n);
     float* q = (float*)malloc(sizeof(float) * (size_t)q_dim);
     float* k = (float*)malloc(sizeof(float) * (size_t)kv_dim);
@@ -728,9 +734,9 @@ int ora_layer_step(const ora_layer* L, float* hidden, int position, int8_t* k_ca
     memcpy(attn_in, hidden, sizeof(float) * (size_t)n);
     ora_rmsnorm(attn_in, L->attn_norm, n, L->eps);
     /* 2. fused QKV + RoPE: fused_qkv_rope_f32_cpu compute.rs:509-529 */
-    layer_matvec(L->wq, L->wtype, attn_in, q_dim, n, q, matvec_mode, threads);
-    layer_matvec(L->wk, L->wtype, attn_in, kv_dim, n, k, matvec_mode, threads);
-    layer_matvec(L->wv, L->wtype, attn_in, kv_dim, n, v, matvec_mode, threads);
+    layer_matvec(L->wq, layer_wtype(L, 0), attn_in, q_dim, n, q, matvec_mode, threads);
+    layer_matvec(L->wk, layer_wtype(L, 1), attn_in, kv_dim, n, k, matvec_mode, threads);
+    layer_matvec(L->wv, layer_wtype(L, 2), attn_in, kv_dim, n, v, matvec_mode, threads);
     ora_rope_multi_head(q, q_dim, hd, L->n_head, position, L->theta);
     ora_rope_multi_head(k, kv_dim, hd, L->n_head_kv, position, L->theta);
     /* kv_cache.append: QuantizedLayerKvCache::append quantized_kv_cache.rs:107-110 */
@@ -739,15 +745,15 @@ int ora_layer_step(const ora_layer* L, float* hidden, int position, int8_t* k_ca
     /* attention over positions 0..=position: attention.rs:198-236 */
     ora_attention_int8(q, k_cache, k_scales, v_cache, v_scales, position + 1, L->n_head,
                        L->n_head_kv, hd, attn);
-    layer_matvec(L->wo, L->wtype, attn, n, n, attn_out, matvec_mode, threads);
+    layer_matvec(L->wo, layer_wtype(L, 3), attn, n, n, attn_out, matvec_mode, threads);
     /* 3. residual + FFN norm: fused_post_attn_norm_f32_cpu compute.rs:536-555 */
     ora_fused_post_attn_norm(hidden, attn_out, L->ffn_norm, n, L->eps, ffn_in);
     /* 4. SwiGLU FFN: feed_forward feed_forward.rs:17-44 */
-    layer_matvec(L->w_gate, L->wtype, ffn_in, ff, n, gate, matvec_mode, threads);
+    layer_matvec(L->w_gate, layer_wtype(L, 4), ffn_in, ff, n, gate, matvec_mode, threads);
     ora_silu(gate, ff);
-    layer_matvec(L->w_up, L->wtype, ffn_in, ff, n, up, matvec_mode, threads);
+    layer_matvec(L->w_up, layer_wtype(L, 5), ffn_in, ff, n, up, matvec_mode, threads);
     for (int i = 0; i < ff; i++) gate[i] *= up[i];
-    layer_matvec(L->w_down, L->wtype, gate, n, ff, down, matvec_mode, threads);
+    layer_matvec(L->w_down, layer_wtype(L, 6), gate, n, ff, down, matvec_mode, threads);
     /* 5. residual: transformer.rs:369-371 */
     for (int i = 0; i < n; i++) hidden[i] += down[i];
 

@@ -108,6 +108,9 @@ typedef struct {
     const uint8_t *wq, *wk, *wv, *wo, *w_gate, *w_up, *w_down;
     const float *attn_norm, *ffn_norm;
     float theta, eps;
+    /* per-matrix types (wq, wk, wv, wo, w_gate, w_up, w_down) where the file mixes them,
+     * as the reference's per-tensor dispatch allows (compute.rs:648-675); -1 = wtype */
+    int wtypes[7];
 } ora_layer;
 
 int ora_layer_step(const ora_layer* L, float* hidden, int position, int8_t* k_cache,

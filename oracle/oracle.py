@@ -80,7 +80,7 @@ class OraLayer(ctypes.Structure):
                 ("head_dim", ctypes.c_int), ("n_ff", ctypes.c_int), ("wtype", ctypes.c_int),
                 ("wq", _u8p), ("wk", _u8p), ("wv", _u8p), ("wo", _u8p), ("w_gate", _u8p),
                 ("w_up", _u8p), ("w_down", _u8p), ("attn_norm", _fp), ("ffn_norm", _fp),
-                ("theta", ctypes.c_float), ("eps", ctypes.c_float)]
+                ("theta", ctypes.c_float), ("eps", ctypes.c_float), ("wtypes", ctypes.c_int * 7)]
 
 
 def _f(a):
@@ -218,14 +218,17 @@ class Layer:
     """Packed layer weights in reference layout + norms, for ora_layer_step."""
 
     def __init__(self, n_embd, n_head, n_head_kv, head_dim, n_ff, wtype, wq, wk, wv, wo,
-                 w_gate, w_up, w_down, attn_norm, ffn_norm, theta=10000.0, eps=1e-5):
+                 w_gate, w_up, w_down, attn_norm, ffn_norm, theta=10000.0, eps=1e-5,
+                 wtypes=None):
+        """wtypes: per-matrix types (wq, wk, wv, wo, w_gate, w_up, w_down); default wtype."""
         self._keep = [np.ascontiguousarray(a, dtype=np.uint8)
                       for a in (wq, wk, wv, wo, w_gate, w_up, w_down)]
         self._norms = [f32c(attn_norm), f32c(ffn_norm)]
         k = self._keep
         self.s = OraLayer(n_embd, n_head, n_head_kv, head_dim, n_ff, wtype, _u8(k[0]), _u8(k[1]),
                           _u8(k[2]), _u8(k[3]), _u8(k[4]), _u8(k[5]), _u8(k[6]),
-                          _f(self._norms[0]), _f(self._norms[1]), theta, eps)
+                          _f(self._norms[0]), _f(self._norms[1]), theta, eps,
+                          (ctypes.c_int * 7)(*(wtypes if wtypes is not None else [-1] * 7)))
 
     def step(self, hidden, position, k_cache, k_scales, v_cache, v_scales, mode=0, threads=1):
         """Runs one decode step in place on hidden / caches (numpy arrays)."""

@@ -414,7 +414,8 @@ extern "C" int ssd_model_load_gguf(ssd_model* m, const ssd_gguf* g, int n_layers
         SSD_REQ(t != nullptr, SSD_ERR_ARG, "GGUF: tensor %s missing", file_name.c_str());
         buf.resize(t->size);
         SSD_TRY(ssd_gguf_read(g, (uint64_t)(t - g->tensors.data()), buf.data(), buf.size()));
-        return ssd_model_set_tensor(m, model_name, layer, buf.data(), buf.size());
+        return ssd_model_set_tensor_typed(m, model_name, layer, buf.data(), buf.size(),
+                                          (int)t->type);  // each tensor's own type
     };
     for (int l = 0; l < n_layers; l++)
         for (const char* nm : kLayer)

@@ -380,8 +380,8 @@ static void take_pending(ssd_model* m, MvArgs& a, Pending& p) {
 }
 
 // Launches a partial-sum producer (Wo or down at TP > 1) and leaves the pending sum.
-static int produce_partial(ssd_model* m, MvArgs a, float* nccl_buf, bool use_p2p, int call,
-                           Pending& p, cudaStream_t s) {
+static int produce_partial(ssd_model* m, int type, MvArgs a, float* nccl_buf, bool use_p2p,
+                           int call, Pending& p, cudaStream_t s) {
     const auto& c = m->cfg;
     if (use_p2p) {
         const int N = tp_size(m), me = c.tp_rank, slot = call % kArSlots;
@@ -394,11 +394,11 @@ static int produce_partial(ssd_model* m, MvArgs a, float* nccl_buf, bool use_p2p
         a.ar_counter = m->ar_counter;
         a.ar_epoch = m->ar_epoch;
         a.ar_call = call;
-        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_PEERS, a, s, true));
+        SSD_TRY(launch_matvec(m->ctx, type, EPI_PEERS, a, s, true));
         p = Pending{true, true, nullptr, call};
     } else {
         a.y = nccl_buf;
-        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_STORE, a, s, true));
+        SSD_TRY(launch_matvec(m->ctx, type, EPI_STORE, a, s, true));
         SSD_NCCL(ncclAllReduce(nccl_buf, nccl_buf, c.n_embd, ncclFloat32, ncclSum, m->comm, s));
         p = Pending{true, false, nccl_buf, call};
     }
@@ -498,8 +498,8 @@ static int set_norm(ssd_model* m, float** slot, const void* host, size_t bytes) 
     return SSD_OK;
 }
 
-extern "C" int ssd_model_set_tensor(ssd_model* m, const char* cname, int layer, const void* host,
-                                    size_t bytes) {
+extern "C" int ssd_model_set_tensor_typed(ssd_model* m, const char* cname, int layer,
+                                          const void* host, size_t bytes, int ggml_type) {
     SSD_REQ(m && cname && host, SSD_ERR_ARG, "null argument");
     SSD_TRY(check_ctx(m->ctx));
     const std::string name(cname);
@@ -515,6 +515,18 @@ extern "C" int ssd_model_set_tensor(ssd_model* m, const char* cname, int layer, 
     Shard s;
     ssd_weight** slot = nullptr;
     SSD_TRY(shard_of(m, name, layer, s, slot));
+    if (ggml_type >= 0 && ggml_type != s.type) {  // this tensor's own type
+        const bool embd = name == "token_embd";
+        SSD_REQ(ggml_type == SSD_TYPE_Q4_0 || ggml_type == SSD_TYPE_Q8_0 ||
+                    ggml_type == SSD_TYPE_Q4_K || ggml_type == SSD_TYPE_Q6_K ||
+                    (embd && ggml_type == SSD_TYPE_F32),
+                SSD_ERR_TYPE, "%s: ggml type %d not supported here", cname, ggml_type);
+        const int tb = type_block(ggml_type);
+        SSD_REQ(s.cols % tb == 0 && s.col0 % tb == 0 && s.ncols % tb == 0, SSD_ERR_SHAPE,
+                "%s: columns (shard %d + %d of %d) not whole %d-wide blocks", cname, s.col0,
+                s.ncols, s.cols, tb);
+        s.type = ggml_type;
+    }
     const size_t rb = ssd_row_bytes(s.type, s.cols);
     SSD_REQ(rb != 0 && bytes == rb * (size_t)s.rows, SSD_ERR_SHAPE,
             "%s: %zu bytes given, %dx%d of type %d needs %zu", cname, bytes, s.rows, s.cols, s.type,
@@ -530,13 +542,18 @@ extern "C" int ssd_model_set_tensor(ssd_model* m, const char* cname, int layer, 
     SSD_TRY(ssd_weight_upload(m->ctx, buf.data(), buf.size(), s.type, s.nrows, s.ncols, &w));
     ssd_weight_free(*slot);
     *slot = w;
-    if (m->exec) {  // weights changed: the captured graph holds the old pointers
+    if (m->exec) {  // weights changed: the captured graph holds the old pointers (and types)
         cudaGraphExecDestroy(m->exec);
         cudaGraphDestroy(m->graph);
         m->exec = nullptr;
         m->graph = nullptr;
     }
     return SSD_OK;
+}
+
+extern "C" int ssd_model_set_tensor(ssd_model* m, const char* cname, int layer, const void* host,
+                                    size_t bytes) {
+    return ssd_model_set_tensor_typed(m, cname, layer, host, bytes, -1);
 }
 
 extern "C" int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_dev) {
@@ -699,7 +716,12 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     const Layer& L = m->layers[l];
     const bool tp = tp_size(m) > 1;
     float* h_other = (h == m->h_a) ? m->h_b : m->h_a;
-    // 1. QKV + RoPE with the pre-attention RMSNorm folded in
+    // 1. QKV + RoPE with the pre-attention RMSNorm folded in. Each weight keeps its own
+    // type (the reference dispatches every tensor on its dtype, compute.rs:648-675); a V of
+    // another type than Q / K gets its own launch after them.
+    SSD_REQ(L.wq->type == L.wk->type, SSD_ERR_TYPE, "attn_q and attn_k types differ (%d, %d)",
+            L.wq->type, L.wk->type);
+    const bool v_apart = L.wv->type != L.wq->type;
     MvArgs a = {};
     a.qs[0] = L.wq->qs;
     a.qs[1] = L.wk->qs;
@@ -709,9 +731,9 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     a.meta[2] = L.wv->meta;
     a.seg_rows[0] = m->q_rows;
     a.seg_rows[1] = m->kv_rows;
-    a.seg_rows[2] = m->kv_rows;
+    a.seg_rows[2] = v_apart ? 0 : m->kv_rows;
     a.map = MAP_QKV;
-    a.rows = m->q_rows + 2 * m->kv_rows;
+    a.rows = m->q_rows + (v_apart ? 1 : 2) * m->kv_rows;
     a.cols = c.n_embd;
     a.x = h;
     const bool had_pend = pend.on;
@@ -728,11 +750,19 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     a.head_dim = c.head_dim;
     a.theta = c.theta;
     a.position_dev = m->pos;
-    SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_QKV_ROPE, a, s, true));
+    SSD_TRY(launch_matvec(m->ctx, L.wq->type, EPI_QKV_ROPE, a, s, true));
     nl++;
     if (had_pend) {
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
+    }
+    if (v_apart) {  // the same normed input (any pending sum was added and written back)
+        MvArgs va = mv_plain(L.wv, h, m->v);
+        va.norm_w = L.attn_norm;
+        va.eps = c.eps;
+        va.norm_order = 0;
+        SSD_TRY(launch_matvec(m->ctx, L.wv->type, EPI_STORE, va, s, true));
+        nl++;
     }
     // 2-3. INT8 KV append at the current position (fused) and attention over this rank's
     // KV heads
@@ -758,15 +788,17 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     // 4. output projection (+ residual, or a partial sum for the all-reduce)
     MvArgs o = mv_plain(L.wo, m->attn, h_other);
     if (tp) {
-        SSD_TRY(produce_partial(m, o, m->p1, use_p2p, 2 * l, pend, s));
+        SSD_TRY(produce_partial(m, L.wo->type, o, m->p1, use_p2p, 2 * l, pend, s));
     } else {
         o.base = h;
-        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_RESID, o, s, true));
+        SSD_TRY(launch_matvec(m->ctx, L.wo->type, EPI_RESID, o, s, true));
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
     }
     nl++;
-    // 5. gate/up + SwiGLU with the FFN RMSNorm folded in
+    // 5. gate/up + SwiGLU with the FFN RMSNorm folded in (one fused launch: one type)
+    SSD_REQ(L.wg->type == L.wu->type, SSD_ERR_TYPE, "ffn_gate and ffn_up types differ (%d, %d)",
+            L.wg->type, L.wu->type);
     MvArgs g = {};
     g.qs[0] = L.wg->qs;
     g.qs[1] = L.wu->qs;
@@ -787,7 +819,7 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     g.eps = c.eps;
     g.norm_order = 1;
     g.y = m->act;
-    SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_SWIGLU, g, s, true));
+    SSD_TRY(launch_matvec(m->ctx, L.wg->type, EPI_SWIGLU, g, s, true));
     nl++;
     if (had_pend2) {
         h = h_other;
@@ -796,10 +828,10 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     // 6. down projection (+ residual, or a partial sum for the all-reduce)
     MvArgs d = mv_plain(L.wd, m->act, h_other);
     if (tp) {
-        SSD_TRY(produce_partial(m, d, m->p2, use_p2p, 2 * l + 1, pend, s));
+        SSD_TRY(produce_partial(m, L.wd->type, d, m->p2, use_p2p, 2 * l + 1, pend, s));
     } else {
         d.base = h;
-        SSD_TRY(launch_matvec(m->ctx, c.wtype, EPI_RESID, d, s, true));
+        SSD_TRY(launch_matvec(m->ctx, L.wd->type, EPI_RESID, d, s, true));
         h = h_other;
     }
     nl++;
@@ -823,7 +855,7 @@ static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl) {
     a.norm_order = 1;
     a.argmax_key = m->key;
     a.index_offset = m->vocab0;
-    SSD_TRY(launch_matvec(m->ctx, c.out_type, EPI_ARGMAX, a, s, true));
+    SSD_TRY(launch_matvec(m->ctx, m->output->type, EPI_ARGMAX, a, s, true));
     nl++;
     if (tp_size(m) > 1)
         SSD_NCCL(ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s));
@@ -1134,7 +1166,7 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
     a.norm_order = 1;
     a.argmax_key = m->key;
     a.index_offset = m->vocab0;
-    SSD_TRY(launch_matvec(m->ctx, c.out_type, EPI_ARGMAX, a, s, false));
+    SSD_TRY(launch_matvec(m->ctx, m->output->type, EPI_ARGMAX, a, s, false));
     SSD_TRY(launch_finalize(m->key, m->token, m->pos, nullptr, 0, s, false));
     SSD_CK(cudaMemcpyAsync(&m->pinned[1], m->token, 4, cudaMemcpyDeviceToHost, s));
     SSD_CK(cudaStreamSynchronize(s));

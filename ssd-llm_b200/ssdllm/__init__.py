@@ -118,6 +118,8 @@ _SIGS = {
     "ssd_model_synth_weights": ([_vp, ctypes.c_uint64, ctypes.c_float], ctypes.c_int),
     "ssd_model_set_tensor": ([_vp, ctypes.c_char_p, ctypes.c_int, _vp, ctypes.c_size_t],
                              ctypes.c_int),
+    "ssd_model_set_tensor_typed": ([_vp, ctypes.c_char_p, ctypes.c_int, _vp, ctypes.c_size_t,
+                                    ctypes.c_int], ctypes.c_int),
     "ssd_model_synth_kv": ([_vp, ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
     "ssd_model_set_position": ([_vp, ctypes.c_int], ctypes.c_int),
     "ssd_model_get_position": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
@@ -518,10 +520,16 @@ class Model:
     def synth_weights(self, seed: int, std: float = 0.02):
         check(lib().ssd_model_synth_weights(self.h, seed, std))
 
-    def set_tensor(self, name: str, layer: int, raw: np.ndarray):
+    def set_tensor(self, name: str, layer: int, raw: np.ndarray, wtype: int | None = None):
+        """raw: the full tensor in the reference layout; wtype: its own ggml type when it
+        differs from the model config's type for that name (files may mix types)."""
         raw = np.ascontiguousarray(raw)
-        check(lib().ssd_model_set_tensor(self.h, name.encode(), layer, raw.ctypes.data,
-                                         raw.nbytes))
+        if wtype is None:
+            check(lib().ssd_model_set_tensor(self.h, name.encode(), layer, raw.ctypes.data,
+                                             raw.nbytes))
+        else:
+            check(lib().ssd_model_set_tensor_typed(self.h, name.encode(), layer,
+                                                   raw.ctypes.data, raw.nbytes, wtype))
 
     def synth_kv(self, seed: int, n: int):
         check(lib().ssd_model_synth_kv(self.h, seed, n))

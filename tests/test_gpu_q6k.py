@@ -166,3 +166,93 @@ def test_q6k_model_greedy_decode_matches_oracle(ctx):
             srt = np.sort(logits)
             assert (srt[-1] - srt[-2]) / np.max(np.abs(logits)) < 1e-4, (pos, gpu[pos], t)
             return
+
+
+def test_mixed_type_model_greedy_decode_matches_oracle(ctx):
+    """Weights of different types per tensor, as GGUF files mix them (the reference
+    dispatches each tensor on its own dtype): Q4_K attn_q / attn_k, Q6_K attn_v (its own
+    launch), Q4_0 attn_output, Q8_0 gate / up, Q6_K down and output, Q4_K token_embd, set
+    through ssd_model_set_tensor_typed. 32 greedy tokens equal the oracle's decode loop."""
+    Q4_0, Q8_0, Q4_K = ora.Q4_0, ora.Q8_0, ora.Q4_K
+    E, nh, nkv, hd, F, vocab, nl = 256, 4, 2, 64, 512, 512, 2
+    cfg = dict(n_layers=nl, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=vocab,
+               wtype=Q4_0, out_type=Q4_0, embd_type=Q4_0, kv_capacity=48, theta=1e4, eps=1e-5,
+               tp_rank=0, tp_size=1)
+    rng = np.random.default_rng(75)
+    names = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+    types = (Q4_K, Q4_K, Q6_K, Q4_0, Q8_0, Q8_0, Q6_K)
+    shapes = ((nh * hd, E), (nkv * hd, E), (nkv * hd, E), (E, E), (F, E), (F, E), (E, F))
+
+    def mk(t, s):
+        if t == Q6_K:
+            return raw_q6k(rng, *s)
+        return ora.quantize((rng.standard_normal(s) * 0.02).astype(np.float32), t)
+
+    layers = []
+    for _ in range(nl):
+        L = {n: mk(t, s) for n, t, s in zip(names, types, shapes)}
+        L["attn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+        L["ffn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+        layers.append(L)
+    emb = ora.quantize(rng.standard_normal((vocab, E)).astype(np.float32), Q4_K)
+    out = raw_q6k(rng, vocab, E)
+    onorm = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
+    m = ssdllm.Model(ctx, **cfg)
+    try:
+        for li, L in enumerate(layers):
+            for n, t in zip(names, types):
+                m.set_tensor(n, li, L[n], wtype=t)
+            m.set_tensor("attn_norm", li, L["attn_norm"])
+            m.set_tensor("ffn_norm", li, L["ffn_norm"])
+        m.set_tensor("token_embd", -1, emb, wtype=Q4_K)
+        m.set_tensor("output", -1, out, wtype=Q6_K)
+        m.set_tensor("output_norm", -1, onorm)
+        m.set_position(0)
+        gpu, t = [], 9
+        for _ in range(32):
+            t = m.decode_token(t, use_graph=True)
+            gpu.append(t)
+        # embed, 2 x (QKV, V, attention partial + combine, o_proj, gate/up, down), logits, finalize
+        assert m.launches_per_step() == 1 + nl * 7 + 2
+    finally:
+        m.free()
+
+    OL = [ora.Layer(E, nh, nkv, hd, F, Q4_0, *(L[n] for n in names), L["attn_norm"],
+                    L["ffn_norm"], theta=1e4, eps=1e-5, wtypes=list(types)) for L in layers]
+    embf = ora.dequantize(emb, Q4_K, vocab * E).reshape(vocab, E)
+    outf = ora.dequantize(out, Q6_K, vocab * E).reshape(vocab, E)
+    kvd = nkv * hd
+    caches = [(np.zeros((48, kvd), np.int8), np.zeros(48, np.float32),
+               np.zeros((48, kvd), np.int8), np.zeros(48, np.float32)) for _ in range(nl)]
+    t = 9
+    for pos in range(32):
+        h = embf[t].copy()
+        for li in range(nl):
+            kc, ks, vc, vs = caches[li]
+            OL[li].step(h, pos, kc, ks, vc, vs, mode=0, threads=4)
+        logits = ora.fused_rmsnorm_linear(h, onorm, outf, vocab, E)
+        t = ora.argmax(logits)
+        if gpu[pos] != t:
+            srt = np.sort(logits)
+            assert (srt[-1] - srt[-2]) / np.max(np.abs(logits)) < 1e-4, (pos, gpu[pos], t)
+            return
+
+
+def test_mixed_types_that_cannot_fuse_are_rejected(ctx):
+    """attn_q / attn_k (and ffn_gate / ffn_up) run as one fused launch, so they must share
+    a type: a decode step with them differing fails with SSD_ERR_TYPE, not a wrong result."""
+    E, nh, nkv, hd, F = 256, 4, 2, 64, 512
+    cfg = dict(n_layers=1, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=64,
+               wtype=ora.Q4_0, out_type=ora.Q4_0, embd_type=ora.Q4_0, kv_capacity=8, theta=1e4,
+               eps=1e-5, tp_rank=0, tp_size=1)
+    m = ssdllm.Model(ctx, **cfg)
+    try:
+        m.synth_weights(seed=3, std=0.02)
+        rng = np.random.default_rng(76)
+        m.set_tensor("attn_k", 0, raw_q6k(rng, nkv * hd, E), wtype=Q6_K)
+        m.set_position(0)
+        with pytest.raises(ssdllm.SsdError) as e:
+            m.decode_token(1, use_graph=False)
+        assert e.value.status == 2  # SSD_ERR_TYPE
+    finally:
+        m.free()
