@@ -85,6 +85,7 @@ size_t ora_row_bytes(int type, int64_t n) {
         case ORA_Q4_0: return (size_t)(n / 32) * 18;
         case ORA_Q8_0: return (size_t)(n / 32) * 34;
         case ORA_Q4_K: return (size_t)(n / 256) * 144;
+        case ORA_Q5_K: return (size_t)(n / 256) * 176;
         case ORA_Q6_K: return (size_t)(n / 256) * 210;
         default: return 0;
     }
@@ -227,6 +228,17 @@ static int q6k_q(const uint8_t* blk, int idx) {
     return ((high2 << 4) | low4) - 32;
 }
 
+/* Q5_K super-block (256 weights, 176 bytes) as matvec_q5_k_cpu reads it
+ * (src/metal/compute.rs:845-899): f16 d, f16 dmin, 12 bytes of 6-bit (scale, min) packed
+ * as Q4_K's, qh[32] high bits (element idx: bit idx % 8 of qh[idx / 8]), ql[128] low
+ * nibbles (sub-block sb at ql[16 sb], element 2j low / 2j + 1 high nibble of byte j). */
+static int q5k_q(const uint8_t* blk, int idx) {
+    const uint8_t b = blk[48 + (idx / 32) * 16 + (idx % 32) / 2];
+    const int low4 = (idx & 1) ? (b >> 4) & 0x0F : b & 0x0F;
+    const int hbit = (blk[16 + idx / 8] >> (idx % 8)) & 1;
+    return low4 | (hbit << 4);
+}
+
 int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
     switch (type) {
         case ORA_F32: memcpy(out, w, (size_t)n * 4); return 0;
@@ -250,6 +262,19 @@ int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
                     int hi = (int)((byte >> 4) & 0x0F) - 8;
                     out[b * 32 + 2 * j] = (float)lo * scale;
                     out[b * 32 + 2 * j + 1] = (float)hi * scale;
+                }
+            }
+            return 0;
+        case ORA_Q5_K: /* element value of matvec_q5_k_cpu src/metal/compute.rs:863-892 */
+            for (int64_t b = 0; b < n / 256; b++) {
+                const uint8_t* blk = w + b * 176;
+                const float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+                for (int sb = 0; sb < 8; sb++) {
+                    uint8_t s, m;
+                    q4k_scale_min(blk + 4, sb, &s, &m);
+                    const float scale = d * (float)s, min_val = dmin * (float)m;
+                    for (int j = 0; j < 32; j++)
+                        out[b * 256 + sb * 32 + j] = scale * (float)q5k_q(blk, sb * 32 + j) - min_val;
                 }
             }
             return 0;
@@ -352,6 +377,30 @@ static float row_q4_k(const uint8_t* w, const float* x, int in_dim, int row) {
     return sum;
 }
 
+/* matvec_q5_k_cpu src/metal/compute.rs:845-899, one row: pairs of elements,
+ * sum += v0 * x0 + v1 * x1. */
+static float row_q5_k(const uint8_t* w, const float* x, int in_dim, int row) {
+    int bpr = in_dim / 256;
+    const uint8_t* r = w + (size_t)row * bpr * 176;
+    float sum = 0.0f;
+    for (int b = 0; b < bpr; b++) {
+        const uint8_t* blk = r + (size_t)b * 176;
+        const float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+        for (int sb = 0; sb < 8; sb++) {
+            uint8_t s, m;
+            q4k_scale_min(blk + 4, sb, &s, &m);
+            const float scale = d * (float)s, min_val = dmin * (float)m;
+            for (int j = 0; j < 16; j++) {
+                const int i0 = sb * 32 + 2 * j;
+                const float v0 = scale * (float)q5k_q(blk, i0) - min_val;
+                const float v1 = scale * (float)q5k_q(blk, i0 + 1) - min_val;
+                sum += v0 * x[b * 256 + i0] + v1 * x[b * 256 + i0 + 1];
+            }
+        }
+    }
+    return sum;
+}
+
 /* matvec_q6_k_cpu src/metal/compute.rs:752-790, one row: sum += (d * scale) * q * x in
  * element order. */
 static float row_q6_k(const uint8_t* w, const float* x, int in_dim, int row) {
@@ -408,6 +457,7 @@ static row_fn pick_row(int type) {
         case ORA_Q4_0: return row_q4_0;
         case ORA_Q8_0: return row_q8_0;
         case ORA_Q4_K: return row_q4_k;
+        case ORA_Q5_K: return row_q5_k;
         case ORA_Q6_K: return row_q6_k;
         case ORA_F16: return row_f16;
         default: return NULL;
