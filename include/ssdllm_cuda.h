@@ -55,10 +55,14 @@ extern "C" {
 #define SSD_TYPE_Q4_0 2
 #define SSD_TYPE_Q8_0 8
 #define SSD_TYPE_Q4_K 12
+/* Q5_K in the reference's block layout (matvec_q5_k_cpu, src/metal/compute.rs:845-899):
+ * 256 weights in 176 bytes, f16 d, f16 dmin, 12 bytes of 6-bit (scale, min) as Q4_K, 32 B
+ * of high bits, 128 B of low nibbles; weight = d * sc * (low4 | hbit << 4) - dmin * m. */
+#define SSD_TYPE_Q5_K 13
 /* Q6_K in the reference's own block layout (matvec_q6_k_cpu, src/metal/compute.rs:752-790):
  * 256 weights in 210 bytes, ql[128] low nibbles, qh[64] 2-bit high parts, 16 int8 scales,
- * f16 d; weight = (d * scale) * ((high2 << 4 | low4) - 32). Accepted by ssd_weight_upload,
- * ssd_dequantize, the matvec entry points and the prefill matmul. */
+ * f16 d; weight = (d * scale) * ((high2 << 4 | low4) - 32). Q5_K and Q6_K are accepted by
+ * ssd_weight_upload, ssd_dequantize, the matvec entry points and the prefill matmul. */
 #define SSD_TYPE_Q6_K 14
 
 typedef struct ssd_ctx ssd_ctx;

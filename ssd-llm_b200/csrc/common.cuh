@@ -67,11 +67,13 @@ struct ssd_ctx {
 //   Q4_0: qs = [rows][cols/32][16 B nibbles], meta = [rows][cols/32] f16 scales
 //   Q8_0: qs = [rows][cols/32][32 B int8],   meta = [rows][cols/32] f16 scales
 //   Q4_K: qs = [rows][cols/256][128 B],      meta = [rows][cols/256][16 B: d, dmin, 12 B sc]
+//   Q5_K: qs = [rows][cols/32][32 B: q ^ 0x80, q = low4 | hbit << 4, element order],
+//         meta = [rows][cols/256][16 B: d, dmin, 12 B 6-bit scales] (as Q4_K)
 //   Q6_K: qs = [rows][cols/32][32 B int8 q - 32, element order],
 //         meta = [rows][cols/32][4 B: int8 scale of elements 0-15, of 16-31, f16 d]
 //   F32 : qs = [rows][cols] f32
-// The bytes are the reference's bytes, regrouped; nothing is re-quantized (Q6_K's two
-// bit fields are joined into one signed byte per weight, d repeated per 32 weights).
+// The bytes are the reference's bytes, regrouped; nothing is re-quantized (Q5_K's and Q6_K's
+// two bit fields are joined into one byte per weight; Q6_K's d is repeated per 32 weights).
 struct ssd_weight {
     ssd_ctx* ctx = nullptr;
     int type = 0;
@@ -159,6 +161,24 @@ __device__ __forceinline__ void dequant8(const ssd_weight& w, int64_t e0, float 
         const float s = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.meta)[blk]);
         const int8_t* q = reinterpret_cast<const int8_t*>(w.qs) + e0;
         for (int t = 0; t < 8; t++) v[t] = __fmul_rn((float)q[t], s);
+    } else if (w.type == SSD_TYPE_Q5_K) {  // scale * q - min, compute.rs:863-892
+        const int64_t sbk = e0 / 256;
+        const int sb = (int)(e0 % 256) / 32;
+        const uint8_t* m = w.meta + sbk * 16;
+        const float d = f16_bits_to_f32((uint16_t)(m[0] | (m[1] << 8)));
+        const float dmin = f16_bits_to_f32((uint16_t)(m[2] | (m[3] << 8)));
+        const uint8_t* sc = m + 4;
+        int s6, m6;
+        if (sb < 4) {
+            s6 = sc[sb] & 0x3F;
+            m6 = sc[sb + 4] & 0x3F;
+        } else {
+            s6 = (sc[sb - 4] >> 6) | ((sc[sb + 4] & 0x0F) << 2);
+            m6 = (sc[sb] >> 6) | ((sc[sb + 4] >> 4) << 2);
+        }
+        const float scale = __fmul_rn(d, (float)s6), mn = __fmul_rn(dmin, (float)m6);
+        const uint8_t* q = w.qs + e0;
+        for (int t = 0; t < 8; t++) v[t] = __fsub_rn(__fmul_rn(scale, (float)(q[t] ^ 0x80)), mn);
     } else if (w.type == SSD_TYPE_Q6_K) {  // (d * scale) * q, compute.rs:768-785
         const int64_t c = e0 / 32;
         const uint32_t m = reinterpret_cast<const uint32_t*>(w.meta)[c];
@@ -280,6 +300,7 @@ inline int type_block(int type) {
         case SSD_TYPE_Q4_0:
         case SSD_TYPE_Q8_0: return 32;
         case SSD_TYPE_Q4_K:
+        case SSD_TYPE_Q5_K:
         case SSD_TYPE_Q6_K: return 256;
         case SSD_TYPE_F32:
         case SSD_TYPE_F16: return 1;
@@ -291,6 +312,7 @@ inline int type_block_bytes(int type) {
         case SSD_TYPE_Q4_0: return 18;
         case SSD_TYPE_Q8_0: return 34;
         case SSD_TYPE_Q4_K: return 144;
+        case SSD_TYPE_Q5_K: return 176;
         case SSD_TYPE_Q6_K: return 210;
         case SSD_TYPE_F32: return 4;
         case SSD_TYPE_F16: return 2;

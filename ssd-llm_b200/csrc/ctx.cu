@@ -143,6 +143,17 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int64_t nblo
         for (int j = 0; j < 32; j++) d[j] = s[2 + j];
         meta[2 * i] = s[0];
         meta[2 * i + 1] = s[1];
+    } else if (type == SSD_TYPE_Q5_K) {  // one byte per weight (q ^ 0x80) + the header
+        const uint8_t* s = raw + i * 176;
+        uint8_t* d = qs + i * 256;
+        for (int idx = 0; idx < 256; idx++) {  // compute.rs:877-890
+            const uint8_t b = s[48 + (idx / 32) * 16 + (idx % 32) / 2];
+            const int low4 = (idx & 1) ? (b >> 4) & 0x0F : b & 0x0F;
+            const int hbit = (s[16 + idx / 8] >> (idx % 8)) & 1;
+            d[idx] = (uint8_t)((low4 | (hbit << 4)) ^ 0x80);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) meta[i * 16 + j] = s[j];
     } else if (type == SSD_TYPE_Q6_K) {  // one signed byte per weight + a word per 32
         const uint8_t* s = raw + i * 210;
         int8_t* d = reinterpret_cast<int8_t*>(qs) + i * 256;
@@ -183,6 +194,15 @@ __global__ void k_unpack(const uint8_t* __restrict__ qs, const uint8_t* __restri
         d[0] = meta[2 * i];
         d[1] = meta[2 * i + 1];
         for (int j = 0; j < 32; j++) d[2 + j] = qs[i * 32 + j];
+    } else if (type == SSD_TYPE_Q5_K) {  // exact inverse of k_repack
+        uint8_t* d = raw + i * 176;
+        for (int j = 0; j < 16; j++) d[j] = meta[i * 16 + j];
+        for (int j = 16; j < 176; j++) d[j] = 0;
+        for (int idx = 0; idx < 256; idx++) {
+            const int v = qs[i * 256 + idx] ^ 0x80;
+            d[48 + (idx / 32) * 16 + (idx % 32) / 2] |= (uint8_t)((v & 0x0F) << (4 * (idx & 1)));
+            d[16 + idx / 8] |= (uint8_t)(((v >> 4) & 1) << (idx % 8));
+        }
     } else if (type == SSD_TYPE_Q6_K) {  // exact inverse of k_repack
         uint8_t* d = raw + i * 210;
         for (int j = 0; j < 192; j++) d[j] = 0;
@@ -512,9 +532,9 @@ namespace ssd {
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
-                type == SSD_TYPE_Q6_K || type == SSD_TYPE_F32,
-            SSD_ERR_TYPE, "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q6_K=14, F32=0)",
-            type);
+                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_F32,
+            SSD_ERR_TYPE,
+            "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14, F32=0)", type);
     SSD_REQ(rows > 0 && cols > 0, SSD_ERR_SHAPE, "empty tensor %dx%d", rows, cols);
     int bs = type_block(type);
     SSD_REQ(cols % bs == 0, SSD_ERR_SHAPE, "cols %d not a multiple of block %d", cols, bs);
@@ -528,6 +548,9 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
         meta_bytes = nb * 2;
     } else if (type == SSD_TYPE_Q4_K) {
         qs_bytes = nb * 128;
+        meta_bytes = nb * 16;
+    } else if (type == SSD_TYPE_Q5_K) {
+        qs_bytes = nb * 256;
         meta_bytes = nb * 16;
     } else if (type == SSD_TYPE_Q6_K) {
         qs_bytes = nb * 256;

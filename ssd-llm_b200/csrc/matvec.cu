@@ -64,6 +64,11 @@ struct Chunk<SSD_TYPE_Q4_K> {
     uint4 m;
 };
 template <>
+struct Chunk<SSD_TYPE_Q5_K> {
+    uint4 q0, q1;  // 32 bytes q ^ 0x80, q = low4 | hbit << 4
+    uint4 m;       // the super-block header (as Q4_K)
+};
+template <>
 struct Chunk<SSD_TYPE_Q6_K> {
     uint4 q0, q1;  // 32 signed bytes q - 32
     uint32_t m;    // int8 scale of elements 0-15, of 16-31, f16 d
@@ -87,6 +92,9 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
     } else if constexpr (FMT == SSD_TYPE_Q6_K) {
         qs = q + (size_t)lr * nc * 32;
         meta = m + (size_t)lr * nc * 4;
+    } else if constexpr (FMT == SSD_TYPE_Q5_K) {
+        qs = q + (size_t)lr * nc * 32;
+        meta = m + (size_t)lr * (nc >> 3) * 16;
     } else {
         qs = q + (size_t)lr * nc * 16;
         meta = m + (size_t)lr * (nc >> 3) * 16;
@@ -100,8 +108,9 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
 // the aligned 4-byte word holding the chunk's f16 d; Q4_K: the super-block's 16 bytes).
 template <int FMT>
 struct Slot {
-    static constexpr int QB = FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K ? 32 : 16;
-    static constexpr int MB = FMT == SSD_TYPE_Q4_K ? 16 : 4;
+    static constexpr int QB =
+        FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K || FMT == SSD_TYPE_Q5_K ? 32 : 16;
+    static constexpr int MB = FMT == SSD_TYPE_Q4_K || FMT == SSD_TYPE_Q5_K ? 16 : 4;
 };
 template <int FMT, int R, int U>
 __host__ __device__ constexpr int stage_bytes() {
@@ -122,8 +131,8 @@ template <int FMT>
 __device__ __forceinline__ void issue_chunk(uint32_t qdst, uint32_t mdst, const uint8_t* qp,
                                             const uint8_t* mp) {
     cp_async16_s(qdst, qp);
-    if constexpr (FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K) cp_async16_s(qdst + 16, qp + 16);
-    if constexpr (FMT == SSD_TYPE_Q4_K)
+    if constexpr (Slot<FMT>::QB == 32) cp_async16_s(qdst + 16, qp + 16);
+    if constexpr (Slot<FMT>::MB == 16)
         cp_async16_s(mdst, mp);
     else
         cp_async4_s(mdst, mp);
@@ -144,6 +153,10 @@ __device__ __forceinline__ void read_chunk(Chunk<FMT>& k, const uint8_t* qsrc, c
         k.q0 = *reinterpret_cast<const uint4*>(qsrc);
         k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
         k.m = *reinterpret_cast<const uint32_t*>(msrc);
+    } else if constexpr (FMT == SSD_TYPE_Q5_K) {
+        k.q0 = *reinterpret_cast<const uint4*>(qsrc);
+        k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
+        k.m = *reinterpret_cast<const uint4*>(msrc);
     } else {
         k.q = *reinterpret_cast<const uint4*>(qsrc);
         k.m = *reinterpret_cast<const uint4*>(msrc);
@@ -152,7 +165,7 @@ __device__ __forceinline__ void read_chunk(Chunk<FMT>& k, const uint8_t* qsrc, c
 // Bytes by which the stage pointers advance per chunk step of 32 chunks.
 template <int FMT>
 __host__ __device__ constexpr int q_step() {
-    return FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K ? 1024 : 512;
+    return Slot<FMT>::QB * 32;
 }
 // Scale bytes per chunk (Q4_K: 16 B per 8 chunks) and per chunk step of 32 chunks.
 template <int FMT>
@@ -170,7 +183,7 @@ template <int FMT>
 __device__ __forceinline__ size_t q_lane(int l) { return (size_t)l * Slot<FMT>::QB; }
 template <int FMT>
 __device__ __forceinline__ size_t m_lane(int l) {
-    return FMT == SSD_TYPE_Q4_K ? (size_t)(l >> 3) * 16 : (size_t)l * m_chunk<FMT>();
+    return Slot<FMT>::MB == 16 ? (size_t)(l >> 3) * 16 : (size_t)l * m_chunk<FMT>();
 }
 
 __device__ __forceinline__ uint32_t word_of(const uint4& q, int m) {
@@ -370,6 +383,37 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const u
             const float s1 = __fmul_rn(d, (float)(int)(int8_t)((mw >> 8) & 0xFF));
             acc[r] = fmaf(s1, sum_f2(eh[r]) + b2, fmaf(s0, sum_f2(eo[r]) + b, acc[r]));
         }
+    } else if constexpr (FMT == SSD_TYPE_Q5_K) {
+        // bytes q ^ 0x80 decoded as Q8_0's (q read back unsigned), then Q4_K's per
+        // sub-block scale and min: sum (scale q - min) x = scale sum q x - min X
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            uint64_t x01, x23;
+            lds_x<XOFF>(xq[m], x01, x23);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const uint32_t w = word_of(m < 4 ? ch[r].q0 : ch[r].q1, m & 3);
+                if (m == 0)
+                    byte_word<true>(eo[r], w, x01, x23);
+                else
+                    byte_word<false>(eo[r], w, x01, x23);
+            }
+        }
+        const float X = b;
+        const int sb = lane & 7, sh = 8 * (sb & 3);
+        const uint32_t sa = sb < 4 ? 0u : 6u, ma = sb < 4 ? 63u : 3u, m8 = sb < 4 ? 0u : 15u;
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const uint4 m = ch[r].m;
+            const float d = f16_bits_to_f32((uint16_t)(m.x & 0xFFFF));
+            const float dmin = f16_bits_to_f32((uint16_t)(m.x >> 16));
+            const uint32_t yb = m.y >> sh, zb = m.z >> sh, wb = m.w >> sh;
+            const uint32_t s6 = ((yb >> sa) & ma) | ((wb & m8) << 2);
+            const uint32_t m6 = ((zb >> sa) & ma) | (((wb >> 4) & m8) << 2);
+            const float scale = __fmul_rn(d, (float)s6);
+            const float mn = __fmul_rn(dmin, (float)m6);
+            acc[r] = fmaf(-mn, X, fmaf(scale, sum_f2(eo[r]), acc[r]));
+        }
     } else {  // Q4_K: this lane's sub-block index is c & 7 == lane & 7
         uint4 q[R];
 #pragma unroll
@@ -435,7 +479,7 @@ __host__ __device__ inline SmemPlan smem_plan(int cols, int nw, int ring_per_war
 // Power-of-two pre-scale of element position k (0..7) within a 32-bit word.
 template <int FMT>
 __device__ __forceinline__ float pos_scale(int k) {
-    const int s = FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K ? byte_pos(k & 3) : nib_pos(k);
+    const int s = Slot<FMT>::QB == 32 ? byte_pos(k & 3) : nib_pos(k);
     return __uint_as_float((uint32_t)(127 + kScaleBias - s) << 23);
 }
 
@@ -496,7 +540,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             lm[r] = m0 + m_lane<FMT>(lane < nc ? lane : 0);
             // Q4_0 / Q8_0: the aligned 4-byte word holding the d (stays aligned: the
             // pointer advances by multiples of 64 bytes)
-            if constexpr (FMT != SSD_TYPE_Q4_K)
+            if constexpr (has_doff<FMT>())
                 lm[r] = reinterpret_cast<const uint8_t*>((uintptr_t)lm[r] & ~(uintptr_t)3);
         }
     };
@@ -572,7 +616,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             }
         }
         // word position of v.x
-        const int k0 = (FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K) ? 0 : 4 * (i & 1);
+        const int k0 = Slot<FMT>::QB == 32 ? 0 : 4 * (i & 1);
         v.x = __fmul_rn(v.x, pos_scale<FMT>(k0 + 0));
         v.y = __fmul_rn(v.y, pos_scale<FMT>(k0 + 1));
         v.z = __fmul_rn(v.z, pos_scale<FMT>(k0 + 2));
@@ -890,11 +934,16 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
         case SSD_TYPE_Q4_K:
             SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q4_K cols %d not a multiple of 256", a.cols);
             return launch_fmt<SSD_TYPE_Q4_K>(ctx, epi, a, s, pdl);
+        case SSD_TYPE_Q5_K:
+            SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q5_K cols %d not a multiple of 256", a.cols);
+            return launch_fmt<SSD_TYPE_Q5_K>(ctx, epi, a, s, pdl);
         case SSD_TYPE_Q6_K:
             SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q6_K cols %d not a multiple of 256", a.cols);
             return launch_fmt<SSD_TYPE_Q6_K>(ctx, epi, a, s, pdl);
         default:
-            set_error("matvec: ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q6_K=14)", type);
+            set_error("matvec: ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, "
+                      "Q6_K=14)",
+                      type);
             return SSD_ERR_TYPE;
     }
 }
@@ -906,7 +955,7 @@ using namespace ssd;
 static int check_w(const ssd_weight* w) {
     SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
     SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
-                w->type == SSD_TYPE_Q6_K,
+                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K,
             SSD_ERR_TYPE, "matvec: ggml type %d not supported", w->type);
     return SSD_OK;
 }
@@ -1017,7 +1066,7 @@ extern "C" int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, siz
     SSD_TRY(check_ctx(ctx));
     SSD_REQ(w_raw && x && y, SSD_ERR_ARG, "null pointer");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
-                type == SSD_TYPE_Q6_K,
+                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K,
             SSD_ERR_TYPE, "matvec_quantized: ggml type %d not supported", type);
     ssd_weight* w = nullptr;
     SSD_TRY(ssd_weight_upload(ctx, w_raw, w_bytes, type, out_dim, in_dim, &w));
