@@ -87,6 +87,7 @@ size_t ora_row_bytes(int type, int64_t n) {
         case ORA_Q4_K: return (size_t)(n / 256) * 144;
         case ORA_Q5_K: return (size_t)(n / 256) * 176;
         case ORA_Q6_K: return (size_t)(n / 256) * 210;
+        case ORA_Q8_K: return (size_t)(n / 256) * 292;
         default: return 0;
     }
 }
@@ -265,6 +266,15 @@ int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
                 }
             }
             return 0;
+        case ORA_Q8_K: /* element value of matvec_q8_k_cpu src/metal/compute.rs:983-988:
+                          f32 d (little-endian), 256 int8, 32 bytes of block sums unused */
+            for (int64_t b = 0; b < n / 256; b++) {
+                const uint8_t* blk = w + b * 292;
+                float d;
+                memcpy(&d, blk, 4);
+                for (int j = 0; j < 256; j++) out[b * 256 + j] = d * (float)(int8_t)blk[4 + j];
+            }
+            return 0;
         case ORA_Q5_K: /* element value of matvec_q5_k_cpu src/metal/compute.rs:863-892 */
             for (int64_t b = 0; b < n / 256; b++) {
                 const uint8_t* blk = w + b * 176;
@@ -377,6 +387,20 @@ static float row_q4_k(const uint8_t* w, const float* x, int in_dim, int row) {
     return sum;
 }
 
+/* matvec_q8_k_cpu src/metal/compute.rs:971-993, one row: sum += d * q * x. */
+static float row_q8_k(const uint8_t* w, const float* x, int in_dim, int row) {
+    int bpr = in_dim / 256;
+    const uint8_t* r = w + (size_t)row * bpr * 292;
+    float sum = 0.0f;
+    for (int b = 0; b < bpr; b++) {
+        const uint8_t* blk = r + (size_t)b * 292;
+        float d;
+        memcpy(&d, blk, 4);
+        for (int j = 0; j < 256; j++) sum += d * (float)(int8_t)blk[4 + j] * x[b * 256 + j];
+    }
+    return sum;
+}
+
 /* matvec_q5_k_cpu src/metal/compute.rs:845-899, one row: pairs of elements,
  * sum += v0 * x0 + v1 * x1. */
 static float row_q5_k(const uint8_t* w, const float* x, int in_dim, int row) {
@@ -459,6 +483,7 @@ static row_fn pick_row(int type) {
         case ORA_Q4_K: return row_q4_k;
         case ORA_Q5_K: return row_q5_k;
         case ORA_Q6_K: return row_q6_k;
+        case ORA_Q8_K: return row_q8_k;
         case ORA_F16: return row_f16;
         default: return NULL;
     }

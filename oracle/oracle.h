@@ -23,7 +23,7 @@ extern "C" {
 
 /* GgmlType ids: src/model/gguf.rs:16-47 */
 enum { ORA_F32 = 0, ORA_F16 = 1, ORA_Q4_0 = 2, ORA_Q8_0 = 8, ORA_Q4_K = 12, ORA_Q5_K = 13,
-       ORA_Q6_K = 14 };
+       ORA_Q6_K = 14, ORA_Q8_K = 15 };
 
 /* f16 -> f32 (half::f16::to_f32, used by f16_to_f32 src/metal/compute.rs:2244-2247). */
 float ora_f16_to_f32(uint16_t h);
@@ -42,7 +42,8 @@ void ora_quantize_q4_k(const float* w, int64_t n, uint8_t* out);
 /* Dequantize to f32: src/ssd/streamer.rs:93-180 (Q4_0, Q8_0, F16, F32); Q4_K uses
  * the element formula of matvec_q4_k_cpu src/metal/compute.rs:707-750, Q6_K that of
  * matvec_q6_k_cpu src/metal/compute.rs:752-790 ((d * scale) * q), Q5_K that of
- * matvec_q5_k_cpu src/metal/compute.rs:845-899 (scale * q - min). Returns 0,
+ * matvec_q5_k_cpu src/metal/compute.rs:845-899 (scale * q - min), Q8_K that of
+ * matvec_q8_k_cpu src/metal/compute.rs:971-993 (d * q). Returns 0,
  * or -1 for an unsupported type. */
 int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out);
 
