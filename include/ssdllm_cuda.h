@@ -61,9 +61,13 @@ extern "C" {
 #define SSD_TYPE_Q5_K 13
 /* Q6_K in the reference's own block layout (matvec_q6_k_cpu, src/metal/compute.rs:752-790):
  * 256 weights in 210 bytes, ql[128] low nibbles, qh[64] 2-bit high parts, 16 int8 scales,
- * f16 d; weight = (d * scale) * ((high2 << 4 | low4) - 32). Q5_K and Q6_K are accepted by
+ * f16 d; weight = (d * scale) * ((high2 << 4 | low4) - 32). Q5_K, Q6_K and Q8_K are accepted by
  * ssd_weight_upload, ssd_dequantize, the matvec entry points and the prefill matmul. */
 #define SSD_TYPE_Q6_K 14
+/* Q8_K in the reference's block layout (matvec_q8_k_cpu, src/metal/compute.rs:971-993):
+ * 256 weights in 292 bytes, f32 d, 256 int8, 32 bytes of block sums (not read by the
+ * matvec, kept for the download); weight = d * q. */
+#define SSD_TYPE_Q8_K 15
 
 typedef struct ssd_ctx ssd_ctx;
 typedef struct ssd_weight ssd_weight;

@@ -71,6 +71,8 @@ struct ssd_ctx {
 //         meta = [rows][cols/256][16 B: d, dmin, 12 B 6-bit scales] (as Q4_K)
 //   Q6_K: qs = [rows][cols/32][32 B int8 q - 32, element order],
 //         meta = [rows][cols/32][4 B: int8 scale of elements 0-15, of 16-31, f16 d]
+//   Q8_K: qs = [rows][cols/32][32 B int8], meta = [rows][cols/32] f32 d, then the
+//         block sums of every super-block ([rows][cols/256][32 B], kept for the download)
 //   F32 : qs = [rows][cols] f32
 // The bytes are the reference's bytes, regrouped; nothing is re-quantized (Q5_K's and Q6_K's
 // two bit fields are joined into one byte per weight; Q6_K's d is repeated per 32 weights).
@@ -179,6 +181,10 @@ __device__ __forceinline__ void dequant8(const ssd_weight& w, int64_t e0, float 
         const float scale = __fmul_rn(d, (float)s6), mn = __fmul_rn(dmin, (float)m6);
         const uint8_t* q = w.qs + e0;
         for (int t = 0; t < 8; t++) v[t] = __fsub_rn(__fmul_rn(scale, (float)(q[t] ^ 0x80)), mn);
+    } else if (w.type == SSD_TYPE_Q8_K) {  // d * q, compute.rs:985-987
+        const float dd = reinterpret_cast<const float*>(w.meta)[e0 / 32];
+        const int8_t* q = reinterpret_cast<const int8_t*>(w.qs) + e0;
+        for (int t = 0; t < 8; t++) v[t] = __fmul_rn(dd, (float)q[t]);
     } else if (w.type == SSD_TYPE_Q6_K) {  // (d * scale) * q, compute.rs:768-785
         const int64_t c = e0 / 32;
         const uint32_t m = reinterpret_cast<const uint32_t*>(w.meta)[c];
@@ -301,7 +307,8 @@ inline int type_block(int type) {
         case SSD_TYPE_Q8_0: return 32;
         case SSD_TYPE_Q4_K:
         case SSD_TYPE_Q5_K:
-        case SSD_TYPE_Q6_K: return 256;
+        case SSD_TYPE_Q6_K:
+        case SSD_TYPE_Q8_K: return 256;
         case SSD_TYPE_F32:
         case SSD_TYPE_F16: return 1;
         default: return 0;
@@ -314,6 +321,7 @@ inline int type_block_bytes(int type) {
         case SSD_TYPE_Q4_K: return 144;
         case SSD_TYPE_Q5_K: return 176;
         case SSD_TYPE_Q6_K: return 210;
+        case SSD_TYPE_Q8_K: return 292;
         case SSD_TYPE_F32: return 4;
         case SSD_TYPE_F16: return 2;
         default: return 0;

@@ -143,6 +143,13 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int64_t nblo
         for (int j = 0; j < 32; j++) d[j] = s[2 + j];
         meta[2 * i] = s[0];
         meta[2 * i + 1] = s[1];
+    } else if (type == SSD_TYPE_Q8_K) {  // bytes as they are, d per 32, sums aside
+        const uint8_t* s = raw + i * 292;
+        for (int j = 0; j < 256; j++) qs[i * 256 + j] = s[4 + j];
+        for (int c = 0; c < 8; c++)
+            for (int j = 0; j < 4; j++) meta[(i * 8 + c) * 4 + j] = s[j];
+        uint8_t* sums = meta + nblocks * 32;
+        for (int j = 0; j < 32; j++) sums[i * 32 + j] = s[260 + j];
     } else if (type == SSD_TYPE_Q5_K) {  // one byte per weight (q ^ 0x80) + the header
         const uint8_t* s = raw + i * 176;
         uint8_t* d = qs + i * 256;
@@ -194,6 +201,11 @@ __global__ void k_unpack(const uint8_t* __restrict__ qs, const uint8_t* __restri
         d[0] = meta[2 * i];
         d[1] = meta[2 * i + 1];
         for (int j = 0; j < 32; j++) d[2 + j] = qs[i * 32 + j];
+    } else if (type == SSD_TYPE_Q8_K) {  // exact inverse of k_repack
+        uint8_t* d = raw + i * 292;
+        for (int j = 0; j < 4; j++) d[j] = meta[i * 32 + j];
+        for (int j = 0; j < 256; j++) d[4 + j] = qs[i * 256 + j];
+        for (int j = 0; j < 32; j++) d[260 + j] = meta[nblocks * 32 + i * 32 + j];
     } else if (type == SSD_TYPE_Q5_K) {  // exact inverse of k_repack
         uint8_t* d = raw + i * 176;
         for (int j = 0; j < 16; j++) d[j] = meta[i * 16 + j];
@@ -532,9 +544,12 @@ namespace ssd {
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
-                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_F32,
+                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K ||
+                type == SSD_TYPE_F32,
             SSD_ERR_TYPE,
-            "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14, F32=0)", type);
+            "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14, Q8_K=15, "
+            "F32=0)",
+            type);
     SSD_REQ(rows > 0 && cols > 0, SSD_ERR_SHAPE, "empty tensor %dx%d", rows, cols);
     int bs = type_block(type);
     SSD_REQ(cols % bs == 0, SSD_ERR_SHAPE, "cols %d not a multiple of block %d", cols, bs);
@@ -552,6 +567,9 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     } else if (type == SSD_TYPE_Q5_K) {
         qs_bytes = nb * 256;
         meta_bytes = nb * 16;
+    } else if (type == SSD_TYPE_Q8_K) {
+        qs_bytes = nb * 256;
+        meta_bytes = nb * 64;
     } else if (type == SSD_TYPE_Q6_K) {
         qs_bytes = nb * 256;
         meta_bytes = nb * 32;

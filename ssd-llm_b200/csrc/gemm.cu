@@ -370,7 +370,8 @@ extern "C" int ssd_prefill_matmul(ssd_ctx* ctx, const ssd_weight* w, const float
     SSD_TRY(check_ctx(ctx));
     SSD_REQ(w && x_dev && y_dev, SSD_ERR_ARG, "null argument");
     SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
-                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_F32,
+                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_Q8_K ||
+                w->type == SSD_TYPE_F32,
             SSD_ERR_TYPE, "prefill matmul: ggml type %d not supported", w->type);
     SSD_REQ(n_tokens > 0 && n_tokens % 128 == 0, SSD_ERR_SHAPE,
             "n_tokens %d must be a positive multiple of 128", n_tokens);

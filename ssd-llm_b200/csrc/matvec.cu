@@ -69,6 +69,11 @@ struct Chunk<SSD_TYPE_Q5_K> {
     uint4 m;       // the super-block header (as Q4_K)
 };
 template <>
+struct Chunk<SSD_TYPE_Q8_K> {
+    uint4 q0, q1;  // 32 int8
+    uint32_t m;    // f32 d of the super-block
+};
+template <>
 struct Chunk<SSD_TYPE_Q6_K> {
     uint4 q0, q1;  // 32 signed bytes q - 32
     uint32_t m;    // int8 scale of elements 0-15, of 16-31, f16 d
@@ -89,7 +94,7 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
     } else if constexpr (FMT == SSD_TYPE_Q8_0) {
         qs = q + (size_t)lr * nc * 32;
         meta = m + (size_t)lr * nc * 2;
-    } else if constexpr (FMT == SSD_TYPE_Q6_K) {
+    } else if constexpr (FMT == SSD_TYPE_Q6_K || FMT == SSD_TYPE_Q8_K) {
         qs = q + (size_t)lr * nc * 32;
         meta = m + (size_t)lr * nc * 4;
     } else if constexpr (FMT == SSD_TYPE_Q5_K) {
@@ -109,7 +114,10 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
 template <int FMT>
 struct Slot {
     static constexpr int QB =
-        FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K || FMT == SSD_TYPE_Q5_K ? 32 : 16;
+        FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q6_K || FMT == SSD_TYPE_Q5_K ||
+                FMT == SSD_TYPE_Q8_K
+            ? 32
+            : 16;
     static constexpr int MB = FMT == SSD_TYPE_Q4_K || FMT == SSD_TYPE_Q5_K ? 16 : 4;
 };
 template <int FMT, int R, int U>
@@ -149,7 +157,7 @@ __device__ __forceinline__ void read_chunk(Chunk<FMT>& k, const uint8_t* qsrc, c
         k.q0 = *reinterpret_cast<const uint4*>(qsrc);
         k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
         k.d = *reinterpret_cast<const uint16_t*>(msrc);
-    } else if constexpr (FMT == SSD_TYPE_Q6_K) {
+    } else if constexpr (FMT == SSD_TYPE_Q6_K || FMT == SSD_TYPE_Q8_K) {
         k.q0 = *reinterpret_cast<const uint4*>(qsrc);
         k.q1 = *reinterpret_cast<const uint4*>(qsrc + 16);
         k.m = *reinterpret_cast<const uint32_t*>(msrc);
@@ -169,7 +177,9 @@ __host__ __device__ constexpr int q_step() {
 }
 // Scale bytes per chunk (Q4_K: 16 B per 8 chunks) and per chunk step of 32 chunks.
 template <int FMT>
-__host__ __device__ constexpr int m_chunk() { return FMT == SSD_TYPE_Q6_K ? 4 : 2; }
+__host__ __device__ constexpr int m_chunk() {
+    return FMT == SSD_TYPE_Q6_K || FMT == SSD_TYPE_Q8_K ? 4 : 2;
+}
 template <int FMT>
 __host__ __device__ constexpr int m_step() { return 32 * m_chunk<FMT>(); }
 // Q4_0 / Q8_0 copy the aligned word holding a chunk's 2-byte d: the half to read varies.
@@ -353,6 +363,22 @@ __device__ __forceinline__ void compute_chunk(const Chunk<FMT> (&ch)[R], const u
 #pragma unroll
         for (int r = 0; r < R; r++)
             acc[r] = fmaf(f16_bits_to_f32((uint16_t)ch[r].d), sum_f2(eo[r]) + b, acc[r]);
+    } else if constexpr (FMT == SSD_TYPE_Q8_K) {  // Q8_0's decode, f32 d per super-block
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            uint64_t x01, x23;
+            lds_x<XOFF>(xq[m], x01, x23);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const uint32_t w = word_of(m < 4 ? ch[r].q0 : ch[r].q1, m & 3);
+                if (m == 0)
+                    byte_word<true>(eo[r], w, x01, x23);
+                else
+                    byte_word<false>(eo[r], w, x01, x23);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = fmaf(__uint_as_float(ch[r].m), sum_f2(eo[r]) + b, acc[r]);
     } else if constexpr (FMT == SSD_TYPE_Q6_K) {
         // signed bytes q - 32 decoded as Q8_0's (q + 128 read unsigned); elements 0-15 and
         // 16-31 have their own scale, so each half has its own pair and bias (b, b2):
@@ -612,7 +638,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             t += __shfl_xor_sync(gmask, t, 4);
             if ((i & 7) == 0) {
                 const float X = __fmul_rn(t, 1.0f / kUnscale);
-                csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X : (FMT == SSD_TYPE_Q8_0 ? -128.0f * X : X);
+                csum[c] = FMT == SSD_TYPE_Q4_0 ? -8.0f * X
+                          : (FMT == SSD_TYPE_Q8_0 || FMT == SSD_TYPE_Q8_K) ? -128.0f * X
+                                                                           : X;
             }
         }
         // word position of v.x
@@ -940,9 +968,12 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
         case SSD_TYPE_Q6_K:
             SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q6_K cols %d not a multiple of 256", a.cols);
             return launch_fmt<SSD_TYPE_Q6_K>(ctx, epi, a, s, pdl);
+        case SSD_TYPE_Q8_K:
+            SSD_REQ(a.cols % 256 == 0, SSD_ERR_SHAPE, "Q8_K cols %d not a multiple of 256", a.cols);
+            return launch_fmt<SSD_TYPE_Q8_K>(ctx, epi, a, s, pdl);
         default:
             set_error("matvec: ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, "
-                      "Q6_K=14)",
+                      "Q6_K=14, Q8_K=15)",
                       type);
             return SSD_ERR_TYPE;
     }
@@ -955,7 +986,7 @@ using namespace ssd;
 static int check_w(const ssd_weight* w) {
     SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
     SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
-                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K,
+                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_Q8_K,
             SSD_ERR_TYPE, "matvec: ggml type %d not supported", w->type);
     return SSD_OK;
 }
@@ -1066,7 +1097,7 @@ extern "C" int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, siz
     SSD_TRY(check_ctx(ctx));
     SSD_REQ(w_raw && x && y, SSD_ERR_ARG, "null pointer");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
-                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K,
+                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K,
             SSD_ERR_TYPE, "matvec_quantized: ggml type %d not supported", type);
     ssd_weight* w = nullptr;
     SSD_TRY(ssd_weight_upload(ctx, w_raw, w_bytes, type, out_dim, in_dim, &w));

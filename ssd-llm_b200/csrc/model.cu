@@ -158,7 +158,8 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
             "column shards must be whole %d-wide blocks", bs);
     SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
                 c->embd_type == SSD_TYPE_Q8_0 || c->embd_type == SSD_TYPE_Q4_K ||
-                c->embd_type == SSD_TYPE_Q5_K || c->embd_type == SSD_TYPE_Q6_K,
+                c->embd_type == SSD_TYPE_Q5_K || c->embd_type == SSD_TYPE_Q6_K ||
+                c->embd_type == SSD_TYPE_Q8_K,
             SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
     SSD_REQ(type_block(c->out_type) == 32 || type_block(c->out_type) == 256, SSD_ERR_TYPE,
             "output type %d not supported", c->out_type);
@@ -519,7 +520,7 @@ extern "C" int ssd_model_set_tensor_typed(ssd_model* m, const char* cname, int l
         const bool embd = name == "token_embd";
         SSD_REQ(ggml_type == SSD_TYPE_Q4_0 || ggml_type == SSD_TYPE_Q8_0 ||
                     ggml_type == SSD_TYPE_Q4_K || ggml_type == SSD_TYPE_Q5_K ||
-                    ggml_type == SSD_TYPE_Q6_K ||
+                    ggml_type == SSD_TYPE_Q6_K || ggml_type == SSD_TYPE_Q8_K ||
                     (embd && ggml_type == SSD_TYPE_F32),
                 SSD_ERR_TYPE, "%s: ggml type %d not supported here", cname, ggml_type);
         const int tb = type_block(ggml_type);
