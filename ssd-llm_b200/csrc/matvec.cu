@@ -108,9 +108,11 @@ __device__ __forceinline__ void row_ptr(const MvArgs& a, int R, int v, const uin
 
 // ---- cp.async staging of weights. Each lane copies its own chunks of a stage into
 // its own 16-byte slots of the warp's ring and later reads them back, so completion
-// only needs the thread's own cp.async.wait_group (no cross-lane synchronisation).
+// only needs the thread's own cp.async.wait_group (Q4_K / Q5_K headers: the group's
+// first lane copies, a __syncwarp after the wait publishes it to the other 7).
 // Ring slot sizes per (row, chunk): payload QB bytes, metadata MB bytes (Q4_0 / Q8_0:
-// the aligned 4-byte word holding the chunk's f16 d; Q4_K: the super-block's 16 bytes).
+// the aligned 4-byte word holding the chunk's f16 d; Q4_K / Q5_K: the super-block's 16
+// bytes, one slot per group of 8 lanes).
 template <int FMT>
 struct Slot {
     static constexpr int QB =
@@ -119,10 +121,14 @@ struct Slot {
             ? 32
             : 16;
     static constexpr int MB = FMT == SSD_TYPE_Q4_K || FMT == SSD_TYPE_Q5_K ? 16 : 4;
+    // Q4_K / Q5_K: the 8 lanes of a group read chunks of one super-block, so its 16-byte
+    // header is copied once per group (by the group's first lane) into a slot they share
+    static constexpr bool HDR = MB == 16;
+    static constexpr int MSLOT = HDR ? 4 * 16 : 32 * MB;  // metadata bytes per (row, step)
 };
 template <int FMT, int R, int U>
 __host__ __device__ constexpr int stage_bytes() {
-    return R * U * 32 * (Slot<FMT>::QB + Slot<FMT>::MB);
+    return R * U * (32 * Slot<FMT>::QB + Slot<FMT>::MSLOT);
 }
 
 // Issues the copies of chunk step u of a stage for one row into the shared addresses
@@ -137,13 +143,14 @@ __device__ __forceinline__ void cp_async4_s(uint32_t dst, const void* src) {
 }
 template <int FMT>
 __device__ __forceinline__ void issue_chunk(uint32_t qdst, uint32_t mdst, const uint8_t* qp,
-                                            const uint8_t* mp) {
+                                            const uint8_t* mp, bool copy_hdr) {
     cp_async16_s(qdst, qp);
     if constexpr (Slot<FMT>::QB == 32) cp_async16_s(qdst + 16, qp + 16);
-    if constexpr (Slot<FMT>::MB == 16)
-        cp_async16_s(mdst, mp);
-    else
+    if constexpr (Slot<FMT>::HDR) {
+        if (copy_hdr) cp_async16_s(mdst, mp);
+    } else {
         cp_async4_s(mdst, mp);
+    }
 }
 
 // Reads one (row, chunk) slot back: qsrc = payload slot, msrc = metadata slot (for
@@ -573,9 +580,12 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     if (lrg < n_rg) set_rows();
     const bool any_tail = nc % (32 * U) != 0 || nc < 32;
     // this lane's slots: payload at ring_q + stage + (r*U+u)*32*QB, metadata at
-    // ring_m + stage + (r*U+u)*32*MB (compile-time offsets from two lane pointers)
+    // ring_m + stage + (r*U+u)*MSLOT (compile-time offsets from two lane pointers; Q4_K /
+    // Q5_K lanes point at their group's shared header slot)
     uint8_t* const ring_q = ring + (size_t)lane * QB;
-    uint8_t* const ring_m = ring + (size_t)R * U * 32 * QB + (size_t)lane * MB;
+    uint8_t* const ring_m = ring + (size_t)R * U * 32 * QB +
+                            (Slot<FMT>::HDR ? (size_t)(lane >> 3) * 16 : (size_t)lane * MB);
+    const bool copy_hdr = (lane & 7) == 0;
     const uint32_t ring_qs = smem_u32(ring_q), ring_ms = smem_u32(ring_m);  // copy targets
     int ist = 0;  // byte offset of the stage being issued
     auto issue = [&]() {  // the next stage into the ring, then commit
@@ -586,8 +596,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
 #pragma unroll
                     for (int u = 0; u < U; u++)
                         issue_chunk<FMT>(ring_qs + ist + (r * U + u) * 32 * QB,
-                                         ring_ms + ist + (r * U + u) * 32 * MB,
-                                         lq[r] + u * q_step<FMT>(), lm[r] + u * m_step<FMT>());
+                                         ring_ms + ist + (r * U + u) * Slot<FMT>::MSLOT,
+                                         lq[r] + u * q_step<FMT>(), lm[r] + u * m_step<FMT>(),
+                                         copy_hdr);
                 }
             } else {  // tail stage: chunks past the row end re-read the lane's last chunk
 #pragma unroll
@@ -601,9 +612,10 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
 #pragma unroll
                     for (int r = 0; r < R; r++)
                         issue_chunk<FMT>(ring_qs + ist + (r * U + u) * 32 * QB,
-                                         ring_ms + ist + (r * U + u) * 32 * MB,
+                                         ring_ms + ist + (r * U + u) * Slot<FMT>::MSLOT,
                                          lq[r] + u * q_step<FMT>() + dc * (q_step<FMT>() / 32),
-                                         lm[r] + u * m_step<FMT>() + dc * m_chunk<FMT>());
+                                         lm[r] + u * m_step<FMT>() + dc * m_chunk<FMT>(),
+                                         copy_hdr);
                 }
             }
 #pragma unroll
@@ -683,6 +695,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
 
     for (int k = 0; k < total; k++) {
         cp_wait<kStages - 2>();  // this thread's copies of stage k have landed
+        // the group's shared header was copied by its first lane: make it visible
+        if constexpr (Slot<FMT>::HDR) __syncwarp();
         const uint8_t* sq = ring_q + cst_off;
         const uint8_t* sm = ring_m + cst_off;
         uint32_t xst[8];  // x'' units of this stage's first chunk step
@@ -695,7 +709,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
 #pragma unroll
             for (int r = 0; r < R; r++)
                 read_chunk<FMT>(ch[r], sq + (r * U + u) * 32 * QB,
-                                sm + (r * U + u) * 32 * MB + (has_doff<FMT>() ? doff[r] : 0));
+                                sm + (r * U + u) * Slot<FMT>::MSLOT + (has_doff<FMT>() ? doff[r] : 0));
             constexpr int CPC = csum_per_chunk<FMT>();
             compute_chunk<FMT, R, u * 4096>(ch, xst, cs[32 * u * CPC], CPC == 2 ? cs[32 * u * CPC + 1] : 0.0f,
                                             lane, acc);
@@ -863,7 +877,7 @@ static int launch_t(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
 // else 8 warps.
 template <int FMT, int EPI>
 static int launch_fmt_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
-    constexpr int U = FMT == SSD_TYPE_Q4_0 ? 2 : 1;
+    constexpr int U = FMT == SSD_TYPE_Q4_0 || FMT == SSD_TYPE_Q4_K ? 2 : 1;
     const Cfg c = env_cfg();
     if (c.R) {  // tuning: any instantiated (R, U, NW)
         if (c.U == U && c.NW == 8 && c.R == 2) return launch_t<FMT, EPI, 2, U, 8>(ctx, a, s, pdl);
