@@ -81,7 +81,8 @@ static inline void wr_f16(uint8_t* p, uint16_t h) {
 size_t ora_row_bytes(int type, int64_t n) {
     switch (type) {
         case ORA_F32: return (size_t)n * 4;
-        case ORA_F16: return (size_t)n * 2;
+        case ORA_F16:
+        case ORA_BF16: return (size_t)n * 2;
         case ORA_Q4_0: return (size_t)(n / 32) * 18;
         case ORA_Q8_0: return (size_t)(n / 32) * 34;
         case ORA_Q4_K: return (size_t)(n / 256) * 144;
@@ -243,6 +244,12 @@ static int q5k_q(const uint8_t* blk, int idx) {
 int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
     switch (type) {
         case ORA_F32: memcpy(out, w, (size_t)n * 4); return 0;
+        case ORA_BF16: /* bf16_to_f32 src/metal/compute.rs:2250-2253: bits << 16 */
+            for (int64_t i = 0; i < n; i++) {
+                const uint32_t b = ((uint32_t)w[2 * i] | ((uint32_t)w[2 * i + 1] << 8)) << 16;
+                memcpy(&out[i], &b, 4);
+            }
+            return 0;
         case ORA_F16: /* src/ssd/streamer.rs:99-106 */
             for (int64_t i = 0; i < n; i++) out[i] = rd_f16(w + 2 * i);
             return 0;
@@ -445,6 +452,19 @@ static float row_q6_k(const uint8_t* w, const float* x, int in_dim, int row) {
     return sum;
 }
 
+/* matvec_bf16_cpu src/metal/compute.rs:2256-2269, one row. */
+static float row_bf16(const uint8_t* w, const float* x, int in_dim, int row) {
+    const uint8_t* r = w + (size_t)row * in_dim * 2;
+    float sum = 0.0f;
+    for (int c = 0; c < in_dim; c++) {
+        const uint32_t b = ((uint32_t)r[2 * c] | ((uint32_t)r[2 * c + 1] << 8)) << 16;
+        float v;
+        memcpy(&v, &b, 4);
+        sum += v * x[c];
+    }
+    return sum;
+}
+
 /* f16 matvec src/metal/compute.rs:2272-2285, one row. */
 static float row_f16(const uint8_t* w, const float* x, int in_dim, int row) {
     const uint8_t* r = w + (size_t)row * in_dim * 2;
@@ -485,6 +505,7 @@ static row_fn pick_row(int type) {
         case ORA_Q6_K: return row_q6_k;
         case ORA_Q8_K: return row_q8_k;
         case ORA_F16: return row_f16;
+        case ORA_BF16: return row_bf16;
         default: return NULL;
     }
 }

@@ -23,7 +23,7 @@ extern "C" {
 
 /* GgmlType ids: src/model/gguf.rs:16-47 */
 enum { ORA_F32 = 0, ORA_F16 = 1, ORA_Q4_0 = 2, ORA_Q8_0 = 8, ORA_Q4_K = 12, ORA_Q5_K = 13,
-       ORA_Q6_K = 14, ORA_Q8_K = 15 };
+       ORA_Q6_K = 14, ORA_Q8_K = 15, ORA_BF16 = 30 };
 
 /* f16 -> f32 (half::f16::to_f32, used by f16_to_f32 src/metal/compute.rs:2244-2247). */
 float ora_f16_to_f32(uint16_t h);
