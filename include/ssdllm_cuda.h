@@ -68,6 +68,11 @@ extern "C" {
  * 256 weights in 292 bytes, f32 d, 256 int8, 32 bytes of block sums (not read by the
  * matvec, kept for the download); weight = d * q. */
 #define SSD_TYPE_Q8_K 15
+/* 16-bit dense weights, row-major, 2 bytes each: F16 (IEEE half, matvec_f16_cpu,
+ * src/metal/compute.rs:2272-2285) and BF16 (the top half of an f32, matvec_bf16_cpu,
+ * :2250-2269). Accepted by ssd_weight_upload, ssd_dequantize and the plain matvec entry
+ * points (any column count). */
+#define SSD_TYPE_BF16 30
 
 typedef struct ssd_ctx ssd_ctx;
 typedef struct ssd_weight ssd_weight;

@@ -73,6 +73,7 @@ struct ssd_ctx {
 //         meta = [rows][cols/32][4 B: int8 scale of elements 0-15, of 16-31, f16 d]
 //   Q8_K: qs = [rows][cols/32][32 B int8], meta = [rows][cols/32] f32 d, then the
 //         block sums of every super-block ([rows][cols/256][32 B], kept for the download)
+//   F16 / BF16: qs = [rows][cols] 2 bytes each (as in the file)
 //   F32 : qs = [rows][cols] f32
 // The bytes are the reference's bytes, regrouped; nothing is re-quantized (Q5_K's and Q6_K's
 // two bit fields are joined into one byte per weight; Q6_K's d is repeated per 32 weights).
@@ -149,6 +150,12 @@ __device__ __forceinline__ float synth_normal(uint64_t seed, uint32_t tid, uint6
 __device__ __forceinline__ void dequant8(const ssd_weight& w, int64_t e0, float (&v)[8]) {
     if (w.type == SSD_TYPE_F32) {
         for (int t = 0; t < 8; t++) v[t] = reinterpret_cast<const float*>(w.qs)[e0 + t];
+    } else if (w.type == SSD_TYPE_F16) {
+        for (int t = 0; t < 8; t++)
+            v[t] = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(w.qs)[e0 + t]);
+    } else if (w.type == SSD_TYPE_BF16) {  // bits << 16, compute.rs:2250-2253
+        for (int t = 0; t < 8; t++)
+            v[t] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(w.qs)[e0 + t] << 16);
     } else if (w.type == SSD_TYPE_Q4_0) {
         const int64_t blk = e0 / 32;
         const int j0 = (int)(e0 % 32) / 2;  // byte index
@@ -310,7 +317,8 @@ inline int type_block(int type) {
         case SSD_TYPE_Q6_K:
         case SSD_TYPE_Q8_K: return 256;
         case SSD_TYPE_F32:
-        case SSD_TYPE_F16: return 1;
+        case SSD_TYPE_F16:
+        case SSD_TYPE_BF16: return 1;
         default: return 0;
     }
 }
@@ -323,7 +331,8 @@ inline int type_block_bytes(int type) {
         case SSD_TYPE_Q6_K: return 210;
         case SSD_TYPE_Q8_K: return 292;
         case SSD_TYPE_F32: return 4;
-        case SSD_TYPE_F16: return 2;
+        case SSD_TYPE_F16:
+        case SSD_TYPE_BF16: return 2;
         default: return 0;
     }
 }

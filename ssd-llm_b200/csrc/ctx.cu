@@ -545,7 +545,7 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
                 type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K ||
-                type == SSD_TYPE_F32,
+                type == SSD_TYPE_F16 || type == SSD_TYPE_BF16 || type == SSD_TYPE_F32,
             SSD_ERR_TYPE,
             "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14, Q8_K=15, "
             "F32=0)",
@@ -573,8 +573,8 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     } else if (type == SSD_TYPE_Q6_K) {
         qs_bytes = nb * 256;
         meta_bytes = nb * 32;
-    } else {
-        qs_bytes = (size_t)rows * cols * 4;
+    } else {  // dense: F32, F16, BF16
+        qs_bytes = (size_t)rows * cols * type_block_bytes(type);
         meta_bytes = 0;
     }
     size_t qs_pad = (qs_bytes + 255) & ~(size_t)255;
@@ -610,7 +610,7 @@ extern "C" int ssd_weight_upload_device(ssd_ctx* ctx, const void* raw_dev, size_
     ssd_weight* w = nullptr;
     SSD_TRY(alloc_weight(ctx, type, rows, cols, &w));
     cudaStream_t s = pick_stream(ctx, stream);
-    if (type == SSD_TYPE_F32) {
+    if (type_block(type) == 1) {  // dense: the bytes as they are
         if (cudaMemcpyAsync(w->qs, raw_dev, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
             ssd_weight_free(w);
             SSD_CK(cudaGetLastError());
@@ -662,7 +662,7 @@ extern "C" int ssd_weight_download(ssd_ctx* ctx, const ssd_weight* w, void* host
     SSD_REQ(w && host_raw, SSD_ERR_ARG, "null argument");
     size_t need = ssd_row_bytes(w->type, w->cols) * (size_t)w->rows;
     SSD_REQ(bytes == need, SSD_ERR_SHAPE, "need %zu bytes, got %zu", need, bytes);
-    if (w->type == SSD_TYPE_F32) {
+    if (type_block(w->type) == 1) {
         SSD_CK(cudaMemcpy(host_raw, w->qs, bytes, cudaMemcpyDeviceToHost));
         return SSD_OK;
     }

@@ -928,9 +928,66 @@ static int launch_fmt(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bo
 
 static inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
+// 16-bit dense rows (matvec_f16_cpu / matvec_bf16_cpu, src/metal/compute.rs:2256-2285):
+// a warp per row; 16-byte loads of 8 weights when rows are whole multiples of 8 (one
+// weight per lane per step otherwise), fp32 products summed per lane, then across the
+// warp. y = W x, or base + W x (EPI_RESID).
+template <bool BF, int EPI>
+__global__ void __launch_bounds__(256) k_matvec_dense(const MvArgs a) {
+    pdl_wait();
+    const int lane = threadIdx.x & 31, nwarp = gridDim.x * 8;
+    const bool vec = (a.cols & 7) == 0;
+    auto cvt = [](uint32_t h) {
+        return BF ? __uint_as_float((h & 0xFFFFu) << 16) : f16_bits_to_f32((uint16_t)h);
+    };
+    for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < a.rows; row += nwarp) {
+        const uint16_t* w = reinterpret_cast<const uint16_t*>(a.qs[0]) + (size_t)row * a.cols;
+        float s = 0.0f;
+        if (vec) {
+            for (int c = 8 * lane; c < a.cols; c += 256) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(w + c));
+                const float4 x0 = __ldg(reinterpret_cast<const float4*>(a.x + c));
+                const float4 x1 = __ldg(reinterpret_cast<const float4*>(a.x + c + 4));
+                s = fmaf(cvt(q.x), x0.x, s);
+                s = fmaf(cvt(q.x >> 16), x0.y, s);
+                s = fmaf(cvt(q.y), x0.z, s);
+                s = fmaf(cvt(q.y >> 16), x0.w, s);
+                s = fmaf(cvt(q.z), x1.x, s);
+                s = fmaf(cvt(q.z >> 16), x1.y, s);
+                s = fmaf(cvt(q.w), x1.z, s);
+                s = fmaf(cvt(q.w >> 16), x1.w, s);
+            }
+        } else {
+            for (int c = lane; c < a.cols; c += 32) s = fmaf(cvt(w[c]), a.x[c], s);
+        }
+        s = warp_sum(s);
+        if (lane == 0) a.y[row] = EPI == EPI_RESID ? __fadd_rn(a.base[row], s) : s;
+    }
+}
+
+template <bool BF>
+static int launch_dense(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bool pdl) {
+    const int grid = (a.rows + 7) / 8 < ctx->num_sms * 8 ? (a.rows + 7) / 8 : ctx->num_sms * 8;
+    if (epi == EPI_RESID)
+        SSD_CK(launch_pdl(k_matvec_dense<BF, EPI_RESID>, dim3(grid), dim3(256), 0, s, pdl, a));
+    else
+        SSD_CK(launch_pdl(k_matvec_dense<BF, EPI_STORE>, dim3(grid), dim3(256), 0, s, pdl, a));
+    return SSD_OK;
+}
+
 int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_t s, bool pdl) {
     MvArgs a = a0;
     if (!a.status) a.status = ctx->dev_status;
+    if (type == SSD_TYPE_F16 || type == SSD_TYPE_BF16) {
+        SSD_REQ(a.rows > 0 && a.cols > 0, SSD_ERR_SHAPE, "empty matrix");
+        SSD_REQ(a.x && a.y && ((uintptr_t)a.x & 15) == 0, SSD_ERR_ARG,
+                "x and y must be non-null, x 16-byte aligned");
+        SSD_REQ((epi == EPI_STORE || (epi == EPI_RESID && a.base)) && a.map == MAP_PLAIN &&
+                    !a.x_add && !a.norm_w && a.ar_in_n == 0,
+                SSD_ERR_ARG, "16-bit dense weights: plain or residual matvec only");
+        return type == SSD_TYPE_BF16 ? launch_dense<true>(ctx, epi, a, s, pdl)
+                                     : launch_dense<false>(ctx, epi, a, s, pdl);
+    }
     SSD_REQ(a.cols > 0 && a.cols % 32 == 0, SSD_ERR_SHAPE, "cols %d not a multiple of 32", a.cols);
     SSD_REQ(a.rows > 0, SSD_ERR_SHAPE, "no rows");
     // x, x_add, x_writeback and norm_w are read by TMA / written as float4
@@ -1000,7 +1057,8 @@ using namespace ssd;
 static int check_w(const ssd_weight* w) {
     SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
     SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
-                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_Q8_K,
+                w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_Q8_K ||
+                w->type == SSD_TYPE_F16 || w->type == SSD_TYPE_BF16,
             SSD_ERR_TYPE, "matvec: ggml type %d not supported", w->type);
     return SSD_OK;
 }
@@ -1111,7 +1169,8 @@ extern "C" int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, siz
     SSD_TRY(check_ctx(ctx));
     SSD_REQ(w_raw && x && y, SSD_ERR_ARG, "null pointer");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
-                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K,
+                type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K ||
+                type == SSD_TYPE_F16 || type == SSD_TYPE_BF16,
             SSD_ERR_TYPE, "matvec_quantized: ggml type %d not supported", type);
     ssd_weight* w = nullptr;
     SSD_TRY(ssd_weight_upload(ctx, w_raw, w_bytes, type, out_dim, in_dim, &w));

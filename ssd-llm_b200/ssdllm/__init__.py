@@ -17,9 +17,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(HERE, "libssdllm_cuda.so")
 
-F32, F16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K = 0, 1, 2, 8, 12, 13, 14, 15
+F32, F16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 0, 1, 2, 8, 12, 13, 14, 15, 30
 BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
-         Q8_K: (256, 292), F32: (1, 4)}
+         Q8_K: (256, 292), F16: (1, 2), BF16: (1, 2), F32: (1, 4)}
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported ggml type", 3: "shape mismatch",
           4: "CUDA error", 5: "device wait timed out", 6: "NCCL error",
           7: "out of device memory", 8: "invalid state"}
