@@ -355,6 +355,35 @@ def case_matvec_q6k(ctx, torch, ssdllm, peak, rows=11008, cols=4096, reps=20):
             "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
 
 
+def case_matvec_dense16(ctx, torch, ssdllm, peak, wtype=30, rows=11008, cols=4096, reps=20):
+    """16-bit dense (BF16 = 30, F16 = 1) matvec at a config-1 shape: random normal rows
+    scaled by 0.05, rotating copies > 2x L2 in total, uploaded through ssd_weight_upload."""
+    import numpy as np
+    raw_bytes = rows * cols * 2
+    copies = min(16, max(2, -(-int(2.2 * L2_BYTES) // raw_bytes)))
+    rng = np.random.default_rng(12)
+    ws = []
+    for _ in range(copies):
+        f = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32)
+        raw = (f.astype(np.float16).view(np.uint16) if wtype == 1
+               else (f.view(np.uint32) >> 16).astype(np.uint16))
+        ws.append(ssdllm.Weight.upload(ctx, raw.view(np.uint8), wtype, rows, cols))
+    x = torch.randn(cols, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+    y = torch.zeros(rows, device="cuda")
+    n = max(copies, 64 // copies * copies)
+    alg = rows * cols * 2 + cols * 4 + rows * 4
+    ctx.set_pdl(True)
+    us = _graph_time(torch, [lambda w=ws[i % copies]: ssdllm.matvec(ctx, w, x, y)
+                             for i in range(n)], reps)
+    ctx.set_pdl(False)
+    for w in ws:
+        w.free()
+    return {"type": "F16" if wtype == 1 else "BF16", "shape": [rows, cols],
+            "algorithmic_bytes": alg, "rotating_copies": copies,
+            "us_per_launch": round(us, 3), "gbs": round(alg / us / 1e3, 1),
+            "frac_of_peak": round(alg / us / 1e3 / peak, 4)}
+
+
 def case_attention(ctx, torch, ssdllm, peak, n_head=64, n_head_kv=8, head_dim=128, seq=4096,
                    reps=20):
     """Split-K flash-decode over the INT8 KV cache (70B shape: 64 q / 8 kv heads,
@@ -588,6 +617,8 @@ CASES = {
     "q4_k_11008x4096": lambda c, t, s, p: case_matvec(c, t, s, p, 12, 11008, 4096),
     "q4_k_4096x11008": lambda c, t, s, p: case_matvec(c, t, s, p, 12, 4096, 11008),
     "q6_k_11008x4096": case_matvec_q6k,
+    "bf16_11008x4096": case_matvec_dense16,
+    "f16_11008x4096": lambda c, t, s, p: case_matvec_dense16(c, t, s, p, wtype=1),
     "swiglu_q4_0_70b": case_swiglu_70b,
     "attn_int8_70b_4096": case_attention,
     "layer_7b_q4_0": case_layer_7b,

@@ -928,51 +928,98 @@ static int launch_fmt(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bo
 
 static inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
-// 16-bit dense rows (matvec_f16_cpu / matvec_bf16_cpu, src/metal/compute.rs:2256-2285):
-// a warp per row; 16-byte loads of 8 weights when rows are whole multiples of 8 (one
-// weight per lane per step otherwise), fp32 products summed per lane, then across the
-// warp. y = W x, or base + W x (EPI_RESID).
+// 16-bit dense rows (matvec_f16_cpu / matvec_bf16_cpu, src/metal/compute.rs:2256-2285).
+// Each CTA takes a contiguous, balanced range of rows (counts differ by at most one
+// between CTAs, so no half-empty second pass over a few leftover rows), four rows at a
+// time: its 256 threads split the columns (thread t owns columns 8t..8t+7 of every
+// 2048-column step, one 16-byte load per row, when cols % 8 == 0; single columns
+// otherwise), x is loaded once per step for the four rows, each warp sums its share, and
+// thread i adds the 8 warp partials of row i in warp order. y = W x, or base + W x.
+constexpr int kDenseRows = 4;
+
 template <bool BF, int EPI>
 __global__ void __launch_bounds__(256) k_matvec_dense(const MvArgs a) {
+    __shared__ float part[8][kDenseRows];
     pdl_wait();
-    const int lane = threadIdx.x & 31, nwarp = gridDim.x * 8;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = (int)((int64_t)a.rows * blockIdx.x / gridDim.x);
+    const int r1 = (int)((int64_t)a.rows * (blockIdx.x + 1) / gridDim.x);
     const bool vec = (a.cols & 7) == 0;
+    const uint16_t* wbase = reinterpret_cast<const uint16_t*>(a.qs[0]);
     auto cvt = [](uint32_t h) {
         return BF ? __uint_as_float((h & 0xFFFFu) << 16) : f16_bits_to_f32((uint16_t)h);
     };
-    for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < a.rows; row += nwarp) {
-        const uint16_t* w = reinterpret_cast<const uint16_t*>(a.qs[0]) + (size_t)row * a.cols;
-        float s = 0.0f;
+    for (int g = r0; g < r1; g += kDenseRows) {
+        const int nr = r1 - g < kDenseRows ? r1 - g : kDenseRows;
+        const uint16_t* w[kDenseRows];
+#pragma unroll
+        for (int i = 0; i < kDenseRows; i++)  // rows past the range re-read the last one
+            w[i] = wbase + (size_t)(g + (i < nr ? i : nr - 1)) * a.cols;
+        float s[kDenseRows];
+#pragma unroll
+        for (int i = 0; i < kDenseRows; i++) s[i] = 0.0f;
         if (vec) {
-            for (int c = 8 * lane; c < a.cols; c += 256) {
-                const uint4 q = __ldg(reinterpret_cast<const uint4*>(w + c));
+            for (int c = 8 * threadIdx.x; c < a.cols; c += 2048) {
+                uint4 q[kDenseRows];
+#pragma unroll
+                for (int i = 0; i < kDenseRows; i++)
+                    q[i] = __ldg(reinterpret_cast<const uint4*>(w[i] + c));
                 const float4 x0 = __ldg(reinterpret_cast<const float4*>(a.x + c));
                 const float4 x1 = __ldg(reinterpret_cast<const float4*>(a.x + c + 4));
-                s = fmaf(cvt(q.x), x0.x, s);
-                s = fmaf(cvt(q.x >> 16), x0.y, s);
-                s = fmaf(cvt(q.y), x0.z, s);
-                s = fmaf(cvt(q.y >> 16), x0.w, s);
-                s = fmaf(cvt(q.z), x1.x, s);
-                s = fmaf(cvt(q.z >> 16), x1.y, s);
-                s = fmaf(cvt(q.w), x1.z, s);
-                s = fmaf(cvt(q.w >> 16), x1.w, s);
+#pragma unroll
+                for (int i = 0; i < kDenseRows; i++) {
+                    s[i] = fmaf(cvt(q[i].x), x0.x, s[i]);
+                    s[i] = fmaf(cvt(q[i].x >> 16), x0.y, s[i]);
+                    s[i] = fmaf(cvt(q[i].y), x0.z, s[i]);
+                    s[i] = fmaf(cvt(q[i].y >> 16), x0.w, s[i]);
+                    s[i] = fmaf(cvt(q[i].z), x1.x, s[i]);
+                    s[i] = fmaf(cvt(q[i].z >> 16), x1.y, s[i]);
+                    s[i] = fmaf(cvt(q[i].w), x1.z, s[i]);
+                    s[i] = fmaf(cvt(q[i].w >> 16), x1.w, s[i]);
+                }
             }
         } else {
-            for (int c = lane; c < a.cols; c += 32) s = fmaf(cvt(w[c]), a.x[c], s);
+            for (int c = threadIdx.x; c < a.cols; c += 256) {
+                const float xv = a.x[c];
+#pragma unroll
+                for (int i = 0; i < kDenseRows; i++) s[i] = fmaf(cvt(w[i][c]), xv, s[i]);
+            }
         }
-        s = warp_sum(s);
-        if (lane == 0) a.y[row] = EPI == EPI_RESID ? __fadd_rn(a.base[row], s) : s;
+#pragma unroll
+        for (int i = 0; i < kDenseRows; i++) {
+            const float v = warp_sum(s[i]);
+            if (lane == 0) part[warp][i] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < nr) {
+            float t = part[0][threadIdx.x];
+#pragma unroll
+            for (int k = 1; k < 8; k++) t += part[k][threadIdx.x];
+            const int row = g + threadIdx.x;
+            a.y[row] = EPI == EPI_RESID ? __fadd_rn(a.base[row], t) : t;
+        }
+        __syncthreads();
     }
+}
+
+template <bool BF, int EPI>
+static int launch_dense_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
+    static int per_sm = 0;  // resident CTAs per SM (same on every device of one build)
+    if (per_sm == 0) {
+        int n = 0;
+        SSD_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_matvec_dense<BF, EPI>, 256, 0));
+        per_sm = n > 0 ? n : 1;
+    }
+    const int full = ctx->num_sms * per_sm;
+    const int grid = a.rows < full ? a.rows : full;
+    SSD_CK(launch_pdl(k_matvec_dense<BF, EPI>, dim3(grid), dim3(256), 0, s, pdl, a));
+    return SSD_OK;
 }
 
 template <bool BF>
 static int launch_dense(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bool pdl) {
-    const int grid = (a.rows + 7) / 8 < ctx->num_sms * 8 ? (a.rows + 7) / 8 : ctx->num_sms * 8;
-    if (epi == EPI_RESID)
-        SSD_CK(launch_pdl(k_matvec_dense<BF, EPI_RESID>, dim3(grid), dim3(256), 0, s, pdl, a));
-    else
-        SSD_CK(launch_pdl(k_matvec_dense<BF, EPI_STORE>, dim3(grid), dim3(256), 0, s, pdl, a));
-    return SSD_OK;
+    return epi == EPI_RESID ? launch_dense_epi<BF, EPI_RESID>(ctx, a, s, pdl)
+                            : launch_dense_epi<BF, EPI_STORE>(ctx, a, s, pdl);
 }
 
 int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_t s, bool pdl) {
