@@ -159,7 +159,8 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
                 c->embd_type == SSD_TYPE_Q8_0 || c->embd_type == SSD_TYPE_Q4_K ||
                 c->embd_type == SSD_TYPE_Q5_K || c->embd_type == SSD_TYPE_Q6_K ||
-                c->embd_type == SSD_TYPE_Q8_K,
+                c->embd_type == SSD_TYPE_Q8_K || c->embd_type == SSD_TYPE_F16 ||
+                c->embd_type == SSD_TYPE_BF16,
             SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
     SSD_REQ(type_block(c->out_type) == 32 || type_block(c->out_type) == 256, SSD_ERR_TYPE,
             "output type %d not supported", c->out_type);
@@ -521,7 +522,8 @@ extern "C" int ssd_model_set_tensor_typed(ssd_model* m, const char* cname, int l
         SSD_REQ(ggml_type == SSD_TYPE_Q4_0 || ggml_type == SSD_TYPE_Q8_0 ||
                     ggml_type == SSD_TYPE_Q4_K || ggml_type == SSD_TYPE_Q5_K ||
                     ggml_type == SSD_TYPE_Q6_K || ggml_type == SSD_TYPE_Q8_K ||
-                    (embd && ggml_type == SSD_TYPE_F32),
+                    (embd && (ggml_type == SSD_TYPE_F32 || ggml_type == SSD_TYPE_F16 ||
+                              ggml_type == SSD_TYPE_BF16)),
                 SSD_ERR_TYPE, "%s: ggml type %d not supported here", cname, ggml_type);
         const int tb = type_block(ggml_type);
         SSD_REQ(s.cols % tb == 0 && s.col0 % tb == 0 && s.ncols % tb == 0, SSD_ERR_SHAPE,

@@ -607,8 +607,8 @@ __global__ void k_finalize(unsigned long long* key, int32_t* token, int* pos,
 
 int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
                  bool pdl) {
-    SSD_REQ(type_block(emb->type) != 0 && emb->type != SSD_TYPE_F16 && emb->cols % 8 == 0,
-            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K)",
+    SSD_REQ(type_block(emb->type) != 0 && emb->cols % 8 == 0, SSD_ERR_TYPE,
+            "token_embd type %d not supported (F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K)",
             emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(1), dim3(256), 0, s, pdl, *emb, token_dev, hidden));
     return SSD_OK;
@@ -616,8 +616,8 @@ int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden,
 
 int launch_embed_rows(const ssd_weight* emb, const int32_t* tokens_dev, int n, float* hidden,
                       cudaStream_t s) {
-    SSD_REQ(type_block(emb->type) != 0 && emb->type != SSD_TYPE_F16 && emb->cols % 8 == 0,
-            SSD_ERR_TYPE, "token_embd type %d not supported (F32, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K)",
+    SSD_REQ(type_block(emb->type) != 0 && emb->cols % 8 == 0, SSD_ERR_TYPE,
+            "token_embd type %d not supported (F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K)",
             emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(n), dim3(256), 0, s, false, *emb, tokens_dev, hidden));
     return SSD_OK;

@@ -1,7 +1,8 @@
 """16-bit dense weights (F16, BF16) on the GPU against the oracle (matvec_f16_cpu /
 matvec_bf16_cpu, src/metal/compute.rs:2250-2285): the reference's own known-answer tests
 through the host-pointer entry point (2 x 2 matrices: any column count), bit-exact
-dequantization, byte round trip, and random matrices within rel. error 1e-3 (fp64 arbiter)."""
+dequantization, byte round trip, random matrices within rel. error 1e-3 (fp64 arbiter), and
+models whose token_embd is F16 / BF16 decoding like the oracle."""
 import numpy as np
 import pytest
 
@@ -37,10 +38,10 @@ def test_kats_through_the_host_entry_point(comp):
         assert np.allclose(y, expect, atol=1e-2), (t, y)
 
 
-def raw16(rng, rows, cols, t):
+def raw16(rng, rows, cols, t, scale=0.05):
     if t == F16:
-        return (rng.standard_normal((rows, cols)) * 0.05).astype(np.float16).view(np.uint8)
-    f = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32)
+        return (rng.standard_normal((rows, cols)) * scale).astype(np.float16).view(np.uint8)
+    f = (rng.standard_normal((rows, cols)) * scale).astype(np.float32)
     return (f.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
 
 
@@ -69,3 +70,49 @@ def test_matvec_and_dequant(comp, t, rows, cols):
     exact = wf.reshape(rows, cols).astype(np.float64) @ x.astype(np.float64)
     got = y.cpu().numpy()
     assert parity(got, ref, exact), (rel_err(got, ref), rel_err(ref, exact))
+
+
+@pytest.mark.parametrize("t,how", [(F16, "config"), (BF16, "set_tensor_typed")])
+def test_model_with_16bit_token_embd_decodes_like_oracle(comp, t, how):
+    """A Q4_0 model whose token_embd is F16 or BF16 (common in GGUF files), given as the
+    config's embd_type or per tensor: 24 greedy tokens equal the oracle's decode loop (a
+    near-tie below fp32 reordering noise may end the comparison early)."""
+    from test_gpu_model import build_model, make_weights, oracle_layers
+    ctx = comp.ctx
+    E, nh, nkv, hd, F, vocab, nl = 256, 4, 2, 64, 512, 384, 2
+    cfg = dict(n_layers=nl, n_embd=E, n_head=nh, n_head_kv=nkv, head_dim=hd, n_ff=F, vocab=vocab,
+               wtype=ora.Q4_0, out_type=ora.Q4_0, embd_type=t if how == "config" else ora.Q4_0,
+               kv_capacity=32, theta=1e4, eps=1e-5, tp_rank=0, tp_size=1)
+    rng = np.random.default_rng(81 + t)
+    layers, glob = make_weights(rng, E, nh, nkv, hd, F, vocab, nl)
+    emb_raw = raw16(rng, vocab, E, t, scale=1.0).reshape(vocab, 2 * E)
+    glob = dict(glob)
+    del glob["token_embd"]
+    m = build_model(ctx, cfg, layers, glob)
+    try:
+        m.set_tensor("token_embd", -1, emb_raw, wtype=None if how == "config" else t)
+        m.set_position(0)
+        gpu, tok = [], 7
+        for _ in range(24):
+            tok = m.decode_token(tok, use_graph=True)
+            gpu.append(tok)
+    finally:
+        m.free()
+    OL = oracle_layers(cfg, layers)
+    emb = ora.dequantize(emb_raw, t, vocab * E).reshape(vocab, E)
+    out_w = ora.dequantize(glob["output"], ora.Q4_0, vocab * E).reshape(vocab, E)
+    kvd = nkv * hd
+    caches = [(np.zeros((32, kvd), np.int8), np.zeros(32, np.float32),
+               np.zeros((32, kvd), np.int8), np.zeros(32, np.float32)) for _ in range(nl)]
+    tok = 7
+    for pos in range(24):
+        h = emb[tok].copy()
+        for li in range(nl):
+            kc, ks, vc, vs = caches[li]
+            OL[li].step(h, pos, kc, ks, vc, vs, mode=0, threads=4)
+        logits = ora.fused_rmsnorm_linear(h, glob["output_norm"], out_w, vocab, E)
+        tok = ora.argmax(logits)
+        if gpu[pos] != tok:
+            srt = np.sort(logits)
+            assert (srt[-1] - srt[-2]) / np.max(np.abs(logits)) < 1e-4, (pos, gpu[pos], tok)
+            return
