@@ -1,8 +1,8 @@
 """16-bit dense weights (F16, BF16) on the GPU against the oracle (matvec_f16_cpu /
 matvec_bf16_cpu, src/metal/compute.rs:2250-2285): the reference's own known-answer tests
 through the host-pointer entry point (2 x 2 matrices: any column count), bit-exact
-dequantization, byte round trip, random matrices within rel. error 1e-3 (fp64 arbiter), and
-models whose token_embd is F16 / BF16 decoding like the oracle."""
+dequantization, byte round trip, random matrices within rel. error 1e-3 (fp64 arbiter), the residual epilogue, the refusal
+of fused epilogues, and models whose token_embd is F16 / BF16 decoding like the oracle."""
 import numpy as np
 import pytest
 
@@ -116,3 +116,32 @@ def test_model_with_16bit_token_embd_decodes_like_oracle(comp, t, how):
             srt = np.sort(logits)
             assert (srt[-1] - srt[-2]) / np.max(np.abs(logits)) < 1e-4, (pos, gpu[pos], tok)
             return
+
+
+@pytest.mark.parametrize("t", [F16, BF16])
+def test_residual_matvec_and_refused_fused_epilogues(comp, t):
+    """y = base + W x on 16-bit rows within rel. error 1e-3 of the oracle; the fused RMSNorm /
+    SwiGLU prologue + epilogue is not offered for these types and fails with an error
+    instead of a wrong result."""
+    ctx = comp.ctx
+    rng = np.random.default_rng(90 + t)
+    rows, cols = 2048, 1024
+    raw = raw16(rng, rows, cols, t).reshape(rows, 2 * cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    base = rng.standard_normal(rows).astype(np.float32)
+    w = ssdllm.Weight.upload(ctx, raw, t, rows, cols)
+    try:
+        y = torch.zeros(rows, device=DEV)
+        ssdllm.matvec_residual(ctx, w, torch.from_numpy(x).to(DEV),
+                               torch.from_numpy(base).to(DEV), y)
+        torch.cuda.synchronize()
+        got = y.cpu().numpy()
+        with pytest.raises(ssdllm.SsdError):
+            ssdllm.fused_swiglu(ctx, w, w, torch.from_numpy(x).to(DEV),
+                                torch.ones(cols, device=DEV), 1e-5,
+                                torch.zeros(rows, device=DEV))
+        torch.cuda.synchronize()
+    finally:
+        w.free()
+    ref = base + ora.matvec_quantized(raw, x, rows, cols, t, threads=8)
+    assert rel_err(got, ref) <= 1e-3
