@@ -85,6 +85,12 @@ struct ssd_weight {
     uint8_t* meta = nullptr;
     void* base = nullptr;  // allocation
     size_t alloc_bytes = 0;
+    // Split-K scratch of the tensor-core matvec (matvec_i8.cu), inside the same allocation:
+    // arrival counters per row tile (zeroed at allocation, reset by each launch's last
+    // arrival) and two partial rows of 128 floats per CTA. Calls that use the same weight
+    // must not overlap on the GPU.
+    unsigned int* fix_counter = nullptr;
+    float* fix_partial = nullptr;
 };
 
 struct ssd_kv_cache {
@@ -361,7 +367,13 @@ int encode_rows_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint6
 // shared row r at u ^ (r & 7) when box_rows is 8). row_bytes must be a multiple of 128.
 int encode_blocks_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
                       uint32_t box_rows, uint32_t box_blocks);
+// 2-D byte tensor map over `rows` rows of row_bytes at ptr: box = box_bytes x box_rows,
+// the 128-byte swizzle (box_bytes 128) or none; out-of-range rows read as zero.
+int encode_bytes_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
+                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128);
 constexpr int kVecBoxRows = 32;
+// Largest grid of the tensor-core matvec (matvec_i8.cu); sizes the split-K scratch of a weight.
+constexpr int kI8MaxGrid = 160;
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out);
 int ensure_scratch(ssd_ctx* ctx, size_t bytes);
 

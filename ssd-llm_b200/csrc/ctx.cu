@@ -91,6 +91,27 @@ int encode_blocks_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uin
     return SSD_OK;
 }
 
+int encode_bytes_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint64_t rows,
+                     uint32_t box_bytes, uint32_t box_rows, bool swizzle128) {
+    EncodeTiledFn fn;
+    SSD_TRY(tensor_map_fn(&fn));
+    SSD_REQ(ptr && ((uintptr_t)ptr & 15u) == 0 && row_bytes % 16 == 0 && rows >= 1 &&
+                box_bytes % 16 == 0 && box_bytes >= 16 && box_bytes <= (swizzle128 ? 128u : 256u) &&
+                box_rows >= 1 && box_rows <= 256,
+            SSD_ERR_ARG, "tensor map: rows of %llu bytes (box %u x %u) not tileable",
+            (unsigned long long)row_bytes, box_bytes, box_rows);
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {box_bytes, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    SSD_REQ(r == CUDA_SUCCESS, SSD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SSD_OK;
+}
+
 void set_error(const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -578,7 +599,15 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
         meta_bytes = 0;
     }
     size_t qs_pad = (qs_bytes + 255) & ~(size_t)255;
-    size_t total = qs_pad + meta_bytes + 256;
+    size_t meta_pad = (meta_bytes + 255) & ~(size_t)255;
+    // split-K scratch of the tensor-core matvec (quantized types): counters for up to
+    // 2 * ceil(rows / 64) + 16 row tiles (a fused QKV or gate/up launch uses the first
+    // weight's), partial rows for kI8MaxGrid CTAs
+    const bool fix = type_block(type) > 1;
+    const size_t n_counters = fix ? 2 * (((size_t)rows + 63) / 64) + 16 : 0;
+    const size_t counter_bytes = (n_counters * 4 + 255) & ~(size_t)255;
+    const size_t partial_bytes = fix ? (size_t)2 * kI8MaxGrid * 128 * 4 : 0;
+    size_t total = qs_pad + meta_pad + counter_bytes + partial_bytes + 256;
     void* p = nullptr;
     if (cudaMalloc(&p, total) != cudaSuccess) {
         cudaGetLastError();
@@ -594,6 +623,18 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     w->alloc_bytes = total;
     w->qs = (uint8_t*)p;
     w->meta = meta_bytes ? (uint8_t*)p + qs_pad : nullptr;
+    if (fix) {
+        uint8_t* f = (uint8_t*)p + qs_pad + meta_pad;
+        if (cudaMemset(f, 0, counter_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(p);
+            delete w;
+            set_error("weight scratch initialisation failed");
+            return SSD_ERR_CUDA;
+        }
+        w->fix_counter = reinterpret_cast<unsigned int*>(f);
+        w->fix_partial = reinterpret_cast<float*>(f + counter_bytes);
+    }
     *out = w;
     return SSD_OK;
 }

@@ -1060,19 +1060,24 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
     SSD_REQ(epi != EPI_QKV_ROPE || (a.y_k && a.y_v), SSD_ERR_ARG, "null K/V output");
     SSD_REQ(epi != EPI_QKV_ROPE || (a.head_dim > 0 && a.head_dim / 2 <= kMaxRopePairs),
             SSD_ERR_SHAPE, "head_dim %d outside (0, %d]", a.head_dim, 2 * kMaxRopePairs);
-    // Kernel choice: this FMA kernel (nibbles and scales unpacked in registers) for every
-    // shape. The integer tensor-core kernel (matvec_tc.cu) is an opt-in study
-    // (SSD_MV_IMPL=tc, where it covers the shape): measured per decode shape of the 70B
-    // model (bench.py --case mv_shapes_70b) it is faster only on the fused gate/up of
-    // >= 28672 rows (6 % at TP1), and tensor cores are kept for the prefill contractions.
-    // Read per call so that one process can compare the two.
+    // Kernel choice: this FMA kernel (nibbles and scales unpacked in registers, dot products
+    // on the fp32 pipe) for every shape. Two tensor-core kernels cover the common shapes
+    // and are selected per call by SSD_MV_IMPL (read per call so that one process can
+    // compare them): "i8" the tcgen05 kernel (matvec_i8.cu: Q4_0 / Q8_0 / Q4_K / Q5_K /
+    // Q8_K, cols % 256 == 0, a weight with its split-K scratch), "tc" the mma.sync kernel
+    // (matvec_tc.cu). Batch 1 keeps the FMA kernel: a tcgen05.mma of M = 128 issues at
+    // most once per ~93 cycles, so the tcgen05 kernel tops out near the Q4_0 HBM rate
+    // (~44 weights per cycle per SM against ~41 needed) before its fixed costs.
     const char* impl = getenv("SSD_MV_IMPL");
-    const bool force_tc = impl && strcmp(impl, "tc") == 0;
-    const bool want_tc = force_tc;
-    if (want_tc && (type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 ||
-                    (type == SSD_TYPE_Q4_K && a.cols % 256 == 0))) {
+    if (impl && strcmp(impl, "tc") == 0 &&
+        (type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 ||
+         (type == SSD_TYPE_Q4_K && a.cols % 256 == 0))) {
         const int st = launch_matvec_tc(ctx, type, epi, a, s, pdl);
         if (st != kTcNotCovered) return st;
+    }
+    if (impl && strcmp(impl, "i8") == 0) {
+        const int st = launch_matvec_i8(ctx, type, epi, a, s, pdl);
+        if (st != kI8NotCovered) return st;
     }
     switch (type) {
         case SSD_TYPE_Q4_0: return launch_fmt<SSD_TYPE_Q4_0>(ctx, epi, a, s, pdl);
@@ -1167,6 +1172,8 @@ extern "C" int ssd_fused_qkv_rope(ssd_ctx* ctx, const ssd_weight* wq, const ssd_
     a.seg_rows[1] = wk->rows;
     a.seg_rows[2] = wv->rows;
     a.map = MAP_QKV;
+    a.fix_counter = wq->fix_counter;
+    a.fix_partial = wq->fix_partial;
     a.rows = wq->rows + wk->rows + wv->rows;
     a.cols = wq->cols;
     a.x = x;
@@ -1200,6 +1207,8 @@ extern "C" int ssd_fused_swiglu(ssd_ctx* ctx, const ssd_weight* wg, const ssd_we
     a.seg_rows[0] = wg->rows;
     a.seg_rows[1] = wu->rows;
     a.map = MAP_SWIGLU;
+    a.fix_counter = wg->fix_counter;
+    a.fix_partial = wg->fix_partial;
     a.rows = 2 * wg->rows;
     a.cols = wg->cols;
     a.x = x;

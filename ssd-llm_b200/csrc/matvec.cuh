@@ -61,6 +61,10 @@ struct MvArgs {
     unsigned int* ar_counter;
     const unsigned long long* ar_epoch;
     int ar_call;
+    // Split-K scratch of the tensor-core kernel (matvec_i8.cu): per-tile arrival counters
+    // (zero between launches) and per-CTA partial rows, owned by the first weight.
+    unsigned int* fix_counter;
+    float* fix_partial;
 };
 
 // Launches y = f(W x) with the given epilogue. pdl: launch with programmatic
@@ -78,6 +82,8 @@ inline MvArgs mv_plain(const ssd_weight* w, const float* x, float* y) {
     a.cols = w->cols;
     a.x = x;
     a.y = y;
+    a.fix_counter = w->fix_counter;
+    a.fix_partial = w->fix_partial;
     return a;
 }
 

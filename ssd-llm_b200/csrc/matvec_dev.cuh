@@ -243,5 +243,9 @@ static int occupancy(ssd_ctx* ctx, K kern, int threads, size_t smem, int* out) {
 // without launching when the shape is not one it covers.
 constexpr int kTcNotCovered = -1000;
 int launch_matvec_tc(ssd_ctx* ctx, int type, int epi, const MvArgs& a, cudaStream_t s, bool pdl);
+// tcgen05 integer tensor-core kernel (matvec_i8.cu): launches it, or returns kI8NotCovered
+// without launching when the type, shape or row map is not one it covers.
+constexpr int kI8NotCovered = -1001;
+int launch_matvec_i8(ssd_ctx* ctx, int type, int epi, const MvArgs& a, cudaStream_t s, bool pdl);
 
 }  // namespace ssd

@@ -1,7 +1,8 @@
-"""GPU parity of the two matvec kernels: the integer tensor-core kernel (matvec_tc.cu,
-covering cols % 256 == 0, cols >= 2048; opt-in with SSD_MV_IMPL=tc)
-and the FMA kernel (matvec.cu, every shape), each forced in turn with SSD_MV_IMPL=tc /
-fma, which the library reads on each call.
+"""GPU parity of the three matvec kernels: the tcgen05 integer tensor-core kernel
+(matvec_i8.cu, covering cols % 256 == 0; opt-in with SSD_MV_IMPL=i8), the mma.sync
+integer tensor-core kernel (matvec_tc.cu, covering cols % 256 == 0, cols >= 2048; opt-in
+with SSD_MV_IMPL=tc) and the FMA kernel (matvec.cu, every shape), each forced in turn
+with SSD_MV_IMPL=i8 / tc / fma, which the library reads on each call.
 
 Both are checked against the oracle's matvec_quantized (src/metal/compute.rs:680-750,
 :904-925) on shapes that exercise the tensor-core kernel's own structure: ragged row
@@ -24,7 +25,7 @@ from _util import normwise, parity, rel_err  # noqa: E402
 
 TOL = 1e-3
 DEV = "cuda:0"
-IMPLS = ["tc", "fma"]
+IMPLS = ["i8", "tc", "fma"]
 
 
 @pytest.fixture(scope="module")
@@ -106,14 +107,17 @@ def test_matvec_wide_dynamic_range_chunks(ctx, impl, wtype):
     check_matvec(ctx, wtype, rows, cols, wild_x(rng, cols), seed=11)
 
 
-def test_tensor_core_kernel_is_deterministic_and_close_to_fma(ctx, monkeypatch):
+@pytest.mark.parametrize("tc_impl", ["i8", "tc"])
+def test_tensor_core_kernel_is_deterministic_and_close_to_fma(ctx, monkeypatch, tc_impl):
+    """Both tensor-core kernels add their partial sums in a fixed order (the tcgen05 kernel
+    across CTAs of a split tile too), so two calls give identical bits."""
     rng = np.random.default_rng(3)
     rows, cols = 8192, 4096
     raw = ora.quantize(randw(rng, rows, cols), ora.Q4_0)
     w = ssdllm.Weight.upload(ctx, raw, ora.Q4_0, rows, cols)
     x = d(rng.standard_normal(cols).astype(np.float32))
     ys = []
-    for env in ("tc", "tc", "fma"):
+    for env in (tc_impl, tc_impl, "fma"):
         monkeypatch.setenv("SSD_MV_IMPL", env)
         y = torch.zeros(rows, device=DEV)
         ssdllm.matvec(ctx, w, x, y)
