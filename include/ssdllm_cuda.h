@@ -376,6 +376,43 @@ int ssd_model_layer_step(ssd_model* m, int layer);
 /* Kernel launches issued by one decode step. No reference counterpart (reports). */
 int ssd_model_launches_per_step(ssd_model* m, int* launches);
 
+/* ------------------------------------------------ continuous-batch decode */
+/* Sixteen decode slots over one model's weights: BatchScheduler (src/inference/
+ * batch_scheduler.rs:24-129), whose step (:149-403) runs its decoding requests layer-major
+ * (:236-296), each with its own KV cache and position. A slot holds one request; between
+ * steps the caller may give a slot a new request (ssd_batch_set_position to its start,
+ * then its prompt tokens as the slot's input of the next steps), which is the scheduler's
+ * admission of queued requests (:157-166). One GPU (tp_size 1); layer and output weights
+ * Q4_0 / Q8_0 / Q4_K with widths multiple of 256, head_dim <= 128. */
+typedef struct ssd_batch ssd_batch;
+/* BatchScheduler::new with its slots' caches (src/inference/batch_scheduler.rs:89-100,
+ * the per-request KvCache of submit, :103-129);
+ * capacity: INT8 KV positions per slot (every layer, every slot). */
+int ssd_batch_create(ssd_model* m, int capacity, ssd_batch** out);
+int ssd_batch_free(ssd_batch* b);
+int ssd_batch_slots(ssd_batch* b, int* slots);
+/* One step of every slot (BatchScheduler::step's decode phase and sampling,
+ * src/inference/batch_scheduler.rs:225-363): tokens_in (host, one per slot) or NULL to feed
+ * each slot its last output; the greedy next tokens into tokens_out (host, may be NULL); every slot's position
+ * += 1 (stopping at the capacity). Captured into a CUDA graph on first use when
+ * use_graph != 0. */
+int ssd_batch_step(ssd_batch* b, const int32_t* tokens_in, int32_t* tokens_out, int use_graph);
+/* A slot's position (a request's `position`, src/inference/batch_scheduler.rs:231, :350). */
+int ssd_batch_set_position(ssd_batch* b, int slot, int pos);
+int ssd_batch_positions(ssd_batch* b, int* pos);
+/* Fill every slot's cache at positions [0, n) (K / V rows N(0,1), INT8-quantized) and set
+ * every position to n. No reference counterpart (benchmark inputs). */
+int ssd_batch_synth_kv(ssd_batch* b, uint64_t seed, int n);
+/* Device pointers of one (layer, slot) INT8 cache: the layer cache of the slot's request
+ * (src/inference/quantized_kv_cache.rs:101-130). */
+int ssd_batch_kv_pointers(ssd_batch* b, int layer, int slot, int8_t** k, int8_t** v, float** ks,
+                          float** vs);
+/* Device pointer of the slots' hidden states [16][n_embd] after a step (each request's
+ * hidden_state, src/inference/batch_scheduler.rs:300-303). */
+int ssd_batch_state(ssd_batch* b, float** hidden_dev);
+/* Kernel launches issued by one batch step. No reference counterpart (reports). */
+int ssd_batch_launches_per_step(ssd_batch* b, int* launches);
+
 /* ------------------------------------------------------------ GGUF files */
 typedef struct ssd_gguf ssd_gguf;
 /* GgufFile::open (src/model/gguf.rs:233-315): parses the header, metadata and tensor

@@ -29,6 +29,7 @@
 
 #include "gemm.cuh"
 #include "matvec.cuh"
+#include "matvec_b.cuh"
 #include "ops.cuh"
 
 #define SSD_NCCL(call)                                                                \
@@ -1178,3 +1179,434 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
     return SSD_OK;
 }
 
+
+// ====================================================== continuous-batch decode
+// BatchScheduler::step (src/inference/batch_scheduler.rs:149-403) runs its decoding
+// requests layer-major: each layer's weights are loaded once and applied to every request
+// in turn (:236-296), each request with its own KV cache and position. Here the 16 slots of
+// a batch go through each layer together: every projection is one batched tensor-core
+// matvec over the 16 hidden vectors (matvec_b.cu, the weights streamed once for all), the
+// attention one launch over the slots' own INT8 caches (the new K/V rows appended at each
+// slot's position inside it). A slot whose request ends is given a new one between steps
+// (ssd_batch_set_position + its tokens in the next steps' input), which is the scheduler's
+// admission of queued requests (:157-166).
+
+__global__ void k_batch_finalize(unsigned long long* keys, int32_t* tokens, int* pos, int n,
+                                 int capacity) {
+    pdl_wait();
+    const int t = threadIdx.x;
+    if (t < n) {
+        tokens[t] = (int32_t)(uint32_t)(keys[t] & 0xFFFFFFFFull);
+        keys[t] = 0ull;
+        pos[t] = pos[t] + 1 < capacity ? pos[t] + 1 : capacity;
+    }
+}
+
+struct ssd_batch {
+    ssd_model* m = nullptr;
+    int slots = kBatchTokens, capacity = 0;
+    void* alloc = nullptr;
+    int8_t *kk = nullptr, *vv = nullptr;  // [layer][slot][capacity][kv_dim]
+    float *ks = nullptr, *vs = nullptr;   // [layer][slot][capacity]
+    float *h_a = nullptr, *h_b = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
+    float *attn = nullptr, *act = nullptr, *part = nullptr;
+    uint8_t* bop = nullptr;
+    float* cst = nullptr;
+    unsigned int* counter = nullptr;
+    float* partial = nullptr;
+    int32_t* tokens = nullptr;
+    int* pos = nullptr;
+    unsigned long long* keys = nullptr;
+    int32_t* pinned = nullptr;  // [2][slots]: tokens in, tokens out
+    size_t part_stride = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+};
+
+static int batch_check_weight(const ssd_weight* w, const char* what) {
+    SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K,
+            SSD_ERR_TYPE, "batch decode: %s type %d (Q4_0, Q8_0, Q4_K)", what, w->type);
+    SSD_REQ(w->cols % 256 == 0, SSD_ERR_SHAPE, "batch decode: %s cols %d %% 256", what, w->cols);
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_create(ssd_model* m, int capacity, ssd_batch** out) {
+    SSD_REQ(m && out, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_TRY(check_weights(m));
+    const auto& c = m->cfg;
+    SSD_REQ(tp_size(m) == 1, SSD_ERR_ARG, "batch decode runs on one GPU (tp_size 1)");
+    SSD_REQ(capacity > 0, SSD_ERR_SHAPE, "capacity %d", capacity);
+    SSD_REQ(c.head_dim <= 128 && c.head_dim % 16 == 0, SSD_ERR_SHAPE, "batch decode: head_dim %d",
+            c.head_dim);
+    SSD_REQ(m->q_rows % 128 == 0 && m->kv_rows % 128 == 0 && m->ff_local % 64 == 0, SSD_ERR_SHAPE,
+            "batch decode: q / kv rows multiples of 128, n_ff of 64");
+    for (int l = 0; l < c.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        for (const ssd_weight* w : {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd})
+            SSD_TRY(batch_check_weight(w, "layer weight"));
+        SSD_REQ(L.wq->type == L.wk->type && L.wk->type == L.wv->type && L.wg->type == L.wu->type,
+                SSD_ERR_TYPE, "batch decode: fused QKV / gate-up weights of one type");
+    }
+    SSD_TRY(batch_check_weight(m->output, "output"));
+    ssd_batch* b = new ssd_batch();
+    b->m = m;
+    b->capacity = capacity;
+    const int S = b->slots, E = c.n_embd, kvd = m->kv_rows, Q = m->q_rows, F = m->ff_local;
+    const int maxc = E > F ? (E > Q ? E : Q) : (F > Q ? F : Q);
+    b->part_stride = attn_partial_floats(m->nq_local, capacity, c.head_dim);
+    auto pad = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t kvb = (size_t)c.n_layers * S * capacity * kvd;
+    const size_t scb = (size_t)c.n_layers * S * capacity * 4;
+    const int max_tiles = 2 * ((F > c.vocab ? F : c.vocab) / 64 + 16);
+    size_t off[20], o = 0;
+    int i = 0;
+    auto take = [&](size_t bytes) { off[i++] = o; o += pad(bytes); };
+    take(kvb);                                   // 0 kk
+    take(kvb);                                   // 1 vv
+    take(scb);                                   // 2 ks
+    take(scb);                                   // 3 vs
+    take((size_t)S * E * 4);                     // 4 h_a
+    take((size_t)S * E * 4);                     // 5 h_b
+    take((size_t)S * Q * 4);                     // 6 q
+    take((size_t)S * kvd * 4);                   // 7 k
+    take((size_t)S * kvd * 4);                   // 8 v
+    take((size_t)S * Q * 4);                     // 9 attn
+    take((size_t)S * F * 4);                     // 10 act
+    take((size_t)S * b->part_stride * 4);        // 11 attention partials
+    take((size_t)(maxc / 256) * 16384);          // 12 B operand
+    take((size_t)(maxc / 256) * 1024);           // 13 B scale tables
+    take((size_t)max_tiles * 4);                 // 14 counters
+    take((size_t)kI8MaxGrid * 2 * S * 128 * 4);  // 15 split-K partials
+    take((size_t)S * 4);                         // 16 tokens
+    take((size_t)S * 4);                         // 17 positions
+    take((size_t)S * 8);                         // 18 keys
+    if (cudaMalloc(&b->alloc, o) != cudaSuccess) {
+        cudaGetLastError();
+        delete b;
+        set_error("batch allocation of %zu bytes failed", o);
+        return SSD_ERR_NOMEM;
+    }
+    uint8_t* p = (uint8_t*)b->alloc;
+    b->kk = (int8_t*)(p + off[0]);
+    b->vv = (int8_t*)(p + off[1]);
+    b->ks = (float*)(p + off[2]);
+    b->vs = (float*)(p + off[3]);
+    b->h_a = (float*)(p + off[4]);
+    b->h_b = (float*)(p + off[5]);
+    b->q = (float*)(p + off[6]);
+    b->k = (float*)(p + off[7]);
+    b->v = (float*)(p + off[8]);
+    b->attn = (float*)(p + off[9]);
+    b->act = (float*)(p + off[10]);
+    b->part = (float*)(p + off[11]);
+    b->bop = p + off[12];
+    b->cst = (float*)(p + off[13]);
+    b->counter = (unsigned*)(p + off[14]);
+    b->partial = (float*)(p + off[15]);
+    b->tokens = (int32_t*)(p + off[16]);
+    b->pos = (int*)(p + off[17]);
+    b->keys = (unsigned long long*)(p + off[18]);
+    int st = SSD_OK;
+    if (cudaMemset(b->alloc, 0, o) != cudaSuccess ||
+        cudaMallocHost(&b->pinned, (size_t)2 * S * 4) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("batch initialisation failed");
+        st = SSD_ERR_CUDA;
+    }
+    if (st != SSD_OK) {
+        cudaFree(b->alloc);
+        delete b;
+        return st;
+    }
+    *out = b;
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_free(ssd_batch* b) {
+    if (!b) return SSD_OK;
+    cudaSetDevice(b->m->ctx->device);
+    cudaStreamSynchronize(b->m->ctx->stream);
+    if (b->exec) cudaGraphExecDestroy(b->exec);
+    if (b->graph) cudaGraphDestroy(b->graph);
+    if (b->pinned) cudaFreeHost(b->pinned);
+    cudaFree(b->alloc);
+    delete b;
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_slots(ssd_batch* b, int* slots) {
+    SSD_REQ(b && slots, SSD_ERR_ARG, "null argument");
+    *slots = b->slots;
+    return SSD_OK;
+}
+
+// The cache of (layer, slot) as a view (no allocation of its own).
+static ssd_kv_cache batch_kv_view(ssd_batch* b, int layer, int slot) {
+    const auto& c = b->m->cfg;
+    ssd_kv_cache kv;
+    kv.ctx = b->m->ctx;
+    kv.capacity = b->capacity;
+    kv.n_head_kv = c.n_head_kv;
+    kv.head_dim = c.head_dim;
+    kv.kv_dim = b->m->kv_rows;
+    const size_t ls = (size_t)layer * b->slots + slot;
+    kv.k = b->kk + ls * b->capacity * kv.kv_dim;
+    kv.v = b->vv + ls * b->capacity * kv.kv_dim;
+    kv.k_scale = b->ks + ls * b->capacity;
+    kv.v_scale = b->vs + ls * b->capacity;
+    return kv;
+}
+
+extern "C" int ssd_batch_kv_pointers(ssd_batch* b, int layer, int slot, int8_t** k, int8_t** v,
+                                     float** ks, float** vs) {
+    SSD_REQ(b && layer >= 0 && layer < b->m->cfg.n_layers && slot >= 0 && slot < b->slots,
+            SSD_ERR_ARG, "bad arguments");
+    const ssd_kv_cache kv = batch_kv_view(b, layer, slot);
+    if (k) *k = kv.k;
+    if (v) *v = kv.v;
+    if (ks) *ks = kv.k_scale;
+    if (vs) *vs = kv.v_scale;
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_set_position(ssd_batch* b, int slot, int pos) {
+    SSD_REQ(b && slot >= 0 && slot < b->slots, SSD_ERR_ARG, "bad slot");
+    SSD_TRY(check_ctx(b->m->ctx));
+    SSD_REQ(pos >= 0 && pos < b->capacity, SSD_ERR_SHAPE, "position %d outside [0, %d)", pos,
+            b->capacity);
+    SSD_CK(cudaMemcpyAsync(b->pos + slot, &pos, 4, cudaMemcpyHostToDevice, b->m->ctx->stream));
+    SSD_CK(cudaStreamSynchronize(b->m->ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_positions(ssd_batch* b, int* pos) {
+    SSD_REQ(b && pos, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(b->m->ctx));
+    SSD_CK(cudaMemcpyAsync(pos, b->pos, (size_t)b->slots * 4, cudaMemcpyDeviceToHost,
+                           b->m->ctx->stream));
+    SSD_CK(cudaStreamSynchronize(b->m->ctx->stream));
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_synth_kv(ssd_batch* b, uint64_t seed, int n) {
+    SSD_REQ(b != nullptr, SSD_ERR_ARG, "null batch");
+    ssd_model* m = b->m;
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(n >= 0 && n < b->capacity, SSD_ERR_SHAPE, "n %d outside [0, %d)", n, b->capacity);
+    const int kvd = m->kv_rows;
+    cudaStream_t s = m->ctx->stream;
+    if (n > 0) {
+        const int chunk = 256;
+        float* tmp = nullptr;
+        SSD_CK(cudaMalloc(&tmp, (size_t)2 * chunk * kvd * 4));
+        int st = SSD_OK;
+        for (int l = 0; l < m->cfg.n_layers && st == SSD_OK; l++) {
+            for (int sl = 0; sl < b->slots && st == SSD_OK; sl++) {
+                ssd_kv_cache kv = batch_kv_view(b, l, sl);
+                for (int p0 = 0; p0 < n && st == SSD_OK; p0 += chunk) {
+                    const int rows = n - p0 < chunk ? n - p0 : chunk;
+                    // K / V rows N(0, 1): tensors 3000000 + 128 l + 2 slot (+1)
+                    const uint32_t tk = 3000000u + 128u * l + 2u * sl;
+                    st = ssd_synth_f32(m->ctx, seed, tk, 0.0f, 1.0f, kvd, p0, rows, 0, kvd, tmp,
+                                       (void*)s);
+                    if (st == SSD_OK)
+                        st = ssd_synth_f32(m->ctx, seed, tk + 1, 0.0f, 1.0f, kvd, p0, rows, 0, kvd,
+                                           tmp + (size_t)chunk * kvd, (void*)s);
+                    if (st == SSD_OK)
+                        st = launch_kv_append(&kv, tmp, tmp + (size_t)chunk * kvd, p0, nullptr, rows,
+                                              s, false);
+                }
+            }
+        }
+        cudaStreamSynchronize(s);
+        cudaFree(tmp);
+        SSD_TRY(st);
+    }
+    for (int sl = 0; sl < b->slots; sl++) SSD_TRY(ssd_batch_set_position(b, sl, n));
+    return SSD_OK;
+}
+
+// One batched matvec: B operand from x (+ norm), then the tensor-core launch.
+static int batch_mv(ssd_batch* b, const ssd_weight* w0, int epi, MvArgs a, const float* x, int ldx,
+                    const float* norm_w, float eps, int norm_order, int ldy, cudaStream_t s,
+                    int& nl) {
+    ssd_ctx* ctx = b->m->ctx;
+    BPrepArgs p = {};
+    p.x = x;
+    p.ldx = ldx;
+    p.cols = a.cols;
+    p.norm_w = norm_w;
+    p.eps = eps;
+    p.norm_order = norm_order;
+    p.b = b->bop;
+    p.cst = b->cst;
+    SSD_TRY(launch_bprep(ctx, w0->type, p, s, true));
+    BWork wk = {};
+    wk.b = b->bop;
+    wk.cst = b->cst;
+    wk.counter = b->counter;
+    wk.partial = b->partial;
+    wk.ldy = ldy;
+    wk.ldk = b->m->kv_rows;
+    wk.pos = b->pos;
+    wk.keys = b->keys;
+    SSD_TRY(launch_matvec_batch(ctx, w0->type, epi, a, wk, s, true));
+    nl += 2;
+    return SSD_OK;
+}
+
+static int enqueue_batch_step(ssd_batch* b, cudaStream_t s, int& nl) {
+    ssd_model* m = b->m;
+    const auto& c = m->cfg;
+    const int S = b->slots, E = c.n_embd;
+    SSD_TRY(launch_embed_rows(m->tok_embd, b->tokens, S, b->h_a, s));
+    nl++;
+    float* h = b->h_a;
+    float* ho = b->h_b;
+    for (int l = 0; l < c.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        // QKV + RoPE (each slot at its own position), pre-attention RMSNorm in the B prep
+        MvArgs a = {};
+        a.qs[0] = L.wq->qs;
+        a.qs[1] = L.wk->qs;
+        a.qs[2] = L.wv->qs;
+        a.meta[0] = L.wq->meta;
+        a.meta[1] = L.wk->meta;
+        a.meta[2] = L.wv->meta;
+        a.seg_rows[0] = m->q_rows;
+        a.seg_rows[1] = m->kv_rows;
+        a.seg_rows[2] = m->kv_rows;
+        a.map = MAP_QKV;
+        a.rows = m->q_rows + 2 * m->kv_rows;
+        a.cols = E;
+        a.y = b->q;
+        a.y_k = b->k;
+        a.y_v = b->v;
+        a.head_dim = c.head_dim;
+        a.theta = c.theta;
+        SSD_TRY(batch_mv(b, L.wq, EPI_QKV_ROPE, a, h, E, L.attn_norm, c.eps, 0, m->q_rows, s, nl));
+        // attention over each slot's cache, its new K / V row appended at its position
+        ssd_kv_cache kv0 = batch_kv_view(b, l, 0);
+        AttnArgs at = {};
+        at.k_new = b->k;
+        at.v_new = b->v;
+        at.k = kv0.k;
+        at.v = kv0.v;
+        at.ks = kv0.k_scale;
+        at.vs = kv0.v_scale;
+        at.kv_dim = m->kv_rows;
+        at.head_dim = c.head_dim;
+        at.group = c.n_head / c.n_head_kv;
+        at.kv_head0 = 0;
+        at.n_kv_local = m->nkv_local;
+        at.q = b->q;
+        at.out = b->attn;
+        at.partial = b->part;
+        at.pos_dev = b->pos;
+        at.max_seq = b->capacity;
+        at.n_q = S;
+        at.q_stride = m->q_rows;
+        at.out_stride = m->q_rows;
+        at.n_slots = S;
+        at.slot_kv = (size_t)b->capacity * m->kv_rows;
+        at.slot_sc = b->capacity;
+        at.slot_new = m->kv_rows;
+        SSD_TRY(launch_attention(at, s, true));
+        nl += 2;
+        // o_proj + residual
+        MvArgs o = mv_plain(L.wo, nullptr, ho);
+        o.base = h;
+        SSD_TRY(batch_mv(b, L.wo, EPI_RESID, o, b->attn, m->q_rows, nullptr, 0.0f, 0, E, s, nl));
+        std::swap(h, ho);
+        // gate / up + SwiGLU, FFN RMSNorm in the B prep
+        MvArgs g = {};
+        g.qs[0] = L.wg->qs;
+        g.qs[1] = L.wu->qs;
+        g.meta[0] = L.wg->meta;
+        g.meta[1] = L.wu->meta;
+        g.seg_rows[0] = m->ff_local;
+        g.seg_rows[1] = m->ff_local;
+        g.map = MAP_SWIGLU;
+        g.rows = 2 * m->ff_local;
+        g.cols = E;
+        g.y = b->act;
+        SSD_TRY(batch_mv(b, L.wg, EPI_SWIGLU, g, h, E, L.ffn_norm, c.eps, 1, m->ff_local, s, nl));
+        // down + residual
+        MvArgs d = mv_plain(L.wd, nullptr, ho);
+        d.base = h;
+        SSD_TRY(batch_mv(b, L.wd, EPI_RESID, d, b->act, m->ff_local, nullptr, 0.0f, 0, E, s, nl));
+        std::swap(h, ho);
+    }
+    // logits = output * rmsnorm(h) (eps 1e-5, compute.rs:566), argmax per slot
+    MvArgs a = mv_plain(m->output, nullptr, nullptr);
+    a.y = nullptr;
+    a.index_offset = 0;
+    SSD_TRY(batch_mv(b, m->output, EPI_ARGMAX, a, h, E, m->out_norm, 1e-5f, 1, c.vocab, s, nl));
+    SSD_CK(launch_pdl(k_batch_finalize, dim3(1), dim3(32), 0, s, true, b->keys, b->tokens, b->pos,
+                      S, b->capacity));
+    nl++;
+    return SSD_OK;
+}
+
+// One decode step of every slot: tokens_in (host, one per slot, or null to continue from
+// each slot's last output) -> next tokens (host, may be null). Graph-captured on first use.
+extern "C" int ssd_batch_step(ssd_batch* b, const int32_t* tokens_in, int32_t* tokens_out,
+                              int use_graph) {
+    SSD_REQ(b != nullptr, SSD_ERR_ARG, "null batch");
+    ssd_model* m = b->m;
+    SSD_TRY(check_ctx(m->ctx));
+    const int S = b->slots;
+    cudaStream_t s = m->ctx->stream;
+    if (tokens_in) {
+        for (int i = 0; i < S; i++)
+            SSD_REQ(tokens_in[i] >= 0 && tokens_in[i] < m->cfg.vocab, SSD_ERR_ARG,
+                    "slot %d token %d outside vocab", i, tokens_in[i]);
+        memcpy(b->pinned, tokens_in, (size_t)S * 4);  // the previous call synchronised
+        SSD_CK(cudaMemcpyAsync(b->tokens, b->pinned, (size_t)S * 4, cudaMemcpyHostToDevice, s));
+    }
+    if (!use_graph) {
+        int nl = 0;
+        SSD_TRY(enqueue_batch_step(b, s, nl));
+        b->launches = nl;
+    } else {
+        if (!b->exec) {
+            int nl = 0;
+            SSD_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+            int st = enqueue_batch_step(b, s, nl);
+            cudaGraph_t g = nullptr;
+            cudaError_t e = cudaStreamEndCapture(s, &g);
+            SSD_TRY(st);
+            SSD_CK(e);
+            cudaGraphExec_t ex = nullptr;
+            e = cudaGraphInstantiate(&ex, g, 0);
+            if (e != cudaSuccess) {
+                cudaGraphDestroy(g);
+                SSD_CK(e);
+            }
+            b->graph = g;
+            b->exec = ex;
+            b->launches = nl;
+        }
+        SSD_CK(cudaGraphLaunch(b->exec, s));
+    }
+    if (tokens_out) {
+        SSD_CK(cudaMemcpyAsync(b->pinned + S, b->tokens, (size_t)S * 4, cudaMemcpyDeviceToHost, s));
+        SSD_CK(cudaStreamSynchronize(s));
+        memcpy(tokens_out, b->pinned + S, (size_t)S * 4);
+    }
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_launches_per_step(ssd_batch* b, int* launches) {
+    SSD_REQ(b && launches, SSD_ERR_ARG, "null argument");
+    *launches = b->launches;
+    return SSD_OK;
+}
+
+extern "C" int ssd_batch_state(ssd_batch* b, float** hidden) {
+    SSD_REQ(b && hidden, SSD_ERR_ARG, "null argument");
+    *hidden = b->h_a;  // after a step with an even number of swaps per layer
+    return SSD_OK;
+}

@@ -210,7 +210,18 @@ __device__ __forceinline__ uint32_t att_word(const uint4& q, int m) {
 }
 
 template <int HD, int G>
-__global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a) {
+__global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
+    AttnArgs a = a0;
+    if (a0.n_slots > 0) {  // this query's slot: its own cache, position and new rows
+        const int sl = blockIdx.z;
+        a.k += (size_t)sl * a0.slot_kv;
+        a.v += (size_t)sl * a0.slot_kv;
+        a.ks += (size_t)sl * a0.slot_sc;
+        a.vs += (size_t)sl * a0.slot_sc;
+        a.pos_dev += sl;
+        a.k_new += (size_t)sl * a0.slot_new;
+        a.v_new += (size_t)sl * a0.slot_new;
+    }
     constexpr int DPL = HD / 32;  // dims per lane in the P V phase
     __shared__ __align__(16) float qs[G][HD];         // q * 2^85 / 2^77 by byte position
     __shared__ __align__(16) float2 pw[ATT_NW][G][32];  // (weight, weight)
@@ -561,8 +572,10 @@ static int launch_attn_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     SSD_REQ(a.max_seq > 0, SSD_ERR_SHAPE, "empty attention");
-    SSD_REQ(!a.k_new || (a.v_new && a.pos_dev && a.n_q <= 1), SSD_ERR_ARG,
-            "fused KV append needs v_new, pos_dev and a single query");
+    SSD_REQ(!a.k_new || (a.v_new && a.pos_dev && (a.n_q <= 1 || a.n_slots == a.n_q)), SSD_ERR_ARG,
+            "fused KV append needs v_new, pos_dev and one query per cache");
+    SSD_REQ(a.n_slots == 0 || (a.k_new && a.n_q == a.n_slots), SSD_ERR_ARG,
+            "batch attention: one query per slot, with the fused append");
     SSD_REQ((a.max_seq + ATT_P - 1) / ATT_P <= 1024, SSD_ERR_SHAPE,
             "attention over %d positions exceeds %d", a.max_seq, 1024 * ATT_P);
     if (a.head_dim == 128) return launch_attn_hd<128>(a, s, pdl);

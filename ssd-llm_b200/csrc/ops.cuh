@@ -41,6 +41,12 @@ struct AttnArgs {
     // the output-projection GEMM) instead of fp32 out.
     __half* out_hi;
     __half* out_lo;
+    // Continuous-batch decode (n_slots > 0, with the fused append): query z = slot z, whose
+    // cache is k / v + z * slot_kv bytes and ks / vs + z * slot_sc floats, whose position is
+    // pos_dev[z] and whose new rows are k_new / v_new + z * slot_new floats.
+    int n_slots;
+    size_t slot_kv;
+    int slot_sc, slot_new;
 };
 // Causal attention of a prompt batch on the tcgen05 tensor cores (attn_tc.cu): n_q
 // queries (a multiple of 128, head_dim 128) at positions seq0 .., over the cache rows

@@ -156,6 +156,18 @@ _SIGS = {
     "ssd_gguf_model_config": ([_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                ctypes.POINTER(ModelConfig)], ctypes.c_int),
     "ssd_model_load_gguf": ([_vp, _vp, ctypes.c_int], ctypes.c_int),
+    "ssd_batch_create": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_batch_free": ([_vp], ctypes.c_int),
+    "ssd_batch_slots": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "ssd_batch_step": ([_vp, _vp, _vp, ctypes.c_int], ctypes.c_int),
+    "ssd_batch_set_position": ([_vp, ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "ssd_batch_positions": ([_vp, _vp], ctypes.c_int),
+    "ssd_batch_synth_kv": ([_vp, ctypes.c_uint64, ctypes.c_int], ctypes.c_int),
+    "ssd_batch_kv_pointers": ([_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp),
+                               ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp)],
+                              ctypes.c_int),
+    "ssd_batch_state": ([_vp, ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_batch_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
 
 
@@ -600,6 +612,62 @@ class Model:
     def free(self):
         if self.h:
             lib().ssd_model_free(self.h)
+            self.h = None
+
+
+class Batch:
+    """Sixteen decode slots over one model (BatchScheduler's layer-major decode step,
+    src/inference/batch_scheduler.rs:149-403): every slot its own INT8 KV cache and
+    position; step() advances all of them by one token."""
+
+    def __init__(self, model: Model, capacity: int):
+        h = _vp()
+        check(lib().ssd_batch_create(model.h, capacity, ctypes.byref(h)))
+        n = ctypes.c_int()
+        check(lib().ssd_batch_slots(h, ctypes.byref(n)))
+        self.model, self.h, self.slots, self.capacity = model, h, n.value, capacity
+
+    def step(self, tokens=None, use_graph: bool = True) -> np.ndarray:
+        """tokens: one id per slot (None: each slot continues from its last output).
+        Returns the greedy next token of every slot."""
+        out = np.zeros(self.slots, np.int32)
+        tin = None
+        if tokens is not None:
+            tin = np.ascontiguousarray(tokens, dtype=np.int32)
+            assert tin.size == self.slots
+        check(lib().ssd_batch_step(self.h, None if tin is None else tin.ctypes.data,
+                                   out.ctypes.data, int(use_graph)))
+        return out
+
+    def set_position(self, slot: int, pos: int):
+        check(lib().ssd_batch_set_position(self.h, slot, pos))
+
+    def positions(self) -> np.ndarray:
+        p = np.zeros(self.slots, np.int32)
+        check(lib().ssd_batch_positions(self.h, p.ctypes.data))
+        return p
+
+    def synth_kv(self, seed: int, n: int):
+        check(lib().ssd_batch_synth_kv(self.h, seed, n))
+
+    def kv_pointers(self, layer: int, slot: int):
+        v = [_vp() for _ in range(4)]
+        check(lib().ssd_batch_kv_pointers(self.h, layer, slot, *[ctypes.byref(x) for x in v]))
+        return tuple(x.value for x in v)
+
+    def hidden_ptr(self) -> int:
+        p = _vp()
+        check(lib().ssd_batch_state(self.h, ctypes.byref(p)))
+        return p.value
+
+    def launches_per_step(self) -> int:
+        n = ctypes.c_int()
+        check(lib().ssd_batch_launches_per_step(self.h, ctypes.byref(n)))
+        return n.value
+
+    def free(self):
+        if self.h:
+            lib().ssd_batch_free(self.h)
             self.h = None
 
 
