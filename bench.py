@@ -542,6 +542,56 @@ def case_prefill_l3_8b(ctx, torch, ssdllm, peak, reps=3):
             "frac_of_bf16_peak": round(tflops / tpk, 4), "mma_passes": 3}
 
 
+def measure_batch16(ctx, torch, ssdllm, model, cfg, peak, steps=6, warmup=2):
+    """BASELINE config 5, continuous batch 16: the 16 slots of ssdllm.Batch over the model's
+    weights, every slot's INT8 cache filled to PROMPT positions, one graph-captured step =
+    one token for each of the 16 slots (layer-major, the weights streamed once per step)."""
+    import numpy as np
+    b = ssdllm.Batch(model, capacity=cfg["kv_capacity"])
+    try:
+        b.synth_kv(seed=11, n=PROMPT - steps - warmup - 2)
+        stream = torch.cuda.ExternalStream(ssdllm_stream(ctx, ssdllm))
+        b.step(np.arange(16, dtype=np.int32) * 997 % cfg["vocab"])
+        for _ in range(warmup):
+            b.step(None)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            lib_step(ssdllm, b)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        launches = b.launches_per_step()
+    finally:
+        b.free()
+    wbytes = weight_bytes(cfg)
+    kv_bytes = 16 * cfg["n_layers"] * PROMPT * (2 * cfg["n_head_kv"] * cfg["head_dim"] + 8)
+    return {"workload": "llama70b_q4_0_decode_b16", "slots": 16, "context": PROMPT,
+            "ms_per_step": round(ms, 3), "tokens_per_s": round(16 / (ms / 1e3), 1),
+            "weight_stream_gbs": round(wbytes / (ms / 1e3) / 1e9, 1),
+            "hbm_bytes_per_step": int(wbytes + kv_bytes),
+            "frac_of_peak": round((wbytes + kv_bytes) / (ms / 1e3) / 1e9 / peak, 4),
+            "launches_per_step": launches}
+
+
+def lib_step(ssdllm, b):
+    """One batch step without the host copy of the output tokens (device-timed region)."""
+    ssdllm.check(ssdllm.lib().ssd_batch_step(b.h, None, None, 1))
+
+
+def case_decode_b16_70b(ctx, torch, ssdllm, peak):
+    """The 70B-shape model built for this case alone (39 GB of Q4_0 weights + 10.7 GB of
+    slot caches)."""
+    cfg = dict(CFG70B, tp_rank=0, tp_size=1)
+    m = ssdllm.Model(ctx, **cfg)
+    try:
+        m.synth_weights(seed=0, std=0.02)
+        return measure_batch16(ctx, torch, ssdllm, m, cfg, peak)
+    finally:
+        m.free()
+
+
 def measured_tensor_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -625,9 +675,11 @@ CASES = {
     "layer_70b_q4_0": case_layer_70b,
     "prefill_l3_8b_q4_k": case_prefill_l3_8b,
     "mv_shapes_70b": case_mv_shapes,
+    "decode_b16_70b": case_decode_b16_70b,
 }
-# measured on every default run (mv_shapes_70b, a kernel-selection study, only by --case)
-DEFAULT_CASES = [n for n in CASES if n != "mv_shapes_70b"]
+# measured on every default run (mv_shapes_70b, a kernel-selection study, only by --case;
+# decode_b16_70b is measured on the headline run's own model)
+DEFAULT_CASES = [n for n in CASES if n not in ("mv_shapes_70b", "decode_b16_70b")]
 
 
 def run_cases(names, peak):
@@ -758,6 +810,9 @@ def run_cuda(args):
             tt = torch.tensor([dom_us], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             dom_us = float(tt[0])
+        b16 = None
+        if world == 1 and not args.no_kernels:  # config 5's continuous batch 16, same model
+            b16 = measure_batch16(ctx, torch, ssdllm, model, cfg, peak)
         k0 = run_cases(DEFAULT_CASES, peak) if rank == 0 and not args.no_kernels else None
         clocks = clk.summary() if rank == 0 else None
     finally:
@@ -807,6 +862,7 @@ def run_cuda(args):
                      "decode_weight_stream_gbs": weight_bytes(cfg) / world / (ms / args.steps)
                      / 1e6},
         "cpu_baseline": cpu,
+        "decode_b16": b16,
         "gpu_launches": launches * args.steps,
         "clocks": clocks,
         "kernels": k0,

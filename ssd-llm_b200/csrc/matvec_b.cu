@@ -9,7 +9,7 @@
 //
 // Arithmetic (as matvec_i8.cu, per token): A = the block's weights as signed bytes (Q4_0 /
 // Q4_K nibbles unpacked to 16 (q - 8)); B = the tokens' x as exact fixed point per
-// 32-element block, xf = rint(x 2^e), split into four signed byte limbs. Column 4 t + l of
+// 32-element block, xf = rint(x 2^e), split into four signed byte limbs. Column 16 l + t of
 // B is limb l of token t, so one MMA gives the 64 exact int32 limb sums of a block; the
 // readout combines each token's four limbs, rounds once to fp32 and adds d * 2^-e * sum.
 // The exponent e of a block is shared by the 16 tokens (max |x| over the tokens' 32
@@ -23,8 +23,8 @@
 //  * k_mv_b: one CTA per SM over units of 128 rows x 256 columns (tile-major ranges, the
 //    split tiles finished by the last CTA to arrive, adding partial rows in CTA order).
 //    Each unit's stage brings by TMA the packed weights, their scales and the unit's B block
-//    (16 KB) with its scale table; warps 10-13 unpack nibbles, warp 9 issues the MMAs,
-//    warps 0-7 read TMEM back (warps 0-3 tokens 0-7, warps 4-7 tokens 8-15, lanes = rows).
+//    (16 KB) with its scale table; warps 18-21 unpack nibbles, warp 17 issues the MMAs,
+//    warps 0-15 read TMEM back (warp group g = warps 4g..4g+3: tokens 4g..4g+3, lanes = rows).
 // Every mbarrier wait is bounded (timeout -> SSD_ERR_TIMEOUT in the status word, then no
 // role of the CTA waits any longer).
 #include <cstring>
@@ -37,7 +37,10 @@ namespace ssd {
 
 constexpr int kBN = kBatchTokens;     // tokens per launch (16)
 constexpr int kBCols = 4 * kBN;       // MMA N: 4 limbs per token
-constexpr int kBThreads = 448;        // warps 0-7 readout, 8 producer, 9 MMA, 10-13 unpack
+constexpr int kBRW = 16;              // readout warps: 4 warp groups of 4 tokens each
+constexpr int kBTG = kBN / (kBRW / 4);  // tokens per readout thread
+// warps 0-15 readout, 16 producer, 17 MMA, 18-21 unpack
+constexpr int kBThreads = (kBRW + 6) * 32;
 constexpr int kBMaxStages = 6;
 constexpr int kBASlots = 2;
 constexpr int kBDSlots = 2;           // TMEM slots of 4 blocks x 64 columns
@@ -87,25 +90,45 @@ __device__ __forceinline__ uint64_t b_desc_plain(uint32_t saddr, uint32_t lbo, u
     d |= (uint64_t)1u << 46;
     return d;
 }
+// D += A B: every TMEM slot holds the preset kBMagic before its MMAs (see the readout)
 __device__ __forceinline__ void b_umma(uint32_t tmem_d, uint64_t da, uint64_t db) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %3, 0;\n"
         " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %4, p;\n}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(0u), "r"(kBIdesc)
+        "l"(da), "l"(db), "r"(1u), "r"(kBIdesc)
         : "memory");
 }
-// 32 consecutive 32-bit TMEM columns of this thread's lane (no wait).
-__device__ __forceinline__ void b_tmem_ld32(uint32_t taddr, int (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-          "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
-          "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
-          "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr));
+// 0x4B400000 = 1.5 * 2^23 as fp32 bits. An int32 accumulator preset to it and added an
+// exact limb sum c (|c| < 2^19, well inside 2^22) holds the bits of the fp32 value
+// 1.5 * 2^23 + c, so the readout recovers c with one exact subtraction (no conversion).
+constexpr uint32_t kBMagic = 0x4B400000u;
+constexpr float kBMagicF = 12582912.0f;
+__device__ __forceinline__ void b_tmem_st_magic4(uint32_t taddr) {
+    const uint32_t m = kBMagic;
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(m)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+// (a0, a1) += d * (F - M) for the preset-carrying pair F, exact subtraction then one fma
+__device__ __forceinline__ uint64_t b_acc2(uint64_t acc, uint64_t F, uint64_t nM, uint64_t d) {
+    uint64_t g;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(g) : "l"(F), "l"(nM));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(g), "l"(d));
+    return acc;
+}
+// kBTG consecutive 32-bit TMEM columns of this thread's lane (no wait).
+__device__ __forceinline__ void b_tmem_ld4(uint32_t taddr, uint32_t (&v)[kBTG]) {
+    static_assert(kBTG == 4, "x4 loads");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
 }
 __device__ __forceinline__ void b_bar(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -150,6 +173,53 @@ __device__ __forceinline__ void b_scale_min(const uint4& m, int sb, uint32_t& s6
     }
 }
 
+// ----------------------------------------------------------------------- norm stats
+// inv_rms of every token's x_eff (x + x_add): one CTA of 1024 threads per token, all of its
+// row's float4 loads in flight at once, sum of squares fp32 (rmsnorm_f32_fast_scalar,
+// src/metal/compute.rs:580-588: inv_rms = 1 / sqrt(sum_sq / n + eps)).
+__global__ void __launch_bounds__(1024) k_bstats(const BPrepArgs p) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    pdl_wait();
+    const float4* x4 = reinterpret_cast<const float4*>(p.x + (size_t)t * p.ldx);
+    const float4* a4 = p.x_add ? reinterpret_cast<const float4*>(p.x_add + (size_t)t * p.ldx) : nullptr;
+    const int n4 = p.cols / 4;
+    constexpr int kIn = 8;  // float4 per thread per round (rows up to 32768 in one round)
+    float ss = 0.0f;
+    for (int i0 = tid; i0 < n4; i0 += kIn * 1024) {
+        float4 v[kIn];
+#pragma unroll
+        for (int j = 0; j < kIn; j++) {
+            const int i = i0 + j * 1024;
+            v[j] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (a4 && i < n4) {
+                const float4 w = __ldcg(a4 + i);
+                v[j].x = __fadd_rn(v[j].x, w.x);
+                v[j].y = __fadd_rn(v[j].y, w.y);
+                v[j].z = __fadd_rn(v[j].z, w.z);
+                v[j].w = __fadd_rn(v[j].w, w.w);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kIn; j++) {
+            ss = fmaf(v[j].x, v[j].x, ss);
+            ss = fmaf(v[j].y, v[j].y, ss);
+            ss = fmaf(v[j].z, v[j].z, ss);
+            ss = fmaf(v[j].w, v[j].w, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+        float v = red[tid];
+        v = warp_sum(v);
+        if (tid == 0)
+            p.inv[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)p.cols), p.eps)));
+    }
+    pdl_trigger();
+}
+
 // ----------------------------------------------------------------------- B prep
 // One CTA (256 threads) per k-group of 256 columns. Warp w = block w of the group, lane =
 // element; the 16 tokens are looped. NIB: nibble formats (block K order: 16 even elements,
@@ -169,22 +239,8 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
         if (p.x_add) v = __fadd_rn(v, __ldcg(p.x_add + (size_t)t * p.ldx + k));
         return v;
     };
-    if (p.norm_w) {  // per-token inv_rms over the whole row: warp w takes tokens 2w, 2w + 1
-        for (int q = 0; q < 2; q++) {
-            const int t = 2 * warp + q;
-            float ss = 0.0f;
-            for (int k0 = lane; k0 < p.cols; k0 += 8 * 32) {
-                float v[8];
-#pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = k0 + 32 * j < p.cols ? xe(t, k0 + 32 * j) : 0.0f;
-#pragma unroll
-                for (int j = 0; j < 8; j++) ss = fmaf(v[j], v[j], ss);
-            }
-            ss = warp_sum(ss);
-            // inv_rms = 1 / sqrt(sum_sq / n + eps)   (src/metal/compute.rs:583-584)
-            if (lane == 0)
-                inv_s[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.cols), p.eps)));
-        }
+    if (p.norm_w) {
+        if (tid < kBN) inv_s[tid] = __ldcg(p.inv + tid);
         __syncthreads();
     }
     const int c = warp;  // block within the k-group
@@ -211,8 +267,8 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
     int e = mx == 0 ? 0 : 152 - ex;
     e = e < -100 ? -100 : (e > 126 ? 126 : e);
     const float sc = __uint_as_float((uint32_t)(e + 127) << 23);
-    // K position of this element in the block; limb l of token t at
-    // [(2 c + h) * 64 + 4 t + l] * 16 + idx
+    // K position of this element in the block; limb l of token t (B row 16 l + t) at
+    // [(2 c + h) * 64 + 16 l + t] * 16 + idx
     const int pp = NIB ? ((lane & 1) * 16 + (lane >> 1)) : lane;
     const int h = pp >> 4, idx = pp & 15;
     uint8_t* tb = tile + (size_t)(2 * c + h) * kBCols * 16 + idx;
@@ -225,10 +281,10 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
         xf = (xf - l1) >> 8;
         const int l2 = (int)(int8_t)(xf & 0xFF);
         const int l3 = (xf - l2) >> 8;
-        tb[(4 * t + 0) * 16] = (uint8_t)l0;
-        tb[(4 * t + 1) * 16] = (uint8_t)l1;
-        tb[(4 * t + 2) * 16] = (uint8_t)l2;
-        tb[(4 * t + 3) * 16] = (uint8_t)l3;
+        tb[(0 * kBN + t) * 16] = (uint8_t)l0;
+        tb[(1 * kBN + t) * 16] = (uint8_t)l1;
+        tb[(2 * kBN + t) * 16] = (uint8_t)l2;
+        tb[(3 * kBN + t) * 16] = (uint8_t)l3;
         if constexpr (SUMX) {
             const float X = warp_sum(v[t]);
             if (lane == 0) xsum[c][t] = X;
@@ -273,6 +329,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
     uint64_t* d_full = a_empty + kBASlots;
     uint64_t* d_empty = d_full + kBDSlots;
     uint64_t* mma_done = d_empty + kBDSlots;
+    uint64_t* tmem_ready = mma_done + 8;  // every TMEM slot preset (readout warps)
     uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(mma_done + 2);
     int* flag = reinterpret_cast<int*>(mma_done + 3);
@@ -290,7 +347,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
         for (int s = 0; s < S; s++) {
             mbar_init(p_full + s, 1);
             // readout warps, MMA commit, and (nibble formats) unpack warps
-            mbar_init(p_empty + s, F::NIB ? 13 : 9);
+            mbar_init(p_empty + s, F::NIB ? kBRW + 5 : kBRW + 1);
         }
         for (int s = 0; s < kBASlots; s++) {
             mbar_init(a_full + s, 4);
@@ -298,9 +355,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
         }
         for (int s = 0; s < kBDSlots; s++) {
             mbar_init(d_full + s, 1);
-            mbar_init(d_empty + s, 8);
+            mbar_init(d_empty + s, kBRW);
         }
         mbar_init(mma_done, 1);
+        mbar_init(tmem_ready, kBRW);
         *abort = 0;
         fence_mbar_init();
     }
@@ -311,7 +369,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
     const uint32_t tmem = *tslot;
     pdl_trigger();
 
-    if (warp == 8) {
+    if (warp == kBRW) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             // weights of one unit into stage ps (the B block follows separately)
@@ -389,9 +447,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 b_wait(p_full + ps, rnd & 1, abort, a.status);
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == kBRW + 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
+            b_wait(tmem_ready, 0, abort, a.status);
             int ps = 0, rnd = 0, as = 0, aph = 0, ds = 0, dph = 0;
             for (int h = 0; h < 2 * n; h++) {
                 const int hh = h & 1;
@@ -432,10 +491,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
             umma_commit(mma_done);
             if (n > 0) b_wait(mma_done, 0, abort, a.status);
         }
-    } else if (warp >= 10) {
+    } else if (warp >= kBRW + 2) {
         // ------------------------------------------------------------ nibble unpack
         if constexpr (F::NIB) {
-            const int r = tid - 320;
+            const int r = tid - (kBRW + 2) * 32;
             int ps = 0, rnd = 0, as = 0, aph = 0;
             for (int h = 0; h < 2 * n; h++) {
                 const int hh = h & 1;
@@ -476,24 +535,35 @@ __global__ void __launch_bounds__(kBThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------------------ readout warps 0-7
+        // ------------------------------------------------------------ readout warps 0-15
         const int r = tid & 127;       // tile row = TMEM lane
-        const int tg = tid >> 7;       // tokens 8 tg .. 8 tg + 7
+        const int tg = tid >> 7;       // tokens kBTG tg .. kBTG tg + kBTG - 1
         pdl_wait();
         if constexpr (EPI == EPI_QKV_ROPE) {
-            for (int i = tid; i < kBN * (a.head_dim >> 1); i += 256) {
+            for (int i = tid; i < kBN * (a.head_dim >> 1); i += kBRW * 32) {
                 const int t = i / (a.head_dim >> 1), pr = i % (a.head_dim >> 1);
                 rope_tab[t * 64 + pr] = rope_cs(pr, a.head_dim, a.theta, wk.pos[t]);
             }
-            b_bar(1, 256);
+            b_bar(1, kBRW * 32);
         }
-        float acc[8];
+        // accumulators of tokens (8 tg + 2 p, 8 tg + 2 p + 1) as fp32 pairs
+        uint64_t acc2[kBTG / 2];
 #pragma unroll
-        for (int q = 0; q < 8; q++) acc[q] = 0.0f;
+        for (int q = 0; q < kBTG / 2; q++) acc2[q] = 0ull;
         int seg_first = kg0;
         int t = t0, kg = kg0, ps = 0, rnd = 0, ds = 0, dph = 0;
         uint4 meta = make_uint4(0, 0, 0, 0);
-        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * tg);
+        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(kBTG * tg);
+        // preset every slot's columns of this warp group before the first MMA
+#pragma unroll
+        for (int q = 0; q < kBDSlots * 4; q++)
+#pragma unroll
+            for (int l = 0; l < 4; l++) b_tmem_st_magic4(tl + (uint32_t)(q * kBCols + l * kBN));
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_ready);
+        const uint64_t nM = f2pack(-kBMagicF, -kBMagicF);
         for (int h = 0; h < 2 * n; h++) {
             const int i = h >> 1, hh = h & 1;
             const uint8_t* st = base + P.ring + (size_t)ps * F::STAGE;
@@ -506,9 +576,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
             tc_fence_after();
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                int cv[32];
-                b_tmem_ld32(tl + (uint32_t)(ds * 4 * kBCols + j * kBCols), cv);
+                // limb l of this group's tokens: columns 16 l + kBTG tg .. (tl adds kBTG tg)
+                const uint32_t ta = tl + (uint32_t)(ds * 4 * kBCols + j * kBCols);
+                uint32_t cv[4][kBTG];
+#pragma unroll
+                for (int l = 0; l < 4; l++) b_tmem_ld4(ta + (uint32_t)(l * kBN), cv[l]);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int l = 0; l < 4; l++) b_tmem_st_magic4(ta + (uint32_t)(l * kBN));  // next preset
                 const int c = 4 * hh + j;
                 const float sx = cst[c];
                 float dd, bias_s = 0.0f;
@@ -526,17 +601,26 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     const float d = f16_bits_to_f32((uint16_t)((c & 1) ? (mw >> 16) : (mw & 0xFFFF)));
                     dd = __fmul_rn(d, sx);
                 }
+                // limb l weighs 256^l: d * 2^-e * 256^l is exact (a power-of-two scaling)
+                const uint64_t dl[4] = {f2pack(dd, dd), f2pack(dd * 256.0f, dd * 256.0f),
+                                        f2pack(dd * 65536.0f, dd * 65536.0f),
+                                        f2pack(dd * 16777216.0f, dd * 16777216.0f)};
 #pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const int lo = cv[4 * q] + cv[4 * q + 1] * 256;
-                    const int hi = cv[4 * q + 2] + cv[4 * q + 3] * 256;
-                    const float tot = fmaf((float)hi, 65536.0f, (float)lo);
-                    if constexpr (FMT == SSD_TYPE_Q4_K)
-                        acc[q] = fmaf(dd, tot, fmaf(bias_s, cst[8 + c * kBN + 8 * tg + q], acc[q]));
-                    else
-                        acc[q] = fmaf(dd, tot, acc[q]);
+                for (int q = 0; q < kBTG / 2; q++) {
+#pragma unroll
+                    for (int l = 3; l >= 0; l--)
+                        acc2[q] = b_acc2(acc2[q], f2pack(__uint_as_float(cv[l][2 * q]),
+                                                         __uint_as_float(cv[l][2 * q + 1])),
+                                         nM, dl[l]);
+                    if constexpr (FMT == SSD_TYPE_Q4_K) {
+                        const float* X = cst + 8 + c * kBN + kBTG * tg + 2 * q;
+                        asm("fma.rn.f32x2 %0, %1, %2, %0;"
+                            : "+l"(acc2[q])
+                            : "l"(f2pack(bias_s, bias_s)), "l"(f2pack(X[0], X[1])));
+                    }
                 }
             }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -560,11 +644,11 @@ __global__ void __launch_bounds__(kBThreads, 1)
             if (i != n - 1 && kcur != nk - 1) continue;
             const bool whole = seg_first == 0 && kcur == nk - 1;
             seg_first = 0;
-            float res[8];
+            float res[kBTG];
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                res[q] = acc[q];
-                acc[q] = 0.0f;
+            for (int q = 0; q < kBTG / 2; q++) {
+                f2unpack(acc2[q], res[2 * q], res[2 * q + 1]);
+                acc2[q] = 0ull;
             }
             bool do_epi = whole;
             if (!whole) {
@@ -573,8 +657,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 const int slot = tcur == t0 ? 0 : 1;
                 float* pp = wk.partial + ((size_t)b * 2 + slot) * kBN * 128;
 #pragma unroll
-                for (int q = 0; q < 8; q++) pp[(8 * tg + q) * 128 + r] = res[q];
-                b_bar(1, 256);
+                for (int q = 0; q < kBTG; q++) pp[(kBTG * tg + q) * 128 + r] = res[q];
+                b_bar(1, kBRW * 32);
                 const long long U64 = U;
                 const int bf = (int)((((long long)tcur * nk + 1) * G + U64 - 1) / U64) - 1;
                 const int bl = (int)((((long long)tcur * nk + nk) * G + U64 - 1) / U64) - 1;
@@ -588,36 +672,36 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     if (last) wk.counter[tcur] = 0u;
                     flag[0] = last;
                 }
-                b_bar(1, 256);
+                b_bar(1, kBRW * 32);
                 do_epi = flag[0] != 0;
                 if (do_epi) {
 #pragma unroll
-                    for (int q = 0; q < 8; q++) res[q] = 0.0f;
+                    for (int q = 0; q < kBTG; q++) res[q] = 0.0f;
                     for (int bc = bf; bc <= bl; bc++) {
                         const int tf = (int)(((long long)U * bc / G) / nk);
                         const float* pc = wk.partial + ((size_t)bc * 2 + (tcur == tf ? 0 : 1)) * kBN * 128;
 #pragma unroll
-                        for (int q = 0; q < 8; q++) res[q] += __ldcg(pc + (8 * tg + q) * 128 + r);
+                        for (int q = 0; q < kBTG; q++) res[q] += __ldcg(pc + (kBTG * tg + q) * 128 + r);
                     }
                 }
-                b_bar(1, 256);
+                b_bar(1, kBRW * 32);
             }
             if (!do_epi) continue;
             // ---- epilogue of tile tcur, row r, tokens 8 tg + q
             if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll
-                for (int q = 0; q < 8; q++) red[(8 * tg + q) * 128 + r] = res[q];
-                b_bar(1, 256);
+                for (int q = 0; q < kBTG; q++) red[(kBTG * tg + q) * 128 + r] = res[q];
+                b_bar(1, kBRW * 32);
                 const int row = 64 * tcur + r;
                 if (r < 64 && row < a.seg_rows[0]) {
 #pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        const int tt = 8 * tg + q;
+                    for (int q = 0; q < kBTG; q++) {
+                        const int tt = kBTG * tg + q;
                         a.y[(size_t)tt * wk.ldy + row] =
                             swiglu(red[tt * 128 + r], red[tt * 128 + r + 64]);
                     }
                 }
-                b_bar(1, 256);
+                b_bar(1, kBRW * 32);
             } else if constexpr (EPI == EPI_QKV_ROPE) {
                 int seg, lr;
                 map_row<kMap>(a, 128, 128 * tcur + r, seg, lr);
@@ -625,8 +709,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 float* dst = seg == 0 ? a.y : (seg == 1 ? a.y_k : a.y_v);
                 const int ld = seg == 0 ? wk.ldy : wk.ldk;
 #pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const int tt = 8 * tg + q;
+                for (int q = 0; q < kBTG; q++) {
+                    const int tt = kBTG * tg + q;
                     const float other = __shfl_xor_sync(0xffffffffu, res[q], 1);
                     float x0 = (r & 1) ? other : res[q], x1 = (r & 1) ? res[q] : other;
                     if (seg < 2) rope_apply(x0, x1, rope_tab[tt * 64 + ((lr % a.head_dim) >> 1)]);
@@ -638,8 +722,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
                     if (valid) {
 #pragma unroll
-                        for (int q = 0; q < 8; q++) {
-                            const int tt = 8 * tg + q;
+                        for (int q = 0; q < kBTG; q++) {
+                            const int tt = kBTG * tg + q;
                             float v = res[q];
                             if (EPI == EPI_RESID) v = __fadd_rn(a.base[(size_t)tt * wk.ldy + row], v);
                             a.y[(size_t)tt * wk.ldy + row] = v;
@@ -647,8 +731,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     }
                 } else {  // EPI_ARGMAX: one key per token
 #pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        const int tt = 8 * tg + q;
+                    for (int q = 0; q < kBTG; q++) {
+                        const int tt = kBTG * tg + q;
                         unsigned long long key = 0ull;
                         if (valid) {
                             if (a.y) a.y[(size_t)tt * wk.ldy + row] = res[q];
@@ -681,6 +765,10 @@ int launch_bprep(ssd_ctx* ctx, int type, const BPrepArgs& p, cudaStream_t s, boo
     SSD_REQ(p.x && p.b && p.cst, SSD_ERR_ARG, "batch prep: null buffer");
     const bool nib = type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q4_K;
     const int nk = p.cols / 256;
+    if (p.norm_w) {
+        SSD_REQ(p.inv != nullptr && p.cols % 4 == 0, SSD_ERR_ARG, "batch prep: norm needs inv");
+        SSD_CK(launch_pdl(k_bstats, dim3(kBN), dim3(1024), 0, s, pdl, p));
+    }
     if (type == SSD_TYPE_Q4_K)
         SSD_CK(launch_pdl(k_bprep<true, true>, dim3(nk), dim3(256), 0, s, pdl, p));
     else if (nib)

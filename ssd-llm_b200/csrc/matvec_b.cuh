@@ -18,6 +18,7 @@ struct BPrepArgs {
     int norm_order;        // 0: v * (inv * w), 1: (v * inv) * w
     uint8_t* b;            // [cols / 256][16 KB] limbs
     float* cst;            // [cols / 256][256]: 2^-e per block, then X[block][token]
+    float* inv;            // [16] inv_rms of each token (written by the stats kernel)
 };
 
 // Scratch and per-token layout of one batched matvec launch.
@@ -37,6 +38,7 @@ struct I8MapsB {
     CUtensorMap m[3];
 };
 
+// With norm_w set, a stats kernel (inv_rms per token into p.inv) runs first.
 int launch_bprep(ssd_ctx* ctx, int type, const BPrepArgs& p, cudaStream_t s, bool pdl);
 // Y[t] = f(W X[t]) for the 16 tokens of the B operand prepared by launch_bprep. `a` gives
 // the weights and epilogue as for launch_matvec (x / norm fields unused); wk the scratch.

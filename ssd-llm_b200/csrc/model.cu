@@ -1217,6 +1217,7 @@ struct ssd_batch {
     int32_t* tokens = nullptr;
     int* pos = nullptr;
     unsigned long long* keys = nullptr;
+    float* inv = nullptr;       // [slots] inv_rms of the current RMSNorm
     int32_t* pinned = nullptr;  // [2][slots]: tokens in, tokens out
     size_t part_stride = 0;
     cudaGraph_t graph = nullptr;
@@ -1260,7 +1261,7 @@ extern "C" int ssd_batch_create(ssd_model* m, int capacity, ssd_batch** out) {
     const size_t kvb = (size_t)c.n_layers * S * capacity * kvd;
     const size_t scb = (size_t)c.n_layers * S * capacity * 4;
     const int max_tiles = 2 * ((F > c.vocab ? F : c.vocab) / 64 + 16);
-    size_t off[20], o = 0;
+    size_t off[24], o = 0;
     int i = 0;
     auto take = [&](size_t bytes) { off[i++] = o; o += pad(bytes); };
     take(kvb);                                   // 0 kk
@@ -1282,6 +1283,7 @@ extern "C" int ssd_batch_create(ssd_model* m, int capacity, ssd_batch** out) {
     take((size_t)S * 4);                         // 16 tokens
     take((size_t)S * 4);                         // 17 positions
     take((size_t)S * 8);                         // 18 keys
+    take((size_t)S * 4);                         // 19 inv_rms per slot
     if (cudaMalloc(&b->alloc, o) != cudaSuccess) {
         cudaGetLastError();
         delete b;
@@ -1308,6 +1310,7 @@ extern "C" int ssd_batch_create(ssd_model* m, int capacity, ssd_batch** out) {
     b->tokens = (int32_t*)(p + off[16]);
     b->pos = (int*)(p + off[17]);
     b->keys = (unsigned long long*)(p + off[18]);
+    b->inv = (float*)(p + off[19]);
     int st = SSD_OK;
     if (cudaMemset(b->alloc, 0, o) != cudaSuccess ||
         cudaMallocHost(&b->pinned, (size_t)2 * S * 4) != cudaSuccess) {
@@ -1398,7 +1401,7 @@ extern "C" int ssd_batch_synth_kv(ssd_batch* b, uint64_t seed, int n) {
     const int kvd = m->kv_rows;
     cudaStream_t s = m->ctx->stream;
     if (n > 0) {
-        const int chunk = 256;
+        const int chunk = 1024;
         float* tmp = nullptr;
         SSD_CK(cudaMalloc(&tmp, (size_t)2 * chunk * kvd * 4));
         int st = SSD_OK;
@@ -1442,7 +1445,9 @@ static int batch_mv(ssd_batch* b, const ssd_weight* w0, int epi, MvArgs a, const
     p.norm_order = norm_order;
     p.b = b->bop;
     p.cst = b->cst;
+    p.inv = b->inv;
     SSD_TRY(launch_bprep(ctx, w0->type, p, s, true));
+    if (norm_w) nl++;
     BWork wk = {};
     wk.b = b->bop;
     wk.cst = b->cst;

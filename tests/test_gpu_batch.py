@@ -121,8 +121,9 @@ def test_batch_launch_count(ctx):
         b.synth_kv(seed=4, n=20)
         assert np.all(b.positions() == 20)
         b.step(np.arange(16, dtype=np.int32))
-        # embed; per layer 4 x (B prep + matvec) + attention (2); logits (2); finalize
-        assert b.launches_per_step() == 1 + cfg["n_layers"] * (4 * 2 + 2) + 2 + 1
+        # embed; per layer 4 x (B prep + matvec), 2 norm stats, attention (2); logits
+        # (stats, B prep, matvec); finalize
+        assert b.launches_per_step() == 1 + cfg["n_layers"] * (4 * 2 + 2 + 2) + 3 + 1
     finally:
         b.free()
         m.free()
