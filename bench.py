@@ -12,7 +12,7 @@ N(0, 1) rows to ~3968 positions of a 4096 capacity, so decode runs at ~4K contex
 Reported on the same JSON line:
   value      device-timed tokens/s (CUDA events, max over ranks; weights >> L2)
   e2e        the same through ssd_model_decode_token: host token in (pinned H2D),
-             graph, next token out (D2H), synchronised every step
+             graph, next token out (D2H), synchronised every step, timed on the host clock
   roofline   the dominant kernel (gate/up dequant-matvec + SwiGLU) timed alone on
              the model's own layer weights, algorithmic bytes / event time
   kernels    BASELINE configs 0-2 one kernel at a time: Q4_0 4096x4096, Q8_0 / Q4_K at
@@ -24,7 +24,8 @@ Reported on the same JSON line:
              cores, one layer timed and extrapolated to 80 layers + logits; each of the
              configs 0-2 kernel cases also carries its own cpu_baseline (the restated
              matvec or layer step on its shape, 1 thread and all host threads)
-`--impl reference` times that CPU restatement alone (rank 0) and prints its line.
+`--impl reference` times that CPU restatement alone (rank 0) and prints its line: each of its
+steps is one 70B-shape layer step (a bounded sample), the tokens/s extrapolated to 80 layers.
 """
 from __future__ import annotations
 
@@ -229,7 +230,13 @@ def cpu_model_name():
 
 
 def run_reference(args):
-    """--impl reference: the oracle port of the reference CPU path, rank 0 only."""
+    """--impl reference: the oracle port of the reference CPU path, rank 0 only.
+
+    A step is a bounded sample of the workload: one 70B-shape decoder layer step (packed
+    Q4_0, INT8 KV at PROMPT positions, all host threads), i.e. 1/80 of a token's layers;
+    ms_per_step is that step's measured time, so steps x ms_per_step is the timed region.
+    value (tokens/s) is extrapolated from it: 80 x the median layer step + one measured
+    vocab matvec (16032 rows, scaled to the 128256-row vocab)."""
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
@@ -239,15 +246,20 @@ def run_reference(args):
     cfg = dict(CFG70B)
     t0 = time.perf_counter()
     samples = max(1, args.steps)
-    t_tok, t_layers, t_logits = cpu_token_time(cfg, max(1, args.warmup) + samples, threads)
+    _, t_layers, t_logits = cpu_token_time(cfg, max(1, args.warmup) + samples, threads)
     t_layers = t_layers[max(1, args.warmup):]
-    t_tok = cfg["n_layers"] * statistics.median(t_layers) + t_logits
+    t_layer = statistics.median(t_layers)
+    t_tok = cfg["n_layers"] * t_layer + t_logits
     value = 1.0 / t_tok
     line = {
         "impl": "reference", "metric": "decode tokens/s (Llama-70B-shape Q4_0, batch 1)",
-        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t_tok * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": len(t_layers),
+        "warmup": args.warmup, "ms_per_step": statistics.mean(t_layers) * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "step": "one 70B-shape decoder layer step (1/80 of a token's layers); value = 1 / "
+                "(80 x median layer step + vocab matvec), extrapolated",
+        "ms_per_token_extrapolated": t_tok * 1e3,
         "config": {"workload": "llama70b_q4_0_decode_b1", "n_layers": 80, "hidden": 8192,
                    "heads": 64, "kv_heads": 8, "ffn": 28672, "vocab": 128256,
                    "context": PROMPT, "kv": "int8"},
@@ -788,18 +800,16 @@ def run_cuda(args):
             if world > 1:
                 dist.barrier()
         ms = e0.elapsed_time(e1)
-        # e2e: host token in, host token out through the public API, every step
+        # e2e: host token in, host token out through the public API, every step, timed on
+        # the host clock (each call synchronises on its token copy back)
         t = 5
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        f0.record(stream)
+        h0 = time.perf_counter()
         for _ in range(args.steps):
             t = model.decode_token(t, use_graph=True)
-        f1.record(stream)
-        torch.cuda.synchronize()
-        ms_e2e = f0.elapsed_time(f1)
+        ms_e2e = (time.perf_counter() - h0) * 1e3
         if world > 1:
             tt = torch.tensor([ms, ms_e2e], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)

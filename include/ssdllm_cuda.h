@@ -254,7 +254,9 @@ int ssd_attention_int8(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev,
  * call allocates nothing. Limit: n_head * ceil(seq_len / 128) * (head_dim + 2) must
  * be at most 1,048,576 floats (e.g. 64 heads x 16,128 positions at head_dim 128);
  * larger calls return SSD_ERR_SHAPE. The first call on a device looks up the array's
- * device address, so make that first call before any stream capture. All calls share
+ * device address and loads every attention kernel this call may launch (each head_dim
+ * and GQA group), so make that first call, of any shape, before any stream capture;
+ * later calls of every shape only launch. All calls share
  * the one array: calls whose kernels overlap on the GPU (different streams, or
  * different threads without ordering) race and must be serialised by the caller. */
 int ssd_attention_int8_noalloc(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_dev,
@@ -271,6 +273,18 @@ int ssd_attention_prefill(ssd_ctx* ctx, const ssd_kv_cache* kv, const float* q_d
                           void* stream);
 
 /* ------------------------------------------------- host-slice operators */
+/* The consumer side of the tensor-parallel peer all-reduce as an operator:
+ * y = W (x + sum over r < n_ranks of partials[r * cols ..]), the partials added in rank
+ * order once every rank's flag (flags[r], device memory) reaches *epoch + call + 1. Each
+ * wait is bounded (well under a second): a flag that is never raised leaves y undefined and
+ * SSD_ERR_TIMEOUT for ssd_ctx_device_status, and later peer waits of the context return at
+ * once until that status is read. No reference counterpart (the reference's thread row
+ * split has no reduction, src/inference/tensor_parallel.rs:33-105). */
+int ssd_matvec_peer_input(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev,
+                          const float* partials_dev, int n_ranks,
+                          const unsigned long long* flags_dev,
+                          const unsigned long long* epoch_dev, int call, float* y_dev,
+                          void* stream);
 /* MetalCompute::matvec_quantized (src/metal/compute.rs:157-191) with its exact
  * signature semantics: raw weight bytes, x and y on the host; uploads, computes,
  * downloads and synchronises. */

@@ -1219,6 +1219,27 @@ extern "C" int ssd_fused_swiglu(ssd_ctx* ctx, const ssd_weight* wg, const ssd_we
     return launch_matvec(ctx, wg->type, EPI_SWIGLU, a, pick_stream(ctx, stream), ctx->pdl);
 }
 
+extern "C" int ssd_matvec_peer_input(ssd_ctx* ctx, const ssd_weight* w, const float* x,
+                                     const float* partials, int n_ranks,
+                                     const unsigned long long* flags,
+                                     const unsigned long long* epoch, int call, float* y,
+                                     void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_TRY(check_w(w));
+    SSD_REQ(x && y && partials && flags && epoch, SSD_ERR_ARG, "null argument");
+    SSD_REQ(n_ranks >= 1 && n_ranks <= kMaxPeers, SSD_ERR_ARG, "n_ranks %d outside [1, %d]",
+            n_ranks, kMaxPeers);
+    SSD_REQ(w->type != SSD_TYPE_F16 && w->type != SSD_TYPE_BF16, SSD_ERR_TYPE,
+            "peer input: quantized weights only");
+    MvArgs a = mv_plain(w, x, y);
+    a.ar_in = partials;
+    a.ar_in_flag = flags;
+    a.ar_in_n = n_ranks;
+    a.ar_epoch = epoch;
+    a.ar_call = call;
+    return launch_matvec(ctx, w->type, EPI_STORE, a, pick_stream(ctx, stream), ctx->pdl);
+}
+
 extern "C" int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, size_t w_bytes,
                                          const float* x, float* y, int out_dim, int in_dim,
                                          int type) {

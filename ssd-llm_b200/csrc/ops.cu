@@ -866,12 +866,29 @@ static __device__ __align__(256) float g_noalloc_partial[kNoAllocPartialFloats];
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[64] = {nullptr};
 
+// Loads every attention kernel the entry point may launch (each head_dim and GQA group)
+// on the current device. With lazy module loading a kernel's code is otherwise loaded at
+// its first launch, which would make the first call with a new (head_dim, group) do more
+// than launch.
+static int noalloc_preload_kernels() {
+    cudaFuncAttributes fa;
+    const void* fns[] = {
+        (const void*)k_attn_partial<128, 1>, (const void*)k_attn_partial<128, 2>,
+        (const void*)k_attn_partial<128, 4>, (const void*)k_attn_partial<128, 8>,
+        (const void*)k_attn_partial<64, 1>,  (const void*)k_attn_partial<64, 2>,
+        (const void*)k_attn_partial<64, 4>,  (const void*)k_attn_partial<64, 8>,
+        (const void*)k_attn_combine<128>,    (const void*)k_attn_combine<64>};
+    for (const void* f : fns) SSD_CK(cudaFuncGetAttributes(&fa, f));
+    return SSD_OK;
+}
+
 static int noalloc_partial_ptr(int device, float** out) {
     SSD_REQ(device >= 0 && device < 64, SSD_ERR_ARG, "device %d out of range", device);
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_ptr[device]) {
         void* p = nullptr;
         SSD_CK(cudaGetSymbolAddress(&p, g_noalloc_partial));  // check_ctx made `device` current
+        SSD_TRY(noalloc_preload_kernels());
         g_noalloc_ptr[device] = (float*)p;
     }
     *out = g_noalloc_ptr[device];

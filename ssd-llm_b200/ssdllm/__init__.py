@@ -156,6 +156,8 @@ _SIGS = {
     "ssd_gguf_model_config": ([_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                ctypes.POINTER(ModelConfig)], ctypes.c_int),
     "ssd_model_load_gguf": ([_vp, _vp, ctypes.c_int], ctypes.c_int),
+    "ssd_matvec_peer_input": ([_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp,
+                               _vp], ctypes.c_int),
     "ssd_batch_create": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
     "ssd_batch_free": ([_vp], ctypes.c_int),
     "ssd_batch_slots": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
@@ -300,6 +302,12 @@ def matvec(ctx, w: Weight, x, y):
 def prefill_matmul(ctx, w: Weight, x, y):
     """y[t] = W x[t] for every row t of x (torch [n_tokens][cols] -> [n_tokens][rows])."""
     check(lib().ssd_prefill_matmul(ctx.h, w.h, _ptr(x), x.shape[0], _ptr(y), _stream()))
+
+
+def matvec_peer_input(ctx, w: Weight, x, partials, n_ranks, flags, epoch, call, y):
+    """y = W (x + the n_ranks partial rows), after every rank's flag reaches epoch + call + 1."""
+    check(lib().ssd_matvec_peer_input(ctx.h, w.h, _ptr(x), _ptr(partials), n_ranks, _ptr(flags),
+                                      _ptr(epoch), call, _ptr(y), _stream()))
 
 
 def matvec_residual(ctx, w: Weight, x, base, y):
