@@ -13,15 +13,19 @@ def make_weights(rng, E, nh, nkv, hd, F, vocab, n_layers, wtype=ora.Q4_0, out_ty
               "ffn_down": (E, F)}
     layers = []
     for _ in range(n_layers):
-        L = {n: ora.quantize((rng.standard_normal(s) * 0.02).astype(np.float32), wtype)
-             for n, s in shapes.items()}
+        L = {}
+        for n, sh in shapes.items():
+            wf = rng.standard_normal(sh, dtype=np.float32)
+            wf *= np.float32(0.02)
+            L[n] = ora.quantize(wf, wtype)
+            del wf
         L["attn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
         L["ffn_norm"] = (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)
         layers.append(L)
-    glob = {"token_embd": ora.quantize(rng.standard_normal((vocab, E)).astype(np.float32),
-                                       ora.Q4_0),
-            "output": ora.quantize((rng.standard_normal((vocab, E)) * 0.05).astype(np.float32),
-                                   out_type),
+    emb = rng.standard_normal((vocab, E), dtype=np.float32)
+    out = rng.standard_normal((vocab, E), dtype=np.float32)
+    out *= np.float32(0.05)
+    glob = {"token_embd": ora.quantize(emb, ora.Q4_0), "output": ora.quantize(out, out_type),
             "output_norm": (1 + 0.1 * rng.standard_normal(E)).astype(np.float32)}
     return layers, glob
 
@@ -71,3 +75,16 @@ class OracleDecoder:
         t = ora.argmax(logits)
         srt = np.sort(logits)
         return t, float((srt[-1] - srt[-2]) / np.max(np.abs(logits)))
+
+
+def read_cache(ssdllm, ctx, m, layer, n, kvd):
+    """The first n rows of one layer's INT8 cache (K, K scales, V, V scales) on the host."""
+    kp, vp, ksp, vsp = m.kv(layer).pointers()
+    out = []
+    for ptr, shape, dt in ((kp, (n, kvd), np.int8), (ksp, (n,), np.float32),
+                           (vp, (n, kvd), np.int8), (vsp, (n,), np.float32)):
+        a = np.zeros(shape, dt)
+        if n:
+            ssdllm.copy_to_host(ctx, a, ptr)
+        out.append(a)
+    return out
