@@ -5,8 +5,7 @@
  * operator surface that `src/inference` calls on `MetalCompute` / `MetalGpu`.
  * Every entry point below names the reference interface it replaces
  * (path:line inside quantumnic/ssd-llm). The Rust side binds these with an
- * `extern "C"` block and keeps the `MetalCompute` method
- * signatures.
+ * `extern "C"` block and keeps the `MetalCompute` method signatures.
  *
  * Conventions
  *  - Every call returns an int status: SSD_OK (0) or one of SSD_ERR_*. No call
@@ -71,7 +70,9 @@ extern "C" {
 /* 16-bit dense weights, row-major, 2 bytes each: F16 (IEEE half, matvec_f16_cpu,
  * src/metal/compute.rs:2272-2285) and BF16 (the top half of an f32, matvec_bf16_cpu,
  * :2250-2269). Accepted by ssd_weight_upload, ssd_dequantize and the plain matvec entry
- * points (any column count). */
+ * points (any column count). F32 weights (row-major, 4 bytes each; matvec_f32_simd,
+ * :378-424) are accepted by the same calls. ssd_fused_swiglu takes dense gate / up weights
+ * with norm_w NULL (no fused norm). */
 #define SSD_TYPE_BF16 30
 
 typedef struct ssd_ctx ssd_ctx;
@@ -291,6 +292,61 @@ int ssd_matvec_peer_input(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev,
 int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, size_t w_bytes,
                               const float* x, float* y, int out_dim, int in_dim, int ggml_type);
 
+/* ------------------------------------------------ host-slice f32 operators */
+/* The remaining MetalCompute methods (src/metal/compute.rs:145-375) with their slice
+ * semantics: row-major f32 weights [out][in] and vectors on the host; each call copies its
+ * operands to the device, computes on the context's stream, copies the results back and
+ * synchronises (src/metal/gpu.rs:169-205 uploads its weights per call the same way).
+ * Outputs are caller-provided arrays of the sizes the reference returns. */
+/* MetalCompute::matvec_f32 (src/metal/compute.rs:145-153): y[out_dim] = W x. */
+int ssd_matvec_f32_host(ssd_ctx* ctx, const float* w, const float* x, float* y, int out_dim,
+                        int in_dim);
+/* MetalCompute::rmsnorm_f32 (src/metal/compute.rs:193-202), x updated in place. */
+int ssd_rmsnorm_f32_host(ssd_ctx* ctx, float* x, const float* weight, int n, float eps);
+/* MetalCompute::softmax_f32 (src/metal/compute.rs:204-215), x updated in place; n == 0 is a
+ * no-op. */
+int ssd_softmax_f32_host(ssd_ctx* ctx, float* x, int n);
+/* MetalCompute::flash_attention_f32 (src/metal/compute.rs:217-259; the shader
+ * src/metal/shaders/kernels.metal:1360-1440): q [n_head][head_dim], k and v
+ * [seq_len][n_head_kv * head_dim]; each head attends to positions
+ * [window_start, min(window_end, seq_len)) with GQA group n_head / n_head_kv; a head whose
+ * window is empty gets zeros; head_dim <= 256. Only the window's K / V rows are copied.
+ * Where the reference returns None (seq_len < 4 without a GPU) this call still computes. */
+int ssd_flash_attention_f32_host(ssd_ctx* ctx, const float* q, const float* k, const float* v,
+                                 int n_head, int n_head_kv, int head_dim, int seq_len,
+                                 int window_start, int window_end, float* out);
+/* The same attention on device pointers (the kernel behind the host call, for callers that
+ * keep an f32 cache resident; src/inference/flash_attention.rs:146-229 is its CPU twin).
+ * Uses the context scratch for split partials when the window is long. */
+int ssd_flash_attention_f32(ssd_ctx* ctx, const float* q_dev, const float* k_dev,
+                            const float* v_dev, int n_head, int n_head_kv, int head_dim,
+                            int seq_len, int window_start, int window_end, float* out_dev,
+                            void* stream);
+/* MetalCompute::fused_qkv_f32 (src/metal/compute.rs:273-292): q[q_dim], k[kv_dim],
+ * v[kv_dim] from one x[n_embd]. */
+int ssd_fused_qkv_f32_host(ssd_ctx* ctx, const float* wq, const float* wk, const float* wv,
+                           const float* x, int q_dim, int kv_dim, int n_embd, float* q, float* k,
+                           float* v);
+/* MetalCompute::fused_qkv_rope_f32 (src/metal/compute.rs:296-323): as fused_qkv_f32, then
+ * RoPE at `position` on Q and K (rope_f32_multi_head, :482-506). */
+int ssd_fused_qkv_rope_f32_host(ssd_ctx* ctx, const float* wq, const float* wk, const float* wv,
+                                const float* x, int q_dim, int kv_dim, int n_embd, int head_dim,
+                                int position, float theta, float* q, float* k, float* v);
+/* MetalCompute::fused_post_attn_norm_f32 (src/metal/compute.rs:328-343): hidden += attn in
+ * place, out = rmsnorm(hidden) * norm_w. */
+int ssd_fused_post_attn_norm_f32_host(ssd_ctx* ctx, float* hidden, const float* attn,
+                                      const float* norm_w, int n, float eps, float* out);
+/* MetalCompute::fused_rmsnorm_linear_f32 (src/metal/compute.rs:348-374):
+ * logits[vocab] = W_out (x * inv_rms * norm_w), eps 1e-5 as the reference fixes it. */
+int ssd_fused_rmsnorm_linear_f32_host(ssd_ctx* ctx, const float* x, const float* norm_w,
+                                      const float* out_w, int vocab, int n_embd, float* logits);
+/* MetalGpu::feed_forward_f32 (src/metal/gpu.rs:789-838; src/inference/feed_forward.rs:17-43):
+ * out[n_embd] = W_down (silu(W_gate x) * (W_up x)); W_gate and W_up [n_ff][n_embd], W_down
+ * [n_embd][n_ff]. Gate and up rows share one pass over x. n_ff == 0 gives zeros. */
+int ssd_feed_forward_f32_host(ssd_ctx* ctx, const float* x, const float* w_gate,
+                              const float* w_up, const float* w_down, int n_embd, int n_ff,
+                              float* out);
+
 /* ------------------------------------------------------- decode engine */
 /* Llama-shaped decoder with HBM-resident quantized weights, INT8 KV cache and
  * optional row-sharded tensor parallelism. Replaces forward_pass / generate's
@@ -298,9 +354,9 @@ int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, size_t w_bytes
  * tp_size > 1 needs ssd_model_tp_init before building. */
 typedef struct {
     int n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab;
-    int wtype;        /* layer weight type (Q4_0 / Q8_0 / Q4_K) */
-    int out_type;     /* output.weight type */
-    int embd_type;    /* token_embd type (F32 / Q4_0 / Q8_0) */
+    int wtype;        /* layer weight type: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K or Q8_K */
+    int out_type;     /* output.weight type: as wtype */
+    int embd_type;    /* token_embd type: as wtype, or F32 / F16 / BF16 */
     int kv_capacity;  /* INT8 KV positions */
     float theta, eps;
     int tp_rank, tp_size;

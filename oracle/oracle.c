@@ -751,6 +751,71 @@ void ora_flash_attention_int8(const float* q, const int8_t* k, const float* ks, 
     free(acc);
 }
 
+/* Windowed attention over f32 K/V rows [pos][n_head_kv * head_dim]: the shader
+ * flash_attention_f32 (src/metal/shaders/kernels.metal:1360-1440) and its CPU twin
+ * flash_attention_windowed (src/inference/flash_attention.rs:146-229). Positions
+ * [window_start, min(window_end, seq_len)) in order; 4-wide unrolled q.k as the shader
+ * (kernels.metal:1399-1407); a head whose window is empty gets zeros (:1430-1438). */
+void ora_flash_attention_f32(const float* q, const float* k, const float* v, int n_head,
+                             int n_head_kv, int head_dim, int seq_len, int window_start,
+                             int window_end, float* out) {
+    int kv_dim = n_head_kv * head_dim;
+    int group = n_head_kv > 0 ? n_head / n_head_kv : 1;
+    if (group < 1) group = 1;
+    float scale = 1.0f / sqrtf((float)head_dim);
+    int end = window_end < seq_len ? window_end : seq_len;
+    float* acc = (float*)malloc(sizeof(float) * (size_t)(head_dim > 0 ? head_dim : 1));
+    for (int h = 0; h < n_head; h++) {
+        int kv_h = h / group;
+        const float* qh = q + (size_t)h * head_dim;
+        float running_max = -INFINITY, running_sum = 0.0f;
+        for (int d = 0; d < head_dim; d++) acc[d] = 0.0f;
+        for (int p = window_start; p < end; p++) {
+            const float* kh = k + (size_t)p * kv_dim + (size_t)kv_h * head_dim;
+            const float* vh = v + (size_t)p * kv_dim + (size_t)kv_h * head_dim;
+            int hd4 = (head_dim / 4) * 4;
+            float dot = 0.0f;
+            for (int d = 0; d < hd4; d += 4)
+                dot += qh[d] * kh[d] + qh[d + 1] * kh[d + 1] + qh[d + 2] * kh[d + 2] +
+                       qh[d + 3] * kh[d + 3];
+            for (int d = hd4; d < head_dim; d++) dot += qh[d] * kh[d];
+            float score = dot * scale;
+            if (score > running_max) {
+                float correction = expf(running_max - score);
+                running_sum *= correction;
+                for (int d = 0; d < head_dim; d++) acc[d] *= correction;
+                running_max = score;
+            }
+            float weight = expf(score - running_max);
+            running_sum += weight;
+            for (int d = 0; d < head_dim; d++) acc[d] += weight * vh[d];
+        }
+        for (int d = 0; d < head_dim; d++)
+            out[(size_t)h * head_dim + d] = running_sum > 0.0f ? acc[d] * (1.0f / running_sum) : 0.0f;
+    }
+    free(acc);
+}
+
+/* SwiGLU feed-forward (src/inference/feed_forward.rs:17-43): act = silu(W_gate x) * (W_up x),
+ * out = W_down act, each product by matvec_f32_simd (compute.rs:390-424). n_ff == 0 gives
+ * zeros (:25-28). */
+void ora_feed_forward_f32(const float* x, const float* w_gate, const float* w_up,
+                          const float* w_down, int n_embd, int n_ff, float* out) {
+    if (n_ff <= 0) {
+        for (int i = 0; i < n_embd; i++) out[i] = 0.0f;
+        return;
+    }
+    float* g = (float*)malloc(sizeof(float) * (size_t)n_ff);
+    float* u = (float*)malloc(sizeof(float) * (size_t)n_ff);
+    ora_matvec_f32(w_gate, x, n_ff, n_embd, g);
+    ora_silu(g, n_ff);
+    ora_matvec_f32(w_up, x, n_ff, n_embd, u);
+    for (int i = 0; i < n_ff; i++) g[i] *= u[i];
+    ora_matvec_f32(w_down, g, n_embd, n_ff, out);
+    free(u);
+    free(g);
+}
+
 /* ----------------------------------------------------------- layer step */
 
 /* Matvec in one of the two reference CPU paths. Mode 0 (the live path of

@@ -98,6 +98,15 @@ void ora_flash_attention_int8(const float* q, const int8_t* k, const float* ks, 
                               const float* vs, int seq_len, int n_head, int n_head_kv,
                               int head_dim, float* out);
 
+/* f32 K/V windowed attention: flash_attention_f32 (src/metal/shaders/kernels.metal:1360-1440,
+ * flash_attention_windowed src/inference/flash_attention.rs:146-229). */
+void ora_flash_attention_f32(const float* q, const float* k, const float* v, int n_head,
+                             int n_head_kv, int head_dim, int seq_len, int window_start,
+                             int window_end, float* out);
+/* SwiGLU feed-forward, src/inference/feed_forward.rs:17-43. */
+void ora_feed_forward_f32(const float* x, const float* w_gate, const float* w_up,
+                          const float* w_down, int n_embd, int n_ff, float* out);
+
 /* One decoder layer decode step: forward_pass body src/inference/transformer.rs:312-394
  * with multi_head_attention_fused_rope (attention.rs:172-240) over the INT8 cache and
  * feed_forward (feed_forward.rs:17-44). Weights are packed in `wtype` (reference layout).

@@ -54,6 +54,8 @@ def lib():
         L.ora_matvec_quantized_mt.argtypes = [_u8p, _fp, i32, i32, i32, _fp, i32]
         L.ora_matvec_quantized_mt.restype = i32
         L.ora_matvec_f32.argtypes = [_fp, _fp, i32, i32, _fp]
+        L.ora_flash_attention_f32.argtypes = [_fp, _fp, _fp, i32, i32, i32, i32, i32, i32, _fp]
+        L.ora_feed_forward_f32.argtypes = [_fp, _fp, _fp, _fp, i32, i32, _fp]
         L.ora_rmsnorm.argtypes = [_fp, _fp, i32, f32]
         L.ora_fused_residual_rmsnorm.argtypes = [_fp, _fp, _fp, i32, f32]
         L.ora_fused_post_attn_norm.argtypes = [_fp, _fp, _fp, i32, f32, _fp]
@@ -211,6 +213,21 @@ def attention_int8(q, k, ks, v, vs, seq_len, n_head, n_head_kv, head_dim, flash=
     fn(_f(f32c(q)), _i8(np.ascontiguousarray(k, dtype=np.int8)), _f(f32c(ks)),
        _i8(np.ascontiguousarray(v, dtype=np.int8)), _f(f32c(vs)), seq_len, n_head, n_head_kv,
        head_dim, _f(out))
+    return out
+
+
+def flash_attention_f32(q, k, v, n_head, n_head_kv, head_dim, seq_len, window_start,
+                        window_end):
+    out = np.zeros(n_head * head_dim, dtype=np.float32)
+    lib().ora_flash_attention_f32(_f(f32c(q)), _f(f32c(k)), _f(f32c(v)), n_head, n_head_kv,
+                                  head_dim, seq_len, window_start, window_end, _f(out))
+    return out
+
+
+def feed_forward_f32(x, w_gate, w_up, w_down, n_embd, n_ff):
+    out = np.zeros(n_embd, dtype=np.float32)
+    lib().ora_feed_forward_f32(_f(f32c(x)), _f(f32c(w_gate)), _f(f32c(w_up)), _f(f32c(w_down)),
+                               n_embd, n_ff, _f(out))
     return out
 
 

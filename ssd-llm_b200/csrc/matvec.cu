@@ -928,61 +928,100 @@ static int launch_fmt(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bo
 
 static inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
-// 16-bit dense rows (matvec_f16_cpu / matvec_bf16_cpu, src/metal/compute.rs:2256-2285).
-// Each CTA takes a contiguous, balanced range of rows (counts differ by at most one
-// between CTAs, so no half-empty second pass over a few leftover rows), four rows at a
-// time: its 256 threads split the columns (thread t owns columns 8t..8t+7 of every
-// 2048-column step, one 16-byte load per row, when cols % 8 == 0; single columns
-// otherwise), x is loaded once per step for the four rows, each warp sums its share, and
-// thread i adds the 8 warp partials of row i in warp order. y = W x, or base + W x.
+// Dense rows: F16 / BF16 (matvec_f16_cpu / matvec_bf16_cpu, src/metal/compute.rs:2250-2285)
+// and F32 (matvec_f32_simd, :378-424). Each CTA takes a contiguous, balanced range of output
+// rows (counts differ by at most one between CTAs, so no half-empty second pass over a few
+// leftover rows), kDenseRows weight rows at a time: its 256 threads split the columns
+// (thread t owns the 16 bytes at element EPL*t of every 256*EPL-element step, EPL = 8 for
+// 16-bit and 4 for f32 elements, when cols % EPL == 0; single columns otherwise), x is
+// loaded once per step for all rows of the group, each warp sums its share, and thread i
+// adds the 8 warp partials of row i in warp order. y = W x, or base + W x; with EPI_SWIGLU
+// the group's rows are gate r, up r, gate r+1, up r+1 (qs[0], qs[1]) and output r is
+// silu(gate r) * up r (the fused_swiglu_f32 shader, kernels.metal:1475-1500).
 constexpr int kDenseRows = 4;
 
-template <bool BF, int EPI>
+template <int DT>
+__device__ __forceinline__ float dense_elem(const void* base, size_t i) {
+    if (DT == SSD_TYPE_F32) return __ldg(reinterpret_cast<const float*>(base) + i);
+    const uint32_t h = __ldg(reinterpret_cast<const uint16_t*>(base) + i);
+    return DT == SSD_TYPE_BF16 ? __uint_as_float(h << 16) : f16_bits_to_f32((uint16_t)h);
+}
+
+// The 16 bytes q as EPL consecutive elements.
+template <int DT>
+__device__ __forceinline__ void dense_unpack(const uint4 q, float* f) {
+    if (DT == SSD_TYPE_F32) {
+        f[0] = __uint_as_float(q.x);
+        f[1] = __uint_as_float(q.y);
+        f[2] = __uint_as_float(q.z);
+        f[3] = __uint_as_float(q.w);
+    } else {
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            f[2 * j] = DT == SSD_TYPE_BF16 ? __uint_as_float(u[j] << 16)
+                                           : f16_bits_to_f32((uint16_t)(u[j] & 0xFFFFu));
+            f[2 * j + 1] = DT == SSD_TYPE_BF16 ? __uint_as_float(u[j] & 0xFFFF0000u)
+                                               : f16_bits_to_f32((uint16_t)(u[j] >> 16));
+        }
+    }
+}
+
+template <int DT, int EPI>
 __global__ void __launch_bounds__(256) k_matvec_dense(const MvArgs a) {
+    constexpr int ESZ = DT == SSD_TYPE_F32 ? 4 : 2;
+    constexpr int EPL = 16 / ESZ;
+    constexpr bool SW = EPI == EPI_SWIGLU;
+    constexpr int OUT = SW ? kDenseRows / 2 : kDenseRows;  // outputs per group
     __shared__ float part[8][kDenseRows];
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int r0 = (int)((int64_t)a.rows * blockIdx.x / gridDim.x);
-    const int r1 = (int)((int64_t)a.rows * (blockIdx.x + 1) / gridDim.x);
-    const bool vec = (a.cols & 7) == 0;
-    const uint16_t* wbase = reinterpret_cast<const uint16_t*>(a.qs[0]);
-    auto cvt = [](uint32_t h) {
-        return BF ? __uint_as_float((h & 0xFFFFu) << 16) : f16_bits_to_f32((uint16_t)h);
-    };
-    for (int g = r0; g < r1; g += kDenseRows) {
-        const int nr = r1 - g < kDenseRows ? r1 - g : kDenseRows;
-        const uint16_t* w[kDenseRows];
+    const int n_out = SW ? a.seg_rows[0] : a.rows;
+    const int r0 = (int)((int64_t)n_out * blockIdx.x / gridDim.x);
+    const int r1 = (int)((int64_t)n_out * (blockIdx.x + 1) / gridDim.x);
+    const bool vec = (a.cols % EPL) == 0;
+    const char* wb0 = reinterpret_cast<const char*>(a.qs[0]);
+    const char* wb1 = reinterpret_cast<const char*>(SW ? a.qs[1] : a.qs[0]);
+    for (int g = r0; g < r1; g += OUT) {
+        const int nr = r1 - g < OUT ? r1 - g : OUT;
+        const char* w[kDenseRows];
 #pragma unroll
-        for (int i = 0; i < kDenseRows; i++)  // rows past the range re-read the last one
-            w[i] = wbase + (size_t)(g + (i < nr ? i : nr - 1)) * a.cols;
+        for (int i = 0; i < kDenseRows; i++) {  // rows past the range re-read the last one
+            const int o = i / (SW ? 2 : 1);
+            const int row = g + (o < nr ? o : nr - 1);
+            w[i] = (SW && (i & 1) ? wb1 : wb0) + (size_t)row * a.cols * ESZ;
+        }
         float s[kDenseRows];
 #pragma unroll
         for (int i = 0; i < kDenseRows; i++) s[i] = 0.0f;
         if (vec) {
-            for (int c = 8 * threadIdx.x; c < a.cols; c += 2048) {
+            for (int c = EPL * threadIdx.x; c < a.cols; c += 256 * EPL) {
                 uint4 q[kDenseRows];
 #pragma unroll
                 for (int i = 0; i < kDenseRows; i++)
-                    q[i] = __ldg(reinterpret_cast<const uint4*>(w[i] + c));
-                const float4 x0 = __ldg(reinterpret_cast<const float4*>(a.x + c));
-                const float4 x1 = __ldg(reinterpret_cast<const float4*>(a.x + c + 4));
+                    q[i] = __ldg(reinterpret_cast<const uint4*>(w[i] + (size_t)c * ESZ));
+                float xv[EPL];
+#pragma unroll
+                for (int j = 0; j < EPL; j += 4) {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(a.x + c + j));
+                    xv[j] = t.x;
+                    xv[j + 1] = t.y;
+                    xv[j + 2] = t.z;
+                    xv[j + 3] = t.w;
+                }
 #pragma unroll
                 for (int i = 0; i < kDenseRows; i++) {
-                    s[i] = fmaf(cvt(q[i].x), x0.x, s[i]);
-                    s[i] = fmaf(cvt(q[i].x >> 16), x0.y, s[i]);
-                    s[i] = fmaf(cvt(q[i].y), x0.z, s[i]);
-                    s[i] = fmaf(cvt(q[i].y >> 16), x0.w, s[i]);
-                    s[i] = fmaf(cvt(q[i].z), x1.x, s[i]);
-                    s[i] = fmaf(cvt(q[i].z >> 16), x1.y, s[i]);
-                    s[i] = fmaf(cvt(q[i].w), x1.z, s[i]);
-                    s[i] = fmaf(cvt(q[i].w >> 16), x1.w, s[i]);
+                    float f[EPL];
+                    dense_unpack<DT>(q[i], f);
+#pragma unroll
+                    for (int j = 0; j < EPL; j++) s[i] = fmaf(f[j], xv[j], s[i]);
                 }
             }
         } else {
             for (int c = threadIdx.x; c < a.cols; c += 256) {
                 const float xv = a.x[c];
 #pragma unroll
-                for (int i = 0; i < kDenseRows; i++) s[i] = fmaf(cvt(w[i][c]), xv, s[i]);
+                for (int i = 0; i < kDenseRows; i++) s[i] = fmaf(dense_elem<DT>(w[i], c), xv, s[i]);
             }
         }
 #pragma unroll
@@ -991,49 +1030,72 @@ __global__ void __launch_bounds__(256) k_matvec_dense(const MvArgs a) {
             if (lane == 0) part[warp][i] = v;
         }
         __syncthreads();
-        if (threadIdx.x < nr) {
+        if (threadIdx.x < kDenseRows) {
             float t = part[0][threadIdx.x];
 #pragma unroll
             for (int k = 1; k < 8; k++) t += part[k][threadIdx.x];
+            part[0][threadIdx.x] = t;
+        }
+        __syncthreads();
+        if (threadIdx.x < nr) {
             const int row = g + threadIdx.x;
-            a.y[row] = EPI == EPI_RESID ? __fadd_rn(a.base[row], t) : t;
+            if (SW) {
+                // silu(v) = v / (1 + exp(-v)), then gate *= up (feed_forward.rs:31-39)
+                const float gt = part[0][2 * threadIdx.x], up = part[0][2 * threadIdx.x + 1];
+                a.y[row] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+            } else {
+                const float t = part[0][threadIdx.x];
+                a.y[row] = EPI == EPI_RESID ? __fadd_rn(a.base[row], t) : t;
+            }
         }
         __syncthreads();
     }
 }
 
-template <bool BF, int EPI>
+template <int DT, int EPI>
 static int launch_dense_epi(ssd_ctx* ctx, const MvArgs& a, cudaStream_t s, bool pdl) {
     static int per_sm = 0;  // resident CTAs per SM (same on every device of one build)
     if (per_sm == 0) {
         int n = 0;
-        SSD_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_matvec_dense<BF, EPI>, 256, 0));
+        SSD_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_matvec_dense<DT, EPI>, 256, 0));
         per_sm = n > 0 ? n : 1;
     }
     const int full = ctx->num_sms * per_sm;
-    const int grid = a.rows < full ? a.rows : full;
-    SSD_CK(launch_pdl(k_matvec_dense<BF, EPI>, dim3(grid), dim3(256), 0, s, pdl, a));
+    const int n_out = EPI == EPI_SWIGLU ? a.seg_rows[0] : a.rows;
+    const int grid = n_out < full ? n_out : full;
+    SSD_CK(launch_pdl(k_matvec_dense<DT, EPI>, dim3(grid), dim3(256), 0, s, pdl, a));
     return SSD_OK;
 }
 
-template <bool BF>
+template <int DT>
 static int launch_dense(ssd_ctx* ctx, int epi, const MvArgs& a, cudaStream_t s, bool pdl) {
-    return epi == EPI_RESID ? launch_dense_epi<BF, EPI_RESID>(ctx, a, s, pdl)
-                            : launch_dense_epi<BF, EPI_STORE>(ctx, a, s, pdl);
+    switch (epi) {
+        case EPI_RESID: return launch_dense_epi<DT, EPI_RESID>(ctx, a, s, pdl);
+        case EPI_SWIGLU: return launch_dense_epi<DT, EPI_SWIGLU>(ctx, a, s, pdl);
+        default: return launch_dense_epi<DT, EPI_STORE>(ctx, a, s, pdl);
+    }
+}
+
+static bool is_dense(int type) {
+    return type == SSD_TYPE_F16 || type == SSD_TYPE_BF16 || type == SSD_TYPE_F32;
 }
 
 int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_t s, bool pdl) {
     MvArgs a = a0;
     if (!a.status) a.status = ctx->dev_status;
-    if (type == SSD_TYPE_F16 || type == SSD_TYPE_BF16) {
+    if (is_dense(type)) {
         SSD_REQ(a.rows > 0 && a.cols > 0, SSD_ERR_SHAPE, "empty matrix");
         SSD_REQ(a.x && a.y && ((uintptr_t)a.x & 15) == 0, SSD_ERR_ARG,
                 "x and y must be non-null, x 16-byte aligned");
-        SSD_REQ((epi == EPI_STORE || (epi == EPI_RESID && a.base)) && a.map == MAP_PLAIN &&
+        SSD_REQ(((epi == EPI_STORE && a.map == MAP_PLAIN) ||
+                 (epi == EPI_RESID && a.map == MAP_PLAIN && a.base) ||
+                 (epi == EPI_SWIGLU && a.map == MAP_SWIGLU && a.qs[1] &&
+                  a.rows == 2 * a.seg_rows[0])) &&
                     !a.x_add && !a.norm_w && a.ar_in_n == 0,
-                SSD_ERR_ARG, "16-bit dense weights: plain or residual matvec only");
-        return type == SSD_TYPE_BF16 ? launch_dense<true>(ctx, epi, a, s, pdl)
-                                     : launch_dense<false>(ctx, epi, a, s, pdl);
+                SSD_ERR_ARG, "dense weights: plain, residual or un-normed SwiGLU matvec only");
+        if (type == SSD_TYPE_F32) return launch_dense<SSD_TYPE_F32>(ctx, epi, a, s, pdl);
+        return type == SSD_TYPE_BF16 ? launch_dense<SSD_TYPE_BF16>(ctx, epi, a, s, pdl)
+                                     : launch_dense<SSD_TYPE_F16>(ctx, epi, a, s, pdl);
     }
     SSD_REQ(a.cols > 0 && a.cols % 32 == 0, SSD_ERR_SHAPE, "cols %d not a multiple of 32", a.cols);
     SSD_REQ(a.rows > 0, SSD_ERR_SHAPE, "no rows");
@@ -1110,7 +1172,7 @@ static int check_w(const ssd_weight* w) {
     SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
     SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
                 w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_Q8_K ||
-                w->type == SSD_TYPE_F16 || w->type == SSD_TYPE_BF16,
+                is_dense(w->type),
             SSD_ERR_TYPE, "matvec: ggml type %d not supported", w->type);
     return SSD_OK;
 }
@@ -1229,8 +1291,7 @@ extern "C" int ssd_matvec_peer_input(ssd_ctx* ctx, const ssd_weight* w, const fl
     SSD_REQ(x && y && partials && flags && epoch, SSD_ERR_ARG, "null argument");
     SSD_REQ(n_ranks >= 1 && n_ranks <= kMaxPeers, SSD_ERR_ARG, "n_ranks %d outside [1, %d]",
             n_ranks, kMaxPeers);
-    SSD_REQ(w->type != SSD_TYPE_F16 && w->type != SSD_TYPE_BF16, SSD_ERR_TYPE,
-            "peer input: quantized weights only");
+    SSD_REQ(!is_dense(w->type), SSD_ERR_TYPE, "peer input: quantized weights only");
     MvArgs a = mv_plain(w, x, y);
     a.ar_in = partials;
     a.ar_in_flag = flags;

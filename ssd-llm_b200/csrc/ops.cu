@@ -19,18 +19,6 @@ namespace ssd {
 constexpr float kQ80Magic = 8388736.0f;  // 2^23 + 128: (byte ^ 0x80) under 0x4B -> int8 exact
 
 template <int NT>
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.0f;
-#pragma unroll
-    for (int w = 0; w < NT / 32; w++) t += red[w];
-    return t;
-}
-template <int NT>
 __device__ __forceinline__ float block_max(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     v = warp_max(v);

@@ -170,6 +170,23 @@ _SIGS = {
                               ctypes.c_int),
     "ssd_batch_state": ([_vp, ctypes.POINTER(_vp)], ctypes.c_int),
     "ssd_batch_launches_per_step": ([_vp, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "ssd_matvec_f32_host": ([_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "ssd_rmsnorm_f32_host": ([_vp, _vp, _vp, ctypes.c_int, ctypes.c_float], ctypes.c_int),
+    "ssd_softmax_f32_host": ([_vp, _vp, ctypes.c_int], ctypes.c_int),
+    "ssd_flash_attention_f32_host": ([_vp, _vp, _vp, _vp] + [ctypes.c_int] * 6 + [_vp],
+                                     ctypes.c_int),
+    "ssd_flash_attention_f32": ([_vp, _vp, _vp, _vp] + [ctypes.c_int] * 6 + [_vp, _vp],
+                                ctypes.c_int),
+    "ssd_fused_qkv_f32_host": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_int, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_fused_qkv_rope_f32_host": ([_vp, _vp, _vp, _vp, _vp] + [ctypes.c_int] * 5 +
+                                    [ctypes.c_float, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_fused_post_attn_norm_f32_host": ([_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_float,
+                                           _vp], ctypes.c_int),
+    "ssd_fused_rmsnorm_linear_f32_host": ([_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp],
+                                          ctypes.c_int),
+    "ssd_feed_forward_f32_host": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp],
+                                  ctypes.c_int),
 }
 
 
@@ -687,32 +704,58 @@ def shard_range(cfg: ModelConfig, name: str, layer: int):
     return tuple(x.value for x in v)
 
 
-class CudaCompute:
-    """Host-slice mirror of MetalCompute (src/metal/compute.rs:18-373).
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
 
-    Same method names and argument meaning as the reference; numpy arrays stand
-    in for Rust slices. Each call copies in, runs the CUDA kernel, copies out.
-    `new()` mirrors MetalCompute::new() -> Option<Self> but raises instead of
-    returning None when no device is usable (no silent CPU fallback).
+
+class CudaCompute:
+    """Host-slice mirror of MetalCompute (src/metal/compute.rs:18-375) and of
+    MetalGpu::feed_forward_f32 (src/metal/gpu.rs:789-838).
+
+    Same method names and argument meaning as the reference; numpy arrays stand in for
+    Rust slices, and each method is one call of the C entry point a Rust binding would
+    make (ssd_*_host: copy in, run the CUDA kernels, copy out, synchronise). In-place
+    methods update the given array. `new()` mirrors MetalCompute::new() -> Option<Self>
+    but raises instead of returning None when no device is usable (no CPU fallback).
     """
 
     def __init__(self, device: int = 0):
-        import torch
-        self.torch = torch
         self.ctx = Context(device)
-        self.dev = torch.device("cuda", device)
 
     @classmethod
     def new(cls, device: int = 0):
         return cls(device)
 
-    def _d(self, a):
-        return self.torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.dev)
+    @staticmethod
+    def is_available() -> bool:
+        """compute.rs:31-45: a usable CUDA device."""
+        import torch
+        return torch.cuda.is_available()
+
+    def has_gpu(self) -> bool:
+        """compute.rs:261-264."""
+        return True
+
+    def shader_library_path(self):
+        """compute.rs:266-269: no runtime-compiled shader library (sm_100a code in the .so)."""
+        return None
+
+    def should_use_gpu(self, elements: int) -> bool:
+        """compute.rs:140-143: every call runs on the GPU here (no CPU fallback)."""
+        return True
+
+    def matvec_f32(self, w, x, out_dim, in_dim):
+        """compute.rs:145-153."""
+        w, x = _f32(w), _f32(x)
+        y = np.zeros(out_dim, dtype=np.float32)
+        check(lib().ssd_matvec_f32_host(self.ctx.h, w.ctypes.data, x.ctypes.data, y.ctypes.data,
+                                        out_dim, in_dim))
+        return y
 
     def matvec_quantized(self, w_raw, x, out_dim, in_dim, dtype):
         """compute.rs:157-191"""
         w_raw = np.ascontiguousarray(w_raw, dtype=np.uint8)
-        x = np.ascontiguousarray(x, dtype=np.float32)
+        x = _f32(x)
         y = np.zeros(out_dim, dtype=np.float32)
         check(lib().ssd_matvec_quantized_host(self.ctx.h, w_raw.ctypes.data, w_raw.nbytes,
                                               x.ctypes.data, y.ctypes.data, out_dim, in_dim,
@@ -720,46 +763,98 @@ class CudaCompute:
         return y
 
     def rmsnorm_f32(self, x: np.ndarray, weight, eps):
-        """compute.rs:193-202 (in place on x)."""
-        xd, wd = self._d(x), self._d(weight)
-        rmsnorm(self.ctx, xd, wd, eps)
-        x[:] = xd.cpu().numpy()
+        """compute.rs:193-202 (in place on x, a contiguous float32 array)."""
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        w = _f32(weight)
+        check(lib().ssd_rmsnorm_f32_host(self.ctx.h, x.ctypes.data, w.ctypes.data, x.size, eps))
 
     def softmax_f32(self, x: np.ndarray):
-        """compute.rs:204-213 (in place)."""
-        xd = self._d(x)
-        softmax(self.ctx, xd)
-        x[:] = xd.cpu().numpy()
+        """compute.rs:204-215 (in place on x, a contiguous float32 array)."""
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        check(lib().ssd_softmax_f32_host(self.ctx.h, x.ctypes.data, x.size))
+
+    def flash_attention_f32(self, q_heads, k_cache, v_cache, n_head, n_head_kv, head_dim,
+                            seq_len, window_start, window_end):
+        """compute.rs:217-259 (f32 K/V rows [seq][n_head_kv * head_dim])."""
+        q, k, v = _f32(q_heads), _f32(k_cache), _f32(v_cache)
+        out = np.zeros(n_head * head_dim, dtype=np.float32)
+        check(lib().ssd_flash_attention_f32_host(self.ctx.h, q.ctypes.data, k.ctypes.data,
+                                                 v.ctypes.data, n_head, n_head_kv, head_dim,
+                                                 seq_len, window_start, window_end,
+                                                 out.ctypes.data))
+        return out
+
+    def fused_qkv_f32(self, wq, wk, wv, x, q_dim, kv_dim, n_embd):
+        """compute.rs:273-292 -> (q, k, v)."""
+        wq, wk, wv, x = _f32(wq), _f32(wk), _f32(wv), _f32(x)
+        q = np.zeros(q_dim, np.float32)
+        k, v = np.zeros(kv_dim, np.float32), np.zeros(kv_dim, np.float32)
+        check(lib().ssd_fused_qkv_f32_host(self.ctx.h, wq.ctypes.data, wk.ctypes.data,
+                                           wv.ctypes.data, x.ctypes.data, q_dim, kv_dim, n_embd,
+                                           q.ctypes.data, k.ctypes.data, v.ctypes.data))
+        return q, k, v
+
+    def fused_qkv_rope_f32(self, wq, wk, wv, x, q_dim, kv_dim, n_embd, head_dim, position,
+                           theta_base):
+        """compute.rs:296-323 -> (q_rope, k_rope, v)."""
+        wq, wk, wv, x = _f32(wq), _f32(wk), _f32(wv), _f32(x)
+        q = np.zeros(q_dim, np.float32)
+        k, v = np.zeros(kv_dim, np.float32), np.zeros(kv_dim, np.float32)
+        check(lib().ssd_fused_qkv_rope_f32_host(self.ctx.h, wq.ctypes.data, wk.ctypes.data,
+                                                wv.ctypes.data, x.ctypes.data, q_dim, kv_dim,
+                                                n_embd, head_dim, position, theta_base,
+                                                q.ctypes.data, k.ctypes.data, v.ctypes.data))
+        return q, k, v
 
     def fused_post_attn_norm_f32(self, hidden: np.ndarray, attn_output, norm_weight, eps):
-        """compute.rs:328-346: hidden += attn; returns rmsnorm(hidden)."""
-        hd, ad, wd = self._d(hidden), self._d(attn_output), self._d(norm_weight)
-        out = self.torch.empty_like(hd)
-        fused_post_attn_norm(self.ctx, hd, ad, wd, eps, out)
-        hidden[:] = hd.cpu().numpy()
-        return out.cpu().numpy()
+        """compute.rs:328-343: hidden += attn in place (float32 array); returns
+        rmsnorm(hidden) * norm_weight."""
+        assert hidden.dtype == np.float32 and hidden.flags.c_contiguous
+        a, w = _f32(attn_output), _f32(norm_weight)
+        out = np.zeros(hidden.size, np.float32)
+        check(lib().ssd_fused_post_attn_norm_f32_host(self.ctx.h, hidden.ctypes.data,
+                                                      a.ctypes.data, w.ctypes.data, hidden.size,
+                                                      eps, out.ctypes.data))
+        return out
+
+    def fused_rmsnorm_linear_f32(self, x, norm_weight, out_weight, vocab_size, n_embd):
+        """compute.rs:348-374."""
+        x, nw, ow = _f32(x), _f32(norm_weight), _f32(out_weight)
+        out = np.zeros(vocab_size, np.float32)
+        check(lib().ssd_fused_rmsnorm_linear_f32_host(self.ctx.h, x.ctypes.data, nw.ctypes.data,
+                                                      ow.ctypes.data, vocab_size, n_embd,
+                                                      out.ctypes.data))
+        return out
+
+    def feed_forward_f32(self, x, w_gate, w_up, w_down, n_embd):
+        """MetalGpu::feed_forward_f32 (gpu.rs:789-838); n_ff = len(w_gate) / n_embd."""
+        x, wg, wu, wd = _f32(x), _f32(w_gate), _f32(w_up), _f32(w_down)
+        n_ff = wg.size // n_embd
+        out = np.zeros(n_embd, np.float32)
+        check(lib().ssd_feed_forward_f32_host(self.ctx.h, x.ctypes.data, wg.ctypes.data,
+                                              wu.ctypes.data, wd.ctypes.data, n_embd, n_ff,
+                                              out.ctypes.data))
+        return out
 
     def flash_attention_int8(self, q_heads, k_q, k_scale, v_q, v_scale, n_head, n_head_kv,
                              head_dim, seq_len):
-        """compute.rs:217-258 over the INT8 cache (quantized_kv_cache.rs:107-130)."""
+        """The same attention over the INT8 cache (quantized_kv_cache.rs:107-130)."""
+        import torch
         kv = KvCache(self.ctx, seq_len, n_head_kv, head_dim)
         try:
             kp, vp, ksp, vsp = kv.pointers()
-            self._copy_to(kp, np.ascontiguousarray(k_q, dtype=np.int8))
-            self._copy_to(vp, np.ascontiguousarray(v_q, dtype=np.int8))
-            self._copy_to(ksp, np.ascontiguousarray(k_scale, dtype=np.float32))
-            self._copy_to(vsp, np.ascontiguousarray(v_scale, dtype=np.float32))
-            qd = self._d(q_heads)
-            out = self.torch.empty(n_head * head_dim, device=self.dev)
+            torch.cuda.synchronize()
+            copy_to_device(self.ctx, kp, np.ascontiguousarray(k_q, dtype=np.int8))
+            copy_to_device(self.ctx, vp, np.ascontiguousarray(v_q, dtype=np.int8))
+            copy_to_device(self.ctx, ksp, _f32(k_scale))
+            copy_to_device(self.ctx, vsp, _f32(v_scale))
+            qd = torch.from_numpy(_f32(q_heads)).to(torch.device("cuda", self.ctx.device))
+            out = torch.empty(n_head * head_dim, device=qd.device)
             kv.attention(qd, n_head, seq_len, out)
             return out.cpu().numpy()
         finally:
-            self.torch.cuda.synchronize()
+            torch.cuda.synchronize()
             kv.free()
-
-    def _copy_to(self, dev_ptr: int, host: np.ndarray):
-        self.torch.cuda.synchronize()
-        copy_to_device(self.ctx, dev_ptr, host)
 
 
 def copy_to_device(ctx: Context, dev_ptr: int, host: np.ndarray):

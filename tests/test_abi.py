@@ -99,3 +99,87 @@ def test_shard_ranges_cover_each_tensor_exactly():
     cfg = ssdllm.ModelConfig(**base, tp_rank=0, tp_size=1)
     with pytest.raises(ssdllm.SsdError):
         ssdllm.shard_range(cfg, "no_such_tensor", 0)
+
+
+# ------------------------------------------------------------- Rust binding
+RUST = os.path.join(ROOT, "ssd-llm_b200", "rust", "src", "cuda")
+
+
+def _c_params():
+    """{name: [param kind]} from the header's prototypes; kind = (pointer depth, base)."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(?:int|size_t|const char\*)\s+(ssd_\w+)\s*\(([^;]*?)\);", text, re.S):
+        params = [] if m.group(2).strip() == "void" else m.group(2).split(",")
+        kinds = []
+        for p in params:
+            p = " ".join(p.split())
+            arr = re.match(r"(?:const\s+)?(\w+)\s+\w+\[\d+\]$", p)
+            if arr:
+                kinds.append((1, arr.group(1)))
+                continue
+            t = re.match(r"(?:const\s+)?(unsigned long long|\w+)\s*(\**)\s*\w+$", p)
+            assert t, p
+            kinds.append((len(t.group(2)), t.group(1)))
+        out[m.group(1)] = kinds
+    return out
+
+
+_RUST_BASE = {"c_int": "int", "c_float": "float", "usize": "size_t", "i64": "int64_t",
+              "u64": ("uint64_t", "unsigned long long"), "u32": "uint32_t", "i32": "int32_t",
+              "u8": "uint8_t", "i8": "int8_t", "c_void": "void", "c_char": "char",
+              "SsdCtx": "ssd_ctx", "SsdWeight": "ssd_weight", "SsdKvCache": "ssd_kv_cache",
+              "SsdModel": "ssd_model", "SsdGguf": "ssd_gguf", "SsdBatch": "ssd_batch",
+              "SsdModelConfig": "ssd_model_config"}
+
+
+def _rust_params():
+    text = open(os.path.join(RUST, "ffi.rs")).read()
+    block = text[text.index('extern "C" {'):]
+    out = {}
+    for m in re.finditer(r"pub fn (ssd_\w+)\((.*?)\)\s*->", block, re.S):
+        kinds = []
+        for p in [p.strip() for p in m.group(2).split(",") if p.strip()]:
+            ty = p.split(":", 1)[1].strip()
+            depth = ty.count("*")
+            base = ty.replace("*mut", "").replace("*const", "").strip()
+            kinds.append((depth, base))
+        out[m.group(1)] = kinds
+    return out
+
+
+def test_rust_extern_block_matches_the_header():
+    """src/cuda/ffi.rs declares exactly the header's entry points, each with the same
+    number of parameters, pointer depths and base types."""
+    c, r = _c_params(), _rust_params()
+    assert set(c) == set(r), (set(c) ^ set(r))
+    for name, ck in c.items():
+        rk = r[name]
+        assert len(ck) == len(rk), name
+        for (cd, cb), (rd, rb) in zip(ck, rk):
+            want = _RUST_BASE[rb]
+            assert cd == rd and (cb == want or cb in want), (name, cb, rb)
+
+
+# MetalCompute's public methods (src/metal/compute.rs:31-375) and
+# MetalGpu::feed_forward_f32 (src/metal/gpu.rs:789).
+METAL_COMPUTE_METHODS = [
+    "is_available", "new", "should_use_gpu", "matvec_f32", "matvec_quantized", "rmsnorm_f32",
+    "softmax_f32", "flash_attention_f32", "has_gpu", "shader_library_path", "fused_qkv_f32",
+    "fused_qkv_rope_f32", "fused_post_attn_norm_f32", "fused_rmsnorm_linear_f32",
+    "feed_forward_f32"]
+
+
+def test_rust_wrapper_has_every_metal_compute_method():
+    text = open(os.path.join(RUST, "compute.rs")).read()
+    impl = text[text.index("impl CudaCompute {"):text.index("pub struct CudaModel")]
+    have = set(re.findall(r"pub fn (\w+)", impl))
+    assert set(METAL_COMPUTE_METHODS) <= have, set(METAL_COMPUTE_METHODS) - have
+    # every ffi call the wrapper makes is a declared entry point
+    called = set(re.findall(r"ffi::(ssd_\w+)\(", text))
+    assert called <= set(_rust_params()), called - set(_rust_params())
+
+
+def test_python_binding_mirrors_the_same_methods():
+    have = {n for n in dir(ssdllm.CudaCompute) if not n.startswith("_")}
+    assert set(METAL_COMPUTE_METHODS) <= have, set(METAL_COMPUTE_METHODS) - have
