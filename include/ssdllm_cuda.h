@@ -74,6 +74,20 @@ extern "C" {
  * :378-424) are accepted by the same calls. ssd_fused_swiglu takes dense gate / up weights
  * with norm_w NULL (no fused norm). */
 #define SSD_TYPE_BF16 30
+/* Low-bit formats in the reference's own block layouts (matvec_*_cpu, src/metal/compute.rs:
+ * 793-1075, 1964-2240), kept as uploaded: Q2_K (256 weights in 84 B), Q3_K (110 B), IQ2_XXS
+ * (66 B), IQ2_XS (74 B), IQ3_XXS (98 B), IQ4_NL (32 weights in 18 B), IQ3_S (110 B), IQ4_XS
+ * (148 B). Accepted by ssd_weight_upload / _download, ssd_dequantize (the reference's element
+ * values, bit-exact), ssd_matvec, ssd_matvec_residual and ssd_matvec_quantized_host (columns a
+ * multiple of the block, x 16-byte aligned). */
+#define SSD_TYPE_Q2_K 10
+#define SSD_TYPE_Q3_K 11
+#define SSD_TYPE_IQ2_XXS 16
+#define SSD_TYPE_IQ2_XS 17
+#define SSD_TYPE_IQ3_XXS 18
+#define SSD_TYPE_IQ4_NL 20
+#define SSD_TYPE_IQ3_S 21
+#define SSD_TYPE_IQ4_XS 23
 
 typedef struct ssd_ctx ssd_ctx;
 typedef struct ssd_weight ssd_weight;

@@ -89,6 +89,15 @@ size_t ora_row_bytes(int type, int64_t n) {
         case ORA_Q5_K: return (size_t)(n / 256) * 176;
         case ORA_Q6_K: return (size_t)(n / 256) * 210;
         case ORA_Q8_K: return (size_t)(n / 256) * 292;
+        case ORA_Q2_K:
+        case ORA_Q3_K:
+        case ORA_IQ4_NL:
+        case ORA_IQ4_XS:
+        case ORA_IQ3_XXS:
+        case ORA_IQ3_S:
+        case ORA_IQ2_XXS:
+        case ORA_IQ2_XS:
+            return (size_t)(n / ora_lowbit_block(type)) * ora_lowbit_block_bytes(type);
         default: return 0;
     }
 }
@@ -242,6 +251,7 @@ static int q5k_q(const uint8_t* blk, int idx) {
 }
 
 int ora_dequantize(const uint8_t* w, int type, int64_t n, float* out) {
+    if (ora_lowbit_block_bytes(type)) return ora_dequant_lowbit(w, type, n, out);
     switch (type) {
         case ORA_F32: memcpy(out, w, (size_t)n * 4); return 0;
         case ORA_BF16: /* bf16_to_f32 src/metal/compute.rs:2250-2253: bits << 16 */
@@ -512,15 +522,24 @@ static row_fn pick_row(int type) {
 
 typedef struct {
     row_fn fn;
+    int type; /* low-bit formats (fn NULL) */
     const uint8_t* w;
     const float* x;
     int in_dim, r0, r1;
     float* y;
 } mv_job;
 
+static void mv_rows(const mv_job* j) {
+    for (int r = j->r0; r < j->r1; r++) {
+        if (j->fn)
+            j->y[r] = j->fn(j->w, j->x, j->in_dim, r);
+        else
+            ora_row_lowbit(j->type, j->w, j->x, j->in_dim, r, &j->y[r]);
+    }
+}
+
 static void* mv_worker(void* p) {
-    mv_job* j = (mv_job*)p;
-    for (int r = j->r0; r < j->r1; r++) j->y[r] = j->fn(j->w, j->x, j->in_dim, r);
+    mv_rows((const mv_job*)p);
     return NULL;
 }
 
@@ -531,12 +550,13 @@ int ora_matvec_quantized_mt(const uint8_t* w, const float* x, int out_dim, int i
         ora_matvec_f32((const float*)w, x, out_dim, in_dim, y);
         return 0;
     }
-    if (!fn) { /* src/metal/compute.rs:672-675: unsupported -> zeros */
+    if (!fn && !ora_lowbit_block_bytes(type)) { /* compute.rs:672-675: unsupported -> zeros */
         memset(y, 0, sizeof(float) * (size_t)out_dim);
         return -1;
     }
     if (threads <= 1 || out_dim < 2 * threads) {
-        for (int r = 0; r < out_dim; r++) y[r] = fn(w, x, in_dim, r);
+        const mv_job j = {fn, type, w, x, in_dim, 0, out_dim, y};
+        mv_rows(&j);
         return 0;
     }
     if (threads > 256) threads = 256;
@@ -546,7 +566,7 @@ int ora_matvec_quantized_mt(const uint8_t* w, const float* x, int out_dim, int i
     int shard = out_dim / threads, remainder = out_dim % threads, off = 0;
     for (int t = 0; t < threads; t++) {
         int rows = shard + (t < remainder ? 1 : 0);
-        jobs[t] = (mv_job){fn, w, x, in_dim, off, off + rows, y};
+        jobs[t] = (mv_job){fn, type, w, x, in_dim, off, off + rows, y};
         off += rows;
         pthread_create(&th[t], NULL, mv_worker, &jobs[t]);
     }

@@ -22,8 +22,18 @@ extern "C" {
 #endif
 
 /* GgmlType ids: src/model/gguf.rs:16-47 */
-enum { ORA_F32 = 0, ORA_F16 = 1, ORA_Q4_0 = 2, ORA_Q8_0 = 8, ORA_Q4_K = 12, ORA_Q5_K = 13,
-       ORA_Q6_K = 14, ORA_Q8_K = 15, ORA_BF16 = 30 };
+enum { ORA_F32 = 0, ORA_F16 = 1, ORA_Q4_0 = 2, ORA_Q8_0 = 8, ORA_Q2_K = 10, ORA_Q3_K = 11,
+       ORA_Q4_K = 12, ORA_Q5_K = 13, ORA_Q6_K = 14, ORA_Q8_K = 15, ORA_IQ2_XXS = 16,
+       ORA_IQ2_XS = 17, ORA_IQ3_XXS = 18, ORA_IQ4_NL = 20, ORA_IQ3_S = 21, ORA_IQ4_XS = 23,
+       ORA_BF16 = 30 };
+
+/* Low-bit formats in the reference's block layouts (oracle_iq.c, compute.rs:793-1075,
+ * 1964-2240): block size / bytes, one matvec row (-1 for other types), dequantize (the
+ * per-element weight value the reference multiplies x by). */
+int ora_lowbit_block(int type);
+size_t ora_lowbit_block_bytes(int type);
+int ora_row_lowbit(int type, const uint8_t* w, const float* x, int in_dim, int row, float* y);
+int ora_dequant_lowbit(const uint8_t* w, int type, int64_t n, float* out);
 
 /* f16 -> f32 (half::f16::to_f32, used by f16_to_f32 src/metal/compute.rs:2244-2247). */
 float ora_f16_to_f32(uint16_t h);

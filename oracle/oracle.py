@@ -17,6 +17,7 @@ _LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
 _lib = None
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 0, 1, 2, 8, 12, 13, 14, 15, 30
+Q2_K, Q3_K, IQ2_XXS, IQ2_XS, IQ3_XXS, IQ4_NL, IQ3_S, IQ4_XS = 10, 11, 16, 17, 18, 20, 21, 23
 BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
          Q8_K: (256, 292), F16: (1, 2), BF16: (1, 2), F32: (1, 4)}
 

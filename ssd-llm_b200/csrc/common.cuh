@@ -329,7 +329,13 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // ------------------------------------------------------------ host side
-inline int type_block(int type) {
+// The low-bit formats kept in the reference's block layout (lowbit.cuh).
+__host__ __device__ constexpr bool is_lowbit(int t) {
+    return t == SSD_TYPE_Q2_K || t == SSD_TYPE_Q3_K || t == SSD_TYPE_IQ4_NL ||
+           t == SSD_TYPE_IQ4_XS || t == SSD_TYPE_IQ3_XXS || t == SSD_TYPE_IQ3_S ||
+           t == SSD_TYPE_IQ2_XXS || t == SSD_TYPE_IQ2_XS;
+}
+__host__ __device__ constexpr int type_block(int type) {
     switch (type) {
         case SSD_TYPE_Q4_0:
         case SSD_TYPE_Q8_0: return 32;
@@ -340,10 +346,18 @@ inline int type_block(int type) {
         case SSD_TYPE_F32:
         case SSD_TYPE_F16:
         case SSD_TYPE_BF16: return 1;
+        case SSD_TYPE_IQ4_NL: return 32;
+        case SSD_TYPE_Q2_K:
+        case SSD_TYPE_Q3_K:
+        case SSD_TYPE_IQ4_XS:
+        case SSD_TYPE_IQ3_XXS:
+        case SSD_TYPE_IQ3_S:
+        case SSD_TYPE_IQ2_XXS:
+        case SSD_TYPE_IQ2_XS: return 256;
         default: return 0;
     }
 }
-inline int type_block_bytes(int type) {
+__host__ __device__ constexpr int type_block_bytes(int type) {
     switch (type) {
         case SSD_TYPE_Q4_0: return 18;
         case SSD_TYPE_Q8_0: return 34;
@@ -354,6 +368,14 @@ inline int type_block_bytes(int type) {
         case SSD_TYPE_F32: return 4;
         case SSD_TYPE_F16:
         case SSD_TYPE_BF16: return 2;
+        case SSD_TYPE_Q2_K: return 84;
+        case SSD_TYPE_Q3_K: return 110;
+        case SSD_TYPE_IQ4_NL: return 18;
+        case SSD_TYPE_IQ4_XS: return 148;
+        case SSD_TYPE_IQ3_XXS: return 98;
+        case SSD_TYPE_IQ3_S: return 110;
+        case SSD_TYPE_IQ2_XXS: return 66;
+        case SSD_TYPE_IQ2_XS: return 74;
         default: return 0;
     }
 }

@@ -9,6 +9,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "lowbit.cuh"
 
 namespace ssd {
 
@@ -420,6 +421,16 @@ __global__ void k_dequant(const ssd_weight w, float* __restrict__ out) {
     int64_t n = (int64_t)w.rows * w.cols;
     int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;  // 8 elements
     if (e0 >= n) return;
+    if (is_lowbit(w.type)) {  // decode the 32-element group holding e0 .. e0 + 7
+        const int64_t r = e0 / w.cols;
+        const int c = (int)(e0 % w.cols), bs = type_block(w.type);
+        const uint8_t* blk = w.qs + (size_t)r * (w.cols / bs) * type_block_bytes(w.type) +
+                             (size_t)(c / bs) * type_block_bytes(w.type);
+        float g[32];
+        lowbit_group_any(w.type, blk, (c % bs) / 32, g);
+        for (int t = 0; t < 8; t++) out[e0 + t] = g[c % 32 + t];
+        return;
+    }
     float v[8];
     dequant8(w, e0, v);
     for (int t = 0; t < 8; t++) out[e0 + t] = v[t];
@@ -594,6 +605,9 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     } else if (type == SSD_TYPE_Q6_K) {
         qs_bytes = nb * 256;
         meta_bytes = nb * 32;
+    } else if (is_lowbit(type)) {  // the reference's blocks as they are
+        qs_bytes = (size_t)nb * type_block_bytes(type);
+        meta_bytes = 0;
     } else {  // dense: F32, F16, BF16
         qs_bytes = (size_t)rows * cols * type_block_bytes(type);
         meta_bytes = 0;
@@ -603,7 +617,7 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     // split-K scratch of the tensor-core matvec (quantized types): counters for up to
     // 2 * ceil(rows / 64) + 16 row tiles (a fused QKV or gate/up launch uses the first
     // weight's), partial rows for kI8MaxGrid CTAs
-    const bool fix = type_block(type) > 1;
+    const bool fix = type_block(type) > 1 && !is_lowbit(type);
     const size_t n_counters = fix ? 2 * (((size_t)rows + 63) / 64) + 16 : 0;
     const size_t counter_bytes = (n_counters * 4 + 255) & ~(size_t)255;
     const size_t partial_bytes = fix ? (size_t)2 * kI8MaxGrid * 128 * 4 : 0;
@@ -651,7 +665,7 @@ extern "C" int ssd_weight_upload_device(ssd_ctx* ctx, const void* raw_dev, size_
     ssd_weight* w = nullptr;
     SSD_TRY(alloc_weight(ctx, type, rows, cols, &w));
     cudaStream_t s = pick_stream(ctx, stream);
-    if (type_block(type) == 1) {  // dense: the bytes as they are
+    if (type_block(type) == 1 || is_lowbit(type)) {  // dense / low-bit: the bytes as they are
         if (cudaMemcpyAsync(w->qs, raw_dev, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
             ssd_weight_free(w);
             SSD_CK(cudaGetLastError());
@@ -703,7 +717,7 @@ extern "C" int ssd_weight_download(ssd_ctx* ctx, const ssd_weight* w, void* host
     SSD_REQ(w && host_raw, SSD_ERR_ARG, "null argument");
     size_t need = ssd_row_bytes(w->type, w->cols) * (size_t)w->rows;
     SSD_REQ(bytes == need, SSD_ERR_SHAPE, "need %zu bytes, got %zu", need, bytes);
-    if (type_block(w->type) == 1) {
+    if (type_block(w->type) == 1 || is_lowbit(w->type)) {
         SSD_CK(cudaMemcpy(host_raw, w->qs, bytes, cudaMemcpyDeviceToHost));
         return SSD_OK;
     }

@@ -1083,6 +1083,7 @@ static bool is_dense(int type) {
 int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_t s, bool pdl) {
     MvArgs a = a0;
     if (!a.status) a.status = ctx->dev_status;
+    if (is_lowbit(type)) return launch_matvec_lowbit(ctx, type, epi, a, s, pdl);
     if (is_dense(type)) {
         SSD_REQ(a.rows > 0 && a.cols > 0, SSD_ERR_SHAPE, "empty matrix");
         SSD_REQ(a.x && a.y && ((uintptr_t)a.x & 15) == 0, SSD_ERR_ARG,
@@ -1172,7 +1173,7 @@ static int check_w(const ssd_weight* w) {
     SSD_REQ(w != nullptr, SSD_ERR_ARG, "null weight");
     SSD_REQ(w->type == SSD_TYPE_Q4_0 || w->type == SSD_TYPE_Q8_0 || w->type == SSD_TYPE_Q4_K ||
                 w->type == SSD_TYPE_Q5_K || w->type == SSD_TYPE_Q6_K || w->type == SSD_TYPE_Q8_K ||
-                is_dense(w->type),
+                is_dense(w->type) || is_lowbit(w->type),
             SSD_ERR_TYPE, "matvec: ggml type %d not supported", w->type);
     return SSD_OK;
 }
@@ -1291,7 +1292,8 @@ extern "C" int ssd_matvec_peer_input(ssd_ctx* ctx, const ssd_weight* w, const fl
     SSD_REQ(x && y && partials && flags && epoch, SSD_ERR_ARG, "null argument");
     SSD_REQ(n_ranks >= 1 && n_ranks <= kMaxPeers, SSD_ERR_ARG, "n_ranks %d outside [1, %d]",
             n_ranks, kMaxPeers);
-    SSD_REQ(!is_dense(w->type), SSD_ERR_TYPE, "peer input: quantized weights only");
+    SSD_REQ(!is_dense(w->type) && !is_lowbit(w->type), SSD_ERR_TYPE,
+            "peer input: Q4_0 / Q8_0 / Q4_K / Q5_K / Q6_K / Q8_K weights only");
     MvArgs a = mv_plain(w, x, y);
     a.ar_in = partials;
     a.ar_in_flag = flags;
@@ -1308,7 +1310,7 @@ extern "C" int ssd_matvec_quantized_host(ssd_ctx* ctx, const uint8_t* w_raw, siz
     SSD_REQ(w_raw && x && y, SSD_ERR_ARG, "null pointer");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
                 type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K ||
-                type == SSD_TYPE_F16 || type == SSD_TYPE_BF16,
+                type == SSD_TYPE_F16 || type == SSD_TYPE_BF16 || is_lowbit(type),
             SSD_ERR_TYPE, "matvec_quantized: ggml type %d not supported", type);
     ssd_weight* w = nullptr;
     SSD_TRY(ssd_weight_upload(ctx, w_raw, w_bytes, type, out_dim, in_dim, &w));

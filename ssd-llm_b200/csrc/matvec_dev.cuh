@@ -247,5 +247,8 @@ int launch_matvec_tc(ssd_ctx* ctx, int type, int epi, const MvArgs& a, cudaStrea
 // without launching when the type, shape or row map is not one it covers.
 constexpr int kI8NotCovered = -1001;
 int launch_matvec_i8(ssd_ctx* ctx, int type, int epi, const MvArgs& a, cudaStream_t s, bool pdl);
+// Low-bit formats in the reference's block layouts (matvec_lowbit.cu): plain or residual.
+int launch_matvec_lowbit(ssd_ctx* ctx, int type, int epi, const MvArgs& a, cudaStream_t s,
+                         bool pdl);
 
 }  // namespace ssd

@@ -121,6 +121,9 @@ struct ssd_model {
     void* p2p_buf = nullptr;
     float* p2p_rbuf[kMaxPeers] = {};
     unsigned long long* p2p_flag[kMaxPeers] = {};
+    // KV absmax exchange slots ([kArSlots][tp][2] tagged words after the flags)
+    unsigned long long* p2p_xch[kMaxPeers] = {};
+    float* amax = nullptr;  // the (K, V) absmax pair max-reduced by NCCL (no peer path)
     void* p2p_mapped[kMaxPeers] = {};
     bool p2p = false;
     unsigned long long* ar_epoch = nullptr;  // advanced by 2 * n_layers per step
@@ -154,7 +157,8 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
                 c->n_embd % N == 0,
             SSD_ERR_SHAPE, "dimensions do not shard over %d ranks", N);
     const int bs = type_block(c->wtype);
-    SSD_REQ(bs == 32 || bs == 256, SSD_ERR_TYPE, "layer weight type %d not supported", c->wtype);
+    SSD_REQ((bs == 32 || bs == 256) && !is_lowbit(c->wtype), SSD_ERR_TYPE,
+            "layer weight type %d not supported", c->wtype);
     SSD_REQ((c->n_embd / N) % bs == 0 && (c->n_ff / N) % bs == 0, SSD_ERR_SHAPE,
             "column shards must be whole %d-wide blocks", bs);
     SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
@@ -163,7 +167,9 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
                 c->embd_type == SSD_TYPE_Q8_K || c->embd_type == SSD_TYPE_F16 ||
                 c->embd_type == SSD_TYPE_BF16,
             SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
-    SSD_REQ(type_block(c->out_type) == 32 || type_block(c->out_type) == 256, SSD_ERR_TYPE,
+    SSD_REQ((type_block(c->out_type) == 32 || type_block(c->out_type) == 256) &&
+                !is_lowbit(c->out_type),
+            SSD_ERR_TYPE,
             "output type %d not supported", c->out_type);
 
     ssd_model* m = new ssd_model();
@@ -175,7 +181,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     m->kv_head0 = r * m->nkv_local;
     m->nq_local = c->n_head / N;
     m->q_rows = m->nq_local * c->head_dim;
-    m->kv_rows = c->n_head_kv * c->head_dim;  // K/V projections are replicated
+    m->kv_rows = m->nkv_local * c->head_dim;  // this rank's K/V heads
     m->embd_cols_local = c->n_embd / N;
     m->embd0 = r * m->embd_cols_local;
     m->ff_local = c->n_ff / N;
@@ -221,6 +227,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     m->pos = reinterpret_cast<int*>(S + o_misc + 8);
     m->ar_epoch = reinterpret_cast<unsigned long long*>(S + o_misc + 16);
     m->ar_counter = reinterpret_cast<unsigned int*>(S + o_misc + 20);
+    m->amax = S + o_misc + 24;
     if (cudaHostAlloc(&m->pinned, 16, cudaHostAllocDefault) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->state);
@@ -229,7 +236,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
         return SSD_ERR_NOMEM;
     }
     for (auto& L : m->layers) {
-        int st = ssd_kv_create(ctx, c->kv_capacity, c->n_head_kv, c->head_dim, &L.kv);
+        int st = ssd_kv_create(ctx, c->kv_capacity, m->nkv_local, c->head_dim, &L.kv);
         if (st != SSD_OK) {
             ssd_model_free(m);
             return st;
@@ -307,7 +314,7 @@ extern "C" int ssd_model_p2p_handle(ssd_model* m, uint8_t out[64]) {
     static_assert(sizeof(cudaIpcMemHandle_t) == 64, "cudaIpcMemHandle_t size");
     if (!m->p2p_buf) {
         const size_t fl = (p2p_floats(m) * 4 + 255) & ~(size_t)255;
-        const size_t bytes = fl + (size_t)kArSlots * tp_size(m) * 8;
+        const size_t bytes = fl + (size_t)kArSlots * tp_size(m) * 8 * 3;  // flags, exchange
         if (cudaMalloc(&m->p2p_buf, bytes) != cudaSuccess) {
             cudaGetLastError();
             m->p2p_buf = nullptr;
@@ -347,6 +354,7 @@ extern "C" int ssd_model_p2p_open(ssd_model* m, const uint8_t* handles) {
         }
         m->p2p_rbuf[r] = (float*)p;
         m->p2p_flag[r] = (unsigned long long*)((char*)p + fl);
+        m->p2p_xch[r] = m->p2p_flag[r] + (size_t)kArSlots * N;
     }
     m->p2p = true;
     if (m->exec) {  // re-capture with the peer path
@@ -410,11 +418,12 @@ static int produce_partial(ssd_model* m, int type, MvArgs a, float* nccl_buf, bo
 
 // ------------------------------------------------------------------ weights
 
-// Which slice of a global tensor this rank keeps. Row-sharded: attn_q (by heads),
-// ffn_gate, ffn_up, output (by vocab rows). Column-sharded: attn_output (by the
-// rank's q-head columns), ffn_down (by the rank's FFN columns). Replicated:
-// attn_k, attn_v (every rank needs the full K/V row for the INT8 scale, which
-// spans all KV heads: quantized_kv_cache.rs:107-110) and token_embd.
+// Which slice of a global tensor this rank keeps. Row-sharded: attn_q, attn_k, attn_v
+// (by heads: n_head / N query heads and n_head_kv / N KV heads per rank, the KV heads those
+// query heads read), ffn_gate, ffn_up, output (by vocab rows). Column-sharded: attn_output
+// (by the rank's q-head columns), ffn_down (by the rank's FFN columns). Replicated:
+// token_embd. The INT8 KV row scale spans all KV heads (quantized_kv_cache.rs:107-110),
+// so the ranks exchange the absmax of their K / V slices at every append.
 struct Shard {
     int rows, cols;   // global shape
     int row0, nrows;  // kept rows
@@ -427,6 +436,7 @@ static int shard_range(const ssd_model_config& c, const std::string& name, int l
     const int N = c.tp_size < 1 ? 1 : c.tp_size, r = c.tp_rank;
     const int E = c.n_embd, F = c.n_ff, KV = c.n_head_kv * c.head_dim;
     const int qr = (c.n_head / N) * c.head_dim, ec = E / N, fl = F / N, vl = c.vocab / N;
+    const int kvl = (c.n_head_kv / N) * c.head_dim;
     if (layer < 0) {
         if (name == "token_embd") {
             s = Shard{c.vocab, E, 0, c.vocab, 0, E, c.embd_type, 1000001u};
@@ -444,9 +454,9 @@ static int shard_range(const ssd_model_config& c, const std::string& name, int l
     if (name == "attn_q")
         s = Shard{E, E, r * qr, qr, 0, E, c.wtype, base + 0};
     else if (name == "attn_k")
-        s = Shard{KV, E, 0, KV, 0, E, c.wtype, base + 1};
+        s = Shard{KV, E, r * kvl, kvl, 0, E, c.wtype, base + 1};
     else if (name == "attn_v")
-        s = Shard{KV, E, 0, KV, 0, E, c.wtype, base + 2};
+        s = Shard{KV, E, r * kvl, kvl, 0, E, c.wtype, base + 2};
     else if (name == "attn_output")
         s = Shard{E, E, 0, E, r * ec, ec, c.wtype, base + 3};
     else if (name == "ffn_gate")
@@ -627,9 +637,10 @@ extern "C" int ssd_model_synth_kv(ssd_model* m, uint64_t seed, int n) {
                 if (st == SSD_OK)
                     st = ssd_synth_f32(m->ctx, seed, 2000001u + 2u * l, 0.0f, 1.0f, kvd, p0, rows,
                                        0, kvd, tmp + (size_t)chunk * kvd, (void*)m->ctx->stream);
-                if (st == SSD_OK)
-                    st = launch_kv_append(m->layers[l].kv, tmp, tmp + (size_t)chunk * kvd, p0,
-                                          nullptr, rows, m->ctx->stream, false);
+                if (st == SSD_OK)  // whole-row scale, this rank's heads stored
+                    st = launch_kv_append_slice(m->layers[l].kv, tmp, tmp + (size_t)chunk * kvd,
+                                                kvd, m->kv_head0 * c.head_dim, p0, rows,
+                                                m->ctx->stream);
             }
         }
         cudaStreamSynchronize(m->ctx->stream);
@@ -781,13 +792,27 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     at.kv_dim = L.kv->kv_dim;
     at.head_dim = c.head_dim;
     at.group = c.n_head / c.n_head_kv;
-    at.kv_head0 = m->kv_head0;
+    at.kv_head0 = 0;  // the cache holds this rank's heads only
     at.n_kv_local = m->nkv_local;
     at.q = m->q;
     at.out = m->attn;
     at.partial = m->part;
     at.pos_dev = m->pos;
     at.max_seq = c.kv_capacity;
+    if (tp && use_p2p) {  // global row absmax: exchanged inside the attention kernel
+        const int N = tp_size(m), me = c.tp_rank, slot = l % kArSlots;
+        at.xch_n = N;
+        at.xch_call = l;
+        at.xch_epoch = m->ar_epoch;
+        at.xch_in = m->p2p_xch[me] + (size_t)slot * N * 2;
+        for (int r = 0; r < N; r++) at.xch_out[r] = m->p2p_xch[r] + ((size_t)slot * N + me) * 2;
+        at.status = m->ctx->dev_status;
+    } else if (tp) {  // local pair, NCCL max-reduce, then the append reads it
+        SSD_TRY(launch_kv_absmax(m->k, m->v, m->kv_rows, m->amax, s, true));
+        nl++;
+        SSD_NCCL(ncclAllReduce(m->amax, m->amax, 2, ncclFloat32, ncclMax, m->comm, s));
+        at.amax_in = m->amax;
+    }
     SSD_TRY(launch_attention(at, s, true));
     nl += 2;
     // 4. output projection (+ residual, or a partial sum for the all-reduce)

@@ -131,20 +131,23 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* v, int n, int32_t*
 // ------------------------------------------------------------- INT8 KV
 // QuantizedVec::quantize (src/inference/quantized_kv_cache.rs:23-41), bit-exact:
 // absmax = max |v|; zero row -> scale 0; scale = absmax/127; q = clamp(round(v*127/absmax)).
+// Rows of src_dim floats; the scale spans the whole row, columns [col0, col0 + kv_dim) are
+// stored (the whole row when col0 == 0 and src_dim == kv_dim).
 __global__ void __launch_bounds__(256) k_kv_append(const float* __restrict__ k,
                                                    const float* __restrict__ v, int8_t* kc,
                                                    int8_t* vc, float* ksc, float* vsc, int kv_dim,
-                                                   int pos, const int* pos_dev, int capacity) {
+                                                   int pos, const int* pos_dev, int capacity,
+                                                   int src_dim, int col0) {
     __shared__ float red[8];
     pdl_wait();
     const int base_pos = pos_dev ? *pos_dev : pos;
     const int r = blockIdx.x, which = blockIdx.y;
     const int p = base_pos + r;
     if (p < 0 || p >= capacity) return;  // host checks bounds for the direct API
-    const float* src = (which == 0 ? k : v) + (size_t)r * kv_dim;
+    const float* src = (which == 0 ? k : v) + (size_t)r * src_dim;
     int8_t* dst = (which == 0 ? kc : vc) + (size_t)p * kv_dim;
     float am = 0.0f;
-    for (int i = threadIdx.x; i < kv_dim; i += 256) am = fmaxf(am, fabsf(src[i]));
+    for (int i = threadIdx.x; i < src_dim; i += 256) am = fmaxf(am, fabsf(src[i]));
     am = block_max<256>(am, red);
     if (am == 0.0f) {
         for (int i = threadIdx.x; i < kv_dim; i += 256) dst[i] = 0;
@@ -154,11 +157,30 @@ __global__ void __launch_bounds__(256) k_kv_append(const float* __restrict__ k,
     const float scale = __fdiv_rn(am, 127.0f);
     const float inv = __fdiv_rn(127.0f, am);
     for (int i = threadIdx.x; i < kv_dim; i += 256) {
-        float q = roundf(__fmul_rn(src[i], inv));
+        float q = roundf(__fmul_rn(src[col0 + i], inv));
         q = fminf(127.0f, fmaxf(-127.0f, q));
         dst[i] = (int8_t)(int)q;
     }
     if (threadIdx.x == 0) (which == 0 ? ksc : vsc)[p] = scale;
+}
+
+__global__ void __launch_bounds__(256) k_kv_absmax(const float* __restrict__ k,
+                                                   const float* __restrict__ v, int n,
+                                                   float* out) {
+    __shared__ float red[8];
+    pdl_wait();
+    float ak = 0.0f, av = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        ak = fmaxf(ak, fabsf(k[i]));
+        av = fmaxf(av, fabsf(v[i]));
+    }
+    ak = block_max<256>(ak, red);
+    __syncthreads();
+    av = block_max<256>(av, red);
+    if (threadIdx.x == 0) {
+        out[0] = ak;
+        out[1] = av;
+    }
 }
 
 // ------------------------------------------------ split-K decode attention
@@ -217,7 +239,7 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
     __shared__ float mlw[ATT_NW][G][2];  // warp max, sum exp
     __shared__ float fac[ATT_NW][G];
     __shared__ float qbias[G];
-    __shared__ float amred[2][ATT_NW];
+    __shared__ float amred[2][ATT_NW > 8 ? ATT_NW : 8];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y, qi = blockIdx.z;
     const int g_kv = a.kv_head0 + gl;
@@ -331,6 +353,51 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
         for (int w = 0; w < ATT_NW; w++) {
             amk = fmaxf(amk, amred[0][w]);
             amv = fmaxf(amv, amred[1][w]);
+        }
+        if (a.amax_in) {  // the global pair, max-reduced by the caller
+            amk = a.amax_in[0];
+            amv = a.amax_in[1];
+        } else if (a.xch_n > 1) {
+            // publish this rank's pair to every rank (local head 0's CTA), then take the max
+            // of all ranks' pairs once every word carries this call's tag (bounded wait)
+            const uint32_t tag = (uint32_t)(*a.xch_epoch + (unsigned long long)a.xch_call) + 1u;
+            if (gl == 0 && tid < 2 * a.xch_n) {
+                const float val = (tid & 1) ? amv : amk;
+                const unsigned long long w =
+                    ((unsigned long long)__float_as_uint(val) << 32) | (unsigned long long)tag;
+                asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.xch_out[tid >> 1] +
+                                                                        (tid & 1)),
+                             "l"(w)
+                             : "memory");
+            }
+            __syncthreads();  // amred is reused below
+            if (tid < 2 * a.xch_n) {
+                float val = 0.0f;
+                if (*(volatile int*)a.status == SSD_OK) {  // fail fast after a timeout
+                    bool done = false;
+                    for (uint32_t it = 0; it < (1u << 21) && !done; it++) {
+                        unsigned long long w;
+                        asm volatile("ld.acquire.sys.global.u64 %0, [%1];"
+                                     : "=l"(w)
+                                     : "l"(a.xch_in + tid)
+                                     : "memory");
+                        done = (uint32_t)w == tag;
+                        if (done)
+                            val = __uint_as_float((uint32_t)(w >> 32));
+                        else
+                            __nanosleep(100);
+                    }
+                    if (!done) atomicExch(a.status, SSD_ERR_TIMEOUT);  // bytes below are then stale
+                }
+                amred[tid & 1][tid >> 1] = val;
+            }
+            __syncthreads();
+            amk = 0.0f;
+            amv = 0.0f;
+            for (int r = 0; r < a.xch_n; r++) {
+                amk = fmaxf(amk, amred[0][r]);
+                amv = fmaxf(amv, amred[1][r]);
+            }
         }
         const float sk = amk == 0.0f ? 0.0f : __fdiv_rn(amk, 127.0f);
         const float sv = amv == 0.0f ? 0.0f : __fdiv_rn(amv, 127.0f);
@@ -566,6 +633,10 @@ int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
             "batch attention: one query per slot, with the fused append");
     SSD_REQ((a.max_seq + ATT_P - 1) / ATT_P <= 1024, SSD_ERR_SHAPE,
             "attention over %d positions exceeds %d", a.max_seq, 1024 * ATT_P);
+    SSD_REQ(a.xch_n <= 1 || (a.k_new && a.status && a.xch_in && a.xch_epoch && a.xch_n <= 8),
+            SSD_ERR_ARG, "absmax exchange needs the fused append, a status word and its slots");
+    for (int r = 0; r < (a.xch_n > 1 ? a.xch_n : 0); r++)
+        SSD_REQ(a.xch_out[r] != nullptr, SSD_ERR_ARG, "null exchange slot of rank %d", r);
     if (a.head_dim == 128) return launch_attn_hd<128>(a, s, pdl);
     if (a.head_dim == 64) return launch_attn_hd<64>(a, s, pdl);
     set_error("head_dim %d not supported (64, 128)", a.head_dim);
@@ -575,7 +646,24 @@ int launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 int launch_kv_append(const ssd_kv_cache* kv, const float* k, const float* v, int pos,
                      const int* pos_dev, int rows, cudaStream_t s, bool pdl) {
     SSD_CK(launch_pdl(k_kv_append, dim3(rows, 2), dim3(256), 0, s, pdl, k, v, kv->k, kv->v,
-                      kv->k_scale, kv->v_scale, kv->kv_dim, pos, pos_dev, kv->capacity));
+                      kv->k_scale, kv->v_scale, kv->kv_dim, pos, pos_dev, kv->capacity,
+                      kv->kv_dim, 0));
+    return SSD_OK;
+}
+
+int launch_kv_append_slice(const ssd_kv_cache* kv, const float* k, const float* v, int src_dim,
+                           int col0, int pos, int rows, cudaStream_t s) {
+    SSD_REQ(col0 >= 0 && col0 + kv->kv_dim <= src_dim, SSD_ERR_SHAPE,
+            "slice [%d, %d) outside rows of %d", col0, col0 + kv->kv_dim, src_dim);
+    SSD_CK(launch_pdl(k_kv_append, dim3(rows, 2), dim3(256), 0, s, false, k, v, kv->k, kv->v,
+                      kv->k_scale, kv->v_scale, kv->kv_dim, pos, (const int*)nullptr,
+                      kv->capacity, src_dim, col0));
+    return SSD_OK;
+}
+
+int launch_kv_absmax(const float* k, const float* v, int n, float* out, cudaStream_t s,
+                     bool pdl) {
+    SSD_CK(launch_pdl(k_kv_absmax, dim3(1), dim3(256), 0, s, pdl, k, v, n, out));
     return SSD_OK;
 }
 
@@ -608,7 +696,7 @@ __global__ void k_finalize(unsigned long long* key, int32_t* token, int* pos,
 
 int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden, cudaStream_t s,
                  bool pdl) {
-    SSD_REQ(type_block(emb->type) != 0 && emb->cols % 8 == 0, SSD_ERR_TYPE,
+    SSD_REQ(type_block(emb->type) != 0 && !is_lowbit(emb->type) && emb->cols % 8 == 0, SSD_ERR_TYPE,
             "token_embd type %d not supported (F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K)",
             emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(1), dim3(256), 0, s, pdl, *emb, token_dev, hidden));
@@ -617,7 +705,7 @@ int launch_embed(const ssd_weight* emb, const int32_t* token_dev, float* hidden,
 
 int launch_embed_rows(const ssd_weight* emb, const int32_t* tokens_dev, int n, float* hidden,
                       cudaStream_t s) {
-    SSD_REQ(type_block(emb->type) != 0 && emb->cols % 8 == 0, SSD_ERR_TYPE,
+    SSD_REQ(type_block(emb->type) != 0 && !is_lowbit(emb->type) && emb->cols % 8 == 0, SSD_ERR_TYPE,
             "token_embd type %d not supported (F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K)",
             emb->type);
     SSD_CK(launch_pdl(k_embed, dim3(n), dim3(256), 0, s, false, *emb, tokens_dev, hidden));

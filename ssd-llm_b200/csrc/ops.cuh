@@ -47,7 +47,27 @@ struct AttnArgs {
     int n_slots;
     size_t slot_kv;
     int slot_sc, slot_new;
+    // K / V sharded by heads over tensor-parallel ranks (fused append): the INT8 row scale
+    // spans every rank's heads (quantized_kv_cache.rs:107-110), so the global absmax of the
+    // new K and V rows is needed. Either amax_in holds it (K, V; computed and max-reduced
+    // by the caller), or xch_n > 1 ranks exchange their local pair in the kernel: the CTA of
+    // local head 0 in the new position's chunk writes word 2j+w = (absmax bits << 32) | tag
+    // to xch_out[r] for every rank r, and the chunk's CTAs wait (bounded) until all xch_n
+    // pairs of xch_in carry the tag (uint32)(*xch_epoch + xch_call) + 1.
+    const float* amax_in;
+    int xch_n;
+    int xch_call;
+    const unsigned long long* xch_epoch;
+    const unsigned long long* xch_in;
+    unsigned long long* xch_out[8];
 };
+// Local absmax pair (K, V) of the n-float rows k, v into out[0..1] (one CTA).
+int launch_kv_absmax(const float* k, const float* v, int n, float* out, cudaStream_t s, bool pdl);
+// Quantizes `rows` full K / V rows of src_dim floats (row scale over the whole row) and
+// stores columns [col0, col0 + kv->kv_dim) of each at positions pos.. of the cache (a rank's
+// head slice under tensor parallelism; col0 0 and src_dim kv->kv_dim for a whole row).
+int launch_kv_append_slice(const ssd_kv_cache* kv, const float* k, const float* v, int src_dim,
+                           int col0, int pos, int rows, cudaStream_t s);
 // Causal attention of a prompt batch on the tcgen05 tensor cores (attn_tc.cu): n_q
 // queries (a multiple of 128, head_dim 128) at positions seq0 .., over the cache rows
 // [0, seq0 + n_q) already appended. Same arguments as the batched launch_attention.

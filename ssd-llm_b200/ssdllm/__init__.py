@@ -622,7 +622,9 @@ class Model:
         check(lib().ssd_model_kv(self.h, layer, ctypes.byref(h)))
         k = KvCache.__new__(KvCache)
         k.ctx, k.h = self.ctx, h
-        k.capacity, k.n_head_kv, k.head_dim = (self.cfg.kv_capacity, self.cfg.n_head_kv,
+        # the cache holds this rank's KV heads (all of them at tp_size 1)
+        k.capacity, k.n_head_kv, k.head_dim = (self.cfg.kv_capacity,
+                                               self.cfg.n_head_kv // max(self.cfg.tp_size, 1),
                                                self.cfg.head_dim)
         return k
 

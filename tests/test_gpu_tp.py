@@ -5,7 +5,9 @@ Each mode runs tests/tp_worker.py as two ranks (torch.distributed.run, one proce
 GPU). Checks: no device-side wait timed out; the peer-memory path gives the same greedy
 tokens as the NCCL path and first-step logits within 1e-4 of it (only the summation order
 of the two partials differs); both agree with the unsharded model on one GPU within the
-parity tolerance 1e-3. Skipped on machines with fewer than 2 GPUs.
+parity tolerance 1e-3; K / V are sharded by heads, and the ranks' cache slices side by side
+reproduce the unsharded cache (synthesized rows bit-exact; every rank stores the same row
+scales, the global absmax exchanged at each append). Skipped on machines with fewer than 2 GPUs.
 """
 import os
 import subprocess
@@ -34,15 +36,20 @@ def run_ranks(out, mode):
     for k in range(2):
         assert int(res[k]["status"]) == 0, f"rank {k} device status {int(res[k]['status'])}"
     assert np.array_equal(res[0]["toks"], res[1]["toks"])
-    return res[0]["toks"], np.concatenate([res[0]["logits0"], res[1]["logits0"]])
+    # K / V are sharded by heads: every rank stores the same row scales (the exchanged
+    # global absmax), and the ranks' head slices side by side form the whole rows
+    assert np.array_equal(res[0]["scales"], res[1]["scales"])
+    kv = np.concatenate([res[0]["kv"], res[1]["kv"]], axis=-1)
+    return (res[0]["toks"], np.concatenate([res[0]["logits0"], res[1]["logits0"]]), kv,
+            res[0]["scales"])
 
 
 def test_tp2_peer_allreduce_matches_nccl_and_one_gpu(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import ssdllm
-    p_toks, p_log = run_ranks(tmp_path, "p2p")
-    n_toks, n_log = run_ranks(tmp_path, "nccl")
+    p_toks, p_log, p_kv, p_sc = run_ranks(tmp_path, "p2p")
+    n_toks, n_log, n_kv, n_sc = run_ranks(tmp_path, "nccl")
     assert np.array_equal(p_toks, n_toks), (p_toks, n_toks)
     assert rel_err(p_log, n_log) <= 1e-4, rel_err(p_log, n_log)
 
@@ -52,8 +59,18 @@ def test_tp2_peer_allreduce_matches_nccl_and_one_gpu(tmp_path):
         m.synth_weights(seed=3, std=0.02)
         m.synth_kv(seed=4, n=20)
         o_toks, o_log = tp_worker.decode(m, ctx)
+        o_kv, o_sc = tp_worker.read_caches(m, ctx, 20 + tp_worker.STEPS)
     finally:
         m.free()
     assert rel_err(p_log, o_log) <= 1e-3, rel_err(p_log, o_log)
     assert rel_err(n_log, o_log) <= 1e-3, rel_err(n_log, o_log)
     assert p_toks[0] == o_toks[0]
+    # the synthesized prompt rows are bit-identical to the unsharded cache; the decoded rows'
+    # scales are the global row absmax on both paths (same as one GPU up to the projections'
+    # summation order)
+    assert np.array_equal(p_kv[:, :, :20], o_kv[:, :, :20])
+    assert np.array_equal(p_sc[:, :, :20], o_sc[:, :, :20])
+    assert rel_err(p_sc, n_sc) <= 1e-4
+    assert np.max(np.abs(p_kv.astype(int) - n_kv.astype(int))) <= 1
+    assert rel_err(p_sc, o_sc) <= 1e-3
+    assert np.max(np.abs(p_kv.astype(int) - o_kv.astype(int))) <= 1
