@@ -629,8 +629,9 @@ def case_mv_shapes(ctx, torch, ssdllm, peak, reps=10):
 
     for tp in (1, 2, 4, 8):
         hq, ff, ecol, fcol = HQ // tp, F // tp, E // tp, F // tp
+        hkv = HKV // tp  # K / V sharded by heads
         kinds = {
-            "qkv": (hq + 2 * HKV) * E, "o_proj": E * ecol, "gate_up": 2 * ff * E, "down": E * fcol,
+            "qkv": (hq + 2 * hkv) * E, "o_proj": E * ecol, "gate_up": 2 * ff * E, "down": E * fcol,
         }
         for kind, nw in kinds.items():
             wbytes = nw * Q40_BYTES
@@ -639,11 +640,11 @@ def case_mv_shapes(ctx, torch, ssdllm, peak, reps=10):
                             device="cuda", generator=gen)
             nw_ = 1 + 0.1 * torch.randn(E, device="cuda", generator=gen)
             if kind == "qkv":
-                ws = [(synth(hq, E), synth(HKV, E), synth(HKV, E)) for _ in range(copies)]
-                q, k, v = (torch.zeros(n, device="cuda") for n in (hq, HKV, HKV))
+                ws = [(synth(hq, E), synth(hkv, E), synth(hkv, E)) for _ in range(copies)]
+                q, k, v = (torch.zeros(n, device="cuda") for n in (hq, hkv, hkv))
                 mk = lambda w: (lambda: ssdllm.fused_qkv_rope(ctx, *w, x, nw_, 1e-5, 128, 77, 5e5,
                                                               q, k, v))
-                alg = wbytes + E * 4 + (hq + 2 * HKV) * 4
+                alg = wbytes + E * 4 + (hq + 2 * hkv) * 4
             elif kind == "gate_up":
                 ws = [(synth(ff, E), synth(ff, E)) for _ in range(copies)]
                 act = torch.zeros(ff, device="cuda")
@@ -683,6 +684,9 @@ CASES = {
     "f16_11008x4096": lambda c, t, s, p: case_matvec_dense16(c, t, s, p, wtype=1),
     "swiglu_q4_0_70b": case_swiglu_70b,
     "attn_int8_70b_4096": case_attention,
+    # one rank's heads at TP2 / TP8 (K/V sharded by heads)
+    "attn_int8_70b_tp2": lambda c, t, s, p: case_attention(c, t, s, p, n_head=32, n_head_kv=4),
+    "attn_int8_70b_tp8": lambda c, t, s, p: case_attention(c, t, s, p, n_head=8, n_head_kv=1),
     "layer_7b_q4_0": case_layer_7b,
     "layer_70b_q4_0": case_layer_70b,
     "prefill_l3_8b_q4_k": case_prefill_l3_8b,

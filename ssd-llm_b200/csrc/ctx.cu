@@ -577,10 +577,12 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
                 type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K ||
-                type == SSD_TYPE_F16 || type == SSD_TYPE_BF16 || type == SSD_TYPE_F32,
+                type == SSD_TYPE_F16 || type == SSD_TYPE_BF16 || type == SSD_TYPE_F32 ||
+                is_lowbit(type),
             SSD_ERR_TYPE,
-            "ggml type %d not supported (Q4_0=2, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14, Q8_K=15, "
-            "F32=0)",
+            "ggml type %d not supported (F32=0, F16=1, Q4_0=2, Q8_0=8, Q2_K=10, Q3_K=11, "
+            "Q4_K=12, Q5_K=13, Q6_K=14, Q8_K=15, IQ2_XXS=16, IQ2_XS=17, IQ3_XXS=18, IQ4_NL=20, "
+            "IQ3_S=21, IQ4_XS=23, BF16=30)",
             type);
     SSD_REQ(rows > 0 && cols > 0, SSD_ERR_SHAPE, "empty tensor %dx%d", rows, cols);
     int bs = type_block(type);

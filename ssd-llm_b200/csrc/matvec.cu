@@ -517,8 +517,8 @@ __device__ __forceinline__ float pos_scale(int k) {
 }
 
 // Persistent fused dequant-matvec. Grid = resident CTAs (or fewer for small matrices);
-// warp w of the grid owns row-groups (R rows) w, w + W, w + 2W, ... (W = warps in the
-// grid). A "stage" is U chunk steps (32 chunks each) of the R rows of one row-group;
+// warp w of CTA b owns row-groups (R rows) g, g + W, g + 2W, ... with g = b + w * gridDim.x
+// (W = warps in the grid). A "stage" is U chunk steps (32 chunks each) of the R rows of one row-group;
 // each warp keeps kStages - 1 stages of copies in flight in its shared-memory ring,
 // the first ones issued before griddepcontrol.wait.
 template <int FMT, int EPI, int R, int U, int NW>
@@ -545,7 +545,11 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     const int spr = (iters + U - 1) / U;  // stages per row-group
     const int n_rg = (a.rows + R - 1) / R;
     const int W = gridDim.x * NW;
-    const int wg = blockIdx.x * NW + warp;
+    // Row-groups are dealt to the CTAs first (warp w of CTA b starts at b + w * gridDim.x):
+    // every SM then gets ceil or floor of n_rg / gridDim.x row-groups. The SM's issue rate
+    // bounds these kernels, so an even share per SM (its warps finish at different times) is
+    // what balances the tail; dealing per warp would give some SMs twice as many.
+    const int wg = blockIdx.x + gridDim.x * warp;
     const int my_rg = wg < n_rg ? (n_rg - 1 - wg) / W + 1 : 0;
     const int total = my_rg * spr;  // stages this warp computes
 

@@ -199,6 +199,9 @@ __global__ void __launch_bounds__(256) k_kv_absmax(const float* __restrict__ k,
 //    memory, V decoded exactly as signed integers;
 //  * the 4 warps' (m, l, acc) are merged with the online-softmax rescaling into one
 //    partial per (head, chunk); k_attn_combine merges the chunks (:106-134).
+// With few KV heads per GPU (tensor parallelism) a KV head's query group is split over
+// a.hsplit CTAs (template G = group / hsplit query heads each), which read the same K/V
+// chunk (the second and later reads hit L2), so the grid fills the SMs at any head count.
 constexpr int ATT_P = 128;
 constexpr int ATT_NW = ATT_P / 32;
 constexpr float kAttUnscale = 18446744073709551616.0f;  // 2^64
@@ -240,8 +243,12 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
     __shared__ float fac[ATT_NW][G];
     __shared__ float qbias[G];
     __shared__ float amred[2][ATT_NW > 8 ? ATT_NW : 8];
+    __shared__ __align__(16) int8_t nkv[2][HD];  // the new position's K / V bytes (this head)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int gl = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y, qi = blockIdx.z;
+    const int S = a.hsplit > 0 ? a.hsplit : 1;
+    // hg: this CTA's query-head group (local heads hg*G ..); gl: its KV head; hs: its part
+    const int hg = blockIdx.x, gl = hg / S, hs = hg % S;
+    const int chunk = blockIdx.y, nchunks = gridDim.y, qi = blockIdx.z;
     const int g_kv = a.kv_head0 + gl;
     // Decode with the append fused (k_new set): the new K/V row is quantized and written
     // by the CTAs of its chunk. No kernel before this one writes the cache then, so the
@@ -262,8 +269,8 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
                   a.max_seq);
     }
     const int p0 = chunk * ATT_P;
-    const size_t qpart = (size_t)a.n_kv_local * G * nchunks * (HD + 2);
-    float* part = a.partial + qpart * qi + ((size_t)(gl * G) * nchunks + chunk) * (HD + 2);
+    const size_t qpart = (size_t)a.n_kv_local * S * G * nchunks * (HD + 2);
+    float* part = a.partial + qpart * qi + ((size_t)(hg * G) * nchunks + chunk) * (HD + 2);
     const size_t head_stride = (size_t)nchunks * (HD + 2);
     const int p = p0 + 32 * warp + lane;
     // this lane's K row and position scales, and its bytes of the warp's 32 V rows: all in
@@ -306,7 +313,7 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
     // q of the group: all float4 loads issued at once; each HD/4 consecutive float4 are
     // one head, so sub-groups of HD/4 lanes reduce that head's sum for the decode bias
     const float4* qg4 =
-        reinterpret_cast<const float4*>(a.q + (size_t)qi * a.q_stride + (size_t)gl * G * HD);
+        reinterpret_cast<const float4*>(a.q + (size_t)qi * a.q_stride + (size_t)hg * G * HD);
     constexpr int QV = G * HD / 4 / 128 > 0 ? G * HD / 4 / 128 : 1;  // float4 per thread
     float4 qv[QV];
 #pragma unroll
@@ -361,7 +368,7 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
             // publish this rank's pair to every rank (local head 0's CTA), then take the max
             // of all ranks' pairs once every word carries this call's tag (bounded wait)
             const uint32_t tag = (uint32_t)(*a.xch_epoch + (unsigned long long)a.xch_call) + 1u;
-            if (gl == 0 && tid < 2 * a.xch_n) {
+            if (gl == 0 && hs == 0 && tid < 2 * a.xch_n) {
                 const float val = (tid & 1) ? amv : amk;
                 const unsigned long long w =
                     ((unsigned long long)__float_as_uint(val) << 32) | (unsigned long long)tag;
@@ -403,21 +410,27 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
         const float sv = amv == 0.0f ? 0.0f : __fdiv_rn(amv, 127.0f);
         const float ik = amk == 0.0f ? 0.0f : __fdiv_rn(127.0f, amk);
         const float iv = amv == 0.0f ? 0.0f : __fdiv_rn(127.0f, amv);
+        // every CTA of the head quantizes the row into shared memory; the first (hs 0)
+        // stores it in the cache
         int8_t* kc = const_cast<int8_t*>(a.k) + (size_t)pnew * a.kv_dim + (size_t)g_kv * HD;
         int8_t* vc = const_cast<int8_t*>(a.v) + (size_t)pnew * a.kv_dim + (size_t)g_kv * HD;
         for (int d = tid; d < HD; d += 128) {
             const float fk = fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(a.k_new[g_kv * HD + d], ik))));
             const float fv = fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(a.v_new[g_kv * HD + d], iv))));
-            kc[d] = (int8_t)(int)fk;
-            vc[d] = (int8_t)(int)fv;
+            nkv[0][d] = (int8_t)(int)fk;
+            nkv[1][d] = (int8_t)(int)fv;
+            if (hs == 0) {
+                kc[d] = (int8_t)(int)fk;
+                vc[d] = (int8_t)(int)fv;
+            }
         }
-        if (gl == 0 && tid == 0) {
+        if (gl == 0 && hs == 0 && tid == 0) {
             const_cast<float*>(a.ks)[pnew] = sk;
             const_cast<float*>(a.vs)[pnew] = sv;
         }
         __syncthreads();  // the row's bytes are visible to the whole CTA
         if (p == pnew) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kc);
+            const uint4* kr = reinterpret_cast<const uint4*>(&nkv[0][0]);
 #pragma unroll
             for (int j = 0; j < HD / 16; j++) krow[j] = kr[j];
             ksc = sk;
@@ -426,7 +439,7 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
 #pragma unroll
         for (int t = 0; t < 32; t++) {
             if (pw0 + t == pnew) {
-                const int8_t* vr = vc + DPL * lane;
+                const int8_t* vr = &nkv[1][0] + DPL * lane;
                 if constexpr (DPL == 4)
                     vw[t] = *reinterpret_cast<const uint32_t*>(vr);
                 else
@@ -603,25 +616,55 @@ size_t attn_partial_floats(int n_heads, int max_seq, int head_dim) {
     return (size_t)n_heads * nchunks * (head_dim + 2);
 }
 
+// G = query heads per CTA (a.group / a.hsplit).
 template <int HD, int G>
 static int launch_attn_t(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const int nchunks = (a.max_seq + ATT_P - 1) / ATT_P;
     const int nq = a.n_q > 1 ? a.n_q : 1;
-    SSD_CK(launch_pdl(k_attn_partial<HD, G>, dim3(a.n_kv_local, nchunks, nq), dim3(128), 0, s, pdl,
-                      a));
-    SSD_CK(launch_pdl(k_attn_combine<HD>, dim3(a.n_kv_local * G, nq), dim3(HD), 0, s, pdl, a,
-                      nchunks));
+    SSD_CK(launch_pdl(k_attn_partial<HD, G>, dim3(a.n_kv_local * a.hsplit, nchunks, nq), dim3(128),
+                      0, s, pdl, a));
+    SSD_CK(launch_pdl(k_attn_combine<HD>, dim3(a.n_kv_local * a.group, nq), dim3(HD), 0, s, pdl,
+                      a, nchunks));
     return SSD_OK;
 }
 
+static int sm_count() {
+    static int n = [] {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    return n;
+}
+
 template <int HD>
-static int launch_attn_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
-    switch (a.group) {
+static int launch_attn_hd(const AttnArgs& a0, cudaStream_t s, bool pdl) {
+    SSD_REQ(a0.group == 1 || a0.group == 2 || a0.group == 4 || a0.group == 8, SSD_ERR_SHAPE,
+            "GQA group %d not supported (1, 2, 4, 8)", a0.group);
+    AttnArgs a = a0;
+    // decode: split the query group while the grid would still hold under ~one CTA per SM
+    // (measured, 70B heads at 4096 positions: 8 KV heads best unsplit, 14.6 us against 17.7
+    // split in two; 1 KV head best split in four, 7.9 us against 10.4 unsplit and 8.9 split in
+    // eight: each split repeats the K decode, so it pays only while SMs would sit idle)
+    const int nchunks = (a.max_seq + ATT_P - 1) / ATT_P;
+    a.hsplit = 1;
+    static const int forced = [] {  // SSD_ATTN_HSPLIT=n: a fixed split (tuning sweeps)
+        const char* e = getenv("SSD_ATTN_HSPLIT");
+        return e ? atoi(e) : 0;
+    }();
+    if (a.n_q <= 1) {
+        if (forced > 0)
+            while (a.hsplit < forced && a.hsplit < a.group) a.hsplit *= 2;
+        else
+            while (a.hsplit < a.group && 2 * a.n_kv_local * a.hsplit * nchunks <= sm_count())
+                a.hsplit *= 2;
+    }
+    switch (a.group / a.hsplit) {
         case 1: return launch_attn_t<HD, 1>(a, s, pdl);
         case 2: return launch_attn_t<HD, 2>(a, s, pdl);
         case 4: return launch_attn_t<HD, 4>(a, s, pdl);
-        case 8: return launch_attn_t<HD, 8>(a, s, pdl);
-        default: set_error("GQA group %d not supported (1, 2, 4, 8)", a.group); return SSD_ERR_SHAPE;
+        default: return launch_attn_t<HD, 8>(a, s, pdl);
     }
 }
 

@@ -60,6 +60,9 @@ struct AttnArgs {
     const unsigned long long* xch_epoch;
     const unsigned long long* xch_in;
     unsigned long long* xch_out[8];
+    // Set by launch_attention (decode): CTAs per KV head; each takes group / hsplit of its
+    // query heads over the chunk's positions.
+    int hsplit;
 };
 // Local absmax pair (K, V) of the n-float rows k, v into out[0..1] (one CTA).
 int launch_kv_absmax(const float* k, const float* v, int n, float* out, cudaStream_t s, bool pdl);
