@@ -604,6 +604,18 @@ def case_decode_b16_70b(ctx, torch, ssdllm, peak):
         m.free()
 
 
+def case_decode_b16_2l(ctx, torch, ssdllm, peak):
+    """Continuous batch 16 on two Llama-70B-shaped layers (1.6 GB of weights): the small case
+    that profiler captures of the batched kernels run (same kernels and shapes per layer)."""
+    cfg = dict(CFG70B, n_layers=2, tp_rank=0, tp_size=1)
+    m = ssdllm.Model(ctx, **cfg)
+    try:
+        m.synth_weights(seed=0, std=0.02)
+        return measure_batch16(ctx, torch, ssdllm, m, cfg, peak)
+    finally:
+        m.free()
+
+
 def measured_tensor_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -692,10 +704,12 @@ CASES = {
     "prefill_l3_8b_q4_k": case_prefill_l3_8b,
     "mv_shapes_70b": case_mv_shapes,
     "decode_b16_70b": case_decode_b16_70b,
+    "decode_b16_2l": case_decode_b16_2l,
 }
 # measured on every default run (mv_shapes_70b, a kernel-selection study, only by --case;
-# decode_b16_70b is measured on the headline run's own model)
-DEFAULT_CASES = [n for n in CASES if n not in ("mv_shapes_70b", "decode_b16_70b")]
+# decode_b16_70b is measured on the headline run's own model; decode_b16_2l is the profiler's
+# small case)
+DEFAULT_CASES = [n for n in CASES if n not in ("mv_shapes_70b", "decode_b16_70b", "decode_b16_2l")]
 
 
 def run_cases(names, peak):

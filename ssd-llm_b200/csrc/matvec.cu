@@ -517,8 +517,8 @@ __device__ __forceinline__ float pos_scale(int k) {
 }
 
 // Persistent fused dequant-matvec. Grid = resident CTAs (or fewer for small matrices);
-// warp w of CTA b owns row-groups (R rows) g, g + W, g + 2W, ... with g = b + w * gridDim.x
-// (W = warps in the grid). A "stage" is U chunk steps (32 chunks each) of the R rows of one row-group;
+// CTA b owns the contiguous row-groups (R rows) [b n_rg / G, (b + 1) n_rg / G) (G = gridDim.x;
+// counts differ by at most one), its warps taking them round robin. A "stage" is U chunk steps (32 chunks each) of the R rows of one row-group;
 // each warp keeps kStages - 1 stages of copies in flight in its shared-memory ring,
 // the first ones issued before griddepcontrol.wait.
 template <int FMT, int EPI, int R, int U, int NW>
@@ -536,6 +536,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     float* csum = reinterpret_cast<float*>(base + P.csum);
     float* red = reinterpret_cast<float*>(base + P.red);
     unsigned long long* keys = reinterpret_cast<unsigned long long*>(base + P.red + 256);
+    // EPI_PEERS: the CTA's output rows collect in the `red` region (free after the prologue)
+    // when they fit, then go out as contiguous stores
+    float* peer_buf = red;
     uint64_t* bar = reinterpret_cast<uint64_t*>(base + P.bar);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -544,13 +547,15 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     const int iters = (nc + 31) >> 5;     // chunk iterations per lane per row
     const int spr = (iters + U - 1) / U;  // stages per row-group
     const int n_rg = (a.rows + R - 1) / R;
-    const int W = gridDim.x * NW;
-    // Row-groups are dealt to the CTAs first (warp w of CTA b starts at b + w * gridDim.x):
-    // every SM then gets ceil or floor of n_rg / gridDim.x row-groups. The SM's issue rate
-    // bounds these kernels, so an even share per SM (its warps finish at different times) is
-    // what balances the tail; dealing per warp would give some SMs twice as many.
-    const int wg = blockIdx.x + gridDim.x * warp;
-    const int my_rg = wg < n_rg ? (n_rg - 1 - wg) / W + 1 : 0;
+    // Every SM gets floor or ceil of n_rg / gridDim.x row-groups, as one contiguous range. The
+    // SM's issue rate bounds these kernels, so an even share per SM (its warps finish at
+    // different times) is what balances the tail; dealing per warp gave some SMs twice as
+    // many. Contiguous rows let the peer epilogue store a CTA's outputs as whole lines.
+    const int rg_lo = (int)((long long)n_rg * blockIdx.x / gridDim.x);
+    const int rg_hi = (int)((long long)n_rg * (blockIdx.x + 1) / gridDim.x);
+    const int wg = rg_lo + warp;
+    const int my_rg = wg < rg_hi ? (rg_hi - 1 - wg) / NW + 1 : 0;
+    const bool peer_buffered = EPI == EPI_PEERS && (rg_hi - rg_lo) * R <= (64 * 4 + NW * 8) / 4;
     const int total = my_rg * spr;  // stages this warp computes
 
     if (tid == 0) {
@@ -581,7 +586,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
                 lm[r] = reinterpret_cast<const uint8_t*>((uintptr_t)lm[r] & ~(uintptr_t)3);
         }
     };
-    if (lrg < n_rg) set_rows();
+    if (lrg < rg_hi) set_rows();
     const bool any_tail = nc % (32 * U) != 0 || nc < 32;
     // this lane's slots: payload at ring_q + stage + (r*U+u)*32*QB, metadata at
     // ring_m + stage + (r*U+u)*MSLOT (compile-time offsets from two lane pointers; Q4_K /
@@ -631,8 +636,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             ist = ist + SB == kStages * SB ? 0 : ist + SB;
             if (++lst == spr) {
                 lst = 0;
-                lrg += W;
-                if (lrg < n_rg) set_rows();
+                lrg += NW;
+                if (lrg < rg_hi) set_rows();
             }
         }
         cp_commit();  // one group per call, empty or not: wait_group counts stay uniform
@@ -688,7 +693,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             doff[r] = (((lr & 1) * (nc & 1) + lane) & 1) * 2;
         }
     };
-    if (has_doff<FMT>() && crg < n_rg) set_doff();
+    if (has_doff<FMT>() && crg < rg_hi) set_doff();
     int cst_off = 0;  // byte offset of the stage being computed
     // this lane's shared address of x'' unit u of its chunk c = lane (mod 32): row c of
     // 128 bytes, unit u at slot u ^ (c & 7) = u ^ (lane & 7); chunk c + 32 t is 4096 t
@@ -734,8 +739,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
         // row-group finished: reduce across the warp and run the epilogue
         cst = 0;
         const int v0 = crg * R;
-        crg += W;
-        if (has_doff<FMT>() && crg < n_rg) set_doff();
+        crg += NW;
+        if (has_doff<FMT>() && crg < rg_hi) set_doff();
         float res[R];
 #pragma unroll
         for (int r = 0; r < R; r++) {
@@ -749,11 +754,17 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
                 if (lane == r && row < a.rows)
                     a.y[row] = (EPI == EPI_RESID) ? __fadd_rn(a.base[row], res[r]) : res[r];
             }
-        } else if constexpr (EPI == EPI_PEERS) {  // partial row -> every rank's buffer
+        } else if constexpr (EPI == EPI_PEERS) {  // partial rows, sent at the end (below)
 #pragma unroll
             for (int r = 0; r < R; r++) {
                 const int row = v0 + r;
-                if (lane < a.ar_out_n && row < a.rows) a.ar_out[lane][row] = res[r];
+                if (row < a.rows) {
+                    if (peer_buffered) {
+                        if (lane == r) peer_buf[row - rg_lo * R] = res[r];
+                    } else if (lane < a.ar_out_n) {
+                        a.ar_out[lane][row] = res[r];
+                    }
+                }
             }
         } else if constexpr (EPI == EPI_SWIGLU) {  // rows: R/2 gate rows, then R/2 up rows
             constexpr int H = R / 2;
@@ -801,6 +812,12 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     cp_wait<0>();
 
     if constexpr (EPI == EPI_PEERS) {
+        if (peer_buffered) {  // this CTA's contiguous rows, as whole lines to every rank
+            __syncthreads();
+            const int row0 = rg_lo * R, nrow = min(rg_hi * R, a.rows) - row0;
+            for (int p = 0; p < a.ar_out_n; p++)
+                for (int i = tid; i < nrow; i += NW * 32) a.ar_out[p][row0 + i] = peer_buf[i];
+        }
         // publish: every thread's peer stores are made visible system-wide, then the
         // last CTA to finish raises this call's flag on every rank
         __threadfence_system();
