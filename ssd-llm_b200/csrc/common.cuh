@@ -389,6 +389,11 @@ inline cudaStream_t pick_stream(ssd_ctx* ctx, void* s) {
 }
 
 int check_ctx(ssd_ctx* ctx);
+// Zeroes `bytes` at device pointer p and waits until it is done. The context's stream is
+// non-blocking, so a plain cudaMemset (legacy default stream, asynchronous for device
+// memory) would not be ordered before kernels the caller launches next on that stream;
+// every one-time initialisation of device state goes through this.
+int zero_device(ssd_ctx* ctx, void* p, size_t bytes);
 // Encodes a 2-D fp32 tensor map over a vector of n floats viewed as rows of 32 floats
 // (128 B), box = 32 rows, 128-byte swizzle: chunk c's 16-byte unit u lands at unit
 // u ^ (c & 7) of its row, so the 8 units a lane reads are bank-conflict free across a

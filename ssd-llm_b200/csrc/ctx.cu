@@ -126,6 +126,13 @@ int check_ctx(ssd_ctx* ctx) {
     return SSD_OK;
 }
 
+int zero_device(ssd_ctx* ctx, void* p, size_t bytes) {
+    if (!bytes) return SSD_OK;
+    SSD_CK(cudaMemsetAsync(p, 0, bytes, ctx->stream));
+    SSD_CK(cudaStreamSynchronize(ctx->stream));
+    return SSD_OK;
+}
+
 int ensure_scratch(ssd_ctx* ctx, size_t bytes) {
     if (ctx->scratch_bytes >= bytes) return SSD_OK;
     if (ctx->scratch) {  // callers may have work in flight on any stream
@@ -482,7 +489,8 @@ extern "C" int ssd_ctx_create(int device, ssd_ctx** out) {
     snprintf(c->name, sizeof(c->name), "%s", p.name);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->argmax_key, 64) != cudaSuccess ||
-        cudaMemset(c->argmax_key, 0, 64) != cudaSuccess) {
+        cudaMemsetAsync(c->argmax_key, 0, 64, c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess) {
         set_error("context setup failed: %s", cudaGetErrorString(cudaGetLastError()));
         delete c;
         return SSD_ERR_CUDA;
@@ -533,8 +541,7 @@ extern "C" int ssd_ctx_device_status(ssd_ctx* ctx, int* status) {
     SSD_REQ(status != nullptr, SSD_ERR_ARG, "null status");
     SSD_CK(cudaDeviceSynchronize());
     SSD_CK(cudaMemcpy(status, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost));
-    SSD_CK(cudaMemset(ctx->dev_status, 0, sizeof(int)));
-    return SSD_OK;
+    return zero_device(ctx, ctx->dev_status, sizeof(int));
 }
 
 extern "C" int ssd_ctx_set_pdl(ssd_ctx* ctx, int on) {
@@ -641,7 +648,7 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
     w->meta = meta_bytes ? (uint8_t*)p + qs_pad : nullptr;
     if (fix) {
         uint8_t* f = (uint8_t*)p + qs_pad + meta_pad;
-        if (cudaMemset(f, 0, counter_bytes) != cudaSuccess) {
+        if (zero_device(ctx, f, counter_bytes) != SSD_OK) {
             cudaGetLastError();
             cudaFree(p);
             delete w;
@@ -720,7 +727,8 @@ extern "C" int ssd_weight_download(ssd_ctx* ctx, const ssd_weight* w, void* host
     size_t need = ssd_row_bytes(w->type, w->cols) * (size_t)w->rows;
     SSD_REQ(bytes == need, SSD_ERR_SHAPE, "need %zu bytes, got %zu", need, bytes);
     if (type_block(w->type) == 1 || is_lowbit(w->type)) {
-        SSD_CK(cudaMemcpy(host_raw, w->qs, bytes, cudaMemcpyDeviceToHost));
+        SSD_CK(cudaMemcpyAsync(host_raw, w->qs, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+        SSD_CK(cudaStreamSynchronize(ctx->stream));
         return SSD_OK;
     }
     void* staging = nullptr;

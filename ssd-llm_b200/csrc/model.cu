@@ -209,7 +209,11 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
         set_error("decode state allocation failed");
         return SSD_ERR_NOMEM;
     }
-    cudaMemset(m->state, 0, floats * 4);
+    if (zero_device(ctx, m->state, floats * 4) != SSD_OK) {
+        cudaFree(m->state);
+        delete m;
+        return SSD_ERR_CUDA;
+    }
     float* S = (float*)m->state;
     m->h_a = S + o_ha;
     m->h_b = S + o_hb;
@@ -321,8 +325,7 @@ extern "C" int ssd_model_p2p_handle(ssd_model* m, uint8_t out[64]) {
             set_error("peer all-reduce buffer allocation (%zu bytes) failed", bytes);
             return SSD_ERR_NOMEM;
         }
-        SSD_CK(cudaMemset(m->p2p_buf, 0, bytes));
-        SSD_CK(cudaDeviceSynchronize());
+        SSD_TRY(zero_device(m->ctx, m->p2p_buf, bytes));
     }
     cudaIpcMemHandle_t h;
     SSD_CK(cudaIpcGetMemHandle(&h, m->p2p_buf));
@@ -507,7 +510,9 @@ static int set_norm(ssd_model* m, float** slot, const void* host, size_t bytes) 
     const size_t need = (size_t)m->cfg.n_embd * 4;
     SSD_REQ(bytes == need, SSD_ERR_SHAPE, "norm weight needs %zu bytes, got %zu", need, bytes);
     if (!*slot) SSD_CK(cudaMalloc(slot, need));
-    SSD_CK(cudaMemcpy(*slot, host, need, cudaMemcpyHostToDevice));
+    // on the context's (non-blocking) stream, complete before any later launch reads it
+    SSD_CK(cudaMemcpyAsync(*slot, host, need, cudaMemcpyHostToDevice, m->ctx->stream));
+    SSD_CK(cudaStreamSynchronize(m->ctx->stream));
     return SSD_OK;
 }
 
@@ -1041,8 +1046,9 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
         SSD_REQ(tokens[i] >= 0 && tokens[i] < c.vocab, SSD_ERR_ARG, "token %d outside vocab",
                 tokens[i]);
     cudaStream_t s = m->ctx->stream;
-    int pos0 = 0;
-    SSD_CK(cudaMemcpy(&pos0, m->pos, 4, cudaMemcpyDeviceToHost));
+    int pos0 = 0;  // after the stream's pending work (a decode step may advance it)
+    SSD_CK(cudaMemcpyAsync(&pos0, m->pos, 4, cudaMemcpyDeviceToHost, s));
+    SSD_CK(cudaStreamSynchronize(s));
     SSD_REQ(pos0 + n <= c.kv_capacity, SSD_ERR_SHAPE, "positions [%d, %d) exceed capacity %d", pos0,
             pos0 + n, c.kv_capacity);
     SSD_TRY(prepare_prefill_weights(m, s));
@@ -1337,7 +1343,7 @@ extern "C" int ssd_batch_create(ssd_model* m, int capacity, ssd_batch** out) {
     b->keys = (unsigned long long*)(p + off[18]);
     b->inv = (float*)(p + off[19]);
     int st = SSD_OK;
-    if (cudaMemset(b->alloc, 0, o) != cudaSuccess ||
+    if (zero_device(m->ctx, b->alloc, o) != SSD_OK ||
         cudaMallocHost(&b->pinned, (size_t)2 * S * 4) != cudaSuccess) {
         cudaGetLastError();
         set_error("batch initialisation failed");

@@ -555,7 +555,9 @@ __global__ void __launch_bounds__(128) k_attn_partial(const AttnArgs a0) {
 
 // Merges the chunk partials of one query head (flash_attention.rs:106-134): the chunk
 // statistics are loaded in parallel, the rescale factors exp(m_c - M) shared through
-// shared memory, then thread d sums its dimension over the chunks.
+// shared memory, then thread d sums its dimension over the chunks. (Issuing every load of
+// the head at once, with one barrier, measured no faster inside the PDL chain: the partial
+// kernel's tail already hides these round trips.)
 template <int HD>
 __global__ void __launch_bounds__(HD) k_attn_combine(const AttnArgs a, int nchunks) {
     __shared__ float fac[1024];
@@ -836,7 +838,10 @@ extern "C" int ssd_kv_create(ssd_ctx* ctx, int capacity, int n_head_kv, int head
         set_error("KV cache allocation of %zu bytes failed", total);
         return SSD_ERR_NOMEM;
     }
-    SSD_CK(cudaMemset(p, 0, total));
+    if (zero_device(ctx, p, total) != SSD_OK) {
+        cudaFree(p);
+        return SSD_ERR_CUDA;
+    }
     ssd_kv_cache* kv = new ssd_kv_cache();
     kv->ctx = ctx;
     kv->capacity = capacity;
