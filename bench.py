@@ -66,17 +66,28 @@ def measured_peaks():
 
 # ------------------------------------------------------------------ clocks
 class Clocks:
-    """nvidia-smi sampling during the timed region (reads settings, changes none)."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi sampling around the timed region (reads settings, changes none). The
+    sampler is started during the warm-up (nvidia-smi needs ~0.5 s to take its first sample
+    and a timed region of a few hundred ms would otherwise get none); mark() brackets the
+    timed region and summary() keeps the samples taken inside it, or, if it was shorter than
+    the sampling period, the samples nearest to it (their count and window are reported)."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpus):
         self.gpus = gpus
         self.proc = None
+        self.t = [None, None]
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
 
+    def mark(self, which):
+        """which = 0: timed region starts; 1: it ends (wall clock, as nvidia-smi stamps)."""
+        self.t[which] = datetime.datetime.now()
+
     def __enter__(self):
+        if not self.gpus:  # ranks other than 0 sample nothing
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
@@ -86,7 +97,7 @@ class Clocks:
         return self
 
     def __exit__(self, *a):
-        if self.proc:
+        if self.proc and self.proc.poll() is None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -100,21 +111,37 @@ class Clocks:
         rows = []
         for line in open(self.f.name):
             p = [x.strip() for x in line.split(",")]
-            if len(p) < 9:
+            if len(p) < 10:
                 continue
             try:
-                if int(p[0]) in self.gpus:
-                    rows.append(p)
+                ts = datetime.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f")
+                if int(p[1]) in self.gpus:
+                    rows.append((ts, p[1:]))
             except ValueError:
                 continue
         if not rows:
             return None
+        window = "timed"
+        if self.t[0] and self.t[1]:
+            inside = [r for r in rows if self.t[0] <= r[0] <= self.t[1]]
+            if inside:
+                rows = inside
+            else:  # region shorter than the sampling period: the nearest samples, per GPU
+                window = "nearest"
+                mid = self.t[0] + (self.t[1] - self.t[0]) / 2
+                best = {}
+                for r in rows:
+                    g = r[1][0]
+                    if g not in best or abs(r[0] - mid) < abs(best[g][0] - mid):
+                        best[g] = r
+                rows = list(best.values())
+        rows = [r[1] for r in rows]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "window": window}
 
 
 # -------------------------------------------------------------- CPU baseline
@@ -782,6 +809,7 @@ def run_cuda(args):
         cfg["n_layers"] = args.layers
     ctx = ssdllm.Context(local)
     model = ssdllm.Model(ctx, **cfg, tp_rank=rank, tp_size=world)
+    clk = None
     try:
         if world > 1:
             obj = [ssdllm.Model.unique_id() if rank == 0 else None]
@@ -791,6 +819,10 @@ def run_cuda(args):
                 hs = [None] * world
                 dist.all_gather_object(hs, model.p2p_handle())
                 model.p2p_open(hs)
+        # clock sampler running from here (it takes ~0.5 s to start sampling); mark() brackets
+        # the timed region below
+        clk = Clocks(list(range(world)) if rank == 0 else [])
+        clk.__enter__()
         t0 = time.perf_counter()
         model.synth_weights(seed=0, std=0.02)
         total = args.warmup + 2 * args.steps + 1
@@ -806,17 +838,19 @@ def run_cuda(args):
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with Clocks(list(range(world)) if rank == 0 else []) as clk:
-            if world > 1:
-                dist.barrier()
-            torch.cuda.synchronize()
-            e0.record(stream)
-            for _ in range(args.steps):
-                model.decode_step(True)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            if world > 1:
-                dist.barrier()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk.mark(0)
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.decode_step(True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clk.mark(1)
+        clk.__exit__()
+        if world > 1:
+            dist.barrier()
         ms = e0.elapsed_time(e1)
         # e2e: host token in, host token out through the public API, every step, timed on
         # the host clock (each call synchronises on its token copy back)
@@ -844,6 +878,8 @@ def run_cuda(args):
         k0 = run_cases(DEFAULT_CASES, peak) if rank == 0 and not args.no_kernels else None
         clocks = clk.summary() if rank == 0 else None
     finally:
+        if clk is not None:
+            clk.__exit__()  # stops the sampler on every path (a second call is a no-op)
         model.free()  # releases the graph holding NCCL calls before the process group
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -143,15 +143,23 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
             float4 v = xs4[ph];
             if (has_add) {  // hidden[i] += attn_output[i] (src/metal/compute.rs:547-549)
                 float4 r;
-                if (a.ar_in_n > 0) {  // the ranks' partials, summed in rank order (L2 reads)
-                    r = __ldcg(reinterpret_cast<const float4*>(a.ar_in) + i);
-                    for (int p = 1; p < a.ar_in_n; p++) {
-                        const float4 t =
-                            __ldcg(reinterpret_cast<const float4*>(a.ar_in + (size_t)p * a.cols) + i);
-                        r.x = __fadd_rn(r.x, t.x);
-                        r.y = __fadd_rn(r.y, t.y);
-                        r.z = __fadd_rn(r.z, t.z);
-                        r.w = __fadd_rn(r.w, t.w);
+                if (a.ar_in_n > 0) {
+                    // the ranks' partials: all N loads in flight at once (one L2 round trip per
+                    // unit, not N), then summed in rank order
+                    float4 t[kMaxPeers];
+#pragma unroll
+                    for (int p = 0; p < kMaxPeers; p++)
+                        if (p < a.ar_in_n)
+                            t[p] = __ldcg(reinterpret_cast<const float4*>(a.ar_in + (size_t)p * a.cols) + i);
+                    r = t[0];
+#pragma unroll
+                    for (int p = 1; p < kMaxPeers; p++) {
+                        if (p < a.ar_in_n) {
+                            r.x = __fadd_rn(r.x, t[p].x);
+                            r.y = __fadd_rn(r.y, t[p].y);
+                            r.z = __fadd_rn(r.z, t[p].z);
+                            r.w = __fadd_rn(r.w, t[p].w);
+                        }
                     }
                 } else {
                     r = __ldg(reinterpret_cast<const float4*>(a.x_add) + i);
