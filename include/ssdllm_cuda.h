@@ -368,7 +368,8 @@ int ssd_feed_forward_f32_host(ssd_ctx* ctx, const float* x, const float* w_gate,
  * tp_size > 1 needs ssd_model_tp_init before building. */
 typedef struct {
     int n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab;
-    int wtype;        /* layer weight type: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K or Q8_K */
+    int wtype;        /* layer weight type: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K or Q8_K; F16, BF16 or
+                         F32 at tp_size 1 */
     int out_type;     /* output.weight type: as wtype */
     int embd_type;    /* token_embd type: as wtype, or F32 / F16 / BF16 */
     int kv_capacity;  /* INT8 KV positions */

@@ -506,8 +506,14 @@ void ora_matvec_f32(const float* w, const float* x, int out_dim, int in_dim, flo
 
 typedef float (*row_fn)(const uint8_t*, const float*, int, int);
 
+/* F32 rows as bytes: the same matvec_f32_simd row (for layers of F32 weights). */
+static float row_f32b(const uint8_t* w, const float* x, int in_dim, int row) {
+    return row_f32((const float*)w, x, in_dim, row);
+}
+
 static row_fn pick_row(int type) {
     switch (type) {
+        case ORA_F32: return row_f32b;
         case ORA_Q4_0: return row_q4_0;
         case ORA_Q8_0: return row_q8_0;
         case ORA_Q4_K: return row_q4_k;

@@ -30,6 +30,7 @@
 #include "gemm.cuh"
 #include "matvec.cuh"
 #include "matvec_b.cuh"
+#include "matvec_dev.cuh"
 #include "ops.cuh"
 
 #define SSD_NCCL(call)                                                                \
@@ -91,6 +92,81 @@ __global__ void k_add(float* out, const float* a, const float* b, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = __fadd_rn(a[i], b[i]);
 }
+
+// ---- dense (F16 / BF16 / F32) layer weights: the stages the quantized kernels fuse, as
+// separate launches (the dense matvec has no norm prologue, RoPE or argmax epilogue)
+
+// out = rms_norm(x) * w: order 0 x * (inv * w) (transformer.rs:576-579), order 1
+// (x * inv) * w (compute.rs:536-577); one CTA.
+__global__ void __launch_bounds__(1024) k_dense_norm(const float* x, const float* w, int n,
+                                                     float eps, int order, float* out) {
+    __shared__ float red[32];
+    pdl_wait();
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 1024) ss = fmaf(x[i], x[i], ss);
+    ss = block_sum<1024>(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (int i = threadIdx.x; i < n; i += 1024)
+        out[i] = order == 0 ? __fmul_rn(x[i], __fmul_rn(inv, w[i]))
+                            : __fmul_rn(__fmul_rn(x[i], inv), w[i]);
+}
+
+// RoPE on the q and k rows at the device-held position (the pair rotation of the fused
+// QKV epilogue, rope_f32_multi_head, compute.rs:482-506).
+__global__ void k_rope_qk(float* q, int q_rows, float* k, int k_rows, int head_dim, float theta,
+                          const int* pos) {
+    pdl_wait();
+    const int half = head_dim / 2;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;  // pair index over q then k
+    const int nq = q_rows / 2;
+    if (t >= nq + k_rows / 2) return;
+    float* x = t < nq ? q : k;
+    const int pr = t < nq ? t : t - nq;  // pair within the vector
+    const float2 cs = rope_cs(pr % half, head_dim, theta, *pos);
+    float x0 = x[2 * pr], x1 = x[2 * pr + 1];
+    rope_apply(x0, x1, cs);
+    x[2 * pr] = x0;
+    x[2 * pr + 1] = x1;
+}
+
+// The packed (value, index) argmax key of n logits (indices index0 ..), max-combined into
+// *key (zeroed by the step's finalize): the matvec's argmax epilogue for dense outputs.
+__global__ void __launch_bounds__(256) k_argmax_key(const float* v, int n, uint32_t index0,
+                                                    unsigned long long* key) {
+    __shared__ unsigned long long red[8];
+    pdl_wait();
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < n; i += gridDim.x * 256) {
+        const unsigned long long kk = argmax_key(v[i], index0 + (uint32_t)i);
+        best = kk > best ? kk : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; w++) best = red[w] > best ? red[w] : best;
+        if (best) atomicMax(key, best);
+    }
+}
+
+// f32 -> F16 / BF16 bits, round to nearest even (synthetic dense weights).
+__global__ void k_to16(const float* in, uint16_t* out, size_t n, int bf) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (bf) {
+        const uint32_t u = __float_as_uint(in[i]);
+        out[i] = (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+    } else {
+        out[i] = __half_as_ushort(__float2half_rn(in[i]));
+    }
+}
+
+__host__ __device__ constexpr bool dense_type(int t) {
+    return t == SSD_TYPE_F32 || t == SSD_TYPE_F16 || t == SSD_TYPE_BF16;
+}
 }  // namespace ssd
 
 using namespace ssd;
@@ -124,6 +200,7 @@ struct ssd_model {
     // KV absmax exchange slots ([kArSlots][tp][2] tagged words after the flags)
     unsigned long long* p2p_xch[kMaxPeers] = {};
     float* amax = nullptr;  // the (K, V) absmax pair max-reduced by NCCL (no peer path)
+    float* xn = nullptr;    // normed input of the dense-weight stages
     void* p2p_mapped[kMaxPeers] = {};
     bool p2p = false;
     unsigned long long* ar_epoch = nullptr;  // advanced by 2 * n_layers per step
@@ -157,8 +234,9 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
                 c->n_embd % N == 0,
             SSD_ERR_SHAPE, "dimensions do not shard over %d ranks", N);
     const int bs = type_block(c->wtype);
-    SSD_REQ((bs == 32 || bs == 256) && !is_lowbit(c->wtype), SSD_ERR_TYPE,
-            "layer weight type %d not supported", c->wtype);
+    SSD_REQ(((bs == 32 || bs == 256) && !is_lowbit(c->wtype)) || (dense_type(c->wtype) && N == 1),
+            SSD_ERR_TYPE, "layer weight type %d not supported%s", c->wtype,
+            dense_type(c->wtype) ? " with tensor parallelism" : "");
     SSD_REQ((c->n_embd / N) % bs == 0 && (c->n_ff / N) % bs == 0, SSD_ERR_SHAPE,
             "column shards must be whole %d-wide blocks", bs);
     SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
@@ -167,10 +245,10 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
                 c->embd_type == SSD_TYPE_Q8_K || c->embd_type == SSD_TYPE_F16 ||
                 c->embd_type == SSD_TYPE_BF16,
             SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
-    SSD_REQ((type_block(c->out_type) == 32 || type_block(c->out_type) == 256) &&
-                !is_lowbit(c->out_type),
-            SSD_ERR_TYPE,
-            "output type %d not supported", c->out_type);
+    SSD_REQ(((type_block(c->out_type) == 32 || type_block(c->out_type) == 256) &&
+             !is_lowbit(c->out_type)) ||
+                (dense_type(c->out_type) && N == 1),
+            SSD_ERR_TYPE, "output type %d not supported", c->out_type);
 
     ssd_model* m = new ssd_model();
     m->ctx = ctx;
@@ -202,7 +280,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     const size_t o_ha = take(E), o_hb = take(E), o_q = take(m->q_rows), o_k = take(m->kv_rows),
                  o_v = take(m->kv_rows), o_attn = take(m->q_rows), o_act = take(m->ff_local),
                  o_part = take(pf), o_p1 = take(E), o_p2 = take(E), o_log = take(m->vocab_local),
-                 o_misc = take(64);
+                 o_misc = take(64), o_xn = take(E);
     if (cudaMalloc(&m->state, floats * 4) != cudaSuccess) {
         cudaGetLastError();
         delete m;
@@ -232,6 +310,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     m->ar_epoch = reinterpret_cast<unsigned long long*>(S + o_misc + 16);
     m->ar_counter = reinterpret_cast<unsigned int*>(S + o_misc + 20);
     m->amax = S + o_misc + 24;
+    m->xn = S + o_xn;
     if (cudaHostAlloc(&m->pinned, 16, cudaHostAllocDefault) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->state);
@@ -538,8 +617,7 @@ extern "C" int ssd_model_set_tensor_typed(ssd_model* m, const char* cname, int l
         SSD_REQ(ggml_type == SSD_TYPE_Q4_0 || ggml_type == SSD_TYPE_Q8_0 ||
                     ggml_type == SSD_TYPE_Q4_K || ggml_type == SSD_TYPE_Q5_K ||
                     ggml_type == SSD_TYPE_Q6_K || ggml_type == SSD_TYPE_Q8_K ||
-                    (embd && (ggml_type == SSD_TYPE_F32 || ggml_type == SSD_TYPE_F16 ||
-                              ggml_type == SSD_TYPE_BF16)),
+                    (dense_type(ggml_type) && (embd || tp_size(m) == 1)),
                 SSD_ERR_TYPE, "%s: ggml type %d not supported here", cname, ggml_type);
         const int tb = type_block(ggml_type);
         SSD_REQ(s.cols % tb == 0 && s.col0 % tb == 0 && s.ncols % tb == 0, SSD_ERR_SHAPE,
@@ -591,6 +669,23 @@ extern "C" int ssd_model_synth_weights(ssd_model* m, uint64_t seed, float std_de
             SSD_TRY(alloc_weight(m->ctx, SSD_TYPE_F32, s.nrows, s.ncols, &w));
             SSD_TRY(ssd_synth_f32(m->ctx, seed, s.tid, 0.0f, sd, s.cols, s.row0, s.nrows, s.col0,
                                   s.ncols, (float*)w->qs, (void*)m->ctx->stream));
+        } else if (s.type == SSD_TYPE_F16 || s.type == SSD_TYPE_BF16) {  // N(0, sd) rounded
+            const size_t n = (size_t)s.nrows * s.ncols;
+            SSD_TRY(alloc_weight(m->ctx, s.type, s.nrows, s.ncols, &w));
+            float* tmp = nullptr;
+            SSD_CK(cudaMalloc(&tmp, n * 4));
+            int st = ssd_synth_f32(m->ctx, seed, s.tid, 0.0f, sd, s.cols, s.row0, s.nrows, s.col0,
+                                   s.ncols, tmp, (void*)m->ctx->stream);
+            if (st == SSD_OK) {
+                k_to16<<<(unsigned)((n + 255) / 256), 256, 0, m->ctx->stream>>>(
+                    tmp, reinterpret_cast<uint16_t*>(w->qs), n, s.type == SSD_TYPE_BF16);
+                if (cudaStreamSynchronize(m->ctx->stream) != cudaSuccess) st = SSD_ERR_CUDA;
+            }
+            cudaFree(tmp);
+            if (st != SSD_OK) {
+                ssd_weight_free(w);
+                return st;
+            }
         } else {
             SSD_TRY(ssd_weight_synth(m->ctx, s.type, seed, s.tid, sd, s.cols, s.row0, s.nrows,
                                      s.col0, s.ncols, &w, (void*)m->ctx->stream));
@@ -739,7 +834,23 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     float* h_other = (h == m->h_a) ? m->h_b : m->h_a;
     // 1. QKV + RoPE with the pre-attention RMSNorm folded in. Each weight keeps its own
     // type (the reference dispatches every tensor on its dtype, compute.rs:648-675); a V of
-    // another type than Q / K gets its own launch after them.
+    // another type than Q / K gets its own launch after them. Dense (F16 / BF16 / F32)
+    // weights, at tp_size 1: norm, the three matvecs, RoPE at the device-held position.
+    if (dense_type(L.wq->type) || dense_type(L.wk->type) || dense_type(L.wv->type)) {
+        SSD_REQ(!tp && !pend.on, SSD_ERR_TYPE, "dense layer weights run at tp_size 1");
+        k_dense_norm<<<1, 1024, 0, s>>>(h, L.attn_norm, c.n_embd, c.eps, 0, m->xn);
+        SSD_CK_LAUNCH();
+        const ssd_weight* ws[3] = {L.wq, L.wk, L.wv};
+        float* ys[3] = {m->q, m->k, m->v};
+        for (int j = 0; j < 3; j++)
+            SSD_TRY(launch_matvec(m->ctx, ws[j]->type, EPI_STORE, mv_plain(ws[j], m->xn, ys[j]),
+                                  s, true));
+        const int pairs = (m->q_rows + m->kv_rows) / 2;
+        k_rope_qk<<<(pairs + 255) / 256, 256, 0, s>>>(m->q, m->q_rows, m->k, m->kv_rows,
+                                                      c.head_dim, c.theta, m->pos);
+        SSD_CK_LAUNCH();
+        nl += 5;
+    } else {
     SSD_REQ(L.wq->type == L.wk->type, SSD_ERR_TYPE, "attn_q and attn_k types differ (%d, %d)",
             L.wq->type, L.wk->type);
     const bool v_apart = L.wv->type != L.wq->type;
@@ -785,6 +896,7 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
         SSD_TRY(launch_matvec(m->ctx, L.wv->type, EPI_STORE, va, s, true));
         nl++;
     }
+    }  // quantized QKV
     // 2-3. INT8 KV append at the current position (fused) and attention over this rank's
     // KV heads
     AttnArgs at = {};
@@ -834,6 +946,23 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     // 5. gate/up + SwiGLU with the FFN RMSNorm folded in (one fused launch: one type)
     SSD_REQ(L.wg->type == L.wu->type, SSD_ERR_TYPE, "ffn_gate and ffn_up types differ (%d, %d)",
             L.wg->type, L.wu->type);
+    if (dense_type(L.wg->type)) {  // dense: the FFN norm, then the gate / up row pairs
+        SSD_REQ(!tp && !pend.on, SSD_ERR_TYPE, "dense layer weights run at tp_size 1");
+        k_dense_norm<<<1, 1024, 0, s>>>(h, L.ffn_norm, c.n_embd, c.eps, 1, m->xn);
+        SSD_CK_LAUNCH();
+        MvArgs g = {};
+        g.qs[0] = L.wg->qs;
+        g.qs[1] = L.wu->qs;
+        g.seg_rows[0] = m->ff_local;
+        g.seg_rows[1] = m->ff_local;
+        g.map = MAP_SWIGLU;
+        g.rows = 2 * m->ff_local;
+        g.cols = c.n_embd;
+        g.x = m->xn;
+        g.y = m->act;
+        SSD_TRY(launch_matvec(m->ctx, L.wg->type, EPI_SWIGLU, g, s, true));
+        nl += 2;
+    } else {
     MvArgs g = {};
     g.qs[0] = L.wg->qs;
     g.qs[1] = L.wu->qs;
@@ -860,6 +989,7 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
         h = h_other;
         h_other = (h == m->h_a) ? m->h_b : m->h_a;
     }
+    }  // quantized gate / up
     // 6. down projection (+ residual, or a partial sum for the all-reduce)
     MvArgs d = mv_plain(L.wd, m->act, h_other);
     if (tp) {
@@ -883,15 +1013,27 @@ static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl) {
     const bool use_p2p = m->p2p && tp_size(m) > 1;
     for (int l = 0; l < c.n_layers; l++) SSD_TRY(enqueue_layer(m, l, h, pend, use_p2p, s, nl));
     // logits = output * rmsnorm(h) (eps 1e-5 hard-coded at compute.rs:566), argmax
-    MvArgs a = mv_plain(m->output, h, m->logits);
-    take_pending(m, a, pend);
-    a.norm_w = m->out_norm;
-    a.eps = 1e-5f;
-    a.norm_order = 1;
-    a.argmax_key = m->key;
-    a.index_offset = m->vocab0;
-    SSD_TRY(launch_matvec(m->ctx, m->output->type, EPI_ARGMAX, a, s, true));
-    nl++;
+    if (dense_type(m->output->type)) {  // dense output (tp_size 1): norm, matvec, argmax key
+        SSD_REQ(!pend.on, SSD_ERR_TYPE, "dense output weight runs at tp_size 1");
+        k_dense_norm<<<1, 1024, 0, s>>>(h, m->out_norm, c.n_embd, 1e-5f, 1, m->xn);
+        SSD_CK_LAUNCH();
+        SSD_TRY(launch_matvec(m->ctx, m->output->type, EPI_STORE,
+                              mv_plain(m->output, m->xn, m->logits), s, true));
+        k_argmax_key<<<m->ctx->num_sms, 256, 0, s>>>(m->logits, m->vocab_local,
+                                                     (uint32_t)m->vocab0, m->key);
+        SSD_CK_LAUNCH();
+        nl += 3;
+    } else {
+        MvArgs a = mv_plain(m->output, h, m->logits);
+        take_pending(m, a, pend);
+        a.norm_w = m->out_norm;
+        a.eps = 1e-5f;
+        a.norm_order = 1;
+        a.argmax_key = m->key;
+        a.index_offset = m->vocab0;
+        SSD_TRY(launch_matvec(m->ctx, m->output->type, EPI_ARGMAX, a, s, true));
+        nl++;
+    }
     if (tp_size(m) > 1)
         SSD_NCCL(ncclAllReduce(m->key, m->key, 1, ncclUint64, ncclMax, m->comm, s));
     SSD_TRY(launch_finalize(m->key, m->token, m->pos, use_p2p ? m->ar_epoch : nullptr,
