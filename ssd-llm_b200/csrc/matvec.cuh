@@ -43,6 +43,10 @@ struct MvArgs {
     float theta;
     int position;
     const int* position_dev;  // if non-null, position is read from device memory
+    // optional (cos, sin) table of positions [0, rope_rows), head_dim / 2 pairs each, the
+    // values rope_cs gives (filled once per model); other positions compute them
+    const float2* rope_cache;
+    int rope_rows;
     unsigned long long* argmax_key;
     int index_offset;  // added to row index for ARGMAX (tensor-parallel vocab shards)
     int* status;       // device status word for bounded waits (default: the context's)

@@ -181,6 +181,8 @@ __global__ void __launch_bounds__(1024) k_bstats(const BPrepArgs p) {
     __shared__ float red[32];
     const int t = blockIdx.x, tid = threadIdx.x;
     pdl_wait();
+    // the dependent's part before its own wait only reads weights: let it launch now
+    pdl_trigger();
     const float4* x4 = reinterpret_cast<const float4*>(p.x + (size_t)t * p.ldx);
     const float4* a4 = p.x_add ? reinterpret_cast<const float4*>(p.x_add + (size_t)t * p.ldx) : nullptr;
     const int n4 = p.cols / 4;
@@ -217,7 +219,6 @@ __global__ void __launch_bounds__(1024) k_bstats(const BPrepArgs p) {
         if (tid == 0)
             p.inv[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)p.cols), p.eps)));
     }
-    pdl_trigger();
 }
 
 // ----------------------------------------------------------------------- B prep
@@ -233,6 +234,9 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kg = blockIdx.x;
     pdl_wait();
+    // k_mv_b, the dependent, streams its first weight stages before its wait: launching it
+    // now overlaps that with this kernel
+    pdl_trigger();
     // x_eff of token t, element k
     auto xe = [&](int t, int k) {
         float v = __ldcg(p.x + (size_t)t * p.ldx + k);
@@ -308,7 +312,6 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
     if constexpr (SUMX) {
         if (tid < 8 * kBN) cst[8 + tid] = xsum[tid / kBN][tid % kBN];
     }
-    pdl_trigger();
 }
 
 // ----------------------------------------------------------------------- matvec
@@ -542,7 +545,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
         if constexpr (EPI == EPI_QKV_ROPE) {
             for (int i = tid; i < kBN * (a.head_dim >> 1); i += kBRW * 32) {
                 const int t = i / (a.head_dim >> 1), pr = i % (a.head_dim >> 1);
-                rope_tab[t * 64 + pr] = rope_cs(pr, a.head_dim, a.theta, wk.pos[t]);
+                rope_tab[t * 64 + pr] = rope_pair(a, pr, wk.pos[t]);
             }
             b_bar(1, kBRW * 32);
         }

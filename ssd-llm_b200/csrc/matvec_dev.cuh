@@ -82,10 +82,18 @@ __device__ __forceinline__ float swiglu(float g, float up) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
 }
 
+// (cos, sin) of RoPE pair i at position pos: from the model's table when it covers pos (the
+// table holds rope_cs values, so both give the same bits), else computed.
+__device__ __forceinline__ float2 rope_pair(const MvArgs& a, int i, int pos) {
+    if (a.rope_cache && pos >= 0 && pos < a.rope_rows)
+        return __ldg(a.rope_cache + (size_t)pos * (a.head_dim >> 1) + i);
+    return rope_cs(i, a.head_dim, a.theta, pos);
+}
+
 // The x prologue of both kernels, run after the first weight copies are in flight and
-// the barrier is initialised: waits for the previous kernel (PDL), fills the RoPE
-// table, stages x (nc rows of 128 B, 128-byte swizzle: unit u of chunk c at slot
-// c*8 + (u ^ (c & 7))) by TMA, waits for the peers' partials (bounded), then applies
+// the barrier is initialised: waits for the previous kernel (PDL), stages x (nc rows of
+// 128 B, 128-byte swizzle: unit u of chunk c at slot c*8 + (u ^ (c & 7))) by TMA, fills
+// the RoPE pairs of this position meanwhile, waits for the peers' partials (bounded), then applies
 //   x_eff = x (+ x_add or the sum of the peers' partials), written back by CTA 0,
 //   optional RMSNorm (order 0: x * (inv * w); order 1: (x * inv) * w),
 // and hands every 16-byte unit i (chunk c, slot ph, values v) to finish(i, c, ph, v,
@@ -101,15 +109,15 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
     const bool has_add = a.x_add != nullptr || a.ar_in_n > 0, has_norm = a.norm_w != nullptr;
     float4* xs4 = reinterpret_cast<float4*>(xs);
     pdl_wait();
-    if constexpr (EPI == EPI_QKV_ROPE) {  // (cos, sin) of every pair at this position
-        const int pos = a.position_dev ? *a.position_dev : a.position;
-        for (int i = tid; i < (a.head_dim >> 1); i += NTH) rope_tab[i] = rope_cs(i, a.head_dim, a.theta, pos);
-    }
     if (tid == 0) {
         const int nbox = xrows / kVecBoxRows;
         mbar_expect_tx(bar, (uint32_t)xrows * 128u);
         for (int b = 0; b < nbox; b++)
             tma_load_2d(xs + (size_t)b * kVecBoxRows * 128, tm_x, 0, b * kVecBoxRows, bar);
+    }
+    if constexpr (EPI == EPI_QKV_ROPE) {  // (cos, sin) of every pair at this position
+        const int pos = a.position_dev ? *a.position_dev : a.position;
+        for (int i = tid; i < (a.head_dim >> 1); i += NTH) rope_tab[i] = rope_pair(a, i, pos);
     }
     if (a.ar_in_n > 0) {  // wait for every rank's partial of this call (bounded)
         // fail fast: once any wait of this context has timed out, later ones do not wait

@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
         if constexpr (EPI == EPI_QKV_ROPE) {
             const int pos = a.position_dev ? *a.position_dev : a.position;
             for (int i = r; i < (a.head_dim >> 1); i += 128)
-                rope_tab[i] = rope_cs(i, a.head_dim, a.theta, pos);
+                rope_tab[i] = rope_pair(a, i, pos);
         }
         if (a.ar_in_n > 0) {  // wait for every rank's partial of this call (bounded)
             if (warp == 0 && lane < a.ar_in_n && *(volatile int*)a.status == SSD_OK) {

@@ -111,10 +111,25 @@ __global__ void __launch_bounds__(1024) k_dense_norm(const float* x, const float
                             : __fmul_rn(__fmul_rn(x[i], inv), w[i]);
 }
 
+// (cos, sin) of every RoPE pair at every cache position, the values rope_cs gives: the QKV
+// epilogues of the decode steps read their position's row instead of evaluating the
+// double-precision power and sincos on every launch.
+__global__ void k_rope_table(float2* t, int head_dim, float theta) {
+    const int pos = blockIdx.x, half = head_dim / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x)
+        t[(size_t)pos * half + i] = rope_cs(i, head_dim, theta, pos);
+}
+static int fill_rope_table(ssd_ctx* ctx, float2* t, int rows, int head_dim, float theta) {
+    k_rope_table<<<rows, 128, 0, ctx->stream>>>(t, head_dim, theta);
+    SSD_CK_LAUNCH();
+    SSD_CK(cudaStreamSynchronize(ctx->stream));
+    return SSD_OK;
+}
+
 // RoPE on the q and k rows at the device-held position (the pair rotation of the fused
 // QKV epilogue, rope_f32_multi_head, compute.rs:482-506).
 __global__ void k_rope_qk(float* q, int q_rows, float* k, int k_rows, int head_dim, float theta,
-                          const int* pos) {
+                          const int* pos, const float2* tab, int tab_rows) {
     pdl_wait();
     const int half = head_dim / 2;
     const int t = blockIdx.x * blockDim.x + threadIdx.x;  // pair index over q then k
@@ -122,7 +137,9 @@ __global__ void k_rope_qk(float* q, int q_rows, float* k, int k_rows, int head_d
     if (t >= nq + k_rows / 2) return;
     float* x = t < nq ? q : k;
     const int pr = t < nq ? t : t - nq;  // pair within the vector
-    const float2 cs = rope_cs(pr % half, head_dim, theta, *pos);
+    const int p = *pos;
+    const float2 cs = p >= 0 && p < tab_rows ? tab[(size_t)p * half + pr % half]
+                                             : rope_cs(pr % half, head_dim, theta, p);
     float x0 = x[2 * pr], x1 = x[2 * pr + 1];
     rope_apply(x0, x1, cs);
     x[2 * pr] = x0;
@@ -201,6 +218,7 @@ struct ssd_model {
     unsigned long long* p2p_xch[kMaxPeers] = {};
     float* amax = nullptr;  // the (K, V) absmax pair max-reduced by NCCL (no peer path)
     float* xn = nullptr;    // normed input of the dense-weight stages
+    float2* rope = nullptr;  // (cos, sin) of every RoPE pair at every cache position
     void* p2p_mapped[kMaxPeers] = {};
     bool p2p = false;
     unsigned long long* ar_epoch = nullptr;  // advanced by 2 * n_layers per step
@@ -280,14 +298,17 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     const size_t o_ha = take(E), o_hb = take(E), o_q = take(m->q_rows), o_k = take(m->kv_rows),
                  o_v = take(m->kv_rows), o_attn = take(m->q_rows), o_act = take(m->ff_local),
                  o_part = take(pf), o_p1 = take(E), o_p2 = take(E), o_log = take(m->vocab_local),
-                 o_misc = take(64), o_xn = take(E);
+                 o_misc = take(64), o_xn = take(E),
+                 o_rope = take((size_t)c->kv_capacity * c->head_dim);
     if (cudaMalloc(&m->state, floats * 4) != cudaSuccess) {
         cudaGetLastError();
         delete m;
         set_error("decode state allocation failed");
         return SSD_ERR_NOMEM;
     }
-    if (zero_device(ctx, m->state, floats * 4) != SSD_OK) {
+    if (zero_device(ctx, m->state, floats * 4) != SSD_OK ||
+        fill_rope_table(ctx, reinterpret_cast<float2*>((float*)m->state + o_rope),
+                        c->kv_capacity, c->head_dim, c->theta) != SSD_OK) {
         cudaFree(m->state);
         delete m;
         return SSD_ERR_CUDA;
@@ -311,6 +332,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     m->ar_counter = reinterpret_cast<unsigned int*>(S + o_misc + 20);
     m->amax = S + o_misc + 24;
     m->xn = S + o_xn;
+    m->rope = reinterpret_cast<float2*>(S + o_rope);
     if (cudaHostAlloc(&m->pinned, 16, cudaHostAllocDefault) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->state);
@@ -847,7 +869,8 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
                                   s, true));
         const int pairs = (m->q_rows + m->kv_rows) / 2;
         k_rope_qk<<<(pairs + 255) / 256, 256, 0, s>>>(m->q, m->q_rows, m->k, m->kv_rows,
-                                                      c.head_dim, c.theta, m->pos);
+                                                      c.head_dim, c.theta, m->pos, m->rope,
+                                                      c.kv_capacity);
         SSD_CK_LAUNCH();
         nl += 5;
     } else {
@@ -882,6 +905,8 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     a.head_dim = c.head_dim;
     a.theta = c.theta;
     a.position_dev = m->pos;
+    a.rope_cache = m->rope;
+    a.rope_rows = c.kv_capacity;
     SSD_TRY(launch_matvec(m->ctx, L.wq->type, EPI_QKV_ROPE, a, s, true));
     nl++;
     if (had_pend) {
@@ -1664,6 +1689,8 @@ static int enqueue_batch_step(ssd_batch* b, cudaStream_t s, int& nl) {
         a.y_v = b->v;
         a.head_dim = c.head_dim;
         a.theta = c.theta;
+        a.rope_cache = m->rope;
+        a.rope_rows = c.kv_capacity;
         SSD_TRY(batch_mv(b, L.wq, EPI_QKV_ROPE, a, h, E, L.attn_norm, c.eps, 0, m->q_rows, s, nl));
         // attention over each slot's cache, its new K / V row appended at its position
         ssd_kv_cache kv0 = batch_kv_view(b, l, 0);
