@@ -818,22 +818,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             for (int p = 0; p < a.ar_out_n; p++)
                 for (int i = tid; i < nrow; i += NW * 32) a.ar_out[p][row0 + i] = peer_buf[i];
         }
-        // publish: every thread's peer stores are made visible system-wide, then the
-        // last CTA to finish raises this call's flag on every rank
-        __threadfence_system();
-        __syncthreads();
-        if (tid == 0) {
-            const unsigned prev = atomicAdd(a.ar_counter, 1u);
-            if (prev == gridDim.x - 1) {
-                __threadfence_system();
-                *a.ar_counter = 0u;  // zero for the next launch (stream-ordered)
-                const unsigned long long ep = *a.ar_epoch + (unsigned long long)a.ar_call + 1ull;
-                for (int p = 0; p < a.ar_out_n; p++)
-                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.ar_out_flag[p]),
-                                 "l"(ep)
-                                 : "memory");
-            }
-        }
+        peers_publish(a);  // then the last CTA raises the flags on every rank
     }
 
     if constexpr (EPI == EPI_ARGMAX) {

@@ -82,6 +82,71 @@ __device__ __forceinline__ float swiglu(float g, float up) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
 }
 
+// EPI_PEERS publication, called by every thread of the CTA after its peer stores: the
+// barrier orders all of the CTA's stores before thread 0's system-scope fence (a fence is
+// cumulative over the writes the barrier made visible to its thread), so one fence per CTA
+// does what a fence in every thread did at a fraction of the cost; the completion counter's
+// atomics between two fences carry that order to the last CTA, whose release stores raise
+// this call's flag on every rank.
+__device__ __forceinline__ void peers_publish(const MvArgs& a) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned prev = atomicAdd(a.ar_counter, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence_system();
+            *a.ar_counter = 0u;  // zero for the next launch (stream-ordered)
+            const unsigned long long ep = *a.ar_epoch + (unsigned long long)a.ar_call + 1ull;
+            for (int p = 0; p < a.ar_out_n; p++)
+                asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.ar_out_flag[p]), "l"(ep)
+                             : "memory");
+        }
+    }
+}
+
+// x''[unit] += the sum, in rank order, of the n <= NMAX vectors at in + p * cols (the ranks'
+// partials, or one added vector) for the units this thread owns (tid, tid + NTH, ...). The
+// loads of B units (B * NMAX <= 8 float4) are issued together, so a thread waits for one L2
+// round trip per B units instead of one per unit.
+template <int B, int NMAX, int NTH>
+__device__ __forceinline__ void add_partials(const float* in_f, int n, int cols, float4* xs4,
+                                             int nunits, int tid) {
+    const float4* in = reinterpret_cast<const float4*>(in_f);
+    const size_t stride = (size_t)cols / 4;
+    for (int i0 = tid; i0 < nunits; i0 += NTH * B) {
+        float4 t[B][NMAX];
+#pragma unroll
+        for (int b = 0; b < B; b++)
+            if (i0 + b * NTH < nunits)
+#pragma unroll
+                for (int p = 0; p < NMAX; p++)
+                    if (p < n) t[b][p] = __ldcg(in + p * stride + i0 + b * NTH);
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            const int i = i0 + b * NTH;
+            if (i < nunits) {
+                float4 r = t[b][0];
+#pragma unroll
+                for (int p = 1; p < NMAX; p++) {
+                    if (p < n) {
+                        r.x = __fadd_rn(r.x, t[b][p].x);
+                        r.y = __fadd_rn(r.y, t[b][p].y);
+                        r.z = __fadd_rn(r.z, t[b][p].z);
+                        r.w = __fadd_rn(r.w, t[b][p].w);
+                    }
+                }
+                const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
+                float4 v = xs4[ph];
+                v.x = __fadd_rn(v.x, r.x);
+                v.y = __fadd_rn(v.y, r.y);
+                v.z = __fadd_rn(v.z, r.z);
+                v.w = __fadd_rn(v.w, r.w);
+                xs4[ph] = v;
+            }
+        }
+    }
+}
+
 // (cos, sin) of RoPE pair i at position pos: from the model's table when it covers pos (the
 // table holds rope_cs values, so both give the same bits), else computed.
 __device__ __forceinline__ float2 rope_pair(const MvArgs& a, int i, int pos) {
@@ -108,6 +173,17 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
     constexpr int NW = NTH / 32;
     const bool has_add = a.x_add != nullptr || a.ar_in_n > 0, has_norm = a.norm_w != nullptr;
     float4* xs4 = reinterpret_cast<float4*>(xs);
+    const int nunits = nc * 8;  // 16-byte units
+    // The norm weights are weights: like the matrix they never depend on the previous
+    // kernel, so this thread's first kNwPre units load before the wait.
+    constexpr int kNwPre = 4;
+    const float4* nw4 = reinterpret_cast<const float4*>(a.norm_w);
+    float4 nwp[kNwPre];
+#pragma unroll
+    for (int j = 0; j < kNwPre; j++) {
+        nwp[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (has_norm && tid + j * NTH < nunits) nwp[j] = __ldg(nw4 + tid + j * NTH);
+    }
     pdl_wait();
     if (tid == 0) {
         const int nbox = xrows / kVecBoxRows;
@@ -140,45 +216,30 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
     const bool ok = mbar_wait(bar, 0, a.status);
     if (__syncthreads_or(!ok)) return false;  // timed out: status recorded
 
-    const int nunits = nc * 8;  // 16-byte units
     const unsigned gmask = 0xFFu << (lane & 24);
     float inv = 1.0f;
     if (has_add || has_norm) {
         const bool wb = a.x_writeback != nullptr && blockIdx.x == 0;
+        // hidden[i] += attn_output[i] (src/metal/compute.rs:547-549): the ranks' partials
+        // (summed in rank order) or one added vector, into x'' in place
+        if (has_add) {
+            const int n = a.ar_in_n;
+            if (n == 0)
+                add_partials<8, 1, NTH>(a.x_add, 1, a.cols, xs4, nunits, tid);
+            else if (n == 1)
+                add_partials<8, 1, NTH>(a.ar_in, 1, a.cols, xs4, nunits, tid);
+            else if (n == 2)
+                add_partials<4, 2, NTH>(a.ar_in, 2, a.cols, xs4, nunits, tid);
+            else if (n <= 4)
+                add_partials<2, 4, NTH>(a.ar_in, n, a.cols, xs4, nunits, tid);
+            else
+                add_partials<1, kMaxPeers, NTH>(a.ar_in, n, a.cols, xs4, nunits, tid);
+        }
         float ss = 0.0f;
-        for (int i = tid; i < nunits; i += NTH) {
+        for (int i = tid; i < nunits; i += NTH) {  // this thread's own units: no barrier needed
             const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
-            float4 v = xs4[ph];
-            if (has_add) {  // hidden[i] += attn_output[i] (src/metal/compute.rs:547-549)
-                float4 r;
-                if (a.ar_in_n > 0) {
-                    // the ranks' partials: all N loads in flight at once (one L2 round trip per
-                    // unit, not N), then summed in rank order
-                    float4 t[kMaxPeers];
-#pragma unroll
-                    for (int p = 0; p < kMaxPeers; p++)
-                        if (p < a.ar_in_n)
-                            t[p] = __ldcg(reinterpret_cast<const float4*>(a.ar_in + (size_t)p * a.cols) + i);
-                    r = t[0];
-#pragma unroll
-                    for (int p = 1; p < kMaxPeers; p++) {
-                        if (p < a.ar_in_n) {
-                            r.x = __fadd_rn(r.x, t[p].x);
-                            r.y = __fadd_rn(r.y, t[p].y);
-                            r.z = __fadd_rn(r.z, t[p].z);
-                            r.w = __fadd_rn(r.w, t[p].w);
-                        }
-                    }
-                } else {
-                    r = __ldg(reinterpret_cast<const float4*>(a.x_add) + i);
-                }
-                v.x = __fadd_rn(v.x, r.x);
-                v.y = __fadd_rn(v.y, r.y);
-                v.z = __fadd_rn(v.z, r.z);
-                v.w = __fadd_rn(v.w, r.w);
-                xs4[ph] = v;
-                if (wb) reinterpret_cast<float4*>(a.x_writeback)[i] = v;
-            }
+            const float4 v = xs4[ph];
+            if (has_add && wb) reinterpret_cast<float4*>(a.x_writeback)[i] = v;
             ss = fmaf(v.x, v.x, ss);
             ss = fmaf(v.y, v.y, ss);
             ss = fmaf(v.z, v.z, ss);
@@ -195,12 +256,10 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
             inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.cols), a.eps)));
         }
     }
-    const float4* nw4 = reinterpret_cast<const float4*>(a.norm_w);
-    for (int i = tid; i < nunits; i += NTH) {
+    auto unit = [&](int i, float4 w) {
         const int c = i >> 3, ph = c * 8 + ((i & 7) ^ (c & 7));
         float4 v = xs4[ph];
         if (has_norm) {
-            const float4 w = __ldg(nw4 + i);
             if (a.norm_order == 0) {  // x * (inv_rms * w)
                 v.x = __fmul_rn(v.x, __fmul_rn(inv, w.x));
                 v.y = __fmul_rn(v.y, __fmul_rn(inv, w.y));
@@ -214,7 +273,12 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
             }
         }
         finish(i, c, ph, v, gmask);
-    }
+    };
+#pragma unroll
+    for (int j = 0; j < kNwPre; j++)
+        if (tid + j * NTH < nunits) unit(tid + j * NTH, nwp[j]);
+    for (int i = tid + kNwPre * NTH; i < nunits; i += NTH)
+        unit(i, has_norm ? __ldg(nw4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f));
     __syncthreads();
     pdl_trigger();
     return true;

@@ -683,21 +683,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
     }
 
     if constexpr (EPI == EPI_PEERS) {
-        // publish: every thread's peer stores visible system-wide, then the last CTA to
-        // finish raises this call's flag on every rank
-        __threadfence_system();
-        __syncthreads();
-        if (tid == 0) {
-            const unsigned prev = atomicAdd(a.ar_counter, 1u);
-            if (prev == gridDim.x - 1) {
-                __threadfence_system();
-                *a.ar_counter = 0u;
-                const unsigned long long ep = *a.ar_epoch + (unsigned long long)a.ar_call + 1ull;
-                for (int p = 0; p < a.ar_out_n; p++)
-                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.ar_out_flag[p]), "l"(ep)
-                                 : "memory");
-            }
-        }
+        peers_publish(a);  // then the last CTA raises the flags on every rank
     }
     tc_fence_before();
     __syncthreads();
