@@ -233,6 +233,10 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
     __shared__ float sxs[8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kg = blockIdx.x;
+    const int c = warp;  // block within the k-group
+    const int k = kg * 256 + c * 32 + lane;
+    // the norm weight is a weight (never written by the previous kernel): load it first
+    const float w = p.norm_w ? __ldg(p.norm_w + k) : 0.0f;
     pdl_wait();
     // k_mv_b, the dependent, streams its first weight stages before its wait: launching it
     // now overlaps that with this kernel
@@ -243,21 +247,18 @@ __global__ void __launch_bounds__(256) k_bprep(const BPrepArgs p) {
         if (p.x_add) v = __fadd_rn(v, __ldcg(p.x_add + (size_t)t * p.ldx + k));
         return v;
     };
-    if (p.norm_w) {
-        if (tid < kBN) inv_s[tid] = __ldcg(p.inv + tid);
-        __syncthreads();
-    }
-    const int c = warp;  // block within the k-group
-    const int k = kg * 256 + c * 32 + lane;
     float v[kBN];
 #pragma unroll
     for (int t = 0; t < kBN; t++) v[t] = xe(t, k);
+    if (p.norm_w) {  // the tokens' inverse RMS, loaded while the x loads are in flight
+        if (tid < kBN) inv_s[tid] = __ldcg(p.inv + tid);
+        __syncthreads();
+    }
     if (p.x_writeback) {
 #pragma unroll
         for (int t = 0; t < kBN; t++) p.x_writeback[(size_t)t * p.ldx + k] = v[t];
     }
     if (p.norm_w) {
-        const float w = __ldg(p.norm_w + k);
 #pragma unroll
         for (int t = 0; t < kBN; t++)
             v[t] = p.norm_order == 0 ? __fmul_rn(v[t], __fmul_rn(inv_s[t], w))
