@@ -538,6 +538,40 @@ int ssd_gguf_model_config(const ssd_gguf* g, int kv_capacity, int tp_rank, int t
  * this rank's shard, HBM-resident (the layer lookups of transformer.rs:171-180, :557). */
 int ssd_model_load_gguf(ssd_model* m, const ssd_gguf* g, int n_layers);
 
+/* ---------------------------------------------------- SSD -> HBM streaming tier
+ * For models whose layers do not all fit the HBM budget: the layer matrices stay in the GGUF
+ * file and pass through n_slots = hbm_budget / slot_bytes HBM layer slots. */
+typedef struct ssd_stream ssd_stream;
+/* LayerCache's CacheStats (src/model/cache.rs: hits, misses, evictions, prefetch_hits) plus
+ * the loads made, the file bytes read, and the slot count and size the budget bought. */
+typedef struct {
+    uint64_t hits, misses, evictions, prefetch_hits, loads, bytes_read;
+    int n_slots;
+    size_t slot_bytes;
+} ssd_stream_stats;
+/* SsdStreamer::new + Prefetcher::new(LookAhead(lookahead)) + LayerCache::new(budget)
+ * (src/ssd/streamer.rs:19-32, src/ssd/prefetch.rs:24-31, src/model/cache.rs): opens the
+ * file, loads every layer's attn_norm / ffn_norm and token_embd, output_norm, output
+ * (token_embd if absent) into the model, and allocates the slots (each sized for the
+ * largest layer's seven matrices in the library layout), two pinned staging buffers and a
+ * copy stream. The model (from ssd_gguf_model_config of the same file, tp_size 1) must
+ * not hold layer matrices of its own. SSD_ERR_NOMEM if the budget is below one layer. */
+int ssd_stream_open(ssd_model* m, const char* gguf_path, size_t hbm_budget, int lookahead,
+                    ssd_stream** out);
+/* LayerCache::pin (src/model/cache.rs): loads the layer now if needed and never evicts it;
+ * refused (SSD_ERR_NOMEM) if it would leave no slot for the other layers. */
+int ssd_stream_pin(ssd_stream* s, int layer);
+/* ssd_model_decode_token with streamed layers (the layer loop of forward_pass with
+ * layer_cache.get / streamer.load_layer on a miss and prefetcher.on_layer_start before each
+ * layer, src/inference/transformer.rs:151-163): eager launches, each layer's kernels after
+ * its slot is loaded; after them the next `lookahead` layers are loaded. */
+int ssd_stream_decode_token(ssd_stream* s, int32_t token_in, int32_t* token_out);
+/* Counters since ssd_stream_open (LayerCache::stats, src/model/cache.rs). */
+int ssd_stream_stats_get(const ssd_stream* s, ssd_stream_stats* out);
+/* Waits for the model's stream and frees the slots, staging buffers and copy stream; the
+ * model stays usable for ssd_model_free. No reference counterpart beyond Drop. */
+int ssd_stream_close(ssd_stream* s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -416,6 +416,21 @@ int encode_bytes_map(CUtensorMap* map, const void* ptr, uint64_t row_bytes, uint
 constexpr int kVecBoxRows = 32;
 // Largest grid of the tensor-core matvec (matvec_i8.cu); sizes the split-K scratch of a weight.
 constexpr int kI8MaxGrid = 160;
+// Device layout of one weight (library layout, see ssd_weight): the payload, the scales,
+// and the tensor-core kernel's split-K counters and partial rows, each 256-byte aligned.
+struct WeightLayout {
+    size_t qs_pad = 0, meta_bytes = 0, meta_pad = 0, counter_bytes = 0, partial_bytes = 0;
+    size_t total = 0;  // bytes from the weight's base (256-byte aligned)
+    bool fix = false;  // carries split-K scratch (the counters must start at zero)
+};
+int weight_layout(int type, int rows, int cols, WeightLayout* out);
+// Points *w (caller-owned; base left null, so ssd_weight_free does not free it) at the
+// regions of `L` from p (256-byte aligned device memory of L.total bytes).
+void carve_weight(ssd_ctx* ctx, int type, int rows, int cols, const WeightLayout& L, uint8_t* p,
+                  ssd_weight* w);
+// The reference's raw bytes (already on the device) into w's layout on stream s: dense and
+// low-bit types as they are, the others through the repack kernel.
+int upload_raw(ssd_weight* w, const void* raw_dev, cudaStream_t s);
 int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out);
 int ensure_scratch(ssd_ctx* ctx, size_t bytes);
 

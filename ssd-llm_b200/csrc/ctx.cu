@@ -580,8 +580,7 @@ extern "C" size_t ssd_row_bytes(int type, int64_t cols) {
 }
 
 namespace ssd {
-int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
-    SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
+int weight_layout(int type, int rows, int cols, WeightLayout* out) {
     SSD_REQ(type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 || type == SSD_TYPE_Q4_K ||
                 type == SSD_TYPE_Q5_K || type == SSD_TYPE_Q6_K || type == SSD_TYPE_Q8_K ||
                 type == SSD_TYPE_F16 || type == SSD_TYPE_BF16 || type == SSD_TYPE_F32 ||
@@ -621,42 +620,71 @@ int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
         qs_bytes = (size_t)rows * cols * type_block_bytes(type);
         meta_bytes = 0;
     }
-    size_t qs_pad = (qs_bytes + 255) & ~(size_t)255;
-    size_t meta_pad = (meta_bytes + 255) & ~(size_t)255;
+    WeightLayout L;
+    L.qs_pad = (qs_bytes + 255) & ~(size_t)255;
+    L.meta_bytes = meta_bytes;
+    L.meta_pad = (meta_bytes + 255) & ~(size_t)255;
     // split-K scratch of the tensor-core matvec (quantized types): counters for up to
     // 2 * ceil(rows / 64) + 16 row tiles (a fused QKV or gate/up launch uses the first
     // weight's), partial rows for kI8MaxGrid CTAs
-    const bool fix = type_block(type) > 1 && !is_lowbit(type);
-    const size_t n_counters = fix ? 2 * (((size_t)rows + 63) / 64) + 16 : 0;
-    const size_t counter_bytes = (n_counters * 4 + 255) & ~(size_t)255;
-    const size_t partial_bytes = fix ? (size_t)2 * kI8MaxGrid * 128 * 4 : 0;
-    size_t total = qs_pad + meta_pad + counter_bytes + partial_bytes + 256;
-    void* p = nullptr;
-    if (cudaMalloc(&p, total) != cudaSuccess) {
-        cudaGetLastError();
-        set_error("weight allocation of %zu bytes failed", total);
-        return SSD_ERR_NOMEM;
-    }
-    ssd_weight* w = new ssd_weight();
+    L.fix = type_block(type) > 1 && !is_lowbit(type);
+    const size_t n_counters = L.fix ? 2 * (((size_t)rows + 63) / 64) + 16 : 0;
+    L.counter_bytes = (n_counters * 4 + 255) & ~(size_t)255;
+    L.partial_bytes = L.fix ? (size_t)2 * kI8MaxGrid * 128 * 4 : 0;
+    L.total = L.qs_pad + L.meta_pad + L.counter_bytes + L.partial_bytes + 256;
+    *out = L;
+    return SSD_OK;
+}
+
+void carve_weight(ssd_ctx* ctx, int type, int rows, int cols, const WeightLayout& L, uint8_t* p,
+                  ssd_weight* w) {
+    *w = ssd_weight();
     w->ctx = ctx;
     w->type = type;
     w->rows = rows;
     w->cols = cols;
-    w->base = p;
-    w->alloc_bytes = total;
-    w->qs = (uint8_t*)p;
-    w->meta = meta_bytes ? (uint8_t*)p + qs_pad : nullptr;
-    if (fix) {
-        uint8_t* f = (uint8_t*)p + qs_pad + meta_pad;
-        if (zero_device(ctx, f, counter_bytes) != SSD_OK) {
-            cudaGetLastError();
-            cudaFree(p);
-            delete w;
-            set_error("weight scratch initialisation failed");
-            return SSD_ERR_CUDA;
-        }
+    w->alloc_bytes = L.total;
+    w->qs = p;
+    w->meta = L.meta_bytes ? p + L.qs_pad : nullptr;
+    if (L.fix) {
+        uint8_t* f = p + L.qs_pad + L.meta_pad;
         w->fix_counter = reinterpret_cast<unsigned int*>(f);
-        w->fix_partial = reinterpret_cast<float*>(f + counter_bytes);
+        w->fix_partial = reinterpret_cast<float*>(f + L.counter_bytes);
+    }
+}
+
+int upload_raw(ssd_weight* w, const void* raw_dev, cudaStream_t s) {
+    const size_t bytes = ssd_row_bytes(w->type, w->cols) * (size_t)w->rows;
+    if (type_block(w->type) == 1 || is_lowbit(w->type)) {  // dense / low-bit: the bytes as they are
+        SSD_CK(cudaMemcpyAsync(w->qs, raw_dev, bytes, cudaMemcpyDeviceToDevice, s));
+    } else {
+        int64_t nb = (int64_t)w->rows * (w->cols / type_block(w->type));
+        k_repack<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>((const uint8_t*)raw_dev, w->type,
+                                                              nb, w->qs, w->meta);
+        SSD_REQ(cudaGetLastError() == cudaSuccess, SSD_ERR_CUDA, "repack launch failed");
+    }
+    return SSD_OK;
+}
+
+int alloc_weight(ssd_ctx* ctx, int type, int rows, int cols, ssd_weight** out) {
+    SSD_REQ(out != nullptr, SSD_ERR_ARG, "null out");
+    WeightLayout L;
+    SSD_TRY(weight_layout(type, rows, cols, &L));
+    void* p = nullptr;
+    if (cudaMalloc(&p, L.total) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("weight allocation of %zu bytes failed", L.total);
+        return SSD_ERR_NOMEM;
+    }
+    ssd_weight* w = new ssd_weight();
+    carve_weight(ctx, type, rows, cols, L, (uint8_t*)p, w);
+    w->base = p;
+    if (L.fix && zero_device(ctx, w->fix_counter, L.counter_bytes) != SSD_OK) {
+        cudaGetLastError();
+        cudaFree(p);
+        delete w;
+        set_error("weight scratch initialisation failed");
+        return SSD_ERR_CUDA;
     }
     *out = w;
     return SSD_OK;
@@ -673,21 +701,10 @@ extern "C" int ssd_weight_upload_device(ssd_ctx* ctx, const void* raw_dev, size_
             "got %zu bytes, %dx%d of type %d needs %zu", bytes, rows, cols, type, need);
     ssd_weight* w = nullptr;
     SSD_TRY(alloc_weight(ctx, type, rows, cols, &w));
-    cudaStream_t s = pick_stream(ctx, stream);
-    if (type_block(type) == 1 || is_lowbit(type)) {  // dense / low-bit: the bytes as they are
-        if (cudaMemcpyAsync(w->qs, raw_dev, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
-            ssd_weight_free(w);
-            SSD_CK(cudaGetLastError());
-        }
-    } else {
-        int64_t nb = (int64_t)rows * (cols / type_block(type));
-        k_repack<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>((const uint8_t*)raw_dev, type, nb,
-                                                              w->qs, w->meta);
-        if (cudaGetLastError() != cudaSuccess) {
-            ssd_weight_free(w);
-            set_error("repack launch failed");
-            return SSD_ERR_CUDA;
-        }
+    const int st = upload_raw(w, raw_dev, pick_stream(ctx, stream));
+    if (st != SSD_OK) {
+        ssd_weight_free(w);
+        return st;
     }
     *out = w;
     return SSD_OK;

@@ -31,6 +31,7 @@
 #include "matvec.cuh"
 #include "matvec_b.cuh"
 #include "matvec_dev.cuh"
+#include "model.cuh"
 #include "ops.cuh"
 
 #define SSD_NCCL(call)                                                                \
@@ -1029,14 +1030,29 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
 }
 
 // Full decode step: embed -> layers -> norm + logits + argmax -> finalize.
-static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl) {
+static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl, const LayerHooks* hk = nullptr) {
     const auto& c = m->cfg;
     SSD_TRY(launch_embed(m->tok_embd, m->token, m->h_a, s, true));
     nl++;
     float* h = m->h_a;
     Pending pend;
     const bool use_p2p = m->p2p && tp_size(m) > 1;
-    for (int l = 0; l < c.n_layers; l++) SSD_TRY(enqueue_layer(m, l, h, pend, use_p2p, s, nl));
+    for (int l = 0; l < c.n_layers; l++) {
+        if (!hk) {
+            SSD_TRY(enqueue_layer(m, l, h, pend, use_p2p, s, nl));
+            continue;
+        }
+        // streamed matrices: bound for this layer's enqueue only (the kernels take the
+        // pointers by value), so the model never owns them
+        ssd_weight* const* w = nullptr;
+        SSD_TRY(hk->acquire(hk->user, l, s, w));
+        Layer& L = m->layers[l];
+        L.wq = w[0], L.wk = w[1], L.wv = w[2], L.wo = w[3], L.wg = w[4], L.wu = w[5], L.wd = w[6];
+        const int st = enqueue_layer(m, l, h, pend, use_p2p, s, nl);
+        L.wq = L.wk = L.wv = L.wo = L.wg = L.wu = L.wd = nullptr;
+        SSD_TRY(st);
+        SSD_TRY(hk->release(hk->user, l, s));
+    }
     // logits = output * rmsnorm(h) (eps 1e-5 hard-coded at compute.rs:566), argmax
     if (dense_type(m->output->type)) {  // dense output (tp_size 1): norm, matvec, argmax key
         SSD_REQ(!pend.on, SSD_ERR_TYPE, "dense output weight runs at tp_size 1");
@@ -1115,6 +1131,34 @@ extern "C" int ssd_model_decode_token(ssd_model* m, int32_t token_in, int32_t* t
     *token_out = m->pinned[1];
     return SSD_OK;
 }
+
+namespace ssd {
+ssd_ctx* model_ctx(const ssd_model* m) { return m->ctx; }
+const ssd_model_config& model_cfg(const ssd_model* m) { return m->cfg; }
+
+int model_decode_token_hooked(ssd_model* m, int32_t token_in, int32_t* token_out,
+                              const LayerHooks& hk) {
+    SSD_REQ(m && token_out, SSD_ERR_ARG, "null argument");
+    SSD_TRY(check_ctx(m->ctx));
+    SSD_REQ(tp_size(m) == 1, SSD_ERR_ARG, "the streaming tier runs at tp_size 1");
+    SSD_REQ(token_in >= 0 && token_in < m->cfg.vocab, SSD_ERR_ARG, "token %d outside vocab",
+            token_in);
+    for (int l = 0; l < m->cfg.n_layers; l++)
+        SSD_REQ(m->layers[l].attn_norm && m->layers[l].ffn_norm, SSD_ERR_STATE,
+                "layer %d norms unset", l);
+    SSD_REQ(m->tok_embd && m->output && m->out_norm, SSD_ERR_STATE, "global tensors unset");
+    cudaStream_t s = m->ctx->stream;
+    m->pinned[0] = token_in;
+    SSD_CK(cudaMemcpyAsync(m->token, &m->pinned[0], 4, cudaMemcpyHostToDevice, s));
+    int nl = 0;
+    SSD_TRY(enqueue_step(m, s, nl, &hk));
+    m->launches = nl;
+    SSD_CK(cudaMemcpyAsync(&m->pinned[1], m->token, 4, cudaMemcpyDeviceToHost, s));
+    SSD_CK(cudaStreamSynchronize(s));
+    *token_out = m->pinned[1];
+    return SSD_OK;
+}
+}  // namespace ssd
 
 extern "C" int ssd_model_layer_step(ssd_model* m, int layer) {
     SSD_REQ(m != nullptr, SSD_ERR_ARG, "null model");

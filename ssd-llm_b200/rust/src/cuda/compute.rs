@@ -312,6 +312,59 @@ impl Drop for CudaModel {
     }
 }
 
+/// SSD -> HBM streaming tier (SsdStreamer + Prefetcher + LayerCache, src/ssd/streamer.rs,
+/// src/ssd/prefetch.rs, src/model/cache.rs): a model whose layer matrices stay in the GGUF
+/// file and pass through `hbm_budget` bytes of HBM layer slots, `lookahead` layers ahead.
+pub struct CudaStream {
+    s: *mut ffi::SsdStream,
+    _model: CudaModel,
+}
+
+unsafe impl Send for CudaStream {}
+
+impl CudaStream {
+    pub fn open(cc: &CudaCompute, path: &str, kv_capacity: i32, hbm_budget: usize,
+                lookahead: i32) -> Self {
+        let p = CString::new(path).expect("path");
+        let mut g = ptr::null_mut();
+        check(unsafe { ffi::ssd_gguf_open(p.as_ptr(), &mut g) });
+        let mut cfg = ffi::SsdModelConfig::default();
+        let st = unsafe { ffi::ssd_gguf_model_config(g, kv_capacity, 0, 1, &mut cfg) };
+        unsafe { ffi::ssd_gguf_close(g) };
+        check(st);
+        let mut m = ptr::null_mut();
+        check(unsafe { ffi::ssd_model_create(cc.raw(), &cfg, &mut m) });
+        let model = CudaModel { m };
+        let mut s = ptr::null_mut();
+        check(unsafe { ffi::ssd_stream_open(m, p.as_ptr(), hbm_budget, lookahead, &mut s) });
+        Self { s, _model: model }
+    }
+
+    /// LayerCache::pin: the layer stays in HBM.
+    pub fn pin(&mut self, layer: i32) {
+        check(unsafe { ffi::ssd_stream_pin(self.s, layer) });
+    }
+
+    /// One greedy decode step with streamed layers.
+    pub fn decode_token(&mut self, token: i32) -> i32 {
+        let mut out = 0i32;
+        check(unsafe { ffi::ssd_stream_decode_token(self.s, token, &mut out) });
+        out
+    }
+
+    pub fn stats(&self) -> ffi::SsdStreamStats {
+        let mut st = ffi::SsdStreamStats::default();
+        check(unsafe { ffi::ssd_stream_stats_get(self.s, &mut st) });
+        st
+    }
+}
+
+impl Drop for CudaStream {
+    fn drop(&mut self) {
+        unsafe { ffi::ssd_stream_close(self.s) };
+    }
+}
+
 /// Continuous batch (BatchScheduler::step, src/inference/batch_scheduler.rs:149-403): up
 /// to `capacity` sequences decode together, each weight byte streamed once per step for all
 /// of them; a slot joins by setting its position and leaves by being ignored.

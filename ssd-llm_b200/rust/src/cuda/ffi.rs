@@ -35,6 +35,24 @@ pub struct SsdBatch {
 pub struct SsdGguf {
     _p: [u8; 0],
 }
+#[repr(C)]
+pub struct SsdStream {
+    _p: [u8; 0],
+}
+
+/// `ssd_stream_stats`: LayerCache's counters plus the loads, file bytes read and slots.
+#[repr(C)]
+#[derive(Clone, Copy, Debug, Default)]
+pub struct SsdStreamStats {
+    pub hits: u64,
+    pub misses: u64,
+    pub evictions: u64,
+    pub prefetch_hits: u64,
+    pub loads: u64,
+    pub bytes_read: u64,
+    pub n_slots: c_int,
+    pub slot_bytes: usize,
+}
 
 /// `ssd_model_config`: the decode engine's shape (layer weights in one quantized type).
 #[repr(C)]
@@ -636,4 +654,17 @@ extern "C" {
         cfg: *mut SsdModelConfig,
     ) -> c_int;
     pub fn ssd_model_load_gguf(m: *mut SsdModel, g: *const SsdGguf, n_layers: c_int) -> c_int;
+
+    // SSD -> HBM streaming tier (src/ssd/streamer.rs, src/ssd/prefetch.rs, src/model/cache.rs)
+    pub fn ssd_stream_open(
+        m: *mut SsdModel,
+        gguf_path: *const c_char,
+        hbm_budget: usize,
+        lookahead: c_int,
+        out: *mut *mut SsdStream,
+    ) -> c_int;
+    pub fn ssd_stream_pin(s: *mut SsdStream, layer: c_int) -> c_int;
+    pub fn ssd_stream_decode_token(s: *mut SsdStream, token_in: i32, token_out: *mut i32) -> c_int;
+    pub fn ssd_stream_stats_get(s: *const SsdStream, out: *mut SsdStreamStats) -> c_int;
+    pub fn ssd_stream_close(s: *mut SsdStream) -> c_int;
 }

@@ -42,6 +42,12 @@ class ModelConfig(ctypes.Structure):
         ("tp_size", ctypes.c_int)]
 
 
+class StreamStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "hits", "misses", "evictions", "prefetch_hits", "loads", "bytes_read")] + [
+        ("n_slots", ctypes.c_int), ("slot_bytes", ctypes.c_size_t)]
+
+
 _u32p = ctypes.POINTER(ctypes.c_uint32)
 _u64p = ctypes.POINTER(ctypes.c_uint64)
 _ip = ctypes.POINTER(ctypes.c_int)
@@ -156,6 +162,13 @@ _SIGS = {
     "ssd_gguf_model_config": ([_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                ctypes.POINTER(ModelConfig)], ctypes.c_int),
     "ssd_model_load_gguf": ([_vp, _vp, ctypes.c_int], ctypes.c_int),
+    "ssd_stream_open": ([_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int,
+                         ctypes.POINTER(_vp)], ctypes.c_int),
+    "ssd_stream_pin": ([_vp, ctypes.c_int], ctypes.c_int),
+    "ssd_stream_decode_token": ([_vp, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)],
+                                ctypes.c_int),
+    "ssd_stream_stats_get": ([_vp, ctypes.POINTER(StreamStats)], ctypes.c_int),
+    "ssd_stream_close": ([_vp], ctypes.c_int),
     "ssd_matvec_peer_input": ([_vp, _vp, _vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int, _vp,
                                _vp], ctypes.c_int),
     "ssd_batch_create": ([_vp, ctypes.c_int, ctypes.POINTER(_vp)], ctypes.c_int),
@@ -428,6 +441,37 @@ class KvCache:
     def free(self):
         if self.h:
             lib().ssd_kv_free(self.h)
+            self.h = None
+
+
+class Stream:
+    """SSD -> HBM streaming tier over a Model whose layer matrices stay in a GGUF file
+    (SsdStreamer + Prefetcher(LookAhead) + LayerCache, src/ssd/streamer.rs:34-80,
+    src/ssd/prefetch.rs:24-67, src/model/cache.rs): hbm_budget bytes of layer slots."""
+
+    def __init__(self, model, path: str, hbm_budget: int, lookahead: int = 1):
+        self.h = None
+        h = _vp()
+        check(lib().ssd_stream_open(model.h, os.fsencode(path), hbm_budget, lookahead,
+                                    ctypes.byref(h)))
+        self.h, self.model = h, model
+
+    def pin(self, layer: int):
+        check(lib().ssd_stream_pin(self.h, layer))
+
+    def decode_token(self, token: int) -> int:
+        out = ctypes.c_int32()
+        check(lib().ssd_stream_decode_token(self.h, token, ctypes.byref(out)))
+        return out.value
+
+    def stats(self) -> dict:
+        st = StreamStats()
+        check(lib().ssd_stream_stats_get(self.h, ctypes.byref(st)))
+        return {n: getattr(st, n) for n, _ in StreamStats._fields_}
+
+    def close(self):
+        if self.h:
+            check(lib().ssd_stream_close(self.h))
             self.h = None
 
 

@@ -130,7 +130,8 @@ _RUST_BASE = {"c_int": "int", "c_float": "float", "usize": "size_t", "i64": "int
               "u8": "uint8_t", "i8": "int8_t", "c_void": "void", "c_char": "char",
               "SsdCtx": "ssd_ctx", "SsdWeight": "ssd_weight", "SsdKvCache": "ssd_kv_cache",
               "SsdModel": "ssd_model", "SsdGguf": "ssd_gguf", "SsdBatch": "ssd_batch",
-              "SsdModelConfig": "ssd_model_config"}
+              "SsdModelConfig": "ssd_model_config", "SsdStream": "ssd_stream",
+              "SsdStreamStats": "ssd_stream_stats"}
 
 
 def _rust_params():
