@@ -643,6 +643,104 @@ def case_decode_b16_2l(ctx, torch, ssdllm, peak):
         m.free()
 
 
+def _write_gguf_q4_0(path, n_layers, E, n_head, n_head_kv, F, vocab, seed=0):
+    """A Llama-shaped GGUF file of synthetic Q4_0 blocks (random nibbles, f16 scales in
+    [0.001, 0.003)) written tensor by tensor: the layout GgufFile::open reads
+    (src/model/gguf.rs:233-315), alignment 32, ne0 = columns first."""
+    import struct
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    hd = E // n_head
+    kvd = n_head_kv * hd
+    mats = [("attn_q", E, E), ("attn_k", kvd, E), ("attn_v", kvd, E), ("attn_output", E, E),
+            ("ffn_gate", F, E), ("ffn_up", F, E), ("ffn_down", E, F)]
+    tensors = [("token_embd.weight", [E, vocab], Q4_0), ("output_norm.weight", [E], 0),
+               ("output.weight", [E, vocab], Q4_0)]
+    for l in range(n_layers):
+        tensors += [(f"blk.{l}.attn_norm.weight", [E], 0), (f"blk.{l}.ffn_norm.weight", [E], 0)]
+        tensors += [(f"blk.{l}.{n}.weight", [c, r], Q4_0) for n, r, c in mats]
+    size = lambda dims, t: (dims[0] * 4 if t == 0 else
+                            (dims[0] // 32) * 18 * (dims[1] if len(dims) > 1 else 1))
+    S = lambda x: struct.pack("<Q", len(x)) + x.encode()
+    md = [("general.architecture", 8, "llama"), ("llama.block_count", 4, n_layers),
+          ("llama.embedding_length", 4, E), ("llama.feed_forward_length", 4, F),
+          ("llama.attention.head_count", 4, n_head),
+          ("llama.attention.head_count_kv", 4, n_head_kv)]
+    hdr = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(md)))
+    for k, t, v in md:
+        hdr += S(k) + struct.pack("<I", t) + (S(v) if t == 8 else struct.pack("<I", v))
+    off = 0
+    for name, dims, t in tensors:
+        hdr += S(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        hdr += struct.pack("<IQ", t, off)
+        off = (off + size(dims, t) + 31) // 32 * 32
+    hdr += b"\0" * ((-len(hdr)) % 32)
+    with open(path, "wb") as f:
+        f.write(hdr)
+        pos = 0
+        for name, dims, t in tensors:
+            n = size(dims, t)
+            if t == 0:
+                data = (1 + 0.1 * rng.standard_normal(dims[0])).astype(np.float32).tobytes()
+            else:
+                blk = rng.integers(0, 256, size=(n // 18, 18), dtype=np.uint8)
+                d = rng.uniform(0.001, 0.003, n // 18).astype(np.float16)
+                blk[:, :2] = d.view(np.uint8).reshape(-1, 2)
+                data = blk.tobytes()
+            f.write(data)
+            pos += n
+            pad = (-pos) % 32
+            f.write(b"\0" * pad)
+            pos += pad
+
+
+def case_stream_7b(ctx, torch, ssdllm, peak, slots=8, lookahead=2, tokens=6):
+    """SSD -> HBM streaming tier (ssd_stream_*) on a Llama-2-7B-shaped Q4_0 model (32 layers,
+    3.6 GB of layer matrices) written as a GGUF file to the local disk, decoded with an HBM
+    budget of `slots` layer slots and `lookahead` layers ahead: every layer is read again each
+    token (LRU over 32 layers with 8 slots), so tokens/s x layer bytes is the file -> pinned
+    host -> HBM rate. The file was just written, so the reads come from the host page cache:
+    this times the host-to-HBM path, not a disk. Host clock over `tokens` tokens after one."""
+    import tempfile
+    d = tempfile.mkdtemp(prefix="ssd_stream_")
+    path = os.path.join(d, "llama7b_q4_0.gguf")
+    try:
+        _write_gguf_q4_0(path, 32, 4096, 32, 32, 11008, 32000)
+        cfg = ssdllm.GgufFile(path).model_config(kv_capacity=64)
+        m = ssdllm.Model(ctx, **cfg)
+        try:
+            probe = ssdllm.Stream(m, path, 1 << 40, 0)
+            slot_bytes = probe.stats()["slot_bytes"]
+            probe.close()
+            st = ssdllm.Stream(m, path, slots * slot_bytes, lookahead)
+            try:
+                m.set_position(0)
+                t = st.decode_token(1)
+                s0 = st.stats()
+                h0 = time.perf_counter()
+                for _ in range(tokens):
+                    t = st.decode_token(t)
+                dt = time.perf_counter() - h0
+                s1 = st.stats()
+            finally:
+                st.close()
+        finally:
+            m.free()
+        moved = s1["bytes_read"] - s0["bytes_read"]
+        return {"workload": "llama7b_q4_0_streamed", "layers": 32, "hbm_slots": slots,
+                "lookahead": lookahead, "slot_bytes": slot_bytes,
+                "layer_bytes_per_token": moved // tokens,
+                "tokens_per_s": round(tokens / dt, 3),
+                "stream_gbs": round(moved / dt / 1e9, 2),
+                "loads_per_token": (s1["loads"] - s0["loads"]) / tokens,
+                "prefetch_hits": s1["prefetch_hits"] - s0["prefetch_hits"],
+                "source": "host page cache (file just written)"}
+    finally:
+        if os.path.exists(path):
+            os.remove(path)
+        os.rmdir(d)
+
+
 def measured_tensor_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -732,11 +830,13 @@ CASES = {
     "mv_shapes_70b": case_mv_shapes,
     "decode_b16_70b": case_decode_b16_70b,
     "decode_b16_2l": case_decode_b16_2l,
+    "stream_7b_q4_0": case_stream_7b,
 }
 # measured on every default run (mv_shapes_70b, a kernel-selection study, only by --case;
 # decode_b16_70b is measured on the headline run's own model; decode_b16_2l is the profiler's
-# small case)
-DEFAULT_CASES = [n for n in CASES if n not in ("mv_shapes_70b", "decode_b16_70b", "decode_b16_2l")]
+# small case; stream_7b_q4_0 writes a 3.7 GB file, only by --case)
+DEFAULT_CASES = [n for n in CASES if n not in ("mv_shapes_70b", "decode_b16_70b", "decode_b16_2l",
+                                                "stream_7b_q4_0")]
 
 
 def run_cases(names, peak):

@@ -8,8 +8,8 @@
 // (src/ssd/prefetch.rs:24-67) looks `LookAhead(n)` layers ahead (madvise WILLNEED) before
 // each layer runs (transformer.rs:151-163). Here the cache is HBM: n_slots = budget / slot
 // bytes device slots, each sized for the largest layer in the library's weight layout.
-//  * A miss reads the layer's seven matrices from the file (pread into one of two pinned host
-//    buffers), copies them to the device on a copy stream and repacks them into the slot
+//  * A miss reads the layer's seven matrices from the file (pread, up to 8 threads per tensor,
+//    into one of two pinned host buffers), copies them to the device on a copy stream and repacks them into the slot
 //    (the same repack as ssd_weight_upload); the layer's kernels are enqueued once the
 //    slot's `ready` event has completed.
 //  * After a layer's kernels are enqueued, the next `lookahead` layers are loaded the same way
@@ -27,8 +27,10 @@
 #include <fcntl.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <array>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "model.cuh"
@@ -94,6 +96,26 @@ int read_at(int fd, void* dst, size_t n, uint64_t off) {
     return SSD_OK;
 }
 
+// The same from up to 8 host threads for large tensors (page-cache copies and NVMe queues
+// both scale with readers).
+int read_parallel(int fd, void* dst, size_t n, uint64_t off) {
+    constexpr size_t kChunk = (size_t)4 << 20;
+    const int k = (int)std::min<size_t>(8, n / kChunk);
+    if (k < 2) return read_at(fd, dst, n, off);
+    std::vector<std::thread> th;
+    std::vector<int> st(k, SSD_OK);
+    const size_t per = (n + k - 1) / k;
+    for (int i = 0; i < k; i++) {
+        const size_t a = (size_t)i * per, len = std::min(per, n - a);
+        th.emplace_back([&, i, a, len] { st[i] = read_at(fd, (uint8_t*)dst + a, len, off + a); });
+    }
+    for (auto& t : th) t.join();
+    for (int i = 0; i < k; i++)  // errors are recorded per thread: restate it on this one
+        SSD_REQ(st[i] == SSD_OK, st[i], "short read of the model file at offset %llu",
+                (unsigned long long)(off + (size_t)i * per));
+    return SSD_OK;
+}
+
 // Layer l's matrices into slot `si` (after its previous layer's kernels are done).
 int load_layer(ssd_stream* S, int l, int si) {
     Slot& sl = S->slots[si];
@@ -113,7 +135,7 @@ int load_layer(ssd_stream* S, int l, int si) {
         const int b = S->next_host;
         S->next_host ^= 1;
         SSD_CK(cudaEventSynchronize(S->host_free[b]));  // its last copy has left the buffer
-        SSD_TRY(read_at(S->fd, S->host[b], t.raw, t.file_off));
+        SSD_TRY(read_parallel(S->fd, S->host[b], t.raw, t.file_off));
         const bool as_is = type_block(t.type) == 1 || is_lowbit(t.type);
         SSD_CK(cudaMemcpyAsync(as_is ? (void*)sl.w[j].qs : S->raw_dev, S->host[b], t.raw,
                                cudaMemcpyHostToDevice, S->copy));
