@@ -192,6 +192,14 @@ int ssd_prefill_matmul(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev, in
  * and the matvec_q4_0 / matvec_q8_0 / matvec_q4_k Metal kernels
  * (src/metal/shaders/kernels.metal:166-273, :575-604). */
 int ssd_matvec(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev, float* y_dev, void* stream);
+/* ssd_matvec for a series of matvecs that do not feed each other (the reference calls
+ * matvec_quantized, src/metal/compute.rs:157-191, once per matrix, each on inputs already in
+ * memory): the caller guarantees that no kernel enqueued before this call on the stream writes
+ * x_dev or touches y_dev. The kernel then streams its weights and x without waiting for its
+ * predecessor, so consecutive launches overlap; it waits for the predecessor at its end, so
+ * later kernels see everything before it completed. Results are identical to ssd_matvec. */
+int ssd_matvec_independent(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev, float* y_dev,
+                           void* stream);
 /* y = base + W x (base may alias y): matvec plus the residual add of
  * src/inference/transformer.rs:369-371. */
 int ssd_matvec_residual(ssd_ctx* ctx, const ssd_weight* w, const float* x_dev,

@@ -674,6 +674,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
     };
     if (!mv_prologue<NW * 32, EPI>(a, &tm_x, base + P.xs, nc, P.xrows, red, bar, rope_tab, finish)) {
         cp_wait<0>();
+        if (a.x_ready) pdl_wait();
         return;
     }
 
@@ -830,6 +831,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 16 ? 1 : 2)
             if (b) atomicMax(a.argmax_key, b);
         }
     }
+    if (a.x_ready) pdl_wait();  // an independent launch ends after its predecessor
 }
 
 // --------------------------------------------------------------- host side
@@ -1137,15 +1139,21 @@ int launch_matvec(ssd_ctx* ctx, int type, int epi, const MvArgs& a0, cudaStream_
     // (matvec_tc.cu). Batch 1 keeps the FMA kernel: a tcgen05.mma of M = 128 issues at
     // most once per ~93 cycles, so the tcgen05 kernel tops out near the Q4_0 HBM rate
     // (~44 weights per cycle per SM against ~41 needed) before its fixed costs.
+    SSD_REQ(!a.x_ready || (a.ar_in_n == 0 && epi != EPI_PEERS), SSD_ERR_ARG,
+            "an independent launch takes no peer partials");
     const char* impl = getenv("SSD_MV_IMPL");
     if (impl && strcmp(impl, "tc") == 0 &&
         (type == SSD_TYPE_Q4_0 || type == SSD_TYPE_Q8_0 ||
          (type == SSD_TYPE_Q4_K && a.cols % 256 == 0))) {
-        const int st = launch_matvec_tc(ctx, type, epi, a, s, pdl);
+        MvArgs t = a;
+        t.x_ready = 0;  // the other kernels always wait first
+        const int st = launch_matvec_tc(ctx, type, epi, t, s, pdl);
         if (st != kTcNotCovered) return st;
     }
     if (impl && strcmp(impl, "i8") == 0) {
-        const int st = launch_matvec_i8(ctx, type, epi, a, s, pdl);
+        MvArgs t = a;
+        t.x_ready = 0;
+        const int st = launch_matvec_i8(ctx, type, epi, t, s, pdl);
         if (st != kI8NotCovered) return st;
     }
     switch (type) {
@@ -1191,6 +1199,16 @@ extern "C" int ssd_matvec(ssd_ctx* ctx, const ssd_weight* w, const float* x, flo
     SSD_REQ(x && y, SSD_ERR_ARG, "null vector");
     MvArgs a = mv_plain(w, x, y);
     return launch_matvec(ctx, w->type, EPI_STORE, a, pick_stream(ctx, stream), ctx->pdl);
+}
+
+extern "C" int ssd_matvec_independent(ssd_ctx* ctx, const ssd_weight* w, const float* x,
+                                      float* y, void* stream) {
+    SSD_TRY(check_ctx(ctx));
+    SSD_TRY(check_w(w));
+    SSD_REQ(x && y, SSD_ERR_ARG, "null vector");
+    MvArgs a = mv_plain(w, x, y);
+    a.x_ready = 1;
+    return launch_matvec(ctx, w->type, EPI_STORE, a, pick_stream(ctx, stream), true);
 }
 
 extern "C" int ssd_matvec_residual(ssd_ctx* ctx, const ssd_weight* w, const float* x,

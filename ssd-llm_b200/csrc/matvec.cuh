@@ -34,6 +34,12 @@ struct MvArgs {
     const float* norm_w;
     float eps;
     int norm_order;
+    // Independent launch (FMA kernel): no kernel enqueued before this one writes x or the
+    // other inputs, or touches y; the kernel then does not wait for its predecessor before
+    // staging x (consecutive launches overlap) and waits at its end instead, so that its
+    // completion still implies the completion of everything before it. Other kernels ignore
+    // the flag (they always wait first).
+    int x_ready;
     // epilogue
     float* y;           // STORE/RESID/SWIGLU out, QKV q out, ARGMAX logits (may be null)
     const float* base;  // RESID base (may alias y)

@@ -184,7 +184,7 @@ __device__ __forceinline__ bool mv_prologue(const MvArgs& a, const CUtensorMap* 
         nwp[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (has_norm && tid + j * NTH < nunits) nwp[j] = __ldg(nw4 + tid + j * NTH);
     }
-    pdl_wait();
+    if (!a.x_ready) pdl_wait();
     if (tid == 0) {
         const int nbox = xrows / kVecBoxRows;
         mbar_expect_tx(bar, (uint32_t)xrows * 128u);

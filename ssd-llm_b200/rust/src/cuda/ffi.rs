@@ -667,4 +667,12 @@ extern "C" {
     pub fn ssd_stream_decode_token(s: *mut SsdStream, token_in: i32, token_out: *mut i32) -> c_int;
     pub fn ssd_stream_stats_get(s: *const SsdStream, out: *mut SsdStreamStats) -> c_int;
     pub fn ssd_stream_close(s: *mut SsdStream) -> c_int;
+
+    pub fn ssd_matvec_independent(
+        ctx: *mut SsdCtx,
+        w: *const SsdWeight,
+        x_dev: *const c_float,
+        y_dev: *mut c_float,
+        stream: *mut c_void,
+    ) -> c_int;
 }

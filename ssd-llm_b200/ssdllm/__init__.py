@@ -88,6 +88,7 @@ _SIGS = {
                      ctypes.c_int),
     "ssd_dequantize": ([_vp, _vp, _vp, _vp], ctypes.c_int),
     "ssd_matvec": ([_vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "ssd_matvec_independent": ([_vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ssd_matvec_residual": ([_vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ssd_fused_rmsnorm_matvec": ([_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp], ctypes.c_int),
     "ssd_fused_qkv_rope": ([_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_int,
@@ -327,6 +328,12 @@ class Weight:
 # ------------------------------------------------------- device-pointer ops
 def matvec(ctx, w: Weight, x, y):
     check(lib().ssd_matvec(ctx.h, w.h, _ptr(x), _ptr(y), _stream()))
+
+
+def matvec_independent(ctx, w: Weight, x, y):
+    """ssd_matvec for matvecs that do not feed each other: x is not written and y is not
+    touched by any kernel enqueued before it, so consecutive launches overlap."""
+    check(lib().ssd_matvec_independent(ctx.h, w.h, _ptr(x), _ptr(y), _stream()))
 
 
 def prefill_matmul(ctx, w: Weight, x, y):

@@ -118,6 +118,41 @@ def test_matvec_matches_oracle(ctx, wtype, rows, cols):
     assert parity(got, ref, exact), (rel_err(got, ref), rel_err(ref, exact), rel_err(got, exact))
 
 
+@pytest.mark.parametrize("wtype,rows,cols", [(ora.Q4_0, 4096, 4096), (ora.Q8_0, 1000, 2048),
+                                               (ora.Q4_K, 513, 1024)])
+def test_independent_matvecs_equal_ssd_matvec(ctx, wtype, rows, cols):
+    """ssd_matvec_independent: a series of launches that do not wait for each other gives
+    ssd_matvec's results bit for bit, and a dependent launch after the series sees every
+    one of them complete (each independent launch waits for its predecessor at its end)."""
+    rng = np.random.default_rng(rows + cols)
+    raws = [ora.quantize(randw(rng, rows, cols), wtype) for _ in range(6)]
+    ws = [ssdllm.Weight.upload(ctx, r, wtype, rows, cols) for r in raws]
+    x = d(rng.standard_normal(cols).astype(np.float32))
+    ref = []
+    for w in ws:
+        y = torch.zeros(rows, device=DEV)
+        ssdllm.matvec(ctx, w, x, y)
+        ref.append(y)
+    torch.cuda.synchronize()
+    ctx.set_pdl(True)
+    try:
+        ys = [torch.full((rows,), float("nan"), device=DEV) for _ in ws]
+        for w, y in zip(ws, ys):
+            ssdllm.matvec_independent(ctx, w, x, y)
+        # dependent: out = W0 x + ys[0], launched right after the series (PDL on)
+        out = torch.zeros(rows, device=DEV)
+        ssdllm.matvec_residual(ctx, ws[0], x, ys[0], out)
+        torch.cuda.synchronize()
+    finally:
+        ctx.set_pdl(False)
+    for y, r in zip(ys, ref):
+        assert torch.equal(y, r)
+    assert torch.allclose(out, ref[0] + ref[0], rtol=0, atol=0) or \
+        rel_err(out.cpu().numpy(), (ref[0] + ref[0]).cpu().numpy()) <= 1e-6
+    for w in ws:
+        w.free()
+
+
 def test_matvec_residual_and_fused_norm(ctx):
     rng = np.random.default_rng(3)
     rows, cols = 1000, 2048
