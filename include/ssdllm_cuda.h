@@ -376,10 +376,12 @@ int ssd_feed_forward_f32_host(ssd_ctx* ctx, const float* x, const float* w_gate,
  * tp_size > 1 needs ssd_model_tp_init before building. */
 typedef struct {
     int n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab;
-    int wtype;        /* layer weight type: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K or Q8_K; F16, BF16 or
-                         F32 at tp_size 1 */
+    int wtype;        /* layer weight type: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K or Q8_K; at tp_size 1
+                         also F16, BF16, F32 and the low-bit Q2_K, Q3_K, IQ4_NL, IQ4_XS,
+                         IQ3_XXS, IQ3_S, IQ2_XXS, IQ2_XS (decode step only: the batch
+                         prefill refuses low-bit weights) */
     int out_type;     /* output.weight type: as wtype */
-    int embd_type;    /* token_embd type: as wtype, or F32 / F16 / BF16 */
+    int embd_type;    /* token_embd type: Q4_0 .. Q8_K, or F32 / F16 / BF16 */
     int kv_capacity;  /* INT8 KV positions */
     float theta, eps;
     int tp_rank, tp_size;

@@ -868,7 +868,12 @@ static void* lmv_worker(void* p) {
         free(row);
     } else {
         row_fn fn = pick_row(j->wtype);
-        for (int r = j->r0; r < j->r1; r++) j->y[r] = fn(j->w, j->x, j->in_dim, r);
+        for (int r = j->r0; r < j->r1; r++) {
+            if (fn)
+                j->y[r] = fn(j->w, j->x, j->in_dim, r);
+            else  /* low-bit: the reference's matvec_*_cpu row (compute.rs:793-1075, 1964-2240) */
+                ora_row_lowbit(j->wtype, j->w, j->x, j->in_dim, r, &j->y[r]);
+        }
     }
     return NULL;
 }
@@ -904,8 +909,9 @@ int ora_layer_step(const ora_layer* L, float* hidden, int position, int8_t* k_ca
     int n = L->n_embd, hd = L->head_dim;
     int q_dim = L->n_head * hd, kv_dim = L->n_head_kv * hd, ff = L->n_ff;
     if (q_dim != n) return -1;
+    /* every type the row kernels or the low-bit row decoder read (ora_row_bytes > 0) */
     for (int i = 0; i < 7; i++)
-        if (!pick_row(layer_wtype(L, i))) return -1;
+        if (!pick_row(layer_wtype(L, i)) && ora_row_bytes(layer_wtype(L, i), 256) == 0) return -1;
     float* attn_in = (float*)malloc(sizeof(float) * (size_t)n);
     float* q = (float*)malloc(sizeof(float) * (size_t)q_dim);
     float* k = (float*)malloc(sizeof(float) * (size_t)kv_dim);

@@ -127,6 +127,14 @@ static int fill_rope_table(ssd_ctx* ctx, float2* t, int rows, int head_dim, floa
     return SSD_OK;
 }
 
+// act = silu(gate) * up per row (feed_forward.rs:31-39; the SwiGLU epilogue of the fused
+// matvecs, for weight types that have none).
+__global__ void k_swiglu_rows(const float* gate, const float* up, float* act, int n) {
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) act[i] = swiglu(gate[i], up[i]);
+}
+
 // RoPE on the q and k rows at the device-held position (the pair rotation of the fused
 // QKV epilogue, rope_f32_multi_head, compute.rs:482-506).
 __global__ void k_rope_qk(float* q, int q_rows, float* k, int k_rows, int head_dim, float theta,
@@ -185,6 +193,9 @@ __global__ void k_to16(const float* in, uint16_t* out, size_t n, int bf) {
 __host__ __device__ constexpr bool dense_type(int t) {
     return t == SSD_TYPE_F32 || t == SSD_TYPE_F16 || t == SSD_TYPE_BF16;
 }
+// Weight types whose matvec has no fused prologue or epilogue (dense, and the low-bit formats
+// of matvec_lowbit.cu): the decode engine runs their stages as separate launches (tp_size 1).
+__host__ __device__ constexpr bool staged_type(int t) { return dense_type(t) || is_lowbit(t); }
 }  // namespace ssd
 
 using namespace ssd;
@@ -219,6 +230,7 @@ struct ssd_model {
     unsigned long long* p2p_xch[kMaxPeers] = {};
     float* amax = nullptr;  // the (K, V) absmax pair max-reduced by NCCL (no peer path)
     float* xn = nullptr;    // normed input of the dense-weight stages
+    float* gu = nullptr;    // gate and up rows of the low-bit FFN stage
     float2* rope = nullptr;  // (cos, sin) of every RoPE pair at every cache position
     void* p2p_mapped[kMaxPeers] = {};
     bool p2p = false;
@@ -253,9 +265,9 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
                 c->n_embd % N == 0,
             SSD_ERR_SHAPE, "dimensions do not shard over %d ranks", N);
     const int bs = type_block(c->wtype);
-    SSD_REQ(((bs == 32 || bs == 256) && !is_lowbit(c->wtype)) || (dense_type(c->wtype) && N == 1),
+    SSD_REQ(((bs == 32 || bs == 256) && !is_lowbit(c->wtype)) || (staged_type(c->wtype) && N == 1),
             SSD_ERR_TYPE, "layer weight type %d not supported%s", c->wtype,
-            dense_type(c->wtype) ? " with tensor parallelism" : "");
+            staged_type(c->wtype) ? " with tensor parallelism" : "");
     SSD_REQ((c->n_embd / N) % bs == 0 && (c->n_ff / N) % bs == 0, SSD_ERR_SHAPE,
             "column shards must be whole %d-wide blocks", bs);
     SSD_REQ(c->embd_type == SSD_TYPE_F32 || c->embd_type == SSD_TYPE_Q4_0 ||
@@ -266,7 +278,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
             SSD_ERR_TYPE, "token_embd type %d not supported", c->embd_type);
     SSD_REQ(((type_block(c->out_type) == 32 || type_block(c->out_type) == 256) &&
              !is_lowbit(c->out_type)) ||
-                (dense_type(c->out_type) && N == 1),
+                (staged_type(c->out_type) && N == 1),
             SSD_ERR_TYPE, "output type %d not supported", c->out_type);
 
     ssd_model* m = new ssd_model();
@@ -299,7 +311,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     const size_t o_ha = take(E), o_hb = take(E), o_q = take(m->q_rows), o_k = take(m->kv_rows),
                  o_v = take(m->kv_rows), o_attn = take(m->q_rows), o_act = take(m->ff_local),
                  o_part = take(pf), o_p1 = take(E), o_p2 = take(E), o_log = take(m->vocab_local),
-                 o_misc = take(64), o_xn = take(E),
+                 o_misc = take(64), o_xn = take(E), o_gu = take(2 * (size_t)m->ff_local),
                  o_rope = take((size_t)c->kv_capacity * c->head_dim);
     if (cudaMalloc(&m->state, floats * 4) != cudaSuccess) {
         cudaGetLastError();
@@ -333,6 +345,7 @@ extern "C" int ssd_model_create(ssd_ctx* ctx, const ssd_model_config* c, ssd_mod
     m->ar_counter = reinterpret_cast<unsigned int*>(S + o_misc + 20);
     m->amax = S + o_misc + 24;
     m->xn = S + o_xn;
+    m->gu = S + o_gu;
     m->rope = reinterpret_cast<float2*>(S + o_rope);
     if (cudaHostAlloc(&m->pinned, 16, cudaHostAllocDefault) != cudaSuccess) {
         cudaGetLastError();
@@ -640,7 +653,8 @@ extern "C" int ssd_model_set_tensor_typed(ssd_model* m, const char* cname, int l
         SSD_REQ(ggml_type == SSD_TYPE_Q4_0 || ggml_type == SSD_TYPE_Q8_0 ||
                     ggml_type == SSD_TYPE_Q4_K || ggml_type == SSD_TYPE_Q5_K ||
                     ggml_type == SSD_TYPE_Q6_K || ggml_type == SSD_TYPE_Q8_K ||
-                    (dense_type(ggml_type) && (embd || tp_size(m) == 1)),
+                    (dense_type(ggml_type) && (embd || tp_size(m) == 1)) ||
+                    (is_lowbit(ggml_type) && !embd && tp_size(m) == 1),
                 SSD_ERR_TYPE, "%s: ggml type %d not supported here", cname, ggml_type);
         const int tb = type_block(ggml_type);
         SSD_REQ(s.cols % tb == 0 && s.col0 % tb == 0 && s.ncols % tb == 0, SSD_ERR_SHAPE,
@@ -859,8 +873,8 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
     // type (the reference dispatches every tensor on its dtype, compute.rs:648-675); a V of
     // another type than Q / K gets its own launch after them. Dense (F16 / BF16 / F32)
     // weights, at tp_size 1: norm, the three matvecs, RoPE at the device-held position.
-    if (dense_type(L.wq->type) || dense_type(L.wk->type) || dense_type(L.wv->type)) {
-        SSD_REQ(!tp && !pend.on, SSD_ERR_TYPE, "dense layer weights run at tp_size 1");
+    if (staged_type(L.wq->type) || staged_type(L.wk->type) || staged_type(L.wv->type)) {
+        SSD_REQ(!tp && !pend.on, SSD_ERR_TYPE, "dense / low-bit layer weights run at tp_size 1");
         k_dense_norm<<<1, 1024, 0, s>>>(h, L.attn_norm, c.n_embd, c.eps, 0, m->xn);
         SSD_CK_LAUNCH();
         const ssd_weight* ws[3] = {L.wq, L.wk, L.wv};
@@ -988,6 +1002,17 @@ static int enqueue_layer(ssd_model* m, int l, float*& h, Pending& pend, bool use
         g.y = m->act;
         SSD_TRY(launch_matvec(m->ctx, L.wg->type, EPI_SWIGLU, g, s, true));
         nl += 2;
+    } else if (is_lowbit(L.wg->type)) {  // low-bit: the FFN norm, gate, up, then SwiGLU
+        SSD_REQ(!tp && !pend.on, SSD_ERR_TYPE, "low-bit layer weights run at tp_size 1");
+        k_dense_norm<<<1, 1024, 0, s>>>(h, L.ffn_norm, c.n_embd, c.eps, 1, m->xn);
+        SSD_CK_LAUNCH();
+        float* gate = m->gu;
+        float* up = m->gu + m->ff_local;
+        SSD_TRY(launch_matvec(m->ctx, L.wg->type, EPI_STORE, mv_plain(L.wg, m->xn, gate), s, true));
+        SSD_TRY(launch_matvec(m->ctx, L.wu->type, EPI_STORE, mv_plain(L.wu, m->xn, up), s, true));
+        k_swiglu_rows<<<(m->ff_local + 255) / 256, 256, 0, s>>>(gate, up, m->act, m->ff_local);
+        SSD_CK_LAUNCH();
+        nl += 4;
     } else {
     MvArgs g = {};
     g.qs[0] = L.wg->qs;
@@ -1054,8 +1079,8 @@ static int enqueue_step(ssd_model* m, cudaStream_t s, int& nl, const LayerHooks*
         SSD_TRY(hk->release(hk->user, l, s));
     }
     // logits = output * rmsnorm(h) (eps 1e-5 hard-coded at compute.rs:566), argmax
-    if (dense_type(m->output->type)) {  // dense output (tp_size 1): norm, matvec, argmax key
-        SSD_REQ(!pend.on, SSD_ERR_TYPE, "dense output weight runs at tp_size 1");
+    if (staged_type(m->output->type)) {  // dense / low-bit output (tp_size 1): norm, matvec, key
+        SSD_REQ(!pend.on, SSD_ERR_TYPE, "dense / low-bit output weight runs at tp_size 1");
         k_dense_norm<<<1, 1024, 0, s>>>(h, m->out_norm, c.n_embd, 1e-5f, 1, m->xn);
         SSD_CK_LAUNCH();
         SSD_TRY(launch_matvec(m->ctx, m->output->type, EPI_STORE,
@@ -1249,6 +1274,13 @@ extern "C" int ssd_model_prefill(ssd_model* m, const int32_t* tokens, int n, int
     SSD_TRY(check_weights(m));
     const auto& c = m->cfg;
     SSD_REQ(tp_size(m) == 1, SSD_ERR_STATE, "batch prefill runs at tp_size 1");
+    for (const Layer& L : m->layers)
+        for (const ssd_weight* w : {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd})
+            SSD_REQ(!is_lowbit(w->type), SSD_ERR_TYPE,
+                    "batch prefill: low-bit layer weights (type %d) run in the decode step only",
+                    w->type);
+    SSD_REQ(!is_lowbit(m->output->type), SSD_ERR_TYPE,
+            "batch prefill: a low-bit output weight runs in the decode step only");
     SSD_REQ(n > 0 && n % 128 == 0, SSD_ERR_SHAPE, "prefill of %d tokens: a multiple of 128", n);
     const int E = c.n_embd, F = m->ff_local, NQ = m->q_rows + 2 * m->kv_rows;
     SSD_REQ(E % 128 == 0 && F % 128 == 0 && NQ % 128 == 0 && m->q_rows == E, SSD_ERR_SHAPE,
