@@ -565,7 +565,8 @@ typedef struct {
  * (token_embd if absent) into the model, and allocates the slots (each sized for the
  * largest layer's seven matrices in the library layout), two pinned staging buffers and a
  * copy stream. The model (from ssd_gguf_model_config of the same file, tp_size 1) must
- * not hold layer matrices of its own. SSD_ERR_NOMEM if the budget is below one layer. */
+ * not hold layer matrices of its own (SSD_ERR_STATE). SSD_ERR_NOMEM if the budget is below
+ * one layer. */
 int ssd_stream_open(ssd_model* m, const char* gguf_path, size_t hbm_budget, int lookahead,
                     ssd_stream** out);
 /* LayerCache::pin (src/model/cache.rs): loads the layer now if needed and never evicts it;

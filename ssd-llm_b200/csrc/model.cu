@@ -1159,6 +1159,11 @@ extern "C" int ssd_model_decode_token(ssd_model* m, int32_t token_in, int32_t* t
 
 namespace ssd {
 ssd_ctx* model_ctx(const ssd_model* m) { return m->ctx; }
+bool model_has_layer_matrices(const ssd_model* m) {
+    for (const Layer& L : m->layers)
+        if (L.wq || L.wk || L.wv || L.wo || L.wg || L.wu || L.wd) return true;
+    return false;
+}
 const ssd_model_config& model_cfg(const ssd_model* m) { return m->cfg; }
 
 int model_decode_token_hooked(ssd_model* m, int32_t token_in, int32_t* token_out,

@@ -22,6 +22,8 @@ struct LayerHooks {
 int model_decode_token_hooked(ssd_model* m, int32_t token_in, int32_t* token_out,
                               const LayerHooks& hk);
 ssd_ctx* model_ctx(const ssd_model* m);
+// True if any layer holds one of its seven matrices (set_tensor / synth / GGUF load).
+bool model_has_layer_matrices(const ssd_model* m);
 const ssd_model_config& model_cfg(const ssd_model* m);
 
 }  // namespace ssd

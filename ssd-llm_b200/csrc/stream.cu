@@ -239,6 +239,10 @@ extern "C" int ssd_stream_open(ssd_model* m, const char* gguf_path, size_t hbm_b
     SSD_TRY(check_ctx(ctx));
     const ssd_model_config& c = model_cfg(m);
     SSD_REQ(c.tp_size <= 1, SSD_ERR_ARG, "the streaming tier runs at tp_size 1");
+    // the step binds each layer's slot matrices for its enqueue only and leaves the layer
+    // empty: a model with matrices of its own would lose them
+    SSD_REQ(!model_has_layer_matrices(m), SSD_ERR_STATE,
+            "the model already holds layer matrices; the streaming tier supplies them");
     ssd_gguf* g = nullptr;
     SSD_TRY(ssd_gguf_open(gguf_path, &g));
     ssd_stream* S = new ssd_stream();
