@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: Llama-70B-shaped Q4_0 decode on N B200s.
+"""Benchmark: Llama-70B-shaped Q4_0 decode on N B200s (benchmark config 4).
 
 One step = one generated token (batch 1) through the whole model: token embedding,
 80 decoder layers (fused Q4_0 dequant-matvecs, INT8-KV flash-decode attention),
@@ -15,7 +15,7 @@ Reported on the same JSON line:
              graph, next token out (D2H), synchronised every step, timed on the host clock
   roofline   the dominant kernel (gate/up dequant-matvec + SwiGLU) timed alone on
              the model's own layer weights, algorithmic bytes / event time
-  kernels    BASELINE configs 0-2 one kernel at a time: Q4_0 4096x4096, Q8_0 / Q4_K at
+  kernels    benchmark configs 0-2 one kernel at a time: Q4_0 4096x4096, Q8_0 / Q4_K at
              11008x4096 and 4096x11008 (rotating weight copies > 2x L2), the INT8-KV
              attention at the 70B shape, and the Llama-2-7B-shaped layer step (GB/s,
              fraction of the measured HBM peak); `--case NAME` runs one of them alone
@@ -197,7 +197,7 @@ def cpu_token_time(cfg, layer_samples, threads):
 
 
 def cpu_case_baselines(threads):
-    """CPU baselines of the per-kernel cases: the oracle's C
+    """CPU baselines of the per-kernel cases (benchmark configs 0-2): the oracle's C
     restatement of the reference CPU paths on this host, 1 thread (the reference's own CPU
     paths are single-threaded) and all threads (its row split). Matvec configs: the
     restated matvec_quantized_cpu (src/metal/compute.rs:680-750, :904-925) on the case's
@@ -333,7 +333,7 @@ TYPE_NAMES = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K"}
 
 
 def case_matvec(ctx, torch, ssdllm, peak, wtype, rows, cols, reps=20):
-    """Dequant-matvec y = W x (BASELINE configs 0 and 1) over rotating weight copies
+    """Dequant-matvec y = W x (benchmark configs 0 and 1) over rotating weight copies
     whose total exceeds 2x L2, so every launch streams its weights from HBM; with and
     without programmatic dependent launch (PDL); the faster is reported. The variant
     `independent` times the same launches when none depends on the one before."""
@@ -461,7 +461,7 @@ def case_attention(ctx, torch, ssdllm, peak, n_head=64, n_head_kv=8, head_dim=12
 
 
 def case_layer_7b(ctx, torch, ssdllm, peak, n_layers=8, reps=10):
-    """Llama-2-7B-shaped decoder layer decode step (Q4_0, INT8 KV at
+    """benchmark config 2: Llama-2-7B-shaped decoder layer decode step (Q4_0, INT8 KV at
     2048 positions), timed as a CUDA-graph decode step of an n_layers-deep model with a
     256-token vocab (embed + logits add < 0.1% of the bytes); per layer = step / n_layers."""
     cfg = dict(n_layers=n_layers, n_embd=4096, n_head=32, n_head_kv=32, head_dim=128,
@@ -551,7 +551,7 @@ def case_layer_70b(ctx, torch, ssdllm, peak, n_layers=4, reps=10):
 
 
 def case_prefill_l3_8b(ctx, torch, ssdllm, peak, reps=3):
-    """layer-major batch prefill of 512 tokens through Llama-3-8B-shaped
+    """benchmark config 3: layer-major batch prefill of 512 tokens through Llama-3-8B-shaped
     layers (hidden 4096, 32 q / 8 kv heads, FFN 14336, Q4_K weights, RoPE theta 5e5, causal
     attention over the INT8 cache), then the vocab matvec (128256) and argmax of the last
     token. Models of 1 and 3 layers are timed (weight splits prepared by an untimed first
@@ -592,7 +592,7 @@ def case_prefill_l3_8b(ctx, torch, ssdllm, peak, reps=3):
 
 
 def measure_batch16(ctx, torch, ssdllm, model, cfg, peak, steps=6, warmup=2):
-    """BASELINE config 5, continuous batch 16: the 16 slots of ssdllm.Batch over the model's
+    """benchmark config 5, continuous batch 16: the 16 slots of ssdllm.Batch over the model's
     weights, every slot's INT8 cache filled to PROMPT positions, one graph-captured step =
     one token for each of the 16 slots (layer-major, the weights streamed once per step)."""
     import numpy as np
@@ -1072,7 +1072,7 @@ def main():
     ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
                     help="TP partial sums: in-kernel over NVLink peer memory, or ncclAllReduce")
     ap.add_argument("--no-kernels", action="store_true",
-                    help="skip the per-kernel table (BASELINE configs 0-2)")
+                    help="skip the per-kernel table (benchmark configs 0-2)")
     ap.add_argument("--case", default="",
                     help="run only kernel configuration(s) NAME[,NAME] or 'all': " +
                          ", ".join(CASES))

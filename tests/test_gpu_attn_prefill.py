@@ -41,7 +41,7 @@ def exact_attention(q, kd, vd, n_head, n_kv, hd):
 
 
 CASES = [  # n_head, n_kv, head_dim, pos0, n_q, V std, q std
-    (32, 8, 128, 0, 512, 1.0, 1.0),    # BASELINE config 3 shape (Llama-3-8B), fresh prompt
+    (32, 8, 128, 0, 512, 1.0, 1.0),    # benchmark config 3 shape (Llama-3-8B), fresh prompt
     (8, 2, 128, 100, 256, 1.0, 1.0),   # after 100 cached positions (blocks straddle tiles)
     (16, 16, 128, 0, 128, 1e-3, 1.0),  # no GQA; tiny V values (small V scales)
     (8, 2, 64, 7, 128, 1.0, 1.0),      # head_dim 64: the per-query kernels either way

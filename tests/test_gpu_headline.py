@@ -1,4 +1,4 @@
-"""Parity at the headline shapes of the benchmark (3 and 4).
+"""Parity at the headline shapes of the benchmark (benchmark configs 0, 3 and 4).
 
 * config 0 with its stated inputs: W ~ N(0, 0.02) fp32 from seed 0, Q4_0-quantized; x ~
   N(0, 1) from seed 1; y = W x against the oracle's matvec_q4_0_cpu restatement;

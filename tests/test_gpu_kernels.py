@@ -89,7 +89,7 @@ def test_weight_round_trip_and_dequant_bit_exact(ctx, wtype, rows, cols):
 
 # ---------------------------------------------------------------- matvec
 MATVEC_CASES = [
-    (ora.Q4_0, 4096, 4096),
+    (ora.Q4_0, 4096, 4096),   # benchmark config 0
     (ora.Q8_0, 11008, 4096),  # config 1 (gate/up)
     (ora.Q8_0, 4096, 11008),  # config 1 (down)
     (ora.Q4_K, 11008, 4096),

@@ -70,7 +70,7 @@ def read_cache(ctx, m, layer, n, kvd):
 @pytest.mark.parametrize("shape", ["small_gqa", "llama2_7b"])
 def test_layer_step_matches_oracle(ctx, shape):
     """One decoder layer at position P over an INT8 cache holding P positions
-    (BASELINE config 2 at full size: hidden 4096, 32 heads, FFN 11008, L = 2048)."""
+    (benchmark config 2 at full size: hidden 4096, 32 heads, FFN 11008, L = 2048)."""
     if shape == "small_gqa":
         E, nh, nkv, hd, F, P, theta = 512, 8, 2, 64, 1024, 77, 5e5
     else:
