@@ -59,6 +59,13 @@ def test_null_arguments_are_rejected_with_status():
     assert L.ssd_weight_free(None) == 0
     assert L.ssd_matvec(None, None, None, None, None) == 1
     assert b"null" in L.ssd_last_error()
+    assert L.ssd_matvec_independent(None, None, None, None, None) == 1
+    # streaming tier: null model / path / handle
+    assert L.ssd_stream_open(None, b"x.gguf", 1 << 30, 1, None) == 1
+    assert L.ssd_stream_close(None) == 0
+    assert L.ssd_stream_pin(None, 0) == 1
+    assert L.ssd_stream_decode_token(None, 0, None) == 1
+    assert L.ssd_stream_stats_get(None, None) == 1
 
 
 def test_context_creation_fails_loudly_without_gpu():
